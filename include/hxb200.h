@@ -1,0 +1,122 @@
+/* hxb200.h -- C ABI of the B200 (sm_100a) dispatch library.
+ *
+ * These are the dispatch-level entry points that replace the Hexagon HMX
+ * codegen path of RooflineAI/iree-hexagon-plugins for the dense matmul and
+ * attention dispatches. Every pointer argument is a device pointer (CUDA
+ * global memory of the current device) unless it says otherwise; `stream` is
+ * a cudaStream_t (NULL = legacy default stream). Calls are asynchronous on
+ * `stream`; argument errors are reported synchronously through the return
+ * status, device-side wait timeouts through hxb_device_status().
+ *
+ * Reference interfaces replaced (paths inside the reference project):
+ *   - the HMX microkernel ABI the compiler emits calls to,
+ *     plugins/runtime/hexagon/dsp/ukernel/hmx/api.h:22-67
+ *     (acc_clear / pack / mma / acc_read / unpack per 32x32 tile), driven by
+ *     the K-loop of plugins/compiler/hexagon/CodeGen/Transforms/
+ *     HexagonExpandHmxMatmul.cpp:286-331 -- collapsed here into one call per
+ *     linalg.matmul dispatch;
+ *   - the decomposed attention dispatches of
+ *     examples/attention_layer/attention_layer.mlir:17-111.
+ * No torch types appear anywhere in this ABI.
+ */
+#ifndef HXB200_H_
+#define HXB200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HXB_ABI_VERSION 1
+
+typedef enum hxb_status_e {
+  HXB_OK = 0,
+  HXB_STATUS_INVALID_ARGUMENT = 1,
+  HXB_STATUS_UNSUPPORTED = 2,
+  HXB_STATUS_CUDA_ERROR = 3,
+  HXB_STATUS_RESOURCE_EXHAUSTED = 4,
+  HXB_STATUS_DEVICE_TIMEOUT = 5,
+} hxb_status_t;
+
+typedef enum hxb_dtype_e {
+  HXB_DTYPE_F16 = 0,
+  HXB_DTYPE_F32 = 1,
+  HXB_DTYPE_I8 = 2,
+} hxb_dtype_t;
+
+/* Device status bits (hxb_device_status). */
+#define HXB_DEVICE_STATUS_TIMEOUT 1
+
+/* ABI version compiled into the library (HXB_ABI_VERSION). */
+int hxb_abi_version(void);
+
+/* Text of the last error returned on the calling thread. */
+const char* hxb_last_error_message(void);
+
+/* Reads the current device's status word (bits OR-ed in by kernels whose
+ * bounded waits gave up) and clears it if `clear` is non-zero. Synchronous. */
+hxb_status_t hxb_device_status(int clear, int* out_bits);
+
+/* f16 matmul dispatch: C[M,N] = A[M,K] . B (+ C_init), f32 accumulation.
+ *
+ * Replaces the HMX lowering of linalg.matmul (f16 x f16 -> f32 init, or f16
+ * out), i.e. the per-tile calls iree_hexagon_hmx_pack_f16 /
+ * pack_transposed_f16 / mma_f16 / acc_read_f16 / unpack_acc_f16_to_{f32,f16}
+ * (plugins/runtime/hexagon/dsp/ukernel/hmx/api.h:22-67) and the DPS init add
+ * of the unpack (hmx.c:334-336; HexagonConvertMatmulToHmx.cpp:603-607).
+ *
+ *   A       f16, row-major [M,K], leading dimension lda (elements)
+ *   B       f16, row-major [K,N] (transpose_b = 0) or [N,K] (transpose_b = 1,
+ *           the rhs-transposed matmul), leading dimension ldb
+ *   C_init  optional (NULL = zeros) addend of C's type and layout
+ *   C       row-major [M,N], dtype HXB_DTYPE_F16 or HXB_DTYPE_F32, ldc
+ *   workspace / workspace_bytes: device scratch for re-pitching operands
+ *           whose row pitch is not a multiple of 16 bytes (TMA requirement);
+ *           hxb_matmul_f16_workspace_bytes() tells how much. Pass NULL/0 when
+ *           it returns 0.
+ * M, N, K >= 1. Returns HXB_STATUS_INVALID_ARGUMENT for bad shapes/strides or
+ * a too-small workspace. */
+hxb_status_t hxb_matmul_f16(const void* A, int64_t lda, const void* B,
+                            int64_t ldb, int transpose_b, const void* C_init,
+                            void* C, int64_t ldc, hxb_dtype_t c_dtype,
+                            int64_t M, int64_t N, int64_t K, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
+size_t hxb_matmul_f16_workspace_bytes(const void* A, int64_t lda,
+                                      const void* B, int64_t ldb,
+                                      int transpose_b, int64_t M, int64_t N,
+                                      int64_t K);
+
+/* Weight-quantised matmul dispatch:
+ *   C[M,N] f16 = (A[M,K] f16 . W[K,N] int8) * scale[N] f16, f32 accumulation.
+ * The reference has no int8 path (ContractionStrategy.cpp:141 restricts HMX to
+ * f16); its semantics are those of the linalg the builder emits (sitofp
+ * i8->f32, extf scale->f32, mulf, f32 contraction, truncf). int8 -> f16 is
+ * exact, so the per-channel scale factors out of the K sum.
+ * M >= 1; M <= 16 is routed to the bandwidth-bound GEMV kernel. lda % 8 == 0,
+ * ldw % 16 == 0, ldc % 8 == 0 and 16-byte aligned A, W, C, scale. */
+hxb_status_t hxb_matmul_w8a16(const void* A, int64_t lda, const void* W,
+                              int64_t ldw, const void* scale, void* C,
+                              int64_t ldc, int64_t M, int64_t N, int64_t K,
+                              void* stream);
+
+/* Fused attention dispatch: O = softmax(scale * Q.K^T [+ causal mask]) . V,
+ * f32 softmax statistics, f16 in/out. Replaces the decomposed f32 dispatches
+ * of examples/attention_layer/attention_layer.mlir:17-111 (which scale Q and
+ * K^T by sqrt(scale) each; the product is the same scale) including its
+ * fully-masked-row rule (rows whose scores are all -inf produce 0,
+ * :86-103).
+ *   Q [BH, Sq, D], K/V [BH, Skv, D], O [BH, Sq, D], all contiguous f16.
+ * D must be 128. causal != 0 masks key j > query i + (Skv - Sq). */
+hxb_status_t hxb_attention_f16(const void* Q, const void* K, const void* V,
+                               void* O, int64_t BH, int64_t Sq, int64_t Skv,
+                               int64_t D, float scale, int causal,
+                               void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HXB200_H_ */

@@ -1,0 +1,13 @@
+"""B200 (sm_100a) implementation of the iree-hexagon-plugins hot path.
+
+The package directory holds the CUDA kernels and C ABI (csrc/, built into
+libhxb200.so by build.py) and the Python host mirror of the reference's
+plugin/operator surface. Because the directory name is not a Python
+identifier it is imported as `iree_hexagon_plugins_b200` through
+`__graft_entry__.load_package()`.
+"""
+from . import _native
+from ._native import HxbError
+from .dispatch import attention, device_status, matmul, matmul_w8a16
+
+__all__ = ["HxbError", "attention", "device_status", "matmul", "matmul_w8a16", "_native"]

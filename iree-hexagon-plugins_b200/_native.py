@@ -1,0 +1,82 @@
+"""ctypes binding of libhxb200.so, the C ABI declared in include/hxb200.h.
+
+Nothing here computes: every call goes to the CUDA library. If the library is
+missing or cannot be loaded the import fails loudly -- there is no CPU
+fallback anywhere in the product path.
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libhxb200.so"
+
+c_i64 = ctypes.c_int64
+c_int = ctypes.c_int
+c_vp = ctypes.c_void_p
+c_size = ctypes.c_size_t
+c_float = ctypes.c_float
+
+# name -> (restype, argtypes). Kept 1:1 with include/*.h; a test checks that
+# the library exports every function the headers declare.
+SIGNATURES: dict[str, tuple[object, list[object]]] = {
+    "hxb_abi_version": (c_int, []),
+    "hxb_last_error_message": (ctypes.c_char_p, []),
+    "hxb_device_status": (c_int, [c_int, ctypes.POINTER(c_int)]),
+    "hxb_matmul_f16": (c_int, [c_vp, c_i64, c_vp, c_i64, c_int, c_vp, c_vp, c_i64,
+                               c_int, c_i64, c_i64, c_i64, c_vp, c_size, c_vp]),
+    "hxb_matmul_f16_workspace_bytes": (c_size, [c_vp, c_i64, c_vp, c_i64, c_int,
+                                                c_i64, c_i64, c_i64]),
+    "hxb_matmul_w8a16": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_i64,
+                                 c_i64, c_i64, c_i64, c_vp]),
+    "hxb_attention_f16": (c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64,
+                                  c_i64, c_float, c_int, c_vp]),
+}
+
+STATUS_NAMES = {
+    0: "OK",
+    1: "INVALID_ARGUMENT",
+    2: "UNSUPPORTED",
+    3: "CUDA_ERROR",
+    4: "RESOURCE_EXHAUSTED",
+    5: "DEVICE_TIMEOUT",
+}
+
+DTYPE_F16, DTYPE_F32, DTYPE_I8 = 0, 1, 2
+
+
+class HxbError(RuntimeError):
+    """A non-OK status from the dispatch library."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{STATUS_NAMES.get(status, status)}: {message}")
+        self.status = status
+
+
+_lib: ctypes.CDLL | None = None
+
+
+def load(path: Path | None = None) -> ctypes.CDLL:
+    """Loads (once) and types the dispatch library."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    p = Path(path) if path else LIB_PATH
+    if not p.exists():
+        raise OSError(
+            f"{p} is missing: build it with `python iree-hexagon-plugins_b200/build.py` "
+            "(nvcc, sm_100a). There is no fallback implementation.")
+    lib = ctypes.CDLL(str(p))
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    if path is None:
+        _lib = lib
+    return lib
+
+
+def check(status: int) -> None:
+    if status != 0:
+        msg = load().hxb_last_error_message()
+        raise HxbError(status, msg.decode() if msg else "")

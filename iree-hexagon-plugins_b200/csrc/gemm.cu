@@ -1,0 +1,248 @@
+// Host launchers for the tcgen05 GEMM dispatches (f16 and int8-weight).
+#include <string.h>
+
+#include "gemm_sm100.cuh"
+#include "planner.h"
+#include "runtime_common.h"
+
+namespace hxb {
+
+namespace {
+
+template <int BN, int STAGES, int BMODE, int OUT>
+hxb_status_t launch_gemm(const DeviceInfo& dev, const CUtensorMap& tmA,
+                         const CUtensorMap& tmB, const GemmArgs& args,
+                         cudaStream_t stream) {
+  using L = GemmSmem<BN, STAGES, BMODE>;
+  auto kernel = gemm_sm100_kernel<BN, STAGES, BMODE, OUT>;
+  // Per-device attribute: set once per (device, instantiation).
+  static bool configured[64] = {};
+  if (!configured[dev.ordinal]) {
+    cudaError_t e = cudaFuncSetAttribute(
+        kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(gemm)");
+    configured[dev.ordinal] = true;
+  }
+  const int tiles = args.tiles_m * args.tiles_n;
+  const int grid = tiles < dev.num_sms ? tiles : dev.num_sms;
+  kernel<<<grid, GemmShape<BN, BMODE>::kThreads, L::kAlloc, stream>>>(tmA, tmB, args);
+  return cuda_status(cudaGetLastError(), "gemm launch");
+}
+
+template <int BMODE, int OUT>
+hxb_status_t launch_planned(const GemmPlan& plan, const DeviceInfo& dev,
+                            const CUtensorMap& tmA, const CUtensorMap& tmB,
+                            const GemmArgs& args, cudaStream_t stream) {
+  // Stage counts fill ~192 KB of shared memory per CTA.
+  if constexpr (BMODE == kBInt8RowMajorKN) {
+    switch (plan.block_n) {
+      case 256: return launch_gemm<256, 3, BMODE, OUT>(dev, tmA, tmB, args, stream);
+      case 128: return launch_gemm<128, 5, BMODE, OUT>(dev, tmA, tmB, args, stream);
+      default: break;
+    }
+  } else {
+    switch (plan.block_n) {
+      case 256: return launch_gemm<256, 4, BMODE, OUT>(dev, tmA, tmB, args, stream);
+      case 128: return launch_gemm<128, 6, BMODE, OUT>(dev, tmA, tmB, args, stream);
+      case 64: return launch_gemm<64, 8, BMODE, OUT>(dev, tmA, tmB, args, stream);
+      default: break;
+    }
+  }
+  return fail(HXB_STATUS_UNSUPPORTED, "no kernel for block_n=%d", plan.block_n);
+}
+
+int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
+
+// Bytes of re-pitched copy needed for an operand of `rows` x `cols` f16
+// elements whose pitch or base is not TMA-compatible (0 if it is).
+size_t repitch_bytes(const void* p, int64_t ld, int64_t rows, int64_t cols) {
+  if (aligned16(p) && (ld * 2) % 16 == 0) return 0;
+  return (size_t)(rows * round_up(cols, 8) * 2 + 256);
+}
+
+hxb_status_t make_a_map(CUtensorMap* m, const void* A, int64_t lda, int64_t M,
+                        int64_t K) {
+  const uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
+  const uint64_t strides[1] = {(uint64_t)lda * 2};
+  const uint32_t box[2] = {64, 128};
+  return encode_tensor_map(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, A, dims,
+                           strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+}  // namespace
+
+hxb_status_t gemm_f16_impl(const void* A, int64_t lda, const void* B,
+                           int64_t ldb, int transpose_b, const void* C_init,
+                           void* C, int64_t ldc, hxb_dtype_t c_dtype, int64_t M,
+                           int64_t N, int64_t K, void* workspace,
+                           size_t workspace_bytes, cudaStream_t stream) {
+  if (M < 1 || N < 1 || K < 1)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "matmul: M, N, K must be >= 1 (got %lld, %lld, %lld)",
+                (long long)M, (long long)N, (long long)K);
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "matmul: dimensions exceed 2^31-1");
+  if (!A || !B || !C) return fail(HXB_STATUS_INVALID_ARGUMENT, "matmul: null operand");
+  if (lda < K) return fail(HXB_STATUS_INVALID_ARGUMENT, "matmul: lda < K");
+  if (ldb < (transpose_b ? K : N)) return fail(HXB_STATUS_INVALID_ARGUMENT, "matmul: ldb too small");
+  if (ldc < N) return fail(HXB_STATUS_INVALID_ARGUMENT, "matmul: ldc < N");
+  if (c_dtype != HXB_DTYPE_F16 && c_dtype != HXB_DTYPE_F32)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "matmul: C dtype must be f16 or f32");
+
+  DeviceInfo* dev = nullptr;
+  hxb_status_t s = current_device(&dev);
+  if (s != HXB_OK) return s;
+
+  // Operands whose pitch breaks the 16-byte TMA stride rule are re-pitched
+  // into the workspace (the B200 counterpart of HMX's pack into padded tiles,
+  // hmx.c:60-92): a 2-D copy to an 8-element-aligned pitch. The tensor map
+  // keeps the true extent, so TMA zero-fills beyond it.
+  const int64_t b_rows = transpose_b ? N : K, b_cols = transpose_b ? K : N;
+  const size_t need_a = repitch_bytes(A, lda, M, K);
+  const size_t need_b = repitch_bytes(B, ldb, b_rows, b_cols);
+  if (need_a + need_b > 0) {
+    if (!workspace || workspace_bytes < need_a + need_b)
+      return fail(HXB_STATUS_INVALID_ARGUMENT,
+                  "matmul: operands need %zu bytes of workspace for re-pitching, got %zu",
+                  need_a + need_b, workspace_bytes);
+  }
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  if (ws) ws = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(ws) + 255) & ~uintptr_t(255));
+  if (need_a) {
+    const int64_t p = round_up(K, 8);
+    cudaError_t e = cudaMemcpy2DAsync(ws, p * 2, A, lda * 2, K * 2, M,
+                                      cudaMemcpyDeviceToDevice, stream);
+    if (e != cudaSuccess) return cuda_status(e, "re-pitch A");
+    A = ws;
+    lda = p;
+    ws += round_up(M * p * 2, 256);
+  }
+  if (need_b) {
+    const int64_t p = round_up(b_cols, 8);
+    cudaError_t e = cudaMemcpy2DAsync(ws, p * 2, B, ldb * 2, b_cols * 2, b_rows,
+                                      cudaMemcpyDeviceToDevice, stream);
+    if (e != cudaSuccess) return cuda_status(e, "re-pitch B");
+    B = ws;
+    ldb = p;
+  }
+
+  const int bmode = transpose_b ? kBF16RowMajorNK : kBF16RowMajorKN;
+  const GemmPlan plan = plan_gemm((int)M, (int)N, (int)K, bmode, dev->num_sms);
+
+  CUtensorMap tmA, tmB;
+  if ((s = make_a_map(&tmA, A, lda, M, K)) != HXB_OK) return s;
+  if (transpose_b) {
+    const uint64_t dims[2] = {(uint64_t)K, (uint64_t)N};
+    const uint64_t strides[1] = {(uint64_t)ldb * 2};
+    const uint32_t box[2] = {64, (uint32_t)plan.block_n};
+    s = encode_tensor_map(&tmB, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, B, dims,
+                          strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  } else {
+    const uint64_t dims[2] = {(uint64_t)N, (uint64_t)K};
+    const uint64_t strides[1] = {(uint64_t)ldb * 2};
+    const uint32_t box[2] = {64, 64};
+    s = encode_tensor_map(&tmB, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, B, dims,
+                          strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  }
+  if (s != HXB_OK) return s;
+
+  GemmArgs args{};
+  args.M = (int)M;
+  args.N = (int)N;
+  args.K = (int)K;
+  args.C = C;
+  args.ldc = ldc;
+  args.C_init = C_init;
+  args.scale = nullptr;
+  args.status = dev->status_word;
+  args.tiles_m = (int)((M + kBM - 1) / kBM);
+  args.tiles_n = (int)((N + plan.block_n - 1) / plan.block_n);
+  args.group_m = plan.group_m;
+  const int esz = c_dtype == HXB_DTYPE_F16 ? 2 : 4;
+  args.vec_ok = aligned16(C) && (ldc * esz) % 16 == 0 &&
+                (!C_init || aligned16(C_init));
+
+  if (c_dtype == HXB_DTYPE_F16) {
+    return transpose_b
+               ? launch_planned<kBF16RowMajorNK, kOutF16>(plan, *dev, tmA, tmB, args, stream)
+               : launch_planned<kBF16RowMajorKN, kOutF16>(plan, *dev, tmA, tmB, args, stream);
+  }
+  return transpose_b
+             ? launch_planned<kBF16RowMajorNK, kOutF32>(plan, *dev, tmA, tmB, args, stream)
+             : launch_planned<kBF16RowMajorKN, kOutF32>(plan, *dev, tmA, tmB, args, stream);
+}
+
+hxb_status_t gemm_w8_impl(const void* A, int64_t lda, const void* W,
+                          int64_t ldw, const void* scale, void* C, int64_t ldc,
+                          int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
+  DeviceInfo* dev = nullptr;
+  hxb_status_t s = current_device(&dev);
+  if (s != HXB_OK) return s;
+  const GemmPlan plan = plan_gemm((int)M, (int)N, (int)K, kBInt8RowMajorKN, dev->num_sms);
+  CUtensorMap tmA, tmB;
+  if ((s = make_a_map(&tmA, A, lda, M, K)) != HXB_OK) return s;
+  {
+    const uint64_t dims[2] = {(uint64_t)N, (uint64_t)K};
+    const uint64_t strides[1] = {(uint64_t)ldw};
+    const uint32_t box[2] = {(uint32_t)plan.block_n, 64};
+    s = encode_tensor_map(&tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, W, dims,
+                          strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (s != HXB_OK) return s;
+  }
+  GemmArgs args{};
+  args.M = (int)M;
+  args.N = (int)N;
+  args.K = (int)K;
+  args.C = C;
+  args.ldc = ldc;
+  args.C_init = nullptr;
+  args.scale = static_cast<const __half*>(scale);
+  args.status = dev->status_word;
+  args.tiles_m = (int)((M + kBM - 1) / kBM);
+  args.tiles_n = (int)((N + plan.block_n - 1) / plan.block_n);
+  args.group_m = plan.group_m;
+  args.vec_ok = aligned16(C) && (ldc * 2) % 16 == 0 && aligned16(scale);
+  return launch_planned<kBInt8RowMajorKN, kOutF16>(plan, *dev, tmA, tmB, args, stream);
+}
+
+}  // namespace hxb
+
+extern "C" size_t hxb_matmul_f16_workspace_bytes(const void* A, int64_t lda,
+                                                 const void* B, int64_t ldb,
+                                                 int transpose_b, int64_t M,
+                                                 int64_t N, int64_t K) {
+  const int64_t b_rows = transpose_b ? N : K, b_cols = transpose_b ? K : N;
+  return hxb::repitch_bytes(A, lda, M, K) + hxb::repitch_bytes(B, ldb, b_rows, b_cols);
+}
+
+extern "C" hxb_status_t hxb_matmul_f16(const void* A, int64_t lda, const void* B,
+                                       int64_t ldb, int transpose_b,
+                                       const void* C_init, void* C, int64_t ldc,
+                                       hxb_dtype_t c_dtype, int64_t M, int64_t N,
+                                       int64_t K, void* workspace,
+                                       size_t workspace_bytes, void* stream) {
+  return hxb::gemm_f16_impl(A, lda, B, ldb, transpose_b, C_init, C, ldc, c_dtype,
+                            M, N, K, workspace, workspace_bytes,
+                            static_cast<cudaStream_t>(stream));
+}
+
+extern "C" hxb_status_t hxb_matmul_w8a16(const void* A, int64_t lda, const void* W,
+                                         int64_t ldw, const void* scale, void* C,
+                                         int64_t ldc, int64_t M, int64_t N, int64_t K,
+                                         void* stream) {
+  using namespace hxb;
+  if (M < 1 || N < 1 || K < 1)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "matmul_w8a16: M, N, K must be >= 1");
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "matmul_w8a16: dimensions exceed 2^31-1");
+  if (!A || !W || !scale || !C)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "matmul_w8a16: null operand");
+  if (lda < K || ldw < N || ldc < N)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "matmul_w8a16: leading dimension too small");
+  if (lda % 8 || ldw % 16 || ldc % 8 || !aligned16(A) || !aligned16(W) ||
+      !aligned16(C) || !aligned16(scale))
+    return fail(HXB_STATUS_INVALID_ARGUMENT,
+                "matmul_w8a16: A/W/C/scale must be 16-byte aligned with lda%%8 == 0, "
+                "ldw%%16 == 0, ldc%%8 == 0");
+  return gemm_w8_impl(A, lda, W, ldw, scale, C, ldc, M, N, K,
+                      static_cast<cudaStream_t>(stream));
+}

@@ -1,0 +1,400 @@
+// Persistent, warp-specialised tcgen05 GEMM for sm_100a.
+//
+//   C[M,N] = A[M,K] . B  (+ C_init)            f16 x f16 -> f32 accumulate
+//   C[M,N] = (A[M,K] . W[K,N]) * scale[N]      f16 x int8 -> f32 accumulate
+//
+// This is the B200 form of the reference's HMX matmul lowering
+// (plugins/compiler/hexagon/CodeGen/Transforms/HexagonConvertMatmulToHmx.cpp:
+// 558-610 and HexagonExpandHmxMatmul.cpp:286-331): the VTCM double-buffered
+// DMA pipeline (HexagonPipelineVTCMTransfers.cpp) becomes a STAGES-deep ring of
+// shared-memory tiles fed by TMA and guarded by mbarriers, the 32x32 HMX
+// K-loop becomes 128xBNx16 tcgen05.mma instructions into a TMEM accumulator,
+// and hmx unpack (which adds into the destination, hmx.c:334-336) becomes the
+// TMEM -> register epilogue with an optional C_init add.
+//
+// Roles (one CTA per SM, persistent over output tiles):
+//   warp 0      TMA producer (one lane)
+//   warp 1      TMEM owner + MMA issuer (one lane)
+//   warps 2-5   epilogue: TMEM -> registers -> global (128 threads = 128 rows)
+//   warps 6-9   (int8 weights only) int8 -> f16 converters, shared -> shared
+// The accumulator is double-buffered in TMEM so the epilogue of tile t
+// overlaps the main loop of tile t+1.
+#pragma once
+
+#include "sm100.cuh"
+
+namespace hxb {
+
+// B operand forms.
+enum BMode : int {
+  kBF16RowMajorKN = 0,  // B[K,N] row-major f16 (MN-major operand)
+  kBF16RowMajorNK = 1,  // B[N,K] row-major f16, i.e. transposed RHS (K-major)
+  kBInt8RowMajorKN = 2  // W[K,N] row-major int8, dequantised in the main loop
+};
+
+enum OutMode : int { kOutF16 = 0, kOutF32 = 1 };
+
+struct GemmArgs {
+  int M, N, K;
+  void* C;             // output, row-major with leading dimension ldc
+  long long ldc;
+  const void* C_init;  // optional, same type/ld as C; added to the product
+  const __half* scale; // per-output-column scale (int8 weights only)
+  int* status;         // device status word (timeouts), may be null
+  int tiles_m, tiles_n;
+  int group_m;         // L2 raster: tiles walk GROUP_M rows of tiles at a time
+  int vec_ok;          // 1 if C/C_init rows allow 16-byte vector access
+};
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;  // 64 f16 = one 128-byte swizzle row
+
+template <int BN, int STAGES, int BMODE>
+struct GemmSmem {
+  static constexpr int kABytes = kBM * kBK * 2;        // 16 KB
+  static constexpr int kBBytes = BN * kBK * 2;         // f16 tile for the MMA
+  static constexpr int kB8Bytes = (BMODE == kBInt8RowMajorKN) ? BN * kBK : 0;
+  static constexpr int kOffA = 0;
+  static constexpr int kOffB = kOffA + STAGES * kABytes;
+  static constexpr int kOffB8 = kOffB + STAGES * kBBytes;
+  static constexpr int kOffBar = kOffB8 + STAGES * kB8Bytes;
+  // full[S], empty[S], conv[S], tfull[2], tempty[2], drain[1]
+  static constexpr int kNumBars = 3 * STAGES + 5;
+  static constexpr int kOffMisc = kOffBar + kNumBars * 8;
+  static constexpr int kBytes = kOffMisc + 16;
+  static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-B alignment
+};
+
+template <int BN, int BMODE>
+struct GemmShape {
+  static constexpr int kWarps = (BMODE == kBInt8RowMajorKN) ? 10 : 6;
+  static constexpr int kThreads = kWarps * 32;
+  static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
+};
+
+__device__ __forceinline__ void tile_coords(int t, const GemmArgs& a,
+                                            int& tm, int& tn) {
+  // Grouped raster: consecutive tiles sweep group_m tile-rows before moving
+  // to the next tile-column, so concurrently resident CTAs share A and B
+  // tiles in L2.
+  const int per_group = a.group_m * a.tiles_n;
+  const int g = t / per_group;
+  const int first_m = g * a.group_m;
+  const int gm = min(a.tiles_m - first_m, a.group_m);
+  const int r = t - g * per_group;
+  tm = first_m + r % gm;
+  tn = r / gm;
+}
+
+template <int BN, int STAGES, int BMODE, int OUT>
+__global__ void __launch_bounds__(GemmShape<BN, BMODE>::kThreads, 1)
+    gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
+                      const __grid_constant__ CUtensorMap tmB,
+                      const GemmArgs args) {
+  using L = GemmSmem<BN, STAGES, BMODE>;
+  constexpr int kTmemCols = GemmShape<BN, BMODE>::kTmemCols;
+  constexpr uint32_t kIdesc =
+      make_idesc_f16(kBM, BN, 0, BMODE == kBF16RowMajorNK ? 0 : 1);
+  constexpr uint32_t kTxBytes =
+      L::kABytes + (BMODE == kBInt8RowMajorKN ? L::kB8Bytes : L::kBBytes);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* conv = bars + 2 * STAGES;
+  uint64_t* tfull = bars + 3 * STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L::kOffMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_tiles = args.tiles_m * args.tiles_n;
+  const int num_kb = (args.K + kBK - 1) / kBK;
+  const FailState fs{abort_flag, args.status};
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+      mbar_init(&conv[s], 4);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      long long issued = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        int tm, tn;
+        tile_coords(t, args, tm, tn);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, fs)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full[stage], kTxBytes);
+          tma_load_2d(smem + L::kOffA + stage * L::kABytes, &tmA, &full[stage],
+                      kb * kBK, tm * kBM);
+          if constexpr (BMODE == kBF16RowMajorKN) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(smem + L::kOffB + stage * L::kBBytes + j * (kBK * 128),
+                          &tmB, &full[stage], tn * BN + 64 * j, kb * kBK);
+          } else if constexpr (BMODE == kBF16RowMajorNK) {
+            tma_load_2d(smem + L::kOffB + stage * L::kBBytes, &tmB, &full[stage],
+                        kb * kBK, tn * BN);
+          } else {
+            tma_load_2d(smem + L::kOffB8 + stage * L::kB8Bytes, &tmB,
+                        &full[stage], tn * BN, kb * kBK);
+          }
+          ++issued;
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      // Never leave the CTA with bulk copies still landing in its shared
+      // memory: wait for the last STAGES issues (already complete on the
+      // normal path).
+      const long long nd = issued < STAGES ? issued : STAGES;
+      for (long long i = 0; i < nd; ++i) {
+        const long long u = issued - 1 - i;
+        const int s = (int)(u % STAGES);
+        const uint32_t ph = (uint32_t)((u / STAGES) & 1);
+        // bounded even on the failure path
+        const unsigned long long t0 = globaltimer_ns();
+        while (!mbar_try_wait(&full[s], ph) &&
+               globaltimer_ns() - t0 < kWaitLimitNs) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int tl = 0;
+      bool ok = true;
+      bool issued_any = false;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++tl) {
+        const int acc = tl & 1;
+        const uint32_t acc_phase = (tl >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, fs)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          uint64_t* ready = (BMODE == kBInt8RowMajorKN) ? &conv[stage] : &full[stage];
+          if (!mbar_wait(ready, phase, fs)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + L::kOffA + stage * L::kABytes);
+          const uint32_t b_addr = smem_u32(smem + L::kOffB + stage * L::kBBytes);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t adesc =
+                make_smem_desc(a_addr + k * 32, 16, 1024, kLayoutSwizzle128);
+            uint64_t bdesc;
+            if (BMODE == kBF16RowMajorNK)
+              bdesc = make_smem_desc(b_addr + k * 32, 16, 1024, kLayoutSwizzle128);
+            else
+              bdesc = make_smem_desc(b_addr + k * 16 * 128, kBK * 128, 1024,
+                                     kLayoutSwizzle128);
+            umma_f16_ss(d_tmem, adesc, bdesc, kIdesc, (kb | k) != 0);
+          }
+          issued_any = true;
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (ok) umma_commit(&tfull[acc]);
+      }
+      if (!ok && issued_any) {
+        // Failure path: let every MMA already issued retire before TMEM is
+        // released.
+        umma_commit(drain);
+        const unsigned long long t0 = globaltimer_ns();
+        while (!mbar_try_wait(drain, 0) && globaltimer_ns() - t0 < kWaitLimitNs) {
+        }
+      }
+    }
+  } else if (warp < 6) {
+    // ------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int tl = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tl) {
+      int tm, tn;
+      tile_coords(t, args, tm, tn);
+      const int acc = tl & 1;
+      const uint32_t acc_phase = (tl >> 1) & 1;
+      const bool ready = mbar_wait(&tfull[acc], acc_phase, fs);
+      // tcgen05.ld is .sync.aligned: reconverge and agree before touching TMEM
+      if (!__all_sync(0xffffffffu, ready)) break;
+      tc_fence_after();
+      const int row = tm * kBM + q * 32 + lane;
+      const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_row + c, r);
+        tmem_wait_ld();
+        const int col0 = tn * BN + c;
+        if (row >= args.M || col0 >= args.N) continue;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        const bool full_chunk = args.vec_ok && (col0 + 32 <= args.N);
+        if constexpr (BMODE == kBInt8RowMajorKN) {
+          if (full_chunk) {
+            const uint4* sp = reinterpret_cast<const uint4*>(args.scale + col0);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              uint4 s4 = __ldg(sp + u);
+              const __half2* h = reinterpret_cast<const __half2*>(&s4);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                float2 f = __half22float2(h[e]);
+                v[u * 8 + 2 * e] *= f.x;
+                v[u * 8 + 2 * e + 1] *= f.y;
+              }
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < args.N) v[j] *= __half2float(args.scale[col0 + j]);
+          }
+        }
+        if constexpr (OUT == kOutF16) {
+          __half* crow = reinterpret_cast<__half*>(args.C) + (long long)row * args.ldc;
+          const __half* irow =
+              args.C_init ? reinterpret_cast<const __half*>(args.C_init) +
+                                (long long)row * args.ldc
+                          : nullptr;
+          if (full_chunk) {
+            if (irow) {
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                uint4 i4 = *reinterpret_cast<const uint4*>(irow + col0 + u * 8);
+                const __half2* h = reinterpret_cast<const __half2*>(&i4);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  float2 f = __half22float2(h[e]);
+                  v[u * 8 + 2 * e] += f.x;
+                  v[u * 8 + 2 * e + 1] += f.y;
+                }
+              }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              uint4 o;
+              o.x = pack_half2(v[u * 8 + 0], v[u * 8 + 1]);
+              o.y = pack_half2(v[u * 8 + 2], v[u * 8 + 3]);
+              o.z = pack_half2(v[u * 8 + 4], v[u * 8 + 5]);
+              o.w = pack_half2(v[u * 8 + 6], v[u * 8 + 7]);
+              *reinterpret_cast<uint4*>(crow + col0 + u * 8) = o;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (col0 + j < args.N) {
+                float x = v[j];
+                if (irow) x += __half2float(irow[col0 + j]);
+                crow[col0 + j] = __float2half_rn(x);
+              }
+            }
+          }
+        } else {
+          float* crow = reinterpret_cast<float*>(args.C) + (long long)row * args.ldc;
+          const float* irow =
+              args.C_init ? reinterpret_cast<const float*>(args.C_init) +
+                                (long long)row * args.ldc
+                          : nullptr;
+          if (full_chunk) {
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              float4 o = make_float4(v[u * 4], v[u * 4 + 1], v[u * 4 + 2], v[u * 4 + 3]);
+              if (irow) {
+                float4 i4 = *reinterpret_cast<const float4*>(irow + col0 + u * 4);
+                o.x += i4.x; o.y += i4.y; o.z += i4.z; o.w += i4.w;
+              }
+              *reinterpret_cast<float4*>(crow + col0 + u * 4) = o;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (col0 + j < args.N) {
+                float x = v[j];
+                if (irow) x += irow[col0 + j];
+                crow[col0 + j] = x;
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+  } else {
+    // ------------------------------------------------------ int8 -> f16
+    if constexpr (BMODE == kBInt8RowMajorKN) {
+      const int ct = threadIdx.x - 6 * 32;  // 0..127
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, fs)) { ok = false; break; }
+          const uint8_t* src = smem + L::kOffB8 + stage * L::kB8Bytes;
+          uint8_t* dst = smem + L::kOffB + stage * L::kBBytes;
+          constexpr int kUnitsPerRow = BN / 8;
+#pragma unroll 4
+          for (int w = ct; w < kBK * kUnitsPerRow; w += 128) {
+            const int k = w / kUnitsPerRow;
+            const int c8 = w - k * kUnitsPerRow;
+            const uint2 raw = *reinterpret_cast<const uint2*>(src + k * BN + c8 * 8);
+            uint4 o;
+            i8x4_to_f16x4(raw.x, o.x, o.y);
+            i8x4_to_f16x4(raw.y, o.z, o.w);
+            const int j = c8 >> 3, u = c8 & 7;
+            *reinterpret_cast<uint4*>(dst + j * (kBK * 128) + k * 128 +
+                                      ((u ^ (k & 7)) << 4)) = o;
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&conv[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace hxb

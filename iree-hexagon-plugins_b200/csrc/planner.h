@@ -1,0 +1,73 @@
+// Tile planner for the tcgen05 GEMM dispatches: the B200 counterpart of the
+// reference's HMX VTCM tile search (plugins/compiler/hexagon/CodeGen/Strategy/
+// Planning/VTCMPlanning.cpp:186-260). Where the reference enumerates
+// HMX-aligned divisors of M and N under a 2 MiB VTCM budget and ranks them by
+// (over budget, DDR<->VTCM traffic, #tiles, -N), this one enumerates the
+// tcgen05 tile widths whose shared-memory ring fits the 227 KB per-CTA budget
+// and ranks them by (estimated time on the persistent grid, traffic, -N).
+// Shapes measured by the offline sweep are answered from the baked table
+// first.
+#pragma once
+
+#include <stdint.h>
+
+namespace hxb {
+
+struct GemmPlan {
+  int block_n;  // N extent of one output tile (M extent is always 128)
+  int group_m;  // tile-rows per raster group (L2 reuse)
+};
+
+struct TunedGemm {
+  int M, N, K, bmode;
+  int block_n, group_m;
+};
+
+// Filled by the offline tile sweep (tile_table.inc); may be empty.
+extern const TunedGemm kTunedGemms[];
+extern const int kNumTunedGemms;
+
+// Cycles one SM spends on a 128 x bn x 16 tcgen05.mma: the tensor pipe does
+// 128x256x16 in 128 cycles; narrow tiles are bounded by shared-memory operand
+// reads (A 4 KB + B bn*32 B at 128 B/cycle).
+inline int64_t mma_cycles(int bn) {
+  const int64_t tensor = bn / 2;
+  const int64_t smem = (4096 + (int64_t)bn * 32) / 128;
+  return tensor > smem ? tensor : smem;
+}
+
+inline GemmPlan plan_gemm(int M, int N, int K, int bmode, int num_sms) {
+  for (int i = 0; i < kNumTunedGemms; ++i) {
+    const TunedGemm& t = kTunedGemms[i];
+    if (t.M == M && t.N == N && t.K == K && t.bmode == bmode)
+      return GemmPlan{t.block_n, t.group_m};
+  }
+  const int cands_f16[3] = {256, 128, 64};
+  const int cands_i8[2] = {256, 128};
+  const int* cands = bmode == 2 ? cands_i8 : cands_f16;
+  const int ncand = bmode == 2 ? 2 : 3;
+  const int64_t tiles_m = (M + 127) / 128;
+  const int64_t kb = (K + 63) / 64;
+  GemmPlan best{cands[0], 8};
+  int64_t best_cost = -1, best_traffic = -1;
+  for (int i = 0; i < ncand; ++i) {
+    const int bn = cands[i];
+    const int64_t tiles = tiles_m * ((N + bn - 1) / bn);
+    const int64_t waves = (tiles + num_sms - 1) / num_sms;
+    // Per tile: the K loop plus a fixed pipeline fill / drain.
+    const int64_t per_tile = kb * 4 * mma_cycles(bn) + 1500;
+    const int64_t cost = waves * per_tile;
+    // Operand bytes streamed from L2 per tile, summed over tiles.
+    const int64_t traffic = tiles * kb * (128 * 64 + (int64_t)bn * 64);
+    if (best_cost < 0 || cost < best_cost ||
+        (cost == best_cost && traffic < best_traffic)) {
+      best = GemmPlan{bn, 8};
+      best_cost = cost;
+      best_traffic = traffic;
+    }
+  }
+  if (best.group_m > tiles_m) best.group_m = (int)tiles_m;
+  return best;
+}
+
+}  // namespace hxb

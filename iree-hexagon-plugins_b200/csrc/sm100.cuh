@@ -1,0 +1,279 @@
+// sm_100a building blocks shared by the dispatch kernels: mbarriers with
+// bounded waits, TMA tile loads (no multicast, ever), tcgen05 MMA / TMEM
+// management and the shared-memory matrix descriptors the tensor core reads.
+//
+// These replace the Hexagon HMX primitives the reference lowers to
+// (plugins/runtime/hexagon/dsp/ukernel/hmx/api.h:22-67): there is no pack
+// step because TMA writes tiles straight into the 128B-swizzled layout that
+// tcgen05.mma consumes, and the accumulator lives in TMEM in f32 instead of
+// the HMX f16 read-out.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace hxb {
+
+// Every spin-wait in every kernel gives up after this long, records an error
+// in the caller-visible status word and lets the CTA wind down instead of
+// hanging the GPU. Legitimate waits inside one launch are microseconds.
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
+
+// Status bits written into the device status word on a failed wait.
+constexpr int kStatusTimeout = 1;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ---------------------------------------------------------------- mbarrier
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// Makes generic-proxy shared-memory writes visible to the async proxy (TMA
+// and the tensor core read shared memory through it).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar,
+                                                      uint32_t bytes) {
+  asm volatile(
+      "mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "r"(bytes)
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Per-CTA failure state: the first wait that times out raises `abort` in
+// shared memory (so every role of the CTA stops waiting) and ORs
+// kStatusTimeout into the launch's global status word.
+struct FailState {
+  volatile int* abort;  // shared memory
+  int* status;          // global memory, may be null
+};
+
+__device__ __forceinline__ void raise_failure(const FailState& fs) {
+  *fs.abort = 1;
+  if (fs.status) atomicOr(fs.status, kStatusTimeout);
+}
+
+// Waits for the phase of `bar` with parity `parity` to complete. Returns false
+// (after raising the failure state) when the wait exceeds kWaitLimitNs or when
+// another role of this CTA already gave up.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          const FailState& fs) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (*fs.abort) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      raise_failure(fs);
+      return false;
+    }
+  }
+}
+
+// --------------------------------------------------------------------- TMA
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+// 2-D tiled bulk tensor load into this CTA's shared memory; completion is
+// signalled as transaction bytes on `bar`. x is the innermost coordinate.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map,
+                                            uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_"
+      "tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map,
+                                            uint64_t* bar, int x, int y,
+                                            int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_"
+      "tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+// --------------------------------------------------------------- tcgen05
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile(
+      "tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+          smem_u32(dst_smem)),
+      "r"(ncols)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::
+                   : "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(
+                   taddr),
+               "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// D[tmem] (+)= A[smem desc] * B[smem desc], kind::f16 (f16 or bf16 inputs,
+// f32 accumulator). Issued by a single thread.
+__device__ __forceinline__ void umma_f16_ss(uint32_t d_tmem, uint64_t adesc,
+                                            uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives once on `bar` when every tcgen05.mma issued so far by this thread
+// has completed (and its shared-memory operands may be overwritten).
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
+      "[%0];" ::"r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Each thread of the warp reads 32 consecutive f32 columns of its own TMEM
+// lane (lane = warp's quarter * 32 + lane id).
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr,
+                                                   uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+      "%30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]),
+        "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]),
+        "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
+        "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr,
+                                                   uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]),
+        "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]),
+        "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15])
+      : "r"(taddr));
+}
+
+// Shared-memory matrix descriptor (tcgen05 "version 1" format):
+//   [0,14)  start address >> 4
+//   [16,30) leading-dimension byte offset >> 4
+//   [32,46) stride-dimension byte offset >> 4
+//   [46,48) version = 1
+//   [61,64) layout: 0 none, 2 = 128-byte swizzle
+// For a K-major 128B-swizzled operand the rows are 128 bytes of K and SBO is
+// the distance between 8-row groups; for an MN-major one the 128-byte rows run
+// along M/N, LBO steps between 64-element MN chunks and SBO between 8-row K
+// groups.
+constexpr uint32_t kLayoutSwizzle128 = 2;
+
+__device__ __forceinline__ uint64_t make_smem_desc(uint32_t saddr, uint32_t lbo,
+                                                   uint32_t sbo,
+                                                   uint32_t layout) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)(layout & 7u) << 61;
+  return d;
+}
+
+// Instruction descriptor for kind::f16 with f16 A/B and an f32 accumulator.
+// a_mn / b_mn select MN-major (transposed) operands.
+__host__ __device__ constexpr uint32_t make_idesc_f16(int M, int N, int a_mn,
+                                                      int b_mn) {
+  return (1u << 4)                              // D format f32
+         | (0u << 7) | (0u << 10)               // A, B format f16
+         | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16)  // majors
+         | ((uint32_t)(N >> 3) << 17)           // N / 8
+         | ((uint32_t)(M >> 4) << 24);          // M / 16
+}
+
+// --------------------------------------------------------------- numerics
+// Exact int8 -> f16 for four packed signed bytes: biasing to unsigned and
+// splicing each byte under the f16 exponent of 1024 gives 1024 + (b + 128)
+// exactly; subtracting 1152 leaves b. Produces {b0,b1} and {b2,b3}.
+__device__ __forceinline__ void i8x4_to_f16x4(uint32_t packed, uint32_t& lo,
+                                              uint32_t& hi) {
+  const uint32_t u = packed ^ 0x80808080u;
+  uint32_t a, b;
+  asm("prmt.b32 %0, %1, %2, 0x4140;" : "=r"(a) : "r"(u), "r"(0x64646464u));
+  asm("prmt.b32 %0, %1, %2, 0x4342;" : "=r"(b) : "r"(u), "r"(0x64646464u));
+  const uint32_t bias = 0x64806480u;  // {1152, 1152}
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(lo) : "r"(a), "r"(bias));
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(hi) : "r"(b), "r"(bias));
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float x, float y) {
+  __half2 h = __floats2half2_rn(x, y);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+}  // namespace hxb

@@ -1,0 +1,111 @@
+"""Tensor-level entry points over the C ABI, for tests, the bench and Python
+users that hold their buffers in torch.
+
+These mirror the dispatches the reference's integration models exercise
+(integration_tests/models/micro/*/model.py): torch.matmul on f16 operands,
+matmul with a transposed RHS, the int8-weight matmul of BASELINE configuration
+2 and F.scaled_dot_product_attention. torch provides device memory and the
+current stream only; the arithmetic runs in libhxb200.so.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _native
+from ._native import DTYPE_F16, DTYPE_F32, check
+
+
+def _stream_ptr(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _require(cond: bool, msg: str) -> None:
+    if not cond:
+        raise ValueError(msg)
+
+
+def _rowmajor_ld(t: torch.Tensor, name: str) -> int:
+    _require(t.dim() == 2, f"{name} must be 2-D")
+    _require(t.stride(1) == 1, f"{name} must have unit inner stride")
+    return max(t.stride(0), t.shape[1])
+
+
+def matmul(a: torch.Tensor, b: torch.Tensor, *, transpose_b: bool = False,
+           out_dtype: torch.dtype = torch.float16,
+           init: torch.Tensor | None = None,
+           out: torch.Tensor | None = None) -> torch.Tensor:
+    """C = a @ b (or a @ b.T when transpose_b) (+ init), f16 operands, f32
+    accumulation, f16 or f32 result. Semantics of linalg.matmul with a DPS
+    init (examples/matmul/matmul.mlir:2-12)."""
+    lib = _native.load()
+    _require(a.is_cuda and b.is_cuda, "operands must be CUDA tensors")
+    _require(a.dtype == torch.float16 and b.dtype == torch.float16, "operands must be f16")
+    _require(out_dtype in (torch.float16, torch.float32), "out_dtype must be f16 or f32")
+    M, K = a.shape
+    if transpose_b:
+        N, Kb = b.shape
+    else:
+        Kb, N = b.shape
+    _require(K == Kb, f"contraction mismatch {K} vs {Kb}")
+    lda, ldb = _rowmajor_ld(a, "a"), _rowmajor_ld(b, "b")
+    if out is None:
+        out = torch.empty((M, N), dtype=out_dtype, device=a.device)
+    ldc = _rowmajor_ld(out, "out")
+    if init is not None:
+        _require(init.dtype == out.dtype and init.shape == out.shape and
+                 init.stride() == out.stride(), "init must match out")
+    ws_bytes = lib.hxb_matmul_f16_workspace_bytes(a.data_ptr(), lda, b.data_ptr(), ldb,
+                                                  int(transpose_b), M, N, K)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=a.device) if ws_bytes else None
+    check(lib.hxb_matmul_f16(
+        a.data_ptr(), lda, b.data_ptr(), ldb, int(transpose_b),
+        init.data_ptr() if init is not None else None, out.data_ptr(), ldc,
+        DTYPE_F16 if out.dtype == torch.float16 else DTYPE_F32, M, N, K,
+        ws.data_ptr() if ws is not None else None, ws_bytes, _stream_ptr(a)))
+    return out
+
+
+def matmul_w8a16(a: torch.Tensor, w: torch.Tensor, scale: torch.Tensor,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """C[M,N] f16 = (a[M,K] f16 @ w[K,N] int8) * scale[N] f16, f32 accumulation."""
+    lib = _native.load()
+    _require(a.dtype == torch.float16 and w.dtype == torch.int8 and
+             scale.dtype == torch.float16, "dtypes must be f16 / int8 / f16")
+    M, K = a.shape
+    Kw, N = w.shape
+    _require(K == Kw and scale.numel() == N and scale.is_contiguous(), "shape mismatch")
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float16, device=a.device)
+    check(lib.hxb_matmul_w8a16(a.data_ptr(), _rowmajor_ld(a, "a"), w.data_ptr(),
+                               _rowmajor_ld(w, "w"), scale.data_ptr(), out.data_ptr(),
+                               _rowmajor_ld(out, "out"), M, N, K, _stream_ptr(a)))
+    return out
+
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
+              scale: float | None = None, causal: bool = False,
+              out: torch.Tensor | None = None) -> torch.Tensor:
+    """Fused scaled-dot-product attention over [..., S, D] f16 tensors."""
+    lib = _native.load()
+    _require(q.dtype == k.dtype == v.dtype == torch.float16, "q/k/v must be f16")
+    _require(q.is_contiguous() and k.is_contiguous() and v.is_contiguous(),
+             "q/k/v must be contiguous")
+    D = q.shape[-1]
+    Sq, Skv = q.shape[-2], k.shape[-2]
+    BH = q.numel() // (Sq * D)
+    _require(k.numel() // (Skv * D) == BH and v.shape == k.shape, "shape mismatch")
+    if scale is None:
+        scale = D ** -0.5
+    if out is None:
+        out = torch.empty_like(q)
+    check(lib.hxb_attention_f16(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                                BH, Sq, Skv, D, float(scale), int(causal), _stream_ptr(q)))
+    return out
+
+
+def device_status(clear: bool = True) -> int:
+    """Status bits kernels raised on the current device (1 = a wait timed out)."""
+    import ctypes
+    bits = ctypes.c_int(0)
+    check(_native.load().hxb_device_status(int(clear), ctypes.byref(bits)))
+    return bits.value

@@ -1,0 +1,85 @@
+"""The C ABI library loads and exports everything include/*.h declares.
+
+CPU-only: no call here reaches a GPU. Argument validation that happens
+before any device access is exercised too.
+"""
+from __future__ import annotations
+
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+REPO = Path(__file__).resolve().parent.parent
+INCLUDE = REPO / "include"
+
+
+def declared_functions() -> set[str]:
+    names = set()
+    for h in sorted(INCLUDE.glob("*.h")):
+        text = h.read_text()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        text = re.sub(r"//[^\n]*", "", text)
+        text = re.sub(r"#[^\n]*", "", text)
+        # typedef'd function pointer types are not exports
+        text = re.sub(r"typedef[^;]*;", "", text, flags=re.S)
+        for m in re.finditer(r"\b([A-Za-z_]\w*)\s*\(", text):
+            name = m.group(1)
+            if name in {"sizeof", "if", "while", "for", "return", "defined"}:
+                continue
+            names.add(name)
+    return names
+
+
+def exported_symbols(lib: Path) -> set[str]:
+    out = subprocess.run(["nm", "-D", "--defined-only", str(lib)], capture_output=True,
+                         text=True, check=True).stdout
+    return {line.split()[-1] for line in out.splitlines() if line.strip()}
+
+
+def test_headers_declare_functions():
+    names = declared_functions()
+    assert "hxb_matmul_f16" in names and "hxb_matmul_w8a16" in names
+    assert "hxb_attention_f16" in names
+
+
+def test_library_exports_every_declared_function(pkg):
+    lib_path = pkg._native.LIB_PATH
+    exported = exported_symbols(lib_path)
+    missing = sorted(declared_functions() - exported)
+    assert not missing, f"declared in include/*.h but not exported: {missing}"
+
+
+def test_python_binding_covers_every_declared_function(pkg):
+    missing = sorted(declared_functions() - set(pkg._native.SIGNATURES))
+    assert not missing, f"no ctypes signature for: {missing}"
+
+
+def test_abi_version(pkg):
+    assert pkg._native.load().hxb_abi_version() == 1
+
+
+def test_shape_validation_needs_no_device(pkg):
+    lib = pkg._native.load()
+    # M = 0 is rejected before any device access
+    st = lib.hxb_matmul_f16(None, 1, None, 1, 0, None, None, 1, 0, 0, 1, 1, None, 0, None)
+    assert st == 1
+    assert b"must be >= 1" in lib.hxb_last_error_message()
+    st = lib.hxb_matmul_w8a16(None, 1, None, 1, None, None, 1, 4, 4, 0, None)
+    assert st == 1
+
+
+def test_workspace_query_is_host_only(pkg):
+    lib = pkg._native.load()
+    # aligned pointers and pitches need no workspace
+    assert lib.hxb_matmul_f16_workspace_bytes(0x1000, 64, 0x2000, 64, 0, 64, 64, 64) == 0
+    # K = 23 (46-byte rows) breaks the 16-byte TMA pitch rule for A
+    need = lib.hxb_matmul_f16_workspace_bytes(0x1000, 23, 0x2000, 24, 0, 17, 19, 23)
+    assert need >= 17 * 24 * 2
+
+
+def test_no_cpu_fallback_when_library_missing(pkg, tmp_path):
+    with pytest.raises(OSError, match="no fallback"):
+        pkg._native.load(tmp_path / "libhxb200.so")

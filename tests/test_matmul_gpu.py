@@ -1,0 +1,148 @@
+"""Parity of the tcgen05 f16 matmul dispatch (through the C ABI) with the
+oracle and with the reference's golden micro-model outputs."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from _support import (baseline_check, compare, golden_expected, golden_inputs,
+                      golden_manifest, select_rows)
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+
+
+def _guarded_empty(shape, dtype, guard=4096):
+    """Output tensor inside a buffer with canary bands on both sides."""
+    n = int(np.prod(shape))
+    buf = torch.empty(n + 2 * guard, dtype=dtype, device=DEV)
+    buf.view(torch.int16 if dtype == torch.float16 else torch.int32).fill_(0x7E7E)
+    canary = buf.clone()
+    return buf[guard:guard + n].view(shape), buf, canary, guard
+
+
+def _check_canary(buf, canary, guard):
+    # compare bit patterns: the canary is a NaN pattern, and NaN != NaN
+    iv = torch.int16 if buf.dtype == torch.float16 else torch.int32
+    b, c = buf.view(iv), canary.view(iv)
+    assert torch.equal(b[:guard], c[:guard]), "write before the output buffer"
+    assert torch.equal(b[-guard:], c[-guard:]), "write past the output buffer"
+
+
+def test_hmx_known_answer_bit_exact(cuda_pkg, oracle):
+    """accumulator_test.c:14-42: exactly representable inputs, sparse weight;
+    single MMA and two accumulating MMAs (as matmul + init) must be exact."""
+    a, w, e1 = oracle.hmx_known_answer(1)
+    _, _, e2 = oracle.hmx_known_answer(2)
+    at, wt = torch.from_numpy(a).to(DEV), torch.from_numpy(w).to(DEV)
+    c1 = cuda_pkg.matmul(at, wt)
+    c2 = cuda_pkg.matmul(at, wt, init=c1.clone())
+    torch.cuda.synchronize()
+    assert np.array_equal(c1.cpu().numpy(), e1)
+    assert np.array_equal(c2.cpu().numpy(), e2)
+
+
+@pytest.mark.parametrize("M,N,K", [(1024, 1024, 1024), (128, 256, 64), (256, 512, 2048),
+                                   (4096, 4096, 1024), (300, 200, 100), (1, 8, 8)])
+@pytest.mark.parametrize("out", [torch.float16, torch.float32])
+def test_matmul_vs_oracle(cuda_pkg, oracle, M, N, K, out):
+    rng = np.random.default_rng(M * 7 + N * 3 + K)
+    a = rng.uniform(-1, 1, (M, K)).astype(np.float16)
+    b = rng.uniform(-1, 1, (K, N)).astype(np.float16)
+    c, buf, canary, guard = _guarded_empty((M, N), out)
+    cuda_pkg.matmul(torch.from_numpy(a).to(DEV), torch.from_numpy(b).to(DEV),
+                    out_dtype=out, out=c)
+    torch.cuda.synchronize()
+    _check_canary(buf, canary, guard)
+    baseline_check(oracle.matmul_f32(a, b), c.float().cpu().numpy(), f"{M}x{N}x{K}")
+    assert cuda_pkg.device_status() == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(1024, 1024, 1024), (17, 19, 23), (129, 257, 65)])
+def test_matmul_transposed_rhs_vs_oracle(cuda_pkg, oracle, M, N, K):
+    rng = np.random.default_rng(42)
+    a = rng.uniform(-1, 1, (M, K)).astype(np.float16)
+    bt = rng.uniform(-1, 1, (N, K)).astype(np.float16)
+    c = cuda_pkg.matmul(torch.from_numpy(a).to(DEV), torch.from_numpy(bt).to(DEV),
+                        transpose_b=True, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    baseline_check(oracle.matmul_f32(a, bt, transpose_b=True), c.cpu().numpy())
+
+
+@pytest.mark.parametrize("out", [torch.float16, torch.float32])
+def test_matmul_init_is_added(cuda_pkg, oracle, out):
+    """linalg.matmul accumulates into its DPS init (hmx.c:334-336)."""
+    rng = np.random.default_rng(9)
+    M, N, K = 200, 384, 320
+    a = rng.uniform(-1, 1, (M, K)).astype(np.float16)
+    b = rng.uniform(-1, 1, (K, N)).astype(np.float16)
+    init = rng.standard_normal((M, N)).astype(np.float16 if out == torch.float16 else np.float32)
+    c = cuda_pkg.matmul(torch.from_numpy(a).to(DEV), torch.from_numpy(b).to(DEV),
+                        out_dtype=out, init=torch.from_numpy(init).to(DEV))
+    torch.cuda.synchronize()
+    baseline_check(oracle.matmul_f32(a, b, init=init.astype(np.float32)),
+                   c.float().cpu().numpy())
+
+
+def _golden_matmul_keys():
+    return [k for k, e in golden_manifest().items() if "matmul" in e["model"]]
+
+
+@pytest.mark.parametrize("key", _golden_matmul_keys())
+def test_matmul_vs_reference_golden(cuda_pkg, oracle, key):
+    """The reference's micro models (integration_tests/models/micro/hmx/* and
+    matmul-1024x1024x1024-f16) under their own model.yaml tolerances, and the
+    BASELINE bar against the oracle."""
+    entry = golden_manifest()[key]
+    a, b = golden_inputs(key)
+    transposed = "rhs-transposed" in key
+    out = torch.float16 if entry["out_dtype"] == "float16" else torch.float32
+    ad, bd = a.to(DEV), b.to(DEV)
+    if a.dim() == 3:
+        got = torch.stack([cuda_pkg.matmul(ad[i], bd[i], out_dtype=out)
+                           for i in range(a.shape[0])])
+        ref = np.stack([oracle.matmul_f32(a[i].numpy(), b[i].numpy())
+                        for i in range(a.shape[0])])
+    else:
+        got = cuda_pkg.matmul(ad, bd, transpose_b=transposed, out_dtype=out)
+        ref = oracle.matmul_f32(a.numpy(), b.numpy(), transpose_b=transposed)
+    torch.cuda.synchronize()
+    got = got.cpu().numpy()
+    exp, rows = golden_expected(key)
+    tol = entry["tolerances"]
+    c = compare(exp, select_rows(got, rows), tol["atol"], tol["rtol"])
+    assert c.close, f"{key}: {c}"
+    assert c.rel_l2_percent <= tol["relative_l2_percent"], f"{key}: {c}"
+    baseline_check(ref, got.astype(np.float32), key)
+
+
+def test_matmul_strided_operands(cuda_pkg, oracle):
+    """Row pitches larger than the extent, including pitches that need the
+    re-pitch workspace (odd element counts)."""
+    rng = np.random.default_rng(4)
+    M, N, K = 70, 90, 110
+    abig = rng.uniform(-1, 1, (M, K + 5)).astype(np.float16)
+    bbig = rng.uniform(-1, 1, (K, N + 3)).astype(np.float16)
+    ad = torch.from_numpy(abig).to(DEV)[:, :K]
+    bd = torch.from_numpy(bbig).to(DEV)[:, :N]
+    c = cuda_pkg.matmul(ad, bd, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    baseline_check(oracle.matmul_f32(abig[:, :K], bbig[:, :N]), c.cpu().numpy())
+
+
+def test_bad_arguments_raise(cuda_pkg):
+    a = torch.zeros(4, 8, dtype=torch.float16, device=DEV)
+    b = torch.zeros(8, 4, dtype=torch.float16, device=DEV)
+    lib = cuda_pkg._native.load()
+    # ldc < N
+    st = lib.hxb_matmul_f16(a.data_ptr(), 8, b.data_ptr(), 4, 0, None, a.data_ptr(), 2, 0,
+                            4, 4, 8, None, 0, None)
+    assert st == 1
+    # workspace required but missing: ldb = 4 (8-byte rows) breaks the
+    # 16-byte TMA pitch rule, so B must be re-pitched
+    st = lib.hxb_matmul_f16(a.data_ptr(), 8, b.data_ptr(), 4, 0, None, a.data_ptr(), 4, 0,
+                            4, 4, 8, None, 0, None)
+    assert st == 1
+    assert b"workspace" in lib.hxb_last_error_message()
