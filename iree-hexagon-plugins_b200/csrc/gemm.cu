@@ -2,6 +2,8 @@
 #include <string.h>
 
 #include "gemm_sm100.cuh"
+#include "gemm_w8_sm100.cuh"
+#include "gemv_w8_sm100.cuh"
 #include "planner.h"
 #include "runtime_common.h"
 
@@ -29,15 +31,34 @@ hxb_status_t launch_gemm(const DeviceInfo& dev, const CUtensorMap& tmA,
   return cuda_status(cudaGetLastError(), "gemm launch");
 }
 
+template <int BN, int SA, int SW, int SB>
+hxb_status_t launch_w8(const DeviceInfo& dev, const CUtensorMap& tmA,
+                       const CUtensorMap& tmW, const GemmArgs& args,
+                       cudaStream_t stream) {
+  using L = W8Smem<BN, SA, SW, SB>;
+  auto kernel = gemm_w8_sm100_kernel<BN, SA, SW, SB>;
+  static bool configured[64] = {};
+  if (!configured[dev.ordinal]) {
+    cudaError_t e = cudaFuncSetAttribute(
+        kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(gemm_w8)");
+    configured[dev.ordinal] = true;
+  }
+  const int tiles = args.tiles_m * args.tiles_n;
+  const int grid = tiles < dev.num_sms ? tiles : dev.num_sms;
+  kernel<<<grid, L::kThreads, L::kAlloc, stream>>>(tmA, tmW, args);
+  return cuda_status(cudaGetLastError(), "gemm_w8 launch");
+}
+
 template <int BMODE, int OUT>
 hxb_status_t launch_planned(const GemmPlan& plan, const DeviceInfo& dev,
                             const CUtensorMap& tmA, const CUtensorMap& tmB,
                             const GemmArgs& args, cudaStream_t stream) {
-  // Stage counts fill ~192 KB of shared memory per CTA.
+  // Stage counts fill ~192-208 KB of shared memory per CTA.
   if constexpr (BMODE == kBInt8RowMajorKN) {
     switch (plan.block_n) {
-      case 256: return launch_gemm<256, 3, BMODE, OUT>(dev, tmA, tmB, args, stream);
-      case 128: return launch_gemm<128, 5, BMODE, OUT>(dev, tmA, tmB, args, stream);
+      case 256: return launch_w8<256, 4, 3, 3>(dev, tmA, tmB, args, stream);
+      case 128: return launch_w8<128, 6, 6, 3>(dev, tmA, tmB, args, stream);
       default: break;
     }
   } else {
@@ -171,6 +192,63 @@ hxb_status_t gemm_f16_impl(const void* A, int64_t lda, const void* B,
              : launch_planned<kBF16RowMajorKN, kOutF32>(plan, *dev, tmA, tmB, args, stream);
 }
 
+// M <= 16: cluster split-K GEMV (HBM-bound weight stream).
+hxb_status_t gemv_w8_impl(const void* A, int64_t lda, const void* W, int64_t ldw,
+                          const void* scale, void* C, int64_t ldc, int64_t M,
+                          int64_t N, int64_t K, cudaStream_t stream) {
+  constexpr int SW = 6;
+  using L = GemvSmem<SW>;
+  DeviceInfo* dev = nullptr;
+  hxb_status_t s = current_device(&dev);
+  if (s != HXB_OK) return s;
+  CUtensorMap tmX, tmW;
+  {
+    const uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
+    const uint64_t strides[1] = {(uint64_t)lda * 2};
+    const uint32_t box[2] = {64, (uint32_t)kGemvRows};
+    if ((s = encode_tensor_map(&tmX, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, A, dims, strides,
+                               box, CU_TENSOR_MAP_SWIZZLE_128B)) != HXB_OK)
+      return s;
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)N, (uint64_t)K};
+    const uint64_t strides[1] = {(uint64_t)ldw};
+    const uint32_t box[2] = {(uint32_t)kGemvBN, 64};
+    if ((s = encode_tensor_map(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, W, dims, strides,
+                               box, CU_TENSOR_MAP_SWIZZLE_NONE)) != HXB_OK)
+      return s;
+  }
+  GemmArgs args{};
+  args.M = (int)M;
+  args.N = (int)N;
+  args.K = (int)K;
+  args.C = C;
+  args.ldc = ldc;
+  args.scale = static_cast<const __half*>(scale);
+  args.status = dev->status_word;
+  auto kernel = gemv_w8_sm100_kernel<SW>;
+  static bool configured[64] = {};
+  if (!configured[dev->ordinal]) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         L::kAlloc);
+    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(gemv_w8)");
+    configured[dev->ordinal] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((N + kGemvBN - 1) / kGemvBN), kGemvKSplit, 1);
+  cfg.blockDim = dim3(L::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = L::kAlloc;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = kGemvKSplit;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, kernel, tmX, tmW, args), "gemv_w8 launch");
+}
+
 hxb_status_t gemm_w8_impl(const void* A, int64_t lda, const void* W,
                           int64_t ldw, const void* scale, void* C, int64_t ldc,
                           int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
@@ -243,6 +321,9 @@ extern "C" hxb_status_t hxb_matmul_w8a16(const void* A, int64_t lda, const void*
     return fail(HXB_STATUS_INVALID_ARGUMENT,
                 "matmul_w8a16: A/W/C/scale must be 16-byte aligned with lda%%8 == 0, "
                 "ldw%%16 == 0, ldc%%8 == 0");
+  if (M <= hxb::kGemvRows)
+    return gemv_w8_impl(A, lda, W, ldw, scale, C, ldc, M, N, K,
+                        static_cast<cudaStream_t>(stream));
   return gemm_w8_impl(A, lda, W, ldw, scale, C, ldc, M, N, K,
                       static_cast<cudaStream_t>(stream));
 }

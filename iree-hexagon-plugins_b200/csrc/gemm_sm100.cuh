@@ -86,6 +86,125 @@ __device__ __forceinline__ void tile_coords(int t, const GemmArgs& a,
   tn = r / gm;
 }
 
+// Stores the 16 f16 values converted from int8 bytes [16*c16, 16*c16+16) of
+// weight row k into an MN-major, 128B-swizzled operand tile whose 64-column
+// chunks are kBK*128 bytes apart. The two 16-byte halves go to swizzle slots
+// u0^(k&7) and (u0+1)^(k&7); lanes of odd chunks store them in the opposite
+// order so that each 8-lane phase of a 128-bit shared store hits 8 distinct
+// slots (one wavefront) when 8 consecutive lanes cover c16 = 0..7 of a row.
+__device__ __forceinline__ void store_swizzled_pair(uint8_t* dst, int c16, int k,
+                                                    const uint4& o0, const uint4& o1) {
+  const int u0 = (c16 & 3) * 2;
+  uint8_t* row = dst + (c16 >> 2) * (kBK * 128) + k * 128;
+  uint4* p0 = reinterpret_cast<uint4*>(row + ((u0 ^ (k & 7)) << 4));
+  uint4* p1 = reinterpret_cast<uint4*>(row + (((u0 + 1) ^ (k & 7)) << 4));
+  if ((c16 >> 2) & 1) {
+    *p1 = o1;
+    *p0 = o0;
+  } else {
+    *p0 = o0;
+    *p1 = o1;
+  }
+}
+
+// Epilogue for one 32-column chunk of one output row: optional per-column
+// scale (int8 weights), optional C_init add, conversion and store. `r` holds
+// the f32 accumulator bits read from TMEM.
+template <bool SCALED, int OUT>
+__device__ __forceinline__ void store_chunk(const GemmArgs& args, int row,
+                                            int col0, const uint32_t (&r)[32]) {
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+  const bool full_chunk = args.vec_ok && (col0 + 32 <= args.N);
+  if constexpr (SCALED) {
+    if (full_chunk) {
+      const uint4* sp = reinterpret_cast<const uint4*>(args.scale + col0);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        uint4 s4 = __ldg(sp + u);
+        const __half2* h = reinterpret_cast<const __half2*>(&s4);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float2 f = __half22float2(h[e]);
+          v[u * 8 + 2 * e] *= f.x;
+          v[u * 8 + 2 * e + 1] *= f.y;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < args.N) v[j] *= __half2float(args.scale[col0 + j]);
+    }
+  }
+  if constexpr (OUT == kOutF16) {
+    __half* crow = reinterpret_cast<__half*>(args.C) + (long long)row * args.ldc;
+    const __half* irow =
+        args.C_init ? reinterpret_cast<const __half*>(args.C_init) +
+                          (long long)row * args.ldc
+                    : nullptr;
+    if (full_chunk) {
+      if (irow) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          uint4 i4 = *reinterpret_cast<const uint4*>(irow + col0 + u * 8);
+          const __half2* h = reinterpret_cast<const __half2*>(&i4);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float2 f = __half22float2(h[e]);
+            v[u * 8 + 2 * e] += f.x;
+            v[u * 8 + 2 * e + 1] += f.y;
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        uint4 o;
+        o.x = pack_half2(v[u * 8 + 0], v[u * 8 + 1]);
+        o.y = pack_half2(v[u * 8 + 2], v[u * 8 + 3]);
+        o.z = pack_half2(v[u * 8 + 4], v[u * 8 + 5]);
+        o.w = pack_half2(v[u * 8 + 6], v[u * 8 + 7]);
+        *reinterpret_cast<uint4*>(crow + col0 + u * 8) = o;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (col0 + j < args.N) {
+          float x = v[j];
+          if (irow) x += __half2float(irow[col0 + j]);
+          crow[col0 + j] = __float2half_rn(x);
+        }
+      }
+    }
+  } else {
+    float* crow = reinterpret_cast<float*>(args.C) + (long long)row * args.ldc;
+    const float* irow =
+        args.C_init ? reinterpret_cast<const float*>(args.C_init) +
+                          (long long)row * args.ldc
+                    : nullptr;
+    if (full_chunk) {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        float4 o = make_float4(v[u * 4], v[u * 4 + 1], v[u * 4 + 2], v[u * 4 + 3]);
+        if (irow) {
+          float4 i4 = *reinterpret_cast<const float4*>(irow + col0 + u * 4);
+          o.x += i4.x; o.y += i4.y; o.z += i4.z; o.w += i4.w;
+        }
+        *reinterpret_cast<float4*>(crow + col0 + u * 4) = o;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (col0 + j < args.N) {
+          float x = v[j];
+          if (irow) x += irow[col0 + j];
+          crow[col0 + j] = x;
+        }
+      }
+    }
+  }
+}
+
 template <int BN, int STAGES, int BMODE, int OUT>
 __global__ void __launch_bounds__(GemmShape<BN, BMODE>::kThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
@@ -259,96 +378,7 @@ __global__ void __launch_bounds__(GemmShape<BN, BMODE>::kThreads, 1)
         tmem_wait_ld();
         const int col0 = tn * BN + c;
         if (row >= args.M || col0 >= args.N) continue;
-        float v[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-        const bool full_chunk = args.vec_ok && (col0 + 32 <= args.N);
-        if constexpr (BMODE == kBInt8RowMajorKN) {
-          if (full_chunk) {
-            const uint4* sp = reinterpret_cast<const uint4*>(args.scale + col0);
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              uint4 s4 = __ldg(sp + u);
-              const __half2* h = reinterpret_cast<const __half2*>(&s4);
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                float2 f = __half22float2(h[e]);
-                v[u * 8 + 2 * e] *= f.x;
-                v[u * 8 + 2 * e + 1] *= f.y;
-              }
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (col0 + j < args.N) v[j] *= __half2float(args.scale[col0 + j]);
-          }
-        }
-        if constexpr (OUT == kOutF16) {
-          __half* crow = reinterpret_cast<__half*>(args.C) + (long long)row * args.ldc;
-          const __half* irow =
-              args.C_init ? reinterpret_cast<const __half*>(args.C_init) +
-                                (long long)row * args.ldc
-                          : nullptr;
-          if (full_chunk) {
-            if (irow) {
-#pragma unroll
-              for (int u = 0; u < 4; ++u) {
-                uint4 i4 = *reinterpret_cast<const uint4*>(irow + col0 + u * 8);
-                const __half2* h = reinterpret_cast<const __half2*>(&i4);
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  float2 f = __half22float2(h[e]);
-                  v[u * 8 + 2 * e] += f.x;
-                  v[u * 8 + 2 * e + 1] += f.y;
-                }
-              }
-            }
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              uint4 o;
-              o.x = pack_half2(v[u * 8 + 0], v[u * 8 + 1]);
-              o.y = pack_half2(v[u * 8 + 2], v[u * 8 + 3]);
-              o.z = pack_half2(v[u * 8 + 4], v[u * 8 + 5]);
-              o.w = pack_half2(v[u * 8 + 6], v[u * 8 + 7]);
-              *reinterpret_cast<uint4*>(crow + col0 + u * 8) = o;
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if (col0 + j < args.N) {
-                float x = v[j];
-                if (irow) x += __half2float(irow[col0 + j]);
-                crow[col0 + j] = __float2half_rn(x);
-              }
-            }
-          }
-        } else {
-          float* crow = reinterpret_cast<float*>(args.C) + (long long)row * args.ldc;
-          const float* irow =
-              args.C_init ? reinterpret_cast<const float*>(args.C_init) +
-                                (long long)row * args.ldc
-                          : nullptr;
-          if (full_chunk) {
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-              float4 o = make_float4(v[u * 4], v[u * 4 + 1], v[u * 4 + 2], v[u * 4 + 3]);
-              if (irow) {
-                float4 i4 = *reinterpret_cast<const float4*>(irow + col0 + u * 4);
-                o.x += i4.x; o.y += i4.y; o.z += i4.z; o.w += i4.w;
-              }
-              *reinterpret_cast<float4*>(crow + col0 + u * 4) = o;
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if (col0 + j < args.N) {
-                float x = v[j];
-                if (irow) x += irow[col0 + j];
-                crow[col0 + j] = x;
-              }
-            }
-          }
-        }
+        store_chunk<BMODE == kBInt8RowMajorKN, OUT>(args, row, col0, r);
       }
       tc_fence_before();
       __syncwarp();

@@ -8,7 +8,7 @@
 #include <stddef.h>
 #include <stdint.h>
 
-#include "../../include/hxb200.h"
+#include "hxb200.h"
 
 namespace hxb {
 

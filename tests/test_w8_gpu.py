@@ -22,7 +22,8 @@ def _inputs(M, K, N, seed=0):
 
 
 @pytest.mark.parametrize("M,K,N", [(256, 4096, 11008), (1, 4096, 11008), (16, 4096, 11008),
-                                   (200, 320, 520), (5, 64, 48), (129, 1000, 264)])
+                                   (200, 320, 528), (5, 64, 48), (129, 1000, 272),
+                                   (16, 200, 4112), (3, 4104, 96)])
 def test_w8a16_vs_oracle(cuda_pkg, oracle, M, K, N):
     a, w, s = _inputs(M, K, N, seed=M + N)
     c = cuda_pkg.matmul_w8a16(torch.from_numpy(a).to(DEV), torch.from_numpy(w).to(DEV),
@@ -68,3 +69,12 @@ def test_w8a16_exact_dequant_index_math(cuda_pkg):
     torch.cuda.synchronize()
     want = (w[ks].astype(np.float32) * s.astype(np.float32)).astype(np.float16)
     assert np.array_equal(c.cpu().numpy(), want)
+
+
+def test_w8a16_rejects_unaligned_weight_pitch(cuda_pkg):
+    """int8 weight rows must be a multiple of 16 bytes (TMA pitch rule)."""
+    a = torch.zeros(4, 64, dtype=torch.float16, device=DEV)
+    w = torch.zeros(64, 520, dtype=torch.int8, device=DEV)
+    s = torch.ones(520, dtype=torch.float16, device=DEV)
+    with pytest.raises(cuda_pkg.HxbError, match="ldw%16"):
+        cuda_pkg.matmul_w8a16(a, w, s)
