@@ -89,6 +89,30 @@ size_t hxb_matmul_f16_workspace_bytes(const void* A, int64_t lda,
                                       int transpose_b, int64_t M, int64_t N,
                                       int64_t K);
 
+/* Size of the scratch array built into the library for
+ * hxb_matmul_f16_noalloc (bytes, per device). */
+#define HXB_NOALLOC_SCRATCH_BYTES (32u << 20)
+
+/* hxb_matmul_f16 for callers that cannot allocate device memory. This entry
+ * point has no counterpart in the reference; it exists for callers that hold
+ * only the buffers they were handed -- a compiled dispatch function, which
+ * gets its bindings and push constants from the runtime and has no allocator,
+ * or code recording a CUDA stream capture, where cudaMalloc is not allowed.
+ * Same arguments and results as hxb_matmul_f16 minus the workspace: operands
+ * whose row pitch breaks the 16-byte TMA rule are re-pitched into a scratch
+ * array that lives in the library image, HXB_NOALLOC_SCRATCH_BYTES on every
+ * GPU that loads the library, held until the process exits. Operands that
+ * need more re-pitch scratch than that are rejected with
+ * HXB_STATUS_INVALID_ARGUMENT. The call allocates nothing. Its first call on a
+ * device resolves the scratch's device address (make it before any stream
+ * capture). All calls on a device share the scratch and leave their data in
+ * it, so calls that overlap on the GPU race: order them on one stream. */
+hxb_status_t hxb_matmul_f16_noalloc(const void* A, int64_t lda, const void* B,
+                                    int64_t ldb, int transpose_b,
+                                    const void* C_init, void* C, int64_t ldc,
+                                    hxb_dtype_t c_dtype, int64_t M, int64_t N,
+                                    int64_t K, void* stream);
+
 /* Weight-quantised matmul dispatch:
  *   C[M,N] f16 = (A[M,K] f16 . W[K,N] int8) * scale[N] f16, f32 accumulation.
  * The reference has no int8 path (ContractionStrategy.cpp:141 restricts HMX to

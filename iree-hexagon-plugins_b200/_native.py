@@ -27,6 +27,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                c_int, c_i64, c_i64, c_i64, c_vp, c_size, c_vp]),
     "hxb_matmul_f16_workspace_bytes": (c_size, [c_vp, c_i64, c_vp, c_i64, c_int,
                                                 c_i64, c_i64, c_i64]),
+    "hxb_matmul_f16_noalloc": (c_int, [c_vp, c_i64, c_vp, c_i64, c_int, c_vp, c_vp,
+                                       c_i64, c_int, c_i64, c_i64, c_i64, c_vp]),
     "hxb_matmul_w8a16": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_i64,
                                  c_i64, c_i64, c_i64, c_vp]),
     "hxb_attention_f16": (c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64,
