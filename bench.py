@@ -315,7 +315,7 @@ def main():
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
                      "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
                      "peak_source": f"{peak_kind} bf16 dense (burst)",
-                     "kernel": "gemm_sm100_kernel<int8 W>",
+                     "kernel": "gemm_w8_sm100_kernel",
                      "kernel_ms": kernel_ms},
         "e2e": {"value": e2e_value, "unit": "TFLOP/s",
                 "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2},
