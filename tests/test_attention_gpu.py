@@ -1,0 +1,113 @@
+"""Parity of the fused tcgen05 attention dispatch (through the C ABI) with the
+oracle's restatement of examples/attention_layer/attention_layer.mlir:17-111
+and with the reference's golden micro model
+(integration_tests/models/micro/attention-4x1024x128-f16)."""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from _support import (baseline_check, compare, golden_expected, golden_inputs,
+                      golden_manifest, select_rows)
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+
+
+def _qkv(BH, Sq, Skv, seed, D=128):
+    rng = np.random.default_rng(seed)
+    q = rng.standard_normal((BH, Sq, D)).astype(np.float16)
+    k = rng.standard_normal((BH, Skv, D)).astype(np.float16)
+    v = rng.standard_normal((BH, Skv, D)).astype(np.float16)
+    return q, k, v
+
+
+def _run(pkg, q, k, v, causal=False, scale=None):
+    qd, kd, vd = (torch.from_numpy(x).to(DEV) for x in (q, k, v))
+    out = pkg.attention(qd, kd, vd, causal=causal, scale=scale)
+    torch.cuda.synchronize()
+    return out.float().cpu().numpy()
+
+
+@pytest.mark.parametrize("BH,Sq,Skv", [(2, 256, 256), (3, 128, 512), (1, 512, 128),
+                                       (2, 200, 333), (1, 1, 1), (1, 17, 300),
+                                       (5, 300, 129)])
+@pytest.mark.parametrize("causal", [False, True])
+def test_attention_vs_oracle(cuda_pkg, oracle, BH, Sq, Skv, causal):
+    q, k, v = _qkv(BH, Sq, Skv, seed=BH * 1000 + Sq + Skv)
+    got = _run(cuda_pkg, q, k, v, causal=causal)
+    want = oracle.attention_f32(q, k, v, causal=causal)
+    baseline_check(want, got, f"attention {BH}x{Sq}x{Skv} causal={causal}")
+    assert cuda_pkg.device_status() == 0
+
+
+def test_attention_fully_masked_rows_are_zero(cuda_pkg, oracle):
+    """Causal with Sq > Skv: the first Sq - Skv query rows see no key at all;
+    attention_layer.mlir:86-103 selects 0 for them."""
+    q, k, v = _qkv(2, 300, 100, seed=5)
+    got = _run(cuda_pkg, q, k, v, causal=True)
+    assert np.array_equal(got[:, :200], np.zeros_like(got[:, :200]))
+    baseline_check(oracle.attention_f32(q, k, v, causal=True), got, "masked rows")
+
+
+def test_attention_large_scores_rescale(cuda_pkg, oracle):
+    """Keys whose scores grow block after block force the running maximum to
+    move by more than the rescale threshold several times."""
+    BH, S = 2, 1024
+    q, k, v = _qkv(BH, S, S, seed=9)
+    ramp = np.linspace(0.2, 3.0, S, dtype=np.float32)[None, :, None]
+    k = (k.astype(np.float32) * ramp).astype(np.float16)
+    got = _run(cuda_pkg, q, k, v)
+    baseline_check(oracle.attention_f32(q, k, v), got, "rescale")
+
+
+def test_attention_custom_scale(cuda_pkg, oracle):
+    q, k, v = _qkv(2, 256, 384, seed=13)
+    got = _run(cuda_pkg, q, k, v, scale=0.3)
+    baseline_check(oracle.attention_f32(q, k, v, scale=0.3), got, "scale=0.3")
+
+
+def test_attention_vs_reference_golden(cuda_pkg, oracle):
+    """integration_tests/models/micro/attention-4x1024x128-f16: the reference's
+    own torch-eager output under its model.yaml tolerances."""
+    key = "micro__attention-4x1024x128-f16"
+    entry = golden_manifest()[key]
+    q, k, v = (t.numpy() for t in golden_inputs(key))
+    got = _run(cuda_pkg, q, k, v).astype(np.float16)
+    exp, rows = golden_expected(key)
+    tol = entry["tolerances"]
+    c = compare(exp, select_rows(got, rows), tol["atol"], tol["rtol"])
+    assert c.close and c.rel_l2_percent <= tol["relative_l2_percent"], str(c)
+    assert math.isclose(float(got.astype(np.float64).sum()), entry["out_sum"],
+                        rel_tol=1e-3, abs_tol=1.0)
+    baseline_check(oracle.attention_f32(q, k, v), got.astype(np.float32), key)
+
+
+def test_attention_baseline_config_heads(cuda_pkg, oracle):
+    """BASELINE configuration 3 ([4, 32, 2048, 128], scale 1/sqrt(128)) at full
+    size on the GPU; a sample of heads is checked against the oracle, and
+    every output row is a convex combination of V rows (bounded by V's range)."""
+    B, H, S, D = 4, 32, 2048, 128
+    g = torch.Generator(device=DEV).manual_seed(0)
+    q, k, v = (torch.randn(B, H, S, D, device=DEV, generator=g).half() for _ in range(3))
+    out = cuda_pkg.attention(q, k, v)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out).all()
+    vmax = v.float().amax(dim=2, keepdim=True)
+    vmin = v.float().amin(dim=2, keepdim=True)
+    o = out.float()
+    assert bool(((o <= vmax + 1e-2) & (o >= vmin - 1e-2)).all())
+    for b, h in [(0, 0), (1, 17), (3, 31)]:
+        want = oracle.attention_f32(q[b, h].cpu().numpy()[None], k[b, h].cpu().numpy()[None],
+                                    v[b, h].cpu().numpy()[None])
+        baseline_check(want[0], o[b, h].cpu().numpy(), f"cfg3 head ({b},{h})")
+
+
+def test_attention_rejects_unsupported_head_dim(cuda_pkg):
+    q = torch.zeros(1, 16, 64, dtype=torch.float16, device=DEV)
+    with pytest.raises(cuda_pkg.HxbError, match="head dim"):
+        cuda_pkg.attention(q, q, q)
