@@ -192,61 +192,40 @@ hxb_status_t gemm_f16_impl(const void* A, int64_t lda, const void* B,
              : launch_planned<kBF16RowMajorKN, kOutF32>(plan, *dev, tmA, tmB, args, stream);
 }
 
-// M <= 16: cluster split-K GEMV (HBM-bound weight stream).
+// M <= 16: the bandwidth-bound GEMV (gemv_w8_sm100.cuh).
+template <int MROWS>
+hxb_status_t launch_gemv(const DeviceInfo& dev, const GemvArgs& p, cudaStream_t stream) {
+  auto kernel = gemv_w8_kernel<MROWS>;
+  static bool configured[64] = {};
+  if (!configured[dev.ordinal]) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         GemvSmem::kBytes);
+    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(gemv_w8)");
+    configured[dev.ordinal] = true;
+  }
+  const unsigned grid = (unsigned)((p.N + kGemvBN - 1) / kGemvBN);
+  kernel<<<grid, kGemvThreads, GemvSmem::kBytes, stream>>>(p);
+  return cuda_status(cudaGetLastError(), "gemv_w8 launch");
+}
+
 hxb_status_t gemv_w8_impl(const void* A, int64_t lda, const void* W, int64_t ldw,
                           const void* scale, void* C, int64_t ldc, int64_t M,
                           int64_t N, int64_t K, cudaStream_t stream) {
-  constexpr int SW = 6;
-  using L = GemvSmem<SW>;
   DeviceInfo* dev = nullptr;
   hxb_status_t s = current_device(&dev);
   if (s != HXB_OK) return s;
-  CUtensorMap tmX, tmW;
-  {
-    const uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
-    const uint64_t strides[1] = {(uint64_t)lda * 2};
-    const uint32_t box[2] = {64, (uint32_t)kGemvRows};
-    if ((s = encode_tensor_map(&tmX, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, A, dims, strides,
-                               box, CU_TENSOR_MAP_SWIZZLE_128B)) != HXB_OK)
-      return s;
-  }
-  {
-    const uint64_t dims[2] = {(uint64_t)N, (uint64_t)K};
-    const uint64_t strides[1] = {(uint64_t)ldw};
-    const uint32_t box[2] = {(uint32_t)kGemvBN, 64};
-    if ((s = encode_tensor_map(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, W, dims, strides,
-                               box, CU_TENSOR_MAP_SWIZZLE_NONE)) != HXB_OK)
-      return s;
-  }
-  GemmArgs args{};
-  args.M = (int)M;
-  args.N = (int)N;
-  args.K = (int)K;
-  args.C = C;
-  args.ldc = ldc;
-  args.scale = static_cast<const __half*>(scale);
-  args.status = dev->status_word;
-  auto kernel = gemv_w8_sm100_kernel<SW>;
-  static bool configured[64] = {};
-  if (!configured[dev->ordinal]) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         L::kAlloc);
-    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(gemv_w8)");
-    configured[dev->ordinal] = true;
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)((N + kGemvBN - 1) / kGemvBN), kGemvKSplit, 1);
-  cfg.blockDim = dim3(L::kThreads, 1, 1);
-  cfg.dynamicSmemBytes = L::kAlloc;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = kGemvKSplit;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cuda_status(cudaLaunchKernelEx(&cfg, kernel, tmX, tmW, args), "gemv_w8 launch");
+  GemvArgs p{};
+  p.X = static_cast<const __half*>(A);
+  p.W = static_cast<const int8_t*>(W);
+  p.scale = static_cast<const __half*>(scale);
+  p.C = static_cast<__half*>(C);
+  p.ldx = lda;
+  p.ldw = ldw;
+  p.ldc = ldc;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  return M <= 8 ? launch_gemv<8>(*dev, p, stream) : launch_gemv<16>(*dev, p, stream);
 }
 
 hxb_status_t gemm_w8_impl(const void* A, int64_t lda, const void* W,
