@@ -31,43 +31,16 @@ hxb_status_t launch_gemm(const DeviceInfo& dev, const CUtensorMap& tmA,
   return cuda_status(cudaGetLastError(), "gemm launch");
 }
 
-template <int BN, int SA, int SW, int SB>
-hxb_status_t launch_w8(const DeviceInfo& dev, const CUtensorMap& tmA,
-                       const CUtensorMap& tmW, const GemmArgs& args,
-                       cudaStream_t stream) {
-  using L = W8Smem<BN, SA, SW, SB>;
-  auto kernel = gemm_w8_sm100_kernel<BN, SA, SW, SB>;
-  static bool configured[64] = {};
-  if (!configured[dev.ordinal]) {
-    cudaError_t e = cudaFuncSetAttribute(
-        kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
-    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(gemm_w8)");
-    configured[dev.ordinal] = true;
-  }
-  const int tiles = args.tiles_m * args.tiles_n;
-  const int grid = tiles < dev.num_sms ? tiles : dev.num_sms;
-  kernel<<<grid, L::kThreads, L::kAlloc, stream>>>(tmA, tmW, args);
-  return cuda_status(cudaGetLastError(), "gemm_w8 launch");
-}
-
 template <int BMODE, int OUT>
 hxb_status_t launch_planned(const GemmPlan& plan, const DeviceInfo& dev,
                             const CUtensorMap& tmA, const CUtensorMap& tmB,
                             const GemmArgs& args, cudaStream_t stream) {
   // Stage counts fill ~192-208 KB of shared memory per CTA.
-  if constexpr (BMODE == kBInt8RowMajorKN) {
-    switch (plan.block_n) {
-      case 256: return launch_w8<256, 4, 3, 3>(dev, tmA, tmB, args, stream);
-      case 128: return launch_w8<128, 6, 6, 3>(dev, tmA, tmB, args, stream);
-      default: break;
-    }
-  } else {
-    switch (plan.block_n) {
-      case 256: return launch_gemm<256, 4, BMODE, OUT>(dev, tmA, tmB, args, stream);
-      case 128: return launch_gemm<128, 6, BMODE, OUT>(dev, tmA, tmB, args, stream);
-      case 64: return launch_gemm<64, 8, BMODE, OUT>(dev, tmA, tmB, args, stream);
-      default: break;
-    }
+  switch (plan.block_n) {
+    case 256: return launch_gemm<256, 4, BMODE, OUT>(dev, tmA, tmB, args, stream);
+    case 128: return launch_gemm<128, 6, BMODE, OUT>(dev, tmA, tmB, args, stream);
+    case 64: return launch_gemm<64, 8, BMODE, OUT>(dev, tmA, tmB, args, stream);
+    default: break;
   }
   return fail(HXB_STATUS_UNSUPPORTED, "no kernel for block_n=%d", plan.block_n);
 }
@@ -234,16 +207,22 @@ hxb_status_t gemm_w8_impl(const void* A, int64_t lda, const void* W,
   DeviceInfo* dev = nullptr;
   hxb_status_t s = current_device(&dev);
   if (s != HXB_OK) return s;
-  const GemmPlan plan = plan_gemm((int)M, (int)N, (int)K, kBInt8RowMajorKN, dev->num_sms);
-  CUtensorMap tmA, tmB;
-  if ((s = make_a_map(&tmA, A, lda, M, K)) != HXB_OK) return s;
+  CUtensorMap tmA, tmW;
+  {
+    const uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
+    const uint64_t strides[1] = {(uint64_t)lda * 2};
+    const uint32_t box[2] = {64, (uint32_t)kW8BM};
+    if ((s = encode_tensor_map(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, A, dims, strides, box,
+                               CU_TENSOR_MAP_SWIZZLE_128B)) != HXB_OK)
+      return s;
+  }
   {
     const uint64_t dims[2] = {(uint64_t)N, (uint64_t)K};
     const uint64_t strides[1] = {(uint64_t)ldw};
-    const uint32_t box[2] = {(uint32_t)plan.block_n, 64};
-    s = encode_tensor_map(&tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, W, dims,
-                          strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
-    if (s != HXB_OK) return s;
+    const uint32_t box[2] = {(uint32_t)kW8BN, 64};
+    if ((s = encode_tensor_map(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, W, dims, strides, box,
+                               CU_TENSOR_MAP_SWIZZLE_128B)) != HXB_OK)
+      return s;
   }
   GemmArgs args{};
   args.M = (int)M;
@@ -254,11 +233,23 @@ hxb_status_t gemm_w8_impl(const void* A, int64_t lda, const void* W,
   args.C_init = nullptr;
   args.scale = static_cast<const __half*>(scale);
   args.status = dev->status_word;
-  args.tiles_m = (int)((M + kBM - 1) / kBM);
-  args.tiles_n = (int)((N + plan.block_n - 1) / plan.block_n);
-  args.group_m = plan.group_m;
-  args.vec_ok = aligned16(C) && (ldc * 2) % 16 == 0 && aligned16(scale);
-  return launch_planned<kBInt8RowMajorKN, kOutF16>(plan, *dev, tmA, tmB, args, stream);
+  args.tiles_m = (int)((M + kW8BM - 1) / kW8BM);
+  args.tiles_n = (int)((N + kW8BN - 1) / kW8BN);
+  // consecutive tiles sweep all m-tiles of one weight column block, so the
+  // CTAs running at the same time share that int8 block in L2
+  args.group_m = args.tiles_m;
+  args.vec_ok = 0;
+  static bool configured[64] = {};
+  if (!configured[dev->ordinal]) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_w8_sm100_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, W8Smem::kAlloc);
+    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(gemm_w8)");
+    configured[dev->ordinal] = true;
+  }
+  const int tiles = args.tiles_m * args.tiles_n;
+  const int grid = tiles < dev->num_sms ? tiles : dev->num_sms;
+  gemm_w8_sm100_kernel<<<grid, kW8Threads, W8Smem::kAlloc, stream>>>(tmA, tmW, args);
+  return cuda_status(cudaGetLastError(), "gemm_w8 launch");
 }
 
 }  // namespace hxb

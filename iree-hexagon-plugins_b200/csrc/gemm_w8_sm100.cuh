@@ -1,28 +1,64 @@
 // Int8-weight GEMM for sm_100a: C[M,N] f16 = (A[M,K] f16 . W[K,N] int8) * scale[N].
 //
-// The weights are dequantised inside the main loop: TMA lands the raw int8
-// tile, converter warps turn it into f16 (exactly: |w| <= 127) directly in the
-// 128B-swizzled MN-major layout tcgen05.mma reads, and the per-column scale is
-// applied once in the epilogue (it factors out of the K sum).
+// The kernel computes the transposed product D[n, m] = sum_k W[k, n] A[m, k]
+// on the tensor core so that the dequantised weights never pass through
+// shared memory a second time:
+//   * TMA lands the raw int8 weight tile [64 k][128 n] (8 KB, 128-byte
+//     swizzle) and the activation tile [256 m][64 k] f16 (32 KB) in two
+//     independent rings;
+//   * eight converter warps transpose the int8 tile in registers (byte
+//     permutes + xor-shuffles), convert it exactly to f16 (|w| <= 127) and
+//     write it into TMEM with tcgen05.st, where it is the A operand
+//     (M = 128 weight columns) of tcgen05.mma;
+//   * one thread issues tcgen05.mma (A from TMEM, B = activations from shared
+//     memory, N = 256 activation rows) into a 256-column f32 TMEM accumulator;
+//   * four epilogue warps read the accumulator back, apply the per-column
+//     scale once (it factors out of the K sum) and store C transposed.
+// Shared-memory traffic per k-block is the int8 tile (written by TMA, read
+// once by the converters) plus the activation tile (written by TMA, read by
+// the tensor core); the f16 weights live only in registers and TMEM.
 //
-// Three decoupled shared-memory rings keep every stage busy:
-//   A ring   (SA deep)  f16 activations, filled by TMA, freed by the MMA
-//   W8 ring  (SW deep)  raw int8 weights, filled by TMA, freed by converters
-//   B16 ring (SB deep)  converted f16 weights, filled by converters, freed by
-//                       the MMA
-// so the int8 bytes leave shared memory as soon as they are converted and the
-// TMA latency is covered by the deep A / W8 rings rather than by the large f16
-// buffers.
+// Roles (512 threads, one CTA per SM, persistent over output tiles):
+//   warp 0        TMA producer (one lane)
+//   warp 1        TMEM owner + MMA issuer (one lane)
+//   warps 2-3     idle
+//   warps 4-11    int8 -> f16 converters (two per TMEM lane quarter, each half
+//                 of the 64 k rows of a block)
+//   warps 12-15   epilogue
+// TMEM: accumulator in columns [0, 256), kW8SA converted weight stages of 32
+// columns from column 256.
 #pragma once
 
 #include "gemm_sm100.cuh"
+#include "w8_tmem.cuh"
 
 namespace hxb {
 
+constexpr int kW8BN = 128;  // weight columns per tile (MMA M, TMEM lanes)
+constexpr int kW8BM = 256;  // activation rows per tile (MMA N)
+constexpr int kW8SX = 4;    // activation stages
+constexpr int kW8SW = 8;    // int8 weight stages
+constexpr int kW8SA = 6;    // TMEM weight stages
+constexpr int kW8Threads = 16 * 32;
+constexpr int kW8ConvWarps = 8;
+constexpr int kW8EpiWarps = 4;
+
+struct W8Smem {
+  static constexpr int kXBytes = kW8BM * kBK * 2;  // 32 KB
+  static constexpr int kWBytes = kW8BN * kBK;      // 8 KB
+  static constexpr int kOffX = 0;
+  static constexpr int kOffW = kOffX + kW8SX * kXBytes;
+  static constexpr int kOffBar = kOffW + kW8SW * kWBytes;
+  // x_full, x_empty [SX]; w_full, w_empty [SW]; a_full, a_empty [SA];
+  // t_full, t_empty, drain
+  static constexpr int kNumBars = 2 * kW8SX + 2 * kW8SW + 2 * kW8SA + 3;
+  static constexpr int kOffMisc = kOffBar + kNumBars * 8;
+  static constexpr int kBytes = kOffMisc + 16;
+  static constexpr int kAlloc = kBytes + 1024;
+};
+
 // Position in an S-deep ring of mbarrier-guarded slots: slot index and the
-// parity of the phase the slot is in. Advancing is two adds and a compare, so
-// the single-thread producer / MMA loops carry no division on their critical
-// path.
+// parity of the phase the slot is in.
 template <int S>
 struct RingCursor {
   int slot = 0;
@@ -40,7 +76,6 @@ struct RingCursor {
 template <int S>
 __device__ __forceinline__ void drain_ring(uint64_t* full, RingCursor<S> c, int issued) {
   for (int i = 0; i < issued && i < S; ++i) {
-    // step the cursor back by one
     if (c.slot == 0) {
       c.slot = S - 1;
       c.phase ^= 1u;
@@ -53,47 +88,26 @@ __device__ __forceinline__ void drain_ring(uint64_t* full, RingCursor<S> c, int 
   }
 }
 
-template <int BN, int SA, int SW, int SB>
-struct W8Smem {
-  static constexpr int kABytes = kBM * kBK * 2;   // 16 KB
-  static constexpr int kWBytes = BN * kBK;        // int8 tile
-  static constexpr int kBBytes = BN * kBK * 2;    // converted f16 tile
-  static constexpr int kOffA = 0;
-  static constexpr int kOffW = kOffA + SA * kABytes;
-  static constexpr int kOffB = kOffW + SW * kWBytes;
-  static constexpr int kOffBar = kOffB + SB * kBBytes;
-  // full_a, empty_a [SA]; full_w, empty_w [SW]; conv_full, conv_empty [SB];
-  // tfull[2], tempty[2], drain
-  static constexpr int kNumBars = 2 * SA + 2 * SW + 2 * SB + 5;
-  static constexpr int kOffMisc = kOffBar + kNumBars * 8;
-  static constexpr int kBytes = kOffMisc + 16;  // tmem addr, abort, go
-  static constexpr int kAlloc = kBytes + 1024;
-  static constexpr int kThreads = 14 * 32;  // 6 + 8 converter warps
-  static constexpr int kConvWarps = 8;
-  static constexpr int kTmemCols = 2 * BN;
-};
-
-template <int BN, int SA, int SW, int SB>
-__global__ void __launch_bounds__(448, 1)
+__global__ void __launch_bounds__(kW8Threads, 1)
     gemm_w8_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
-                         const __grid_constant__ CUtensorMap tmW,
-                         const GemmArgs args) {
-  using L = W8Smem<BN, SA, SW, SB>;
-  constexpr uint32_t kIdesc = make_idesc_f16(kBM, BN, 0, 1);
+                         const __grid_constant__ CUtensorMap tmW, const GemmArgs args) {
+  using L = W8Smem;
+  // D[128 n x 256 m] += W^T (TMEM, K-major) . A^T (shared, K-major)
+  constexpr uint32_t kIdesc = make_idesc_f16(kW8BN, kW8BM, 0, 0);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
-  uint64_t* full_a = bars;
-  uint64_t* empty_a = full_a + SA;
-  uint64_t* full_w = empty_a + SA;
-  uint64_t* empty_w = full_w + SW;
-  uint64_t* conv_full = empty_w + SW;
-  uint64_t* conv_empty = conv_full + SB;
-  uint64_t* tfull = conv_empty + SB;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* drain = tempty + 2;
+  uint64_t* x_full = bars;
+  uint64_t* x_empty = x_full + kW8SX;
+  uint64_t* w_full = x_empty + kW8SX;
+  uint64_t* w_empty = w_full + kW8SW;
+  uint64_t* a_full = w_empty + kW8SW;
+  uint64_t* a_empty = a_full + kW8SA;
+  uint64_t* t_full = a_empty + kW8SA;
+  uint64_t* t_empty = t_full + 1;
+  uint64_t* drain = t_empty + 1;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 4);
 
@@ -104,10 +118,11 @@ __global__ void __launch_bounds__(448, 1)
   const FailState fs{abort_flag, args.status};
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < SA; ++s) { mbar_init(&full_a[s], 1); mbar_init(&empty_a[s], 1); }
-    for (int s = 0; s < SW; ++s) { mbar_init(&full_w[s], 1); mbar_init(&empty_w[s], 1); }
-    for (int s = 0; s < SB; ++s) { mbar_init(&conv_full[s], 1); mbar_init(&conv_empty[s], 1); }
-    for (int i = 0; i < 2; ++i) { mbar_init(&tfull[i], 1); mbar_init(&tempty[i], 4); }
+    for (int s = 0; s < kW8SX; ++s) { mbar_init(&x_full[s], 1); mbar_init(&x_empty[s], 1); }
+    for (int s = 0; s < kW8SW; ++s) { mbar_init(&w_full[s], 1); mbar_init(&w_empty[s], kW8ConvWarps); }
+    for (int s = 0; s < kW8SA; ++s) { mbar_init(&a_full[s], kW8ConvWarps); mbar_init(&a_empty[s], 1); }
+    mbar_init(t_full, 1);
+    mbar_init(t_empty, kW8EpiWarps);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -117,7 +132,7 @@ __global__ void __launch_bounds__(448, 1)
     tma_prefetch_desc(&tmW);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_holder, L::kTmemCols);
+    tmem_alloc(tmem_holder, 512);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -128,69 +143,62 @@ __global__ void __launch_bounds__(448, 1)
   if (warp == 0) {
     // ------------------------------------------------------ TMA producer
     if (lane == 0) {
-      RingCursor<SW> cw;
-      RingCursor<SA> ca;
-      int issued_w = 0, issued_a = 0;
+      RingCursor<kW8SX> cx;
+      RingCursor<kW8SW> cw;
+      int issued_x = 0, issued_w = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         int tm, tn;
         tile_coords(t, args, tm, tn);
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&empty_w[cw.slot], cw.phase ^ 1, fs)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full_w[cw.slot], L::kWBytes);
-          tma_load_2d(smem + L::kOffW + cw.slot * L::kWBytes, &tmW, &full_w[cw.slot],
-                      tn * BN, kb * kBK);
+          if (!mbar_wait(&w_empty[cw.slot], cw.phase ^ 1, fs)) { ok = false; break; }
+          mbar_arrive_expect_tx(&w_full[cw.slot], L::kWBytes);
+          tma_load_2d(smem + L::kOffW + cw.slot * L::kWBytes, &tmW, &w_full[cw.slot],
+                      tn * kW8BN, kb * kBK);
           cw.advance();
           ++issued_w;
-          if (!mbar_wait(&empty_a[ca.slot], ca.phase ^ 1, fs)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full_a[ca.slot], L::kABytes);
-          tma_load_2d(smem + L::kOffA + ca.slot * L::kABytes, &tmA, &full_a[ca.slot],
-                      kb * kBK, tm * kBM);
-          ca.advance();
-          ++issued_a;
+          if (!mbar_wait(&x_empty[cx.slot], cx.phase ^ 1, fs)) { ok = false; break; }
+          mbar_arrive_expect_tx(&x_full[cx.slot], L::kXBytes);
+          tma_load_2d(smem + L::kOffX + cx.slot * L::kXBytes, &tmA, &x_full[cx.slot],
+                      kb * kBK, tm * kW8BM);
+          cx.advance();
+          ++issued_x;
         }
       }
-      // Wait (bounded) for the last copies of each ring to land before the
-      // CTA may exit; on the normal path they have long completed. Walking
-      // the cursors backwards visits the most recent issue of every slot.
-      drain_ring<SW>(full_w, cw, issued_w);
-      drain_ring<SA>(full_a, ca, issued_a);
+      drain_ring<kW8SW>(w_full, cw, issued_w);
+      drain_ring<kW8SX>(x_full, cx, issued_x);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      RingCursor<SA> ca;
-      RingCursor<SB> cb;
+      RingCursor<kW8SX> cx;
+      RingCursor<kW8SA> ca;
       int tl = 0;
       bool ok = true, issued_any = false;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++tl) {
-        const int acc = tl & 1;
-        if (!mbar_wait(&tempty[acc], ((tl >> 1) & 1) ^ 1, fs)) { ok = false; break; }
+        if (!mbar_wait(t_empty, (uint32_t)(tl & 1) ^ 1, fs)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = 0; kb < num_kb; ++kb) {
-          const int sa = ca.slot, sb = cb.slot;
-          if (!mbar_wait(&full_a[sa], ca.phase, fs) || !mbar_wait(&conv_full[sb], cb.phase, fs)) {
+          const int sx = cx.slot, sa = ca.slot;
+          if (!mbar_wait(&x_full[sx], cx.phase, fs) || !mbar_wait(&a_full[sa], ca.phase, fs)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + L::kOffA + sa * L::kABytes);
-          const uint32_t b_addr = smem_u32(smem + L::kOffB + sb * L::kBBytes);
+          const uint32_t x_addr = smem_u32(smem + L::kOffX + sx * L::kXBytes);
+          const uint32_t a_tmem = tmem_base + 256 + 32 * sa;
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k) {
-            const uint64_t adesc = make_smem_desc(a_addr + k * 32, 16, 1024, kLayoutSwizzle128);
-            const uint64_t bdesc = make_smem_desc(b_addr + k * 16 * 128, kBK * 128, 1024,
-                                                  kLayoutSwizzle128);
-            umma_f16_ss(d_tmem, adesc, bdesc, kIdesc, (kb | k) != 0);
+            const uint64_t bdesc = make_smem_desc(x_addr + k * 32, 16, 1024, kLayoutSwizzle128);
+            umma_f16_ts(tmem_base, a_tmem + 8 * k, bdesc, kIdesc, (kb | k) != 0);
           }
           issued_any = true;
-          umma_commit(&empty_a[sa]);
-          umma_commit(&conv_empty[sb]);
+          umma_commit(&x_empty[sx]);
+          umma_commit(&a_empty[sa]);
+          cx.advance();
           ca.advance();
-          cb.advance();
         }
-        if (ok) umma_commit(&tfull[acc]);
+        if (ok) umma_commit(t_full);
       }
       if (!ok && issued_any) {
         umma_commit(drain);
@@ -199,77 +207,76 @@ __global__ void __launch_bounds__(448, 1)
         }
       }
     }
-  } else if (warp < 6) {
+  } else if (warp >= 4 && warp < 4 + kW8ConvWarps) {
+    // ------------------------------------------------------ int8 -> f16 -> TMEM
+    const int q = warp & 3;
+    const int half = (warp - 4) >> 2;  // k rows [32 half, 32 half + 32) of a block
+    const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
+    RingCursor<kW8SW> cw;
+    RingCursor<kW8SA> ca;
+    bool ok = true;
+    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      for (int kb = 0; kb < num_kb; ++kb) {
+        const int sw = cw.slot, sa = ca.slot;
+        const bool ready = mbar_wait(&w_full[sw], cw.phase, fs) &&
+                           mbar_wait(&a_empty[sa], ca.phase ^ 1, fs);
+        if (!__all_sync(0xffffffffu, ready)) { ok = false; break; }
+        tc_fence_after();
+        const uint8_t* tile = smem + L::kOffW + sw * L::kWBytes;
+        if (half == 0)
+          w8_rows_to_tmem<0, 8>(tile, lane_base, 256 + 32 * sa, q, lane);
+        else
+          w8_rows_to_tmem<8, 8>(tile, lane_base, 256 + 32 * sa, q, lane);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&a_full[sa]);
+          mbar_arrive(&w_empty[sw]);
+        }
+        cw.advance();
+        ca.advance();
+      }
+    }
+  } else if (warp >= 4 + kW8ConvWarps) {
     // ------------------------------------------------------ epilogue
     const int q = warp & 3;
+    const int l = q * 32 + lane;
+    const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
     int tl = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tl) {
       int tm, tn;
       tile_coords(t, args, tm, tn);
-      const int acc = tl & 1;
-      const bool ready = mbar_wait(&tfull[acc], (tl >> 1) & 1, fs);
+      const bool ready = mbar_wait(t_full, (uint32_t)(tl & 1), fs);
       if (!__all_sync(0xffffffffu, ready)) break;
       tc_fence_after();
-      const int row = tm * kBM + q * 32 + lane;
-      const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
+      const int n = tn * kW8BN + w8_lane_to_col(l);
+      const bool n_ok = n < args.N;
+      const float sc = n_ok ? __half2float(args.scale[n]) : 0.0f;
+      __half* cbase = reinterpret_cast<__half*>(args.C) + n;
+      const int m0 = tm * kW8BM;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
+      for (int c = 0; c < kW8BM / 32; ++c) {
         uint32_t r[32];
-        tmem_ld_32x32b_x32(t_row + c, r);
+        tmem_ld_32x32b_x32(lane_base + 32 * c, r);
         tmem_wait_ld();
-        const int col0 = tn * BN + c;
-        if (row >= args.M || col0 >= args.N) continue;
-        store_chunk<true, kOutF16>(args, row, col0, r);
+        const int mc = m0 + 32 * c;
+        if (n_ok) {
+          if (mc + 32 <= args.M) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              cbase[(long long)(mc + e) * args.ldc] = __float2half_rn(__uint_as_float(r[e]) * sc);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (mc + e < args.M)
+                cbase[(long long)(mc + e) * args.ldc] = __float2half_rn(__uint_as_float(r[e]) * sc);
+          }
+        }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
-    }
-  } else {
-    // ------------------------------------------------------ int8 -> f16
-    // One elected converter thread does the mbarrier handshakes; the group
-    // of kConvWarps warps meets on a named barrier, so each k-block costs one
-    // wake-up from the MMA's commit instead of one per warp.
-    const int ct = threadIdx.x - 6 * 32;  // 0..32*kConvWarps-1
-    constexpr int kConvThreads = 32 * L::kConvWarps;
-    volatile int* go = abort_flag + 1;  // per-k-block decision of the leader
-    RingCursor<SW> cw;
-    RingCursor<SB> cb;
-    constexpr int kUnitsPerRow = BN / 16;  // 16-byte int8 units per k row
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
-      bool ok = true;
-      for (int kb = 0; kb < num_kb; ++kb) {
-        const int sw = cw.slot, sb = cb.slot;
-        if (ct == 0)
-          *go = mbar_wait(&full_w[sw], cw.phase, fs) &&
-                mbar_wait(&conv_empty[sb], cb.phase ^ 1, fs);
-        named_barrier_sync(1, kConvThreads);
-        if (!*go) { ok = false; break; }
-        const uint8_t* src = smem + L::kOffW + sw * L::kWBytes;
-        uint8_t* dst = smem + L::kOffB + sb * L::kBBytes;
-#pragma unroll
-        for (int it = 0; it < kBK * kUnitsPerRow / kConvThreads; ++it) {
-          const int w = ct + it * kConvThreads;
-          const int k = w / kUnitsPerRow;
-          const int c16 = w - k * kUnitsPerRow;
-          const uint4 raw = *reinterpret_cast<const uint4*>(src + k * BN + c16 * 16);
-          uint4 o0, o1;
-          i8x4_to_f16x4(raw.x, o0.x, o0.y);
-          i8x4_to_f16x4(raw.y, o0.z, o0.w);
-          i8x4_to_f16x4(raw.z, o1.x, o1.y);
-          i8x4_to_f16x4(raw.w, o1.z, o1.w);
-          store_swizzled_pair(dst, c16, k, o0, o1);
-        }
-        fence_proxy_async_smem();
-        named_barrier_sync(1, kConvThreads);
-        if (ct == 0) {
-          mbar_arrive(&conv_full[sb]);
-          mbar_arrive(&empty_w[sw]);
-        }
-        cw.advance();
-        cb.advance();
-      }
-      if (!ok) break;
+      if (lane == 0) mbar_arrive(t_empty);
     }
   }
 
@@ -278,7 +285,7 @@ __global__ void __launch_bounds__(448, 1)
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, L::kTmemCols);
+    tmem_dealloc(tmem_base, 512);
   }
 }
 
