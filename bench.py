@@ -122,7 +122,9 @@ def make_inputs(torch, dev, seed):
 
 def cpu_baseline_sample(seconds_target: float = 10.0) -> dict:
     """The oracle restatement (test infrastructure) timed on this host's cores
-    on a bounded row sample of the same workload."""
+    on a bounded sample of the same workload: whole dispatches (or a row
+    slice when one dispatch would take longer than the target), repeated
+    until about `seconds_target` of CPU time has been spent."""
     import numpy as np
     from oracle import oracle as ref
     rng = np.random.default_rng(0)
@@ -135,13 +137,17 @@ def cpu_baseline_sample(seconds_target: float = 10.0) -> dict:
     rate = 32 / (time.perf_counter() - t0)  # rows per second
     rows = int(max(32, min(M, rate * seconds_target)) // 32 * 32)
     a = rng.standard_normal((rows, K)).astype(np.float16)
-    t0 = time.perf_counter()
-    ref.matmul_w8a16_f32(a, w, s)
-    dt = time.perf_counter() - t0
-    return {"value": 2.0 * rows * K * N / dt / 1e12, "unit": "TFLOP/s",
-            "cores": os.cpu_count(), "kind": "port",
-            "sample": f"{rows} of {M} activation rows of {WORKLOAD} "
-                      f"(C oracle, OpenMP on {os.cpu_count()} threads), {dt:.1f} s"}
+    reps, dt = 0, 0.0
+    while dt < seconds_target or reps == 0:
+        t0 = time.perf_counter()
+        ref.matmul_w8a16_f32(a, w, s)
+        dt += time.perf_counter() - t0
+        reps += 1
+    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count()))
+    return {"value": 2.0 * rows * K * N * reps / dt / 1e12, "unit": "TFLOP/s",
+            "cores": threads, "kind": "port",
+            "sample": f"{reps} x {rows} of {M} activation rows of {WORKLOAD} "
+                      f"(C oracle, OpenMP on {threads} threads), {dt:.1f} s"}
 
 
 def run_reference(args, rank: int) -> None:
@@ -250,7 +256,11 @@ def main():
     kernel_ms = statistics.mean(per_step_ms)
     achieved = FLOP_PER_STEP / (kernel_ms / 1e3) / 1e12
     peaks, peak_kind = _peaks()
-    peak = peaks["bf16_tflops"]
+    # A kernel timed inside a long back-to-back loop runs under the power cap:
+    # compare it with the sustained GEMM figure; a short burst with the burst one.
+    sustained = total_ms > 500.0 and peaks.get("bf16_tflops_sustained")
+    peak = peaks["bf16_tflops_sustained"] if sustained else peaks["bf16_tflops"]
+    peak_label = f"{peak_kind} bf16 dense ({'sustained' if sustained else 'burst'})"
     traffic = _profile_traffic("w8a16_gemm_4096x4096x11008")
 
     # ---------------- e2e: host buffers through the public API
@@ -314,8 +324,8 @@ def main():
                    "l2": f"{N_SETS} rotating input sets ({N_SETS * 169} MB) > 126 MB L2"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
                      "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
-                     "peak_source": f"{peak_kind} bf16 dense (burst)",
-                     "kernel": "gemm_w8_sm100_kernel",
+                     "peak_source": peak_label,
+                     "kernel": "gemm_w8_sm100_kernel (swap-AB, int8->f16 in TMEM)",
                      "kernel_ms": kernel_ms},
         "e2e": {"value": e2e_value, "unit": "TFLOP/s",
                 "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2},
