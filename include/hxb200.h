@@ -126,6 +126,16 @@ hxb_status_t hxb_matmul_w8a16(const void* A, int64_t lda, const void* W,
                               int64_t ldc, int64_t M, int64_t N, int64_t K,
                               void* stream);
 
+/* hxb_matmul_w8a16 with a residual add: C = (A . W) * scale + R, one f16
+ * rounding of the f32 result. R has C's layout (leading dimension ldc) and may
+ * alias C. Used by the decoder block's output projections (Hugging Face Llama
+ * adds the residual after o_proj and down_proj). */
+hxb_status_t hxb_matmul_w8a16_residual(const void* A, int64_t lda, const void* W,
+                                       int64_t ldw, const void* scale,
+                                       const void* R, void* C, int64_t ldc,
+                                       int64_t M, int64_t N, int64_t K,
+                                       void* stream);
+
 /* Fused attention dispatch: O = softmax(scale * Q.K^T [+ causal mask]) . V,
  * f32 softmax statistics, f16 in/out. Replaces the decomposed f32 dispatches
  * of examples/attention_layer/attention_layer.mlir:17-111 (which scale Q and
@@ -138,6 +148,77 @@ hxb_status_t hxb_attention_f16(const void* Q, const void* K, const void* V,
                                void* O, int64_t BH, int64_t Sq, int64_t Skv,
                                int64_t D, float scale, int causal,
                                void* stream);
+
+/* hxb_attention_f16 on [batch, S, heads * D] matrices: head h of batch b is
+ * columns [h*D, (h+1)*D) of rows [b*S, (b+1)*S) of a row-major matrix with
+ * leading dimension ld (elements, multiple of 8). Q, K and V may be column
+ * blocks of one fused QKV projection output (ld = 3 * heads * D); O is
+ * written in the same [batch, S, heads * D] order, the input layout of the
+ * output projection. Same semantics and limits as hxb_attention_f16. */
+hxb_status_t hxb_attention_f16_bshd(const void* Q, int64_t ldq, const void* K,
+                                    int64_t ldk, const void* V, int64_t ldv,
+                                    void* O, int64_t ldo, int64_t batch,
+                                    int64_t heads, int64_t Sq, int64_t Skv,
+                                    int64_t D, float scale, int causal,
+                                    void* stream);
+
+/* ---- Llama-style decoder block ----------------
+ * The reference has no decoder kernels of its own; its decoder models are
+ * Hugging Face Llama checkpoints run through torch
+ * (integration_tests/models/meta-llama/Llama-3.2-1B-Instruct/model.py). The
+ * entries below follow the arithmetic of those modules on f16 activations. */
+
+/* y = f16(x * rsqrt(mean(x^2) + eps)) * gamma per row (LlamaRMSNorm:
+ * f32 statistics, f16 result times the f16 weight). cols % 8 == 0. */
+hxb_status_t hxb_rmsnorm_f16(const void* x, int64_t ldx, const void* gamma,
+                             void* y, int64_t ldy, int64_t rows, int64_t cols,
+                             float eps, void* stream);
+
+/* In-place rotary embedding of the first `heads` heads (head_dim 128) of every
+ * row: pairs (i, i + 64) rotate by (pos0 + row % seq) * theta^(-2i/128)
+ * (Llama rotate_half convention). For a fused QKV row pass 2 * n_heads to
+ * rotate q and k together. */
+hxb_status_t hxb_rope_f16(void* x, int64_t ldx, int64_t rows, int64_t heads,
+                          int64_t head_dim, int64_t seq, int64_t pos0,
+                          float theta, void* stream);
+
+/* a[r, j] = silu(gu[r, j]) * gu[r, ffn + j] (LlamaMLP: gate columns, then up
+ * columns, of one fused gate/up projection output). ffn % 8 == 0. */
+hxb_status_t hxb_swiglu_f16(const void* gu, int64_t ldgu, void* a, int64_t lda,
+                            int64_t rows, int64_t ffn, void* stream);
+
+/* Weights of one decoder block. int8 matrices are [in, out] row-major with an
+ * f16 per-output-column scale; w_gate_up holds the gate columns then the up
+ * columns ([hidden, 2 * ffn]). Norm weights are f16 [hidden]. */
+typedef struct hxb_decoder_w8_s {
+  int64_t hidden, heads, head_dim, ffn;
+  float rms_eps, rope_theta;
+  const void* attn_norm;
+  const void* w_qkv;      /* [hidden, 3 * hidden]: q, k, v column blocks */
+  const void* s_qkv;
+  const void* w_o;        /* [hidden, hidden] */
+  const void* s_o;
+  const void* ffn_norm;
+  const void* w_gate_up;  /* [hidden, 2 * ffn] */
+  const void* s_gate_up;
+  const void* w_down;     /* [ffn, hidden] */
+  const void* s_down;
+} hxb_decoder_w8_t;
+
+/* Device workspace hxb_decoder_block_w8a16 needs for batch * seq rows
+ * (0 if the weights description is invalid). */
+size_t hxb_decoder_block_workspace_bytes(const hxb_decoder_w8_t* w,
+                                         int64_t batch, int64_t seq);
+
+/* out = decoder_block(x): x, out [batch * seq, hidden] f16 row-major,
+ * causal self-attention over each batch's seq rows at positions pos0 .. The
+ * block runs as a sequence of dispatches on `stream` (RMSNorm, QKV W8 GEMM,
+ * RoPE, attention, O W8 GEMM + residual, RMSNorm, gate/up W8 GEMM, SwiGLU,
+ * down W8 GEMM + residual). */
+hxb_status_t hxb_decoder_block_w8a16(const hxb_decoder_w8_t* w, const void* x,
+                                     void* out, int64_t batch, int64_t seq,
+                                     int64_t pos0, void* workspace,
+                                     size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

@@ -8,6 +8,8 @@ identifier it is imported as `iree_hexagon_plugins_b200` through
 """
 from . import _native
 from ._native import HxbError
-from .dispatch import attention, device_status, matmul, matmul_w8a16
+from .dispatch import (DecoderBlockW8, attention, attention_bshd, device_status, matmul,
+                       matmul_w8a16, rmsnorm, rope_, swiglu)
 
-__all__ = ["HxbError", "attention", "device_status", "matmul", "matmul_w8a16", "_native"]
+__all__ = ["HxbError", "DecoderBlockW8", "attention", "attention_bshd", "device_status",
+           "matmul", "matmul_w8a16", "rmsnorm", "rope_", "swiglu", "_native"]

@@ -33,7 +33,29 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                  c_i64, c_i64, c_i64, c_vp]),
     "hxb_attention_f16": (c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64,
                                   c_i64, c_float, c_int, c_vp]),
+    "hxb_matmul_w8a16_residual": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp,
+                                          c_i64, c_i64, c_i64, c_i64, c_vp]),
+    "hxb_attention_f16_bshd": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64,
+                                       c_i64, c_i64, c_i64, c_i64, c_i64, c_float, c_int,
+                                       c_vp]),
+    "hxb_rmsnorm_f16": (c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_float, c_vp]),
+    "hxb_rope_f16": (c_int, [c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_float, c_vp]),
+    "hxb_swiglu_f16": (c_int, [c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_vp]),
+    "hxb_decoder_block_workspace_bytes": (c_size, [c_vp, c_i64, c_i64]),
+    "hxb_decoder_block_w8a16": (c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp,
+                                        c_size, c_vp]),
 }
+
+
+class DecoderW8(ctypes.Structure):
+    """hxb_decoder_w8_t of include/hxb200.h."""
+
+    _fields_ = [("hidden", c_i64), ("heads", c_i64), ("head_dim", c_i64), ("ffn", c_i64),
+                ("rms_eps", c_float), ("rope_theta", c_float),
+                ("attn_norm", c_vp), ("w_qkv", c_vp), ("s_qkv", c_vp),
+                ("w_o", c_vp), ("s_o", c_vp), ("ffn_norm", c_vp),
+                ("w_gate_up", c_vp), ("s_gate_up", c_vp),
+                ("w_down", c_vp), ("s_down", c_vp)]
 
 STATUS_NAMES = {
     0: "OK",

@@ -65,8 +65,17 @@ struct AttSmem {
   static constexpr int kAlloc = kBytes + 1024;
 };
 
+// Q, K, V and O are row-major matrices of B*S rows; head h of batch b
+// occupies rows [b*S, (b+1)*S) and columns [(h % hpr) * 128, +128) with
+// hpr heads per row: hpr = 1 is the contiguous [B*H, S, D] layout,
+// hpr = H the [B, S, H*D] layout (e.g. the Q/K/V column blocks of a fused QKV
+// projection output). Rows of a tile past S belong to the next head or batch
+// (or lie outside the matrix and read as zeros): their keys are masked and
+// their query rows are not stored.
 struct AttArgs {
   int Sq, Skv;
+  int hpr;            // heads per row
+  long long ldo;      // O row pitch (elements)
   int q_blocks;       // CTAs per head: ceil(Sq / 256)
   int causal;
   int causal_offset;  // Skv - Sq: key j is visible to query i iff j <= i + offset
@@ -136,6 +145,8 @@ __global__ void __launch_bounds__(kAttThreads, 1)
   const int lane = threadIdx.x & 31;
   const int qb = blockIdx.x % args.q_blocks;
   const int bh = blockIdx.x / args.q_blocks;
+  const int hx = (bh % args.hpr) * kAttD;  // column of this head
+  const int hb = bh / args.hpr;            // row block (batch) of this head
   const int q0 = qb * kAttTiles * kAttBM;
   const int n_kv = kv_blocks_for(args, q0);
   const FailState fs{abort_flag, args.status};
@@ -175,8 +186,8 @@ __global__ void __launch_bounds__(kAttThreads, 1)
       mbar_arrive_expect_tx(q_full, kAttTiles * kAttTileBytes);
       for (int t = 0; t < kAttTiles; ++t)
         for (int b = 0; b < 2; ++b)
-          tma_load_3d(smem + L::kOffQ + t * kAttTileBytes + b * kAttBoxBytes, &tmQ, q_full,
-                      64 * b, q0 + t * kAttBM, bh);
+          tma_load_2d(smem + L::kOffQ + t * kAttTileBytes + b * kAttBoxBytes, &tmQ, q_full,
+                      hx + 64 * b, hb * args.Sq + q0 + t * kAttBM);
       Cursor<kAttSlots> c;
       int issued = 0;
       bool ok = true;
@@ -189,8 +200,8 @@ __global__ void __launch_bounds__(kAttThreads, 1)
           mbar_arrive_expect_tx(&kv_full[c.slot], kAttTileBytes);
           const CUtensorMap* map = which ? &tmV : &tmK;
           for (int b = 0; b < 2; ++b)
-            tma_load_3d(smem + L::kOffKV + c.slot * kAttTileBytes + b * kAttBoxBytes, map,
-                        &kv_full[c.slot], 64 * b, j * kAttBN, bh);
+            tma_load_2d(smem + L::kOffKV + c.slot * kAttTileBytes + b * kAttBoxBytes, map,
+                        &kv_full[c.slot], hx + 64 * b, hb * args.Skv + j * kAttBN);
           c.advance();
           ++issued;
         }
@@ -362,7 +373,7 @@ __global__ void __launch_bounds__(kAttThreads, 1)
     const bool all_have = __all_sync(0xffffffffu, have);
     if (all_have) tc_fence_after();
     const float inv = (all_have && l_run > 0.0f) ? 1.0f / l_run : 0.0f;
-    __half* orow = args.O + ((size_t)bh * args.Sq + qrow) * kAttD;
+    __half* orow = args.O + ((long long)hb * args.Sq + qrow) * args.ldo + hx;
     const bool write = (ok || n_kv == 0) && qrow < args.Sq;
 #pragma unroll 1
     for (int ch = 0; ch < 4; ++ch) {
@@ -397,24 +408,25 @@ __global__ void __launch_bounds__(kAttThreads, 1)
   }
 }
 
-hxb_status_t make_head_map(CUtensorMap* m, const void* base, int64_t S, int64_t BH) {
-  const uint64_t dims[3] = {(uint64_t)kAttD, (uint64_t)S, (uint64_t)BH};
-  const uint64_t strides[2] = {(uint64_t)kAttD * 2, (uint64_t)S * kAttD * 2};
-  const uint32_t box[3] = {64, 128, 1};
-  return encode_tensor_map(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, base, dims, strides, box,
+// 2-D map over a row-major [rows, ld] f16 matrix read in [128 rows x 64]
+// boxes (128-byte swizzle).
+hxb_status_t make_rows_map(CUtensorMap* m, const void* base, int64_t rows, int64_t ld) {
+  const uint64_t dims[2] = {(uint64_t)ld, (uint64_t)rows};
+  const uint64_t strides[1] = {(uint64_t)ld * 2};
+  const uint32_t box[2] = {64, 128};
+  return encode_tensor_map(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, dims, strides, box,
                            CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 }  // namespace
-}  // namespace hxb
 
-extern "C" hxb_status_t hxb_attention_f16(const void* Q, const void* K, const void* V,
-                                          void* O, int64_t BH, int64_t Sq, int64_t Skv,
-                                          int64_t D, float scale, int causal,
-                                          void* stream) {
-  using namespace hxb;
-  if (BH < 1 || Sq < 1 || Skv < 1)
-    return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: BH, Sq, Skv must be >= 1");
+// Shared launcher: B batches x H heads; hpr heads per matrix row (see AttArgs).
+hxb_status_t attention_launch(const void* Q, int64_t ldq, const void* K, int64_t ldk,
+                              const void* V, int64_t ldv, void* O, int64_t ldo, int64_t B,
+                              int64_t H, int64_t hpr, int64_t Sq, int64_t Skv, int64_t D,
+                              float scale, int causal, cudaStream_t stream) {
+  if (B < 1 || H < 1 || Sq < 1 || Skv < 1)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: batch, heads, Sq, Skv must be >= 1");
   if (D != kAttD)
     return fail(HXB_STATUS_UNSUPPORTED, "attention: head dim %lld not supported (D = 128 only)",
                 (long long)D);
@@ -422,9 +434,16 @@ extern "C" hxb_status_t hxb_attention_f16(const void* Q, const void* K, const vo
     return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: null operand");
   if (!aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(O))
     return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: Q/K/V/O must be 16-byte aligned");
+  if (ldq % 8 || ldk % 8 || ldv % 8 || ldo % 8)
+    return fail(HXB_STATUS_INVALID_ARGUMENT,
+                "attention: row pitches must be multiples of 8 elements (16 bytes)");
+  if (ldq < hpr * D || ldk < hpr * D || ldv < hpr * D || ldo < hpr * D)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: row pitch smaller than the heads it holds");
   if (!(scale > 0.0f) || !isfinite(scale))
     return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: scale must be finite and > 0");
-  if (Sq > (1 << 30) || Skv > (1 << 30) || BH > (1 << 30))
+  const int64_t BH = B * H;
+  const int64_t rows_q = BH / hpr * Sq, rows_kv = BH / hpr * Skv;
+  if (Sq > (1 << 30) || Skv > (1 << 30) || rows_q > INT32_MAX || rows_kv > INT32_MAX)
     return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: extent too large");
   const int64_t q_blocks = (Sq + kAttTiles * kAttBM - 1) / (kAttTiles * kAttBM);
   if (q_blocks * BH > INT32_MAX)
@@ -434,13 +453,15 @@ extern "C" hxb_status_t hxb_attention_f16(const void* Q, const void* K, const vo
   hxb_status_t s = current_device(&dev);
   if (s != HXB_OK) return s;
   CUtensorMap tmQ, tmK, tmV;
-  if ((s = make_head_map(&tmQ, Q, Sq, BH)) != HXB_OK) return s;
-  if ((s = make_head_map(&tmK, K, Skv, BH)) != HXB_OK) return s;
-  if ((s = make_head_map(&tmV, V, Skv, BH)) != HXB_OK) return s;
+  if ((s = make_rows_map(&tmQ, Q, rows_q, ldq)) != HXB_OK) return s;
+  if ((s = make_rows_map(&tmK, K, rows_kv, ldk)) != HXB_OK) return s;
+  if ((s = make_rows_map(&tmV, V, rows_kv, ldv)) != HXB_OK) return s;
 
   AttArgs args{};
   args.Sq = (int)Sq;
   args.Skv = (int)Skv;
+  args.hpr = (int)hpr;
+  args.ldo = ldo;
   args.q_blocks = (int)q_blocks;
   args.causal = causal ? 1 : 0;
   args.causal_offset = (int)(Skv - Sq);
@@ -456,7 +477,26 @@ extern "C" hxb_status_t hxb_attention_f16(const void* Q, const void* K, const vo
     if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(attention)");
     configured[dev->ordinal] = true;
   }
-  attention_fwd_kernel<<<(unsigned)(q_blocks * BH), kAttThreads, AttSmem::kAlloc,
-                         static_cast<cudaStream_t>(stream)>>>(tmQ, tmK, tmV, args);
+  attention_fwd_kernel<<<(unsigned)(q_blocks * BH), kAttThreads, AttSmem::kAlloc, stream>>>(
+      tmQ, tmK, tmV, args);
   return cuda_status(cudaGetLastError(), "attention launch");
+}
+
+}  // namespace hxb
+
+extern "C" hxb_status_t hxb_attention_f16(const void* Q, const void* K, const void* V,
+                                          void* O, int64_t BH, int64_t Sq, int64_t Skv,
+                                          int64_t D, float scale, int causal,
+                                          void* stream) {
+  return hxb::attention_launch(Q, D, K, D, V, D, O, D, BH, 1, 1, Sq, Skv, D, scale, causal,
+                               static_cast<cudaStream_t>(stream));
+}
+
+extern "C" hxb_status_t hxb_attention_f16_bshd(const void* Q, int64_t ldq, const void* K,
+                                               int64_t ldk, const void* V, int64_t ldv, void* O,
+                                               int64_t ldo, int64_t batch, int64_t heads,
+                                               int64_t Sq, int64_t Skv, int64_t D, float scale,
+                                               int causal, void* stream) {
+  return hxb::attention_launch(Q, ldq, K, ldk, V, ldv, O, ldo, batch, heads, heads, Sq, Skv, D,
+                               scale, causal, static_cast<cudaStream_t>(stream));
 }

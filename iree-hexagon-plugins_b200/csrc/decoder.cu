@@ -1,0 +1,277 @@
+// Llama-style decoder block with int8-weight linears (BASELINE configuration
+// 4) built from the dispatch kernels of this library:
+//
+//   h   = RMSNorm(x) * attn_norm                          rmsnorm_kernel
+//   qkv = h . Wqkv * s_qkv                                W8 GEMM  [S, 3*hidden]
+//   q,k = RoPE(q), RoPE(k)   (in place inside qkv)        rope_kernel
+//   att = causal softmax(q k^T / sqrt(d)) v               attention, [B,S,H*D]
+//   h2  = att . Wo * s_o + x                              W8 GEMM + residual
+//   g,u = RMSNorm(h2) * ffn_norm . Wgu * s_gu             rmsnorm + W8 GEMM
+//   a   = silu(g) * u                                     swiglu_kernel
+//   out = a . Wd * s_d + h2                               W8 GEMM + residual
+//
+// Attention reads q, k and v straight out of the fused QKV output (column
+// blocks of one row-major matrix) and writes its output in [S, H*D] order,
+// the input layout of the O projection, so no transposes are needed. The
+// reference has no such block (its full models come from Hugging Face
+// checkpoints, integration_tests/models/meta-llama/*); the arithmetic follows
+// the Hugging Face Llama modules those tests wrap: RMSNorm in f32 over the
+// row, rounded to f16 and multiplied by the f16 weight; RoPE with
+// inv_freq[i] = theta^(-2i/d) over the rotate-half pairs (i, i + d/2);
+// silu(g) * u. Intermediates are f16 as in an f16 model.
+#include <math.h>
+#include <string.h>
+
+#include "runtime_common.h"
+#include "sm100.cuh"
+
+namespace hxb {
+
+hxb_status_t matmul_w8a16_impl(const void* A, int64_t lda, const void* W, int64_t ldw,
+                               const void* scale, const void* R, void* C, int64_t ldc,
+                               int64_t M, int64_t N, int64_t K, cudaStream_t stream);
+hxb_status_t attention_launch(const void* Q, int64_t ldq, const void* K, int64_t ldk,
+                              const void* V, int64_t ldv, void* O, int64_t ldo, int64_t B,
+                              int64_t H, int64_t hpr, int64_t Sq, int64_t Skv, int64_t D,
+                              float scale, int causal, cudaStream_t stream);
+
+namespace {
+
+// One warp per row; 16-byte vector loads (cols % 8 == 0).
+__global__ void rmsnorm_kernel(const __half* __restrict__ x, long long ldx,
+                               const __half* __restrict__ gamma, __half* __restrict__ y,
+                               long long ldy, int rows, int cols, float eps) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const __half* xr = x + (long long)warp * ldx;
+  __half* yr = y + (long long)warp * ldy;
+  float ss = 0.0f;
+  for (int c = lane * 8; c < cols; c += 256) {
+    const uint4 v = *reinterpret_cast<const uint4*>(xr + c);
+    const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __half22float2(h[e]);
+      ss = fmaf(f.x, f.x, ss);
+      ss = fmaf(f.y, f.y, ss);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float r = rsqrtf(ss / (float)cols + eps);
+  for (int c = lane * 8; c < cols; c += 256) {
+    const uint4 v = *reinterpret_cast<const uint4*>(xr + c);
+    const uint4 g = *reinterpret_cast<const uint4*>(gamma + c);
+    const __half2* h = reinterpret_cast<const __half2*>(&v);
+    const __half2* gh = reinterpret_cast<const __half2*>(&g);
+    uint4 o;
+    __half2* oh = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __half22float2(h[e]);
+      oh[e] = __hmul2(__floats2half2_rn(f.x * r, f.y * r), gh[e]);
+    }
+    *reinterpret_cast<uint4*>(yr + c) = o;
+  }
+}
+
+// In-place rotary embedding of `heads` consecutive 128-wide heads at the
+// start of every row (the q and k blocks of a fused QKV row). One warp per
+// (row, head); lane i handles the rotate-half pairs (i, i + 64) and
+// (i + 32, i + 96). Row r has position pos0 + r % seq.
+__global__ void rope_kernel(__half* __restrict__ x, long long ldx, int rows, int heads, int seq,
+                            int pos0, float log2_theta) {
+  const int wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (wid >= rows * heads) return;
+  const int row = wid / heads, head = wid - row * heads;
+  __half* v = x + (long long)row * ldx + head * 128;
+  const float pos = (float)(pos0 + row % seq);
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int i = lane + 32 * k;
+    const float inv_freq = exp2f(-(2.0f * (float)i / 128.0f) * log2_theta);
+    float sn, cs;
+    sincosf(pos * inv_freq, &sn, &cs);
+    const float a = __half2float(v[i]), b = __half2float(v[i + 64]);
+    v[i] = __float2half_rn(a * cs - b * sn);
+    v[i + 64] = __float2half_rn(b * cs + a * sn);
+  }
+}
+
+// a[r, j] = silu(gu[r, j]) * gu[r, F + j], 8 columns per thread (F % 8 == 0).
+__global__ void swiglu_kernel(const __half* __restrict__ gu, long long ldgu, __half* __restrict__ a,
+                              long long lda, int rows, int F) {
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const int per_row = F / 8;
+  if (idx >= (long long)rows * per_row) return;
+  const int r = (int)(idx / per_row), c = (int)(idx - (long long)r * per_row) * 8;
+  const uint4 g = *reinterpret_cast<const uint4*>(gu + (long long)r * ldgu + c);
+  const uint4 u = *reinterpret_cast<const uint4*>(gu + (long long)r * ldgu + F + c);
+  const __half2* gh = reinterpret_cast<const __half2*>(&g);
+  const __half2* uh = reinterpret_cast<const __half2*>(&u);
+  uint4 o;
+  __half2* oh = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 gf = __half22float2(gh[e]), uf = __half22float2(uh[e]);
+    const float s0 = gf.x / (1.0f + expf(-gf.x)), s1 = gf.y / (1.0f + expf(-gf.y));
+    oh[e] = __floats2half2_rn(s0 * uf.x, s1 * uf.y);
+  }
+  *reinterpret_cast<uint4*>(a + (long long)r * lda + c) = o;
+}
+
+hxb_status_t launch_rmsnorm(const void* x, int64_t ldx, const void* gamma, void* y, int64_t ldy,
+                            int64_t rows, int64_t cols, float eps, cudaStream_t stream) {
+  const int threads = 256;
+  const long long blocks = (rows * 32 + threads - 1) / threads;
+  rmsnorm_kernel<<<(unsigned)blocks, threads, 0, stream>>>(
+      static_cast<const __half*>(x), ldx, static_cast<const __half*>(gamma),
+      static_cast<__half*>(y), ldy, (int)rows, (int)cols, eps);
+  return cuda_status(cudaGetLastError(), "rmsnorm launch");
+}
+
+hxb_status_t launch_rope(void* x, int64_t ldx, int64_t rows, int64_t heads, int64_t seq,
+                         int64_t pos0, float theta, cudaStream_t stream) {
+  const int threads = 256;
+  const long long blocks = (rows * heads * 32 + threads - 1) / threads;
+  rope_kernel<<<(unsigned)blocks, threads, 0, stream>>>(static_cast<__half*>(x), ldx, (int)rows,
+                                                        (int)heads, (int)seq, (int)pos0,
+                                                        log2f(theta));
+  return cuda_status(cudaGetLastError(), "rope launch");
+}
+
+hxb_status_t launch_swiglu(const void* gu, int64_t ldgu, void* a, int64_t lda, int64_t rows,
+                           int64_t F, cudaStream_t stream) {
+  const int threads = 256;
+  const long long blocks = (rows * (F / 8) + threads - 1) / threads;
+  swiglu_kernel<<<(unsigned)blocks, threads, 0, stream>>>(static_cast<const __half*>(gu), ldgu,
+                                                          static_cast<__half*>(a), lda, (int)rows,
+                                                          (int)F);
+  return cuda_status(cudaGetLastError(), "swiglu launch");
+}
+
+size_t round256(size_t b) { return (b + 255) & ~size_t(255); }
+
+struct DecoderBuffers {
+  size_t h, qkv, att, h2, gu, a, total;
+};
+
+DecoderBuffers decoder_layout(const hxb_decoder_w8_t* w, int64_t rows) {
+  DecoderBuffers b{};
+  size_t off = 0;
+  b.h = off;   off += round256((size_t)rows * w->hidden * 2);
+  b.qkv = off; off += round256((size_t)rows * 3 * w->hidden * 2);
+  b.att = off; off += round256((size_t)rows * w->hidden * 2);
+  b.h2 = off;  off += round256((size_t)rows * w->hidden * 2);
+  b.gu = off;  off += round256((size_t)rows * 2 * w->ffn * 2);
+  b.a = off;   off += round256((size_t)rows * w->ffn * 2);
+  b.total = off + 256;  // alignment slack
+  return b;
+}
+
+hxb_status_t check_decoder(const hxb_decoder_w8_t* w, int64_t batch, int64_t seq) {
+  if (!w) return fail(HXB_STATUS_INVALID_ARGUMENT, "decoder: null weights");
+  if (w->head_dim != 128)
+    return fail(HXB_STATUS_UNSUPPORTED, "decoder: head_dim must be 128");
+  if (w->heads < 1 || w->hidden != w->heads * w->head_dim)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "decoder: hidden must equal heads * head_dim");
+  if (w->ffn < 8 || w->ffn % 8)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "decoder: ffn must be a positive multiple of 8");
+  if (batch < 1 || seq < 1 || batch * seq > INT32_MAX)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "decoder: bad batch / seq");
+  if (!w->attn_norm || !w->w_qkv || !w->s_qkv || !w->w_o || !w->s_o || !w->ffn_norm ||
+      !w->w_gate_up || !w->s_gate_up || !w->w_down || !w->s_down)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "decoder: null weight pointer");
+  if (!(w->rope_theta > 1.0f) || !(w->rms_eps >= 0.0f))
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "decoder: bad rope_theta / rms_eps");
+  return HXB_OK;
+}
+
+}  // namespace
+}  // namespace hxb
+
+extern "C" hxb_status_t hxb_rmsnorm_f16(const void* x, int64_t ldx, const void* gamma, void* y,
+                                        int64_t ldy, int64_t rows, int64_t cols, float eps,
+                                        void* stream) {
+  using namespace hxb;
+  if (!x || !gamma || !y || rows < 1 || cols < 8 || cols % 8 || ldx % 8 || ldy % 8 ||
+      ldx < cols || ldy < cols || !aligned16(x) || !aligned16(y) || !aligned16(gamma) ||
+      rows > INT32_MAX / 32)
+    return fail(HXB_STATUS_INVALID_ARGUMENT,
+                "rmsnorm: need cols %% 8 == 0, 16-byte aligned rows, ld >= cols");
+  return launch_rmsnorm(x, ldx, gamma, y, ldy, rows, cols, eps, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" hxb_status_t hxb_rope_f16(void* x, int64_t ldx, int64_t rows, int64_t heads,
+                                     int64_t head_dim, int64_t seq, int64_t pos0, float theta,
+                                     void* stream) {
+  using namespace hxb;
+  if (head_dim != 128) return fail(HXB_STATUS_UNSUPPORTED, "rope: head_dim must be 128");
+  if (!x || rows < 1 || heads < 1 || seq < 1 || ldx < heads * 128 || !(theta > 1.0f) ||
+      rows * heads > INT32_MAX / 32 || pos0 < 0 || pos0 + seq > (1 << 24))
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "rope: bad arguments");
+  return launch_rope(x, ldx, rows, heads, seq, pos0, theta, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" hxb_status_t hxb_swiglu_f16(const void* gu, int64_t ldgu, void* a, int64_t lda,
+                                       int64_t rows, int64_t ffn, void* stream) {
+  using namespace hxb;
+  if (!gu || !a || rows < 1 || ffn < 8 || ffn % 8 || ldgu % 8 || lda % 8 || ldgu < 2 * ffn ||
+      lda < ffn || !aligned16(gu) || !aligned16(a))
+    return fail(HXB_STATUS_INVALID_ARGUMENT,
+                "swiglu: need ffn %% 8 == 0, 16-byte aligned rows, ldgu >= 2*ffn");
+  return launch_swiglu(gu, ldgu, a, lda, rows, ffn, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" size_t hxb_decoder_block_workspace_bytes(const hxb_decoder_w8_t* w, int64_t batch,
+                                                    int64_t seq) {
+  if (hxb::check_decoder(w, batch, seq) != HXB_OK) return 0;
+  return hxb::decoder_layout(w, batch * seq).total;
+}
+
+extern "C" hxb_status_t hxb_decoder_block_w8a16(const hxb_decoder_w8_t* w, const void* x,
+                                                void* out, int64_t batch, int64_t seq,
+                                                int64_t pos0, void* workspace,
+                                                size_t workspace_bytes, void* stream_ptr) {
+  using namespace hxb;
+  hxb_status_t s = check_decoder(w, batch, seq);
+  if (s != HXB_OK) return s;
+  if (!x || !out || !aligned16(x) || !aligned16(out))
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "decoder: x / out must be 16-byte aligned");
+  const int64_t rows = batch * seq, H = w->hidden, F = w->ffn;
+  const DecoderBuffers b = decoder_layout(w, rows);
+  if (!workspace || workspace_bytes < b.total)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "decoder: workspace needs %zu bytes, got %zu",
+                b.total, workspace_bytes);
+  uint8_t* ws = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
+  __half* h = reinterpret_cast<__half*>(ws + b.h);
+  __half* qkv = reinterpret_cast<__half*>(ws + b.qkv);
+  __half* att = reinterpret_cast<__half*>(ws + b.att);
+  __half* h2 = reinterpret_cast<__half*>(ws + b.h2);
+  __half* gu = reinterpret_cast<__half*>(ws + b.gu);
+  __half* a = reinterpret_cast<__half*>(ws + b.a);
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+
+  if ((s = launch_rmsnorm(x, H, w->attn_norm, h, H, rows, H, w->rms_eps, stream)) != HXB_OK) return s;
+  if ((s = matmul_w8a16_impl(h, H, w->w_qkv, 3 * H, w->s_qkv, nullptr, qkv, 3 * H, rows, 3 * H, H,
+                             stream)) != HXB_OK)
+    return s;
+  // q and k are the first 2 * heads heads of every qkv row
+  if ((s = launch_rope(qkv, 3 * H, rows, 2 * w->heads, seq, pos0, w->rope_theta, stream)) != HXB_OK)
+    return s;
+  if ((s = attention_launch(qkv, 3 * H, qkv + H, 3 * H, qkv + 2 * H, 3 * H, att, H, batch,
+                            w->heads, w->heads, seq, seq, w->head_dim,
+                            1.0f / sqrtf((float)w->head_dim), 1, stream)) != HXB_OK)
+    return s;
+  if ((s = matmul_w8a16_impl(att, H, w->w_o, H, w->s_o, x, h2, H, rows, H, H, stream)) != HXB_OK)
+    return s;
+  if ((s = launch_rmsnorm(h2, H, w->ffn_norm, h, H, rows, H, w->rms_eps, stream)) != HXB_OK) return s;
+  if ((s = matmul_w8a16_impl(h, H, w->w_gate_up, 2 * F, w->s_gate_up, nullptr, gu, 2 * F, rows,
+                             2 * F, H, stream)) != HXB_OK)
+    return s;
+  if ((s = launch_swiglu(gu, 2 * F, a, F, rows, F, stream)) != HXB_OK) return s;
+  return matmul_w8a16_impl(a, F, w->w_down, H, w->s_down, h2, out, H, rows, H, F, stream);
+}

@@ -182,7 +182,7 @@ hxb_status_t launch_gemv(const DeviceInfo& dev, const GemvArgs& p, cudaStream_t 
 }
 
 hxb_status_t gemv_w8_impl(const void* A, int64_t lda, const void* W, int64_t ldw,
-                          const void* scale, void* C, int64_t ldc, int64_t M,
+                          const void* scale, const void* R, void* C, int64_t ldc, int64_t M,
                           int64_t N, int64_t K, cudaStream_t stream) {
   DeviceInfo* dev = nullptr;
   hxb_status_t s = current_device(&dev);
@@ -192,6 +192,7 @@ hxb_status_t gemv_w8_impl(const void* A, int64_t lda, const void* W, int64_t ldw
   p.W = static_cast<const int8_t*>(W);
   p.scale = static_cast<const __half*>(scale);
   p.C = static_cast<__half*>(C);
+  p.R = static_cast<const __half*>(R);
   p.ldx = lda;
   p.ldw = ldw;
   p.ldc = ldc;
@@ -202,7 +203,7 @@ hxb_status_t gemv_w8_impl(const void* A, int64_t lda, const void* W, int64_t ldw
 }
 
 hxb_status_t gemm_w8_impl(const void* A, int64_t lda, const void* W,
-                          int64_t ldw, const void* scale, void* C, int64_t ldc,
+                          int64_t ldw, const void* scale, const void* R, void* C, int64_t ldc,
                           int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
   DeviceInfo* dev = nullptr;
   hxb_status_t s = current_device(&dev);
@@ -230,7 +231,7 @@ hxb_status_t gemm_w8_impl(const void* A, int64_t lda, const void* W,
   args.K = (int)K;
   args.C = C;
   args.ldc = ldc;
-  args.C_init = nullptr;
+  args.C_init = R;
   args.scale = static_cast<const __half*>(scale);
   args.status = dev->status_word;
   args.tiles_m = (int)((M + kW8BM - 1) / kW8BM);
@@ -273,11 +274,10 @@ extern "C" hxb_status_t hxb_matmul_f16(const void* A, int64_t lda, const void* B
                             static_cast<cudaStream_t>(stream));
 }
 
-extern "C" hxb_status_t hxb_matmul_w8a16(const void* A, int64_t lda, const void* W,
-                                         int64_t ldw, const void* scale, void* C,
-                                         int64_t ldc, int64_t M, int64_t N, int64_t K,
-                                         void* stream) {
-  using namespace hxb;
+namespace hxb {
+hxb_status_t matmul_w8a16_impl(const void* A, int64_t lda, const void* W, int64_t ldw,
+                               const void* scale, const void* R, void* C, int64_t ldc,
+                               int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
   if (M < 1 || N < 1 || K < 1)
     return fail(HXB_STATUS_INVALID_ARGUMENT, "matmul_w8a16: M, N, K must be >= 1");
   if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX)
@@ -287,13 +287,28 @@ extern "C" hxb_status_t hxb_matmul_w8a16(const void* A, int64_t lda, const void*
   if (lda < K || ldw < N || ldc < N)
     return fail(HXB_STATUS_INVALID_ARGUMENT, "matmul_w8a16: leading dimension too small");
   if (lda % 8 || ldw % 16 || ldc % 8 || !aligned16(A) || !aligned16(W) ||
-      !aligned16(C) || !aligned16(scale))
+      !aligned16(C) || !aligned16(scale) || (R && !aligned16(R)))
     return fail(HXB_STATUS_INVALID_ARGUMENT,
-                "matmul_w8a16: A/W/C/scale must be 16-byte aligned with lda%%8 == 0, "
+                "matmul_w8a16: A/W/C/scale/R must be 16-byte aligned with lda%%8 == 0, "
                 "ldw%%16 == 0, ldc%%8 == 0");
-  if (M <= hxb::kGemvRows)
-    return gemv_w8_impl(A, lda, W, ldw, scale, C, ldc, M, N, K,
-                        static_cast<cudaStream_t>(stream));
-  return gemm_w8_impl(A, lda, W, ldw, scale, C, ldc, M, N, K,
-                      static_cast<cudaStream_t>(stream));
+  if (M <= kGemvRows) return gemv_w8_impl(A, lda, W, ldw, scale, R, C, ldc, M, N, K, stream);
+  return gemm_w8_impl(A, lda, W, ldw, scale, R, C, ldc, M, N, K, stream);
+}
+}  // namespace hxb
+
+extern "C" hxb_status_t hxb_matmul_w8a16(const void* A, int64_t lda, const void* W,
+                                         int64_t ldw, const void* scale, void* C,
+                                         int64_t ldc, int64_t M, int64_t N, int64_t K,
+                                         void* stream) {
+  return hxb::matmul_w8a16_impl(A, lda, W, ldw, scale, nullptr, C, ldc, M, N, K,
+                                static_cast<cudaStream_t>(stream));
+}
+
+extern "C" hxb_status_t hxb_matmul_w8a16_residual(const void* A, int64_t lda, const void* W,
+                                                  int64_t ldw, const void* scale, const void* R,
+                                                  void* C, int64_t ldc, int64_t M, int64_t N,
+                                                  int64_t K, void* stream) {
+  if (!R) return hxb::fail(HXB_STATUS_INVALID_ARGUMENT, "matmul_w8a16_residual: null residual");
+  return hxb::matmul_w8a16_impl(A, lda, W, ldw, scale, R, C, ldc, M, N, K,
+                                static_cast<cudaStream_t>(stream));
 }

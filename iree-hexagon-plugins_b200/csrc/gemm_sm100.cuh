@@ -1,7 +1,6 @@
 // Persistent, warp-specialised tcgen05 GEMM for sm_100a.
 //
 //   C[M,N] = A[M,K] . B  (+ C_init)            f16 x f16 -> f32 accumulate
-//   C[M,N] = (A[M,K] . W[K,N]) * scale[N]      f16 x int8 -> f32 accumulate
 //
 // This is the B200 form of the reference's HMX matmul lowering
 // (plugins/compiler/hexagon/CodeGen/Transforms/HexagonConvertMatmulToHmx.cpp:
@@ -16,7 +15,6 @@
 //   warp 0      TMA producer (one lane)
 //   warp 1      TMEM owner + MMA issuer (one lane)
 //   warps 2-5   epilogue: TMEM -> registers -> global (128 threads = 128 rows)
-//   warps 6-9   (int8 weights only) int8 -> f16 converters, shared -> shared
 // The accumulator is double-buffered in TMEM so the epilogue of tile t
 // overlaps the main loop of tile t+1.
 #pragma once
@@ -29,7 +27,6 @@ namespace hxb {
 enum BMode : int {
   kBF16RowMajorKN = 0,  // B[K,N] row-major f16 (MN-major operand)
   kBF16RowMajorNK = 1,  // B[N,K] row-major f16, i.e. transposed RHS (K-major)
-  kBInt8RowMajorKN = 2  // W[K,N] row-major int8, dequantised in the main loop
 };
 
 enum OutMode : int { kOutF16 = 0, kOutF32 = 1 };
@@ -39,7 +36,7 @@ struct GemmArgs {
   void* C;             // output, row-major with leading dimension ldc
   long long ldc;
   const void* C_init;  // optional, same type/ld as C; added to the product
-  const __half* scale; // per-output-column scale (int8 weights only)
+  const __half* scale; // per-output-column scale (int8-weight dispatch only)
   int* status;         // device status word (timeouts), may be null
   int tiles_m, tiles_n;
   int group_m;         // L2 raster: tiles walk GROUP_M rows of tiles at a time
@@ -53,13 +50,11 @@ template <int BN, int STAGES, int BMODE>
 struct GemmSmem {
   static constexpr int kABytes = kBM * kBK * 2;        // 16 KB
   static constexpr int kBBytes = BN * kBK * 2;         // f16 tile for the MMA
-  static constexpr int kB8Bytes = (BMODE == kBInt8RowMajorKN) ? BN * kBK : 0;
   static constexpr int kOffA = 0;
   static constexpr int kOffB = kOffA + STAGES * kABytes;
-  static constexpr int kOffB8 = kOffB + STAGES * kBBytes;
-  static constexpr int kOffBar = kOffB8 + STAGES * kB8Bytes;
-  // full[S], empty[S], conv[S], tfull[2], tempty[2], drain[1]
-  static constexpr int kNumBars = 3 * STAGES + 5;
+  static constexpr int kOffBar = kOffB + STAGES * kBBytes;
+  // full[S], empty[S], tfull[2], tempty[2], drain[1]
+  static constexpr int kNumBars = 2 * STAGES + 5;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kBytes = kOffMisc + 16;
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-B alignment
@@ -67,7 +62,7 @@ struct GemmSmem {
 
 template <int BN, int BMODE>
 struct GemmShape {
-  static constexpr int kWarps = (BMODE == kBInt8RowMajorKN) ? 10 : 6;
+  static constexpr int kWarps = 6;
   static constexpr int kThreads = kWarps * 32;
   static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
 };
@@ -86,57 +81,15 @@ __device__ __forceinline__ void tile_coords(int t, const GemmArgs& a,
   tn = r / gm;
 }
 
-// Stores the 16 f16 values converted from int8 bytes [16*c16, 16*c16+16) of
-// weight row k into an MN-major, 128B-swizzled operand tile whose 64-column
-// chunks are kBK*128 bytes apart. The two 16-byte halves go to swizzle slots
-// u0^(k&7) and (u0+1)^(k&7); lanes of odd chunks store them in the opposite
-// order so that each 8-lane phase of a 128-bit shared store hits 8 distinct
-// slots (one wavefront) when 8 consecutive lanes cover c16 = 0..7 of a row.
-__device__ __forceinline__ void store_swizzled_pair(uint8_t* dst, int c16, int k,
-                                                    const uint4& o0, const uint4& o1) {
-  const int u0 = (c16 & 3) * 2;
-  uint8_t* row = dst + (c16 >> 2) * (kBK * 128) + k * 128;
-  uint4* p0 = reinterpret_cast<uint4*>(row + ((u0 ^ (k & 7)) << 4));
-  uint4* p1 = reinterpret_cast<uint4*>(row + (((u0 + 1) ^ (k & 7)) << 4));
-  if ((c16 >> 2) & 1) {
-    *p1 = o1;
-    *p0 = o0;
-  } else {
-    *p0 = o0;
-    *p1 = o1;
-  }
-}
-
-// Epilogue for one 32-column chunk of one output row: optional per-column
-// scale (int8 weights), optional C_init add, conversion and store. `r` holds
-// the f32 accumulator bits read from TMEM.
-template <bool SCALED, int OUT>
+// Epilogue for one 32-column chunk of one output row: optional C_init add,
+// conversion and store. `r` holds the f32 accumulator bits read from TMEM.
+template <int OUT>
 __device__ __forceinline__ void store_chunk(const GemmArgs& args, int row,
                                             int col0, const uint32_t (&r)[32]) {
   float v[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
   const bool full_chunk = args.vec_ok && (col0 + 32 <= args.N);
-  if constexpr (SCALED) {
-    if (full_chunk) {
-      const uint4* sp = reinterpret_cast<const uint4*>(args.scale + col0);
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        uint4 s4 = __ldg(sp + u);
-        const __half2* h = reinterpret_cast<const __half2*>(&s4);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          float2 f = __half22float2(h[e]);
-          v[u * 8 + 2 * e] *= f.x;
-          v[u * 8 + 2 * e + 1] *= f.y;
-        }
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (col0 + j < args.N) v[j] *= __half2float(args.scale[col0 + j]);
-    }
-  }
   if constexpr (OUT == kOutF16) {
     __half* crow = reinterpret_cast<__half*>(args.C) + (long long)row * args.ldc;
     const __half* irow =
@@ -214,8 +167,7 @@ __global__ void __launch_bounds__(GemmShape<BN, BMODE>::kThreads, 1)
   constexpr int kTmemCols = GemmShape<BN, BMODE>::kTmemCols;
   constexpr uint32_t kIdesc =
       make_idesc_f16(kBM, BN, 0, BMODE == kBF16RowMajorNK ? 0 : 1);
-  constexpr uint32_t kTxBytes =
-      L::kABytes + (BMODE == kBInt8RowMajorKN ? L::kB8Bytes : L::kBBytes);
+  constexpr uint32_t kTxBytes = L::kABytes + L::kBBytes;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -223,8 +175,7 @@ __global__ void __launch_bounds__(GemmShape<BN, BMODE>::kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
-  uint64_t* conv = bars + 2 * STAGES;
-  uint64_t* tfull = bars + 3 * STAGES;
+  uint64_t* tfull = bars + 2 * STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L::kOffMisc);
@@ -240,7 +191,6 @@ __global__ void __launch_bounds__(GemmShape<BN, BMODE>::kThreads, 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
-      mbar_init(&conv[s], 4);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
@@ -283,12 +233,9 @@ __global__ void __launch_bounds__(GemmShape<BN, BMODE>::kThreads, 1)
             for (int j = 0; j < BN / 64; ++j)
               tma_load_2d(smem + L::kOffB + stage * L::kBBytes + j * (kBK * 128),
                           &tmB, &full[stage], tn * BN + 64 * j, kb * kBK);
-          } else if constexpr (BMODE == kBF16RowMajorNK) {
+          } else {
             tma_load_2d(smem + L::kOffB + stage * L::kBBytes, &tmB, &full[stage],
                         kb * kBK, tn * BN);
-          } else {
-            tma_load_2d(smem + L::kOffB8 + stage * L::kB8Bytes, &tmB,
-                        &full[stage], tn * BN, kb * kBK);
           }
           ++issued;
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -324,8 +271,7 @@ __global__ void __launch_bounds__(GemmShape<BN, BMODE>::kThreads, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = 0; kb < num_kb; ++kb) {
-          uint64_t* ready = (BMODE == kBInt8RowMajorKN) ? &conv[stage] : &full[stage];
-          if (!mbar_wait(ready, phase, fs)) { ok = false; break; }
+          if (!mbar_wait(&full[stage], phase, fs)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(smem + L::kOffA + stage * L::kABytes);
           const uint32_t b_addr = smem_u32(smem + L::kOffB + stage * L::kBBytes);
@@ -356,7 +302,7 @@ __global__ void __launch_bounds__(GemmShape<BN, BMODE>::kThreads, 1)
         }
       }
     }
-  } else if (warp < 6) {
+  } else {
     // ------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     int tl = 0;
@@ -378,43 +324,11 @@ __global__ void __launch_bounds__(GemmShape<BN, BMODE>::kThreads, 1)
         tmem_wait_ld();
         const int col0 = tn * BN + c;
         if (row >= args.M || col0 >= args.N) continue;
-        store_chunk<BMODE == kBInt8RowMajorKN, OUT>(args, row, col0, r);
+        store_chunk<OUT>(args, row, col0, r);
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
-    }
-  } else {
-    // ------------------------------------------------------ int8 -> f16
-    if constexpr (BMODE == kBInt8RowMajorKN) {
-      const int ct = threadIdx.x - 6 * 32;  // 0..127
-      int stage = 0;
-      uint32_t phase = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&full[stage], phase, fs)) { ok = false; break; }
-          const uint8_t* src = smem + L::kOffB8 + stage * L::kB8Bytes;
-          uint8_t* dst = smem + L::kOffB + stage * L::kBBytes;
-          constexpr int kUnitsPerRow = BN / 8;
-#pragma unroll 4
-          for (int w = ct; w < kBK * kUnitsPerRow; w += 128) {
-            const int k = w / kUnitsPerRow;
-            const int c8 = w - k * kUnitsPerRow;
-            const uint2 raw = *reinterpret_cast<const uint2*>(src + k * BN + c8 * 8);
-            uint4 o;
-            i8x4_to_f16x4(raw.x, o.x, o.y);
-            i8x4_to_f16x4(raw.y, o.z, o.w);
-            const int j = c8 >> 3, u = c8 & 7;
-            *reinterpret_cast<uint4*>(dst + j * (kBK * 128) + k * 128 +
-                                      ((u ^ (k & 7)) << 4)) = o;
-          }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&conv[stage]);
-          if (++stage == STAGES) { stage = 0; phase ^= 1; }
-        }
-      }
     }
   }
 

@@ -13,7 +13,8 @@
 //   * one thread issues tcgen05.mma (A from TMEM, B = activations from shared
 //     memory, N = 256 activation rows) into a 256-column f32 TMEM accumulator;
 //   * four epilogue warps read the accumulator back, apply the per-column
-//     scale once (it factors out of the K sum) and store C transposed.
+//     scale once (it factors out of the K sum), add the optional residual and
+//     store C transposed.
 // Shared-memory traffic per k-block is the int8 tile (written by TMA, read
 // once by the converters) plus the activation tile (written by TMA, read by
 // the tensor core); the f16 weights live only in registers and TMEM.
@@ -254,6 +255,9 @@ __global__ void __launch_bounds__(kW8Threads, 1)
       const bool n_ok = n < args.N;
       const float sc = n_ok ? __half2float(args.scale[n]) : 0.0f;
       __half* cbase = reinterpret_cast<__half*>(args.C) + n;
+      // optional residual R (same layout as C): C = acc * scale + R, one rounding
+      const __half* rbase =
+          args.C_init ? reinterpret_cast<const __half*>(args.C_init) + n : nullptr;
       const int m0 = tm * kW8BM;
 #pragma unroll 1
       for (int c = 0; c < kW8BM / 32; ++c) {
@@ -262,14 +266,18 @@ __global__ void __launch_bounds__(kW8Threads, 1)
         tmem_wait_ld();
         const int mc = m0 + 32 * c;
         if (n_ok) {
-          if (mc + 32 <= args.M) {
+          const int cnt = min(32, args.M - mc);
+          if (rbase) {
 #pragma unroll
             for (int e = 0; e < 32; ++e)
-              cbase[(long long)(mc + e) * args.ldc] = __float2half_rn(__uint_as_float(r[e]) * sc);
+              if (e < cnt) {
+                const long long off = (long long)(mc + e) * args.ldc;
+                cbase[off] = __float2half_rn(fmaf(__uint_as_float(r[e]), sc, __half2float(rbase[off])));
+              }
           } else {
 #pragma unroll
             for (int e = 0; e < 32; ++e)
-              if (mc + e < args.M)
+              if (e < cnt)
                 cbase[(long long)(mc + e) * args.ldc] = __float2half_rn(__uint_as_float(r[e]) * sc);
           }
         }

@@ -58,6 +58,7 @@ struct GemvArgs {
   const int8_t* W;  // [K, N], leading dimension ldw (bytes)
   const __half* scale;
   __half* C;        // [M, N], leading dimension ldc
+  const __half* R;  // optional residual, same layout as C: C = X.W * scale + R
   long long ldx, ldw, ldc;
   int M, N, K;
 };
@@ -300,7 +301,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_w8_kernel(const GemvArgs
     float sum = 0.0f;
 #pragma unroll
     for (int w = 0; w < kGemvWarps; ++w) sum += red[w * (kGemvRows * kGemvBN) + o];
-    p.C[(long long)m * p.ldc + n] = __float2half_rn(sum * __half2float(p.scale[n]));
+    const long long off = (long long)m * p.ldc + n;
+    const float rv = p.R ? __half2float(p.R[off]) : 0.0f;
+    p.C[off] = __float2half_rn(fmaf(sum, __half2float(p.scale[n]), rv));
   }
 }
 

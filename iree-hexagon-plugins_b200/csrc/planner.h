@@ -42,10 +42,8 @@ inline GemmPlan plan_gemm(int M, int N, int K, int bmode, int num_sms) {
     if (t.M == M && t.N == N && t.K == K && t.bmode == bmode)
       return GemmPlan{t.block_n, t.group_m};
   }
-  const int cands_f16[3] = {256, 128, 64};
-  const int cands_i8[2] = {256, 128};
-  const int* cands = bmode == 2 ? cands_i8 : cands_f16;
-  const int ncand = bmode == 2 ? 2 : 3;
+  const int cands[3] = {256, 128, 64};
+  const int ncand = 3;
   const int64_t tiles_m = (M + 127) / 128;
   const int64_t kb = (K + 63) / 64;
   GemmPlan best{cands[0], 8};

@@ -66,8 +66,10 @@ def matmul(a: torch.Tensor, b: torch.Tensor, *, transpose_b: bool = False,
 
 
 def matmul_w8a16(a: torch.Tensor, w: torch.Tensor, scale: torch.Tensor,
-                 out: torch.Tensor | None = None) -> torch.Tensor:
-    """C[M,N] f16 = (a[M,K] f16 @ w[K,N] int8) * scale[N] f16, f32 accumulation."""
+                 out: torch.Tensor | None = None,
+                 residual: torch.Tensor | None = None) -> torch.Tensor:
+    """C[M,N] f16 = (a[M,K] f16 @ w[K,N] int8) * scale[N] f16 (+ residual),
+    f32 accumulation."""
     lib = _native.load()
     _require(a.dtype == torch.float16 and w.dtype == torch.int8 and
              scale.dtype == torch.float16, "dtypes must be f16 / int8 / f16")
@@ -76,9 +78,18 @@ def matmul_w8a16(a: torch.Tensor, w: torch.Tensor, scale: torch.Tensor,
     _require(K == Kw and scale.numel() == N and scale.is_contiguous(), "shape mismatch")
     if out is None:
         out = torch.empty((M, N), dtype=torch.float16, device=a.device)
-    check(lib.hxb_matmul_w8a16(a.data_ptr(), _rowmajor_ld(a, "a"), w.data_ptr(),
-                               _rowmajor_ld(w, "w"), scale.data_ptr(), out.data_ptr(),
-                               _rowmajor_ld(out, "out"), M, N, K, _stream_ptr(a)))
+    ldc = _rowmajor_ld(out, "out")
+    if residual is None:
+        check(lib.hxb_matmul_w8a16(a.data_ptr(), _rowmajor_ld(a, "a"), w.data_ptr(),
+                                   _rowmajor_ld(w, "w"), scale.data_ptr(), out.data_ptr(),
+                                   ldc, M, N, K, _stream_ptr(a)))
+    else:
+        _require(residual.shape == out.shape and residual.stride() == out.stride() and
+                 residual.dtype == torch.float16, "residual must match out")
+        check(lib.hxb_matmul_w8a16_residual(a.data_ptr(), _rowmajor_ld(a, "a"), w.data_ptr(),
+                                            _rowmajor_ld(w, "w"), scale.data_ptr(),
+                                            residual.data_ptr(), out.data_ptr(), ldc, M, N,
+                                            K, _stream_ptr(a)))
     return out
 
 
@@ -101,6 +112,99 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     check(lib.hxb_attention_f16(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
                                 BH, Sq, Skv, D, float(scale), int(causal), _stream_ptr(q)))
     return out
+
+
+def attention_bshd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, batch: int,
+                   heads: int, scale: float | None = None, causal: bool = False,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    """Attention over [batch * S, heads * 128] row-major matrices (views with
+    unit inner stride, e.g. column blocks of a fused QKV output)."""
+    lib = _native.load()
+    D = 128
+    Sq, Skv = q.shape[0] // batch, k.shape[0] // batch
+    if scale is None:
+        scale = D ** -0.5
+    if out is None:
+        out = torch.empty((q.shape[0], heads * D), dtype=torch.float16, device=q.device)
+    check(lib.hxb_attention_f16_bshd(
+        q.data_ptr(), _rowmajor_ld(q, "q"), k.data_ptr(), _rowmajor_ld(k, "k"),
+        v.data_ptr(), _rowmajor_ld(v, "v"), out.data_ptr(), _rowmajor_ld(out, "out"),
+        batch, heads, Sq, Skv, D, float(scale), int(causal), _stream_ptr(q)))
+    return out
+
+
+def rmsnorm(x: torch.Tensor, gamma: torch.Tensor, eps: float = 1e-5,
+            out: torch.Tensor | None = None) -> torch.Tensor:
+    lib = _native.load()
+    rows, cols = x.shape
+    if out is None:
+        out = torch.empty_like(x)
+    check(lib.hxb_rmsnorm_f16(x.data_ptr(), _rowmajor_ld(x, "x"), gamma.data_ptr(),
+                              out.data_ptr(), _rowmajor_ld(out, "out"), rows, cols, float(eps),
+                              _stream_ptr(x)))
+    return out
+
+
+def rope_(x: torch.Tensor, heads: int, seq: int, pos0: int = 0,
+          theta: float = 10000.0) -> torch.Tensor:
+    """In-place RoPE on the first `heads` 128-wide heads of every row."""
+    lib = _native.load()
+    check(lib.hxb_rope_f16(x.data_ptr(), _rowmajor_ld(x, "x"), x.shape[0], heads, 128, seq,
+                           pos0, float(theta), _stream_ptr(x)))
+    return x
+
+
+def swiglu(gu: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    lib = _native.load()
+    rows, two_f = gu.shape
+    F = two_f // 2
+    if out is None:
+        out = torch.empty((rows, F), dtype=torch.float16, device=gu.device)
+    check(lib.hxb_swiglu_f16(gu.data_ptr(), _rowmajor_ld(gu, "gu"), out.data_ptr(),
+                             _rowmajor_ld(out, "out"), rows, F, _stream_ptr(gu)))
+    return out
+
+
+class DecoderBlockW8:
+    """Weights of one int8-weight Llama-style decoder block resident on the
+    GPU, and its forward through hxb_decoder_block_w8a16."""
+
+    def __init__(self, *, attn_norm, w_qkv, s_qkv, w_o, s_o, ffn_norm, w_gate_up,
+                 s_gate_up, w_down, s_down, heads: int, rms_eps: float = 1e-5,
+                 rope_theta: float = 10000.0):
+        self.tensors = dict(attn_norm=attn_norm, w_qkv=w_qkv, s_qkv=s_qkv, w_o=w_o, s_o=s_o,
+                            ffn_norm=ffn_norm, w_gate_up=w_gate_up, s_gate_up=s_gate_up,
+                            w_down=w_down, s_down=s_down)
+        for t in self.tensors.values():
+            _require(t.is_cuda and t.is_contiguous(), "weights must be contiguous CUDA tensors")
+        hidden = attn_norm.numel()
+        self.desc = _native.DecoderW8(
+            hidden=hidden, heads=heads, head_dim=hidden // heads, ffn=w_down.shape[0],
+            rms_eps=rms_eps, rope_theta=rope_theta,
+            **{k: v.data_ptr() for k, v in self.tensors.items()})
+        self._ws = None
+
+    def workspace_bytes(self, batch: int, seq: int) -> int:
+        import ctypes
+        return _native.load().hxb_decoder_block_workspace_bytes(ctypes.byref(self.desc),
+                                                                batch, seq)
+
+    def __call__(self, x: torch.Tensor, *, batch: int = 1, pos0: int = 0,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+        import ctypes
+        lib = _native.load()
+        rows = x.shape[0]
+        seq = rows // batch
+        need = self.workspace_bytes(batch, seq)
+        _require(need > 0, "invalid decoder description")
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = torch.empty(need, dtype=torch.uint8, device=x.device)
+        if out is None:
+            out = torch.empty_like(x)
+        check(lib.hxb_decoder_block_w8a16(ctypes.byref(self.desc), x.data_ptr(), out.data_ptr(),
+                                          batch, seq, pos0, self._ws.data_ptr(),
+                                          self._ws.numel(), _stream_ptr(x)))
+        return out
 
 
 def device_status(clear: bool = True) -> int:

@@ -157,3 +157,95 @@ def hmx_vtcm_tile_search(M: int, N: int, K: int, *, lhs_bytes: int = 2,
                 continue
             best, best_rank = [mt, nt, K], rank
     return best
+
+
+# ------------------------------------------------------------ decoder block
+# The reference has no decoder kernels; its decoder models are Hugging Face
+# Llama modules run by torch (integration_tests/models/meta-llama/
+# Llama-3.2-1B-Instruct/model.py:8-16 loads a Llama checkpoint with transformers'
+# AutoModelForCausalLM). These
+# restate the arithmetic of those modules for an f16 model: statistics in f32,
+# every intermediate tensor rounded to f16 where the f16 model stores one.
+
+def rmsnorm_f16(x: np.ndarray, gamma: np.ndarray, eps: float = 1e-5) -> np.ndarray:
+    """LlamaRMSNorm: f32 mean of squares, x * rsqrt(var + eps) rounded to f16,
+    times the f16 weight (one f16 rounding of the product)."""
+    x32 = x.astype(np.float32)
+    var = np.mean(x32.astype(np.float64) ** 2, axis=-1, keepdims=True).astype(np.float32)
+    y = (x32 * (1.0 / np.sqrt(var + np.float32(eps))).astype(np.float32)).astype(np.float16)
+    return (y.astype(np.float32) * gamma.astype(np.float32)).astype(np.float16)
+
+
+def rope_f16(x: np.ndarray, heads: int, seq: int, pos0: int = 0,
+             theta: float = 10000.0) -> np.ndarray:
+    """Llama rotary embedding (rotate_half convention) applied to the first
+    `heads` 128-wide heads of every row; row r has position pos0 + r % seq."""
+    out = x.copy()
+    rows = x.shape[0]
+    i = np.arange(64, dtype=np.float64)
+    inv_freq = theta ** (-2.0 * i / 128.0)
+    pos = (pos0 + np.arange(rows) % seq).astype(np.float64)
+    ang = pos[:, None] * inv_freq[None, :]
+    cs, sn = np.cos(ang), np.sin(ang)
+    for h in range(heads):
+        a = x[:, h * 128:h * 128 + 64].astype(np.float64)
+        b = x[:, h * 128 + 64:h * 128 + 128].astype(np.float64)
+        out[:, h * 128:h * 128 + 64] = (a * cs - b * sn).astype(np.float16)
+        out[:, h * 128 + 64:h * 128 + 128] = (b * cs + a * sn).astype(np.float16)
+    return out
+
+
+def swiglu_f16(gu: np.ndarray) -> np.ndarray:
+    """LlamaMLP activation: silu(gate) * up on a fused [rows, 2F] gate/up output."""
+    F = gu.shape[1] // 2
+    g = gu[:, :F].astype(np.float64)
+    u = gu[:, F:].astype(np.float64)
+    return (g / (1.0 + np.exp(-g)) * u).astype(np.float16)
+
+
+def linear_w8_f16(a: np.ndarray, w: np.ndarray, s: np.ndarray,
+                  residual: np.ndarray | None = None) -> np.ndarray:
+    """f16(a . w * s [+ residual]) with the contraction in f32 (one rounding)."""
+    c = matmul_w8a16_f32(a, w, s)
+    if residual is not None:
+        c = c + residual.astype(np.float32)
+    return c.astype(np.float16)
+
+
+def attention_bshd_f16(qkv_or_q: np.ndarray, *, heads: int, seq: int, batch: int = 1,
+                       k: np.ndarray | None = None, v: np.ndarray | None = None,
+                       causal: bool = True) -> np.ndarray:
+    """Attention over [batch*seq, heads*128] q/k/v matrices (or the q, k, v
+    column blocks of one fused [rows, 3*heads*128] matrix), output in the same
+    [batch*seq, heads*128] order, rounded to f16."""
+    HD = heads * 128
+    if k is None:
+        q, k, v = qkv_or_q[:, :HD], qkv_or_q[:, HD:2 * HD], qkv_or_q[:, 2 * HD:3 * HD]
+    else:
+        q = qkv_or_q
+
+    def to_bh(t):
+        return np.ascontiguousarray(
+            t.reshape(batch, seq, heads, 128).transpose(0, 2, 1, 3).reshape(batch * heads, seq, 128))
+    o = attention_f32(to_bh(q), to_bh(k), to_bh(v), causal=causal).astype(np.float16)
+    return np.ascontiguousarray(o.reshape(batch, heads, seq, 128).transpose(0, 2, 1, 3)
+                                .reshape(batch * seq, HD))
+
+
+def decoder_block_w8(x: np.ndarray, wt: dict, *, heads: int, batch: int = 1, pos0: int = 0,
+                     eps: float = 1e-5, theta: float = 10000.0) -> dict:
+    """Every intermediate of the decoder block for
+    x [batch*seq, hidden] f16; wt holds attn_norm, w_qkv, s_qkv, w_o, s_o,
+    ffn_norm, w_gate_up, s_gate_up, w_down, s_down as numpy arrays."""
+    seq = x.shape[0] // batch
+    r = {}
+    r["h"] = rmsnorm_f16(x, wt["attn_norm"], eps)
+    r["qkv_raw"] = linear_w8_f16(r["h"], wt["w_qkv"], wt["s_qkv"])
+    r["qkv"] = rope_f16(r["qkv_raw"], 2 * heads, seq, pos0, theta)
+    r["att"] = attention_bshd_f16(r["qkv"], heads=heads, seq=seq, batch=batch)
+    r["h2"] = linear_w8_f16(r["att"], wt["w_o"], wt["s_o"], residual=x)
+    r["n2"] = rmsnorm_f16(r["h2"], wt["ffn_norm"], eps)
+    r["gu"] = linear_w8_f16(r["n2"], wt["w_gate_up"], wt["s_gate_up"])
+    r["a"] = swiglu_f16(r["gu"])
+    r["out"] = linear_w8_f16(r["a"], wt["w_down"], wt["s_down"], residual=r["h2"])
+    return r
