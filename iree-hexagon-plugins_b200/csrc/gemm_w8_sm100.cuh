@@ -6,10 +6,10 @@
 //   * TMA lands the raw int8 weight tile [64 k][128 n] (8 KB, 128-byte
 //     swizzle) and the activation tile [256 m][64 k] f16 (32 KB) in two
 //     independent rings;
-//   * eight converter warps transpose the int8 tile in registers (byte
-//     permutes + xor-shuffles), convert it exactly to f16 (|w| <= 127) and
-//     write it into TMEM with tcgen05.st, where it is the A operand
-//     (M = 128 weight columns) of tcgen05.mma;
+//   * eight converter warps transpose the int8 tile on its way out of shared
+//     memory (ldmatrix.trans), convert it exactly to f16 (|w| <= 127) in
+//     registers and write it into TMEM with tcgen05.st, where it is the A
+//     operand (M = 128 weight columns) of tcgen05.mma;
 //   * one thread issues tcgen05.mma (A from TMEM, B = activations from shared
 //     memory, N = 256 activation rows) into a 256-column f32 TMEM accumulator;
 //   * four epilogue warps read the accumulator back, apply the per-column
@@ -23,8 +23,8 @@
 //   warp 0        TMA producer (one lane)
 //   warp 1        TMEM owner + MMA issuer (one lane)
 //   warps 2-3     idle
-//   warps 4-11    int8 -> f16 converters (two per TMEM lane quarter, each half
-//                 of the 64 k rows of a block)
+//   warps 4-11    int8 -> f16 converters (two per TMEM lane quarter, each one
+//                 16-column chunk of the block)
 //   warps 12-15   epilogue
 // TMEM: accumulator in columns [0, 256), kW8SA converted weight stages of 32
 // columns from column 256.
@@ -211,8 +211,8 @@ __global__ void __launch_bounds__(kW8Threads, 1)
   } else if (warp >= 4 && warp < 4 + kW8ConvWarps) {
     // ------------------------------------------------------ int8 -> f16 -> TMEM
     const int q = warp & 3;
-    const int half = (warp - 4) >> 2;  // k rows [32 half, 32 half + 32) of a block
-    const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
+    const int h = (warp - 4) >> 2;  // the warp's 16-column chunk of the quarter
+    const int chunk = 2 * q + h;
     RingCursor<kW8SW> cw;
     RingCursor<kW8SA> ca;
     bool ok = true;
@@ -223,11 +223,8 @@ __global__ void __launch_bounds__(kW8Threads, 1)
                            mbar_wait(&a_empty[sa], ca.phase ^ 1, fs);
         if (!__all_sync(0xffffffffu, ready)) { ok = false; break; }
         tc_fence_after();
-        const uint8_t* tile = smem + L::kOffW + sw * L::kWBytes;
-        if (half == 0)
-          w8_rows_to_tmem<0, 8>(tile, lane_base, 256 + 32 * sa, q, lane);
-        else
-          w8_rows_to_tmem<8, 8>(tile, lane_base, 256 + 32 * sa, q, lane);
+        w8_chunk_to_tmem(smem_u32(smem + L::kOffW + sw * L::kWBytes), tmem_base, 16 * chunk,
+                         256 + 32 * sa, chunk, lane);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
@@ -241,44 +238,59 @@ __global__ void __launch_bounds__(kW8Threads, 1)
     }
   } else if (warp >= 4 + kW8ConvWarps) {
     // ------------------------------------------------------ epilogue
+    // tcgen05.ld.16x256b gives lane t the TMEM lanes t/4 and t/4 + 8 of a
+    // 16-lane group -- weight columns n and n + 1 (see w8_tmem.cuh) -- at
+    // accumulator columns (activation rows) m, m + 1: each pair (n, n + 1) of
+    // one row m is stored as one 4-byte f16x2.
     const int q = warp & 3;
-    const int l = q * 32 + lane;
-    const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
+    const int t = lane;
     int tl = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tl) {
+    for (int tt = blockIdx.x; tt < num_tiles; tt += gridDim.x, ++tl) {
       int tm, tn;
-      tile_coords(t, args, tm, tn);
+      tile_coords(tt, args, tm, tn);
       const bool ready = mbar_wait(t_full, (uint32_t)(tl & 1), fs);
       if (!__all_sync(0xffffffffu, ready)) break;
       tc_fence_after();
-      const int n = tn * kW8BN + w8_lane_to_col(l);
-      const bool n_ok = n < args.N;
-      const float sc = n_ok ? __half2float(args.scale[n]) : 0.0f;
-      __half* cbase = reinterpret_cast<__half*>(args.C) + n;
-      // optional residual R (same layout as C): C = acc * scale + R, one rounding
-      const __half* rbase =
-          args.C_init ? reinterpret_cast<const __half*>(args.C_init) + n : nullptr;
       const int m0 = tm * kW8BM;
 #pragma unroll 1
-      for (int c = 0; c < kW8BM / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(lane_base + 32 * c, r);
-        tmem_wait_ld();
-        const int mc = m0 + 32 * c;
-        if (n_ok) {
-          const int cnt = min(32, args.M - mc);
-          if (rbase) {
+      for (int h = 0; h < 2; ++h) {
+        const int chunk = 2 * q + h;
+        const int n = tn * kW8BN + 16 * chunk + 2 * (t >> 2);
+        const bool n0_ok = n < args.N, n1_ok = n + 1 < args.N;
+        const float s0 = n0_ok ? __half2float(args.scale[n]) : 0.0f;
+        const float s1 = n1_ok ? __half2float(args.scale[n + 1]) : 0.0f;
+        __half* cbase = reinterpret_cast<__half*>(args.C) + n;
+        const __half* rbase =
+            args.C_init ? reinterpret_cast<const __half*>(args.C_init) + n : nullptr;
+        const uint32_t taddr = tmem_base + ((uint32_t)(16 * chunk) << 16);
+#pragma unroll 1
+        for (int c = 0; c < kW8BM / 32; ++c) {
+          uint32_t r[16];
+          tmem_ld_16x256b_x4(taddr + 32 * c, r);
+          tmem_wait_ld();
+          if (!n0_ok) continue;
 #pragma unroll
-            for (int e = 0; e < 32; ++e)
-              if (e < cnt) {
-                const long long off = (long long)(mc + e) * args.ldc;
-                cbase[off] = __float2half_rn(fmaf(__uint_as_float(r[e]), sc, __half2float(rbase[off])));
+          for (int rep = 0; rep < 4; ++rep) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              const int m = m0 + 32 * c + 8 * rep + 2 * (t & 3) + j;
+              if (m >= args.M) continue;
+              float v0 = __uint_as_float(r[4 * rep + j]) * s0;
+              float v1 = __uint_as_float(r[4 * rep + 2 + j]) * s1;
+              const long long off = (long long)m * args.ldc;
+              if (n1_ok) {
+                if (rbase) {
+                  const float2 rv =
+                      __half22float2(*reinterpret_cast<const __half2*>(rbase + off));
+                  v0 += rv.x;
+                  v1 += rv.y;
+                }
+                *reinterpret_cast<__half2*>(cbase + off) = __floats2half2_rn(v0, v1);
+              } else {
+                if (rbase) v0 += __half2float(rbase[off]);
+                cbase[off] = __float2half_rn(v0);
               }
-          } else {
-#pragma unroll
-            for (int e = 0; e < 32; ++e)
-              if (e < cnt)
-                cbase[(long long)(mc + e) * args.ldc] = __float2half_rn(__uint_as_float(r[e]) * sc);
+            }
           }
         }
       }

@@ -11,16 +11,20 @@
 // with the 128-byte swizzle: 16-byte chunk c of row k sits at chunk position
 // c ^ (k & 7).
 //
-// Converter mapping (warps of TMEM lane quarter q, lane t = 4a + b):
-//   * the four lanes a*4 + {0..3} cover one 4-byte word of n values and four
-//     consecutive k rows; lane b loads row 4i+b of that word, then a 4x4 byte
-//     transpose (two xor-shuffles and two byte permutes) leaves lane b with
-//     rows 4i..4i+3 of the single column n = word + b;
-//   * warp q covers 16-byte chunks q and q+4, so the 8 words one load
-//     instruction reads from 4 rows land in 8 distinct bank groups;
-//   * hence TMEM lane 32q + 4a + b holds weight column
-//       n(l) = (a < 4 ? 16q + 4a : 64 + 16q + 4(a-4)) + b,
-//     a fixed permutation the epilogue undoes.
+// The transpose is done by the shared-memory load itself: ldmatrix.trans on
+// 8 x 8 matrices of 16-bit elements, where one element is a pair of
+// neighbouring int8 columns (n, n+1) of one k row. Matrix g of a 16-column
+// chunk is rows k = 8g .. 8g+7 (consecutive rows, so its eight 16-byte rows
+// sit in eight different bank groups under the swizzle); lane t receives
+// {W[k][n0], W[k][n0+1], W[k+1][n0], W[k+1][n0+1]} with k = 8g + 2(t % 4) and
+// n0 = 16c + 2(t / 4). Bytes 0 and 2 are the f16 pair of column n0 for
+// k-pair column 4g + t % 4, bytes 1 and 3 that of column n0 + 1, which is
+// exactly the register layout of tcgen05.st.16x128b: lane t writes TMEM lanes
+// t/4 (column n0) and t/4 + 8 (column n0 + 1) at column t % 4 + 4g.
+//
+// Hence, within the 16 TMEM lanes L0 .. L0+15 that hold chunk c, lane L0 + i
+// holds weight column 16c + 2i for i < 8 and 16c + 2(i - 8) + 1 for i >= 8;
+// warp quarter q holds chunks 2q (lanes 32q .. 32q+15) and 2q + 1.
 #pragma once
 
 #include "sm100.cuh"
@@ -29,13 +33,20 @@ namespace hxb {
 
 // Weight column (0..127 within the tile) held by TMEM lane `l` (0..127).
 __host__ __device__ __forceinline__ int w8_lane_to_col(int l) {
-  const int q = l >> 5, t = l & 31, a = t >> 2, b = t & 3;
-  return (a < 4 ? 16 * q + 4 * a : 64 + 16 * q + 4 * (a - 4)) + b;
+  const int i = l & 15;
+  return 16 * (l >> 4) + (i < 8 ? 2 * i : 2 * (i - 8) + 1);
 }
 
-__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_16x128b_x8(uint32_t taddr, const uint32_t (&r)[16]) {
   asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "tcgen05.st.sync.aligned.16x128b.x8.b32 [%0], "
       "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
       "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
       "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
@@ -43,48 +54,48 @@ __device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_
       : "memory");
 }
 
-// Converts k rows [4 * I0, 4 * (I0 + NI)) of one [64 k][128 n] int8 tile
-// (swizzled, see above) into the 2 * NI TMEM columns starting at
-// `tmem_col + 2 * I0` of this warp's lane quarter: column j holds the f16
-// pair (W[2j][n], W[2j+1][n]) for the lane's weight column n. Called by a
-// whole warp; `quarter` = warp index % 4. Ends with the TMEM stores issued
-// (the caller waits with tmem_wait_st()). All loads are issued before the
-// first shuffle so their latencies overlap.
-template <int I0, int NI>
-__device__ __forceinline__ void w8_rows_to_tmem(const uint8_t* tile, uint32_t tmem_lane_base,
-                                                uint32_t tmem_col, int quarter, int lane) {
-  static_assert(NI == 8 || NI == 16, "8 or 16 row quads");
-  const int a = lane >> 2, b = lane & 3;
-  const int chunk = a < 4 ? quarter : quarter + 4;
-  const int word = (a & 3) * 4;
-  // prmt selectors of the two transpose stages
-  const uint32_t sel1 = (b & 1) ? 0x3715u : 0x6240u;
-  const uint32_t sel2 = (b & 2) ? 0x3276u : 0x5410u;
-  uint32_t x[NI];
+// 16 TMEM lanes x 32 columns: lane t receives, for repetition r = 0..3,
+// {lane t/4: columns 8r + 2(t%4), +1; lane t/4 + 8: the same columns} in
+// registers 4r .. 4r+3.
+__device__ __forceinline__ void tmem_ld_16x256b_x4(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x256b.x4.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+// Converts the 16-column chunk `chunk` (columns 16c .. 16c+15, all 64 k rows)
+// of one int8 tile into the 32 TMEM columns starting at `tmem_col` of the 16
+// TMEM lanes starting at lane `lane0` (a multiple of 16 inside this warp's
+// lane quarter). Called by a whole warp. Ends with the TMEM store issued (the
+// caller waits with tmem_wait_st()).
+__device__ __forceinline__ void w8_chunk_to_tmem(uint32_t tile_s, uint32_t tmem_base, int lane0,
+                                                 uint32_t tmem_col, int chunk, int lane) {
+  // lane t addresses row (t % 8) of matrix t / 8 of each 4-matrix load
+  const int mrow = lane & 7, mat = lane >> 3;
+  uint32_t raw[8];
 #pragma unroll
-  for (int i = 0; i < NI; ++i) {
-    const int k = 4 * (I0 + i) + b;
-    x[i] = *reinterpret_cast<const uint32_t*>(tile + k * 128 + ((chunk ^ (k & 7)) << 4) + word);
-  }
-  uint32_t out[2 * NI];
+  for (int s = 0; s < 2; ++s) {
+    const int k = 8 * (4 * s + mat) + mrow;
+    uint32_t r4[4];
+    ldsm_x4_trans(tile_s + k * 128 + ((chunk ^ (k & 7)) << 4), r4);
 #pragma unroll
-  for (int i = 0; i < NI; ++i) {
-    // stage 1: 2x2 byte blocks with the neighbouring row
-    const uint32_t y = __shfl_xor_sync(0xffffffffu, x[i], 1);
-    uint32_t s1;
-    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(s1) : "r"(x[i]), "r"(y), "r"(sel1));
-    // stage 2: 16-bit halves with the row pair two lanes away
-    const uint32_t z = __shfl_xor_sync(0xffffffffu, s1, 2);
-    uint32_t col;
-    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(col) : "r"(s1), "r"(z), "r"(sel2));
-    // col = {W[4i][n], W[4i+1][n], W[4i+2][n], W[4i+3][n]}
-    i8x4_to_f16x4(col, out[2 * i], out[2 * i + 1]);
+    for (int i = 0; i < 4; ++i) raw[4 * s + i] = r4[i];
   }
-  if constexpr (NI == 16) {
-    tmem_st_32x32b_x32(tmem_lane_base + tmem_col + 2 * I0, out);
-  } else {
-    tmem_st_32x32b_x16(tmem_lane_base + tmem_col + 2 * I0, out);
+  uint32_t out[16];
+#pragma unroll
+  for (int g = 0; g < 8; ++g) {
+    // bytes {0, 2}: column n0, bytes {1, 3}: column n0 + 1; each as
+    // {b ^ 0x80, 0x64} = f16 1024 + (b + 128), minus 1152 -> exact b
+    const uint32_t lo = (raw[g] & 0x00FF00FFu) ^ 0x64806480u;
+    const uint32_t hi = ((raw[g] >> 8) & 0x00FF00FFu) ^ 0x64806480u;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(out[2 * g]) : "r"(lo), "r"(0x64806480u));
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(out[2 * g + 1]) : "r"(hi), "r"(0x64806480u));
   }
+  tmem_st_16x128b_x8(tmem_base + ((uint32_t)lane0 << 16) + tmem_col, out);
 }
 
 }  // namespace hxb
