@@ -11,7 +11,8 @@
 //     registers and write it into TMEM with tcgen05.st, where it is the A
 //     operand (M = 128 weight columns) of tcgen05.mma;
 //   * one thread issues tcgen05.mma (A from TMEM, B = activations from shared
-//     memory, N = 256 activation rows) into a 256-column f32 TMEM accumulator;
+//     memory, N = 192 activation rows) into one of two 192-column f32 TMEM
+//     accumulators, so the epilogue of tile t overlaps the main loop of t+1;
 //   * four epilogue warps read the accumulator back, apply the per-column
 //     scale once (it factors out of the K sum), add the optional residual and
 //     store C transposed.
@@ -26,8 +27,8 @@
 //   warps 4-11    int8 -> f16 converters (two per TMEM lane quarter, each one
 //                 16-column chunk of the block)
 //   warps 12-15   epilogue
-// TMEM: accumulator in columns [0, 256), kW8SA converted weight stages of 32
-// columns from column 256.
+// TMEM: accumulators in columns [0, 192) and [192, 384), kW8SA converted
+// weight stages of 32 columns from column 384.
 #pragma once
 
 #include "gemm_sm100.cuh"
@@ -36,23 +37,24 @@
 namespace hxb {
 
 constexpr int kW8BN = 128;  // weight columns per tile (MMA M, TMEM lanes)
-constexpr int kW8BM = 256;  // activation rows per tile (MMA N)
-constexpr int kW8SX = 4;    // activation stages
+constexpr int kW8BM = 192;  // activation rows per tile (MMA N)
+constexpr int kW8SX = 6;    // activation stages
 constexpr int kW8SW = 8;    // int8 weight stages
-constexpr int kW8SA = 6;    // TMEM weight stages
+constexpr int kW8SA = 4;    // TMEM weight stages
+constexpr int kW8ACol = 2 * kW8BM;  // first TMEM column of the weight stages
 constexpr int kW8Threads = 16 * 32;
 constexpr int kW8ConvWarps = 8;
 constexpr int kW8EpiWarps = 4;
 
 struct W8Smem {
-  static constexpr int kXBytes = kW8BM * kBK * 2;  // 32 KB
+  static constexpr int kXBytes = kW8BM * kBK * 2;  // 24 KB
   static constexpr int kWBytes = kW8BN * kBK;      // 8 KB
   static constexpr int kOffX = 0;
   static constexpr int kOffW = kOffX + kW8SX * kXBytes;
   static constexpr int kOffBar = kOffW + kW8SW * kWBytes;
   // x_full, x_empty [SX]; w_full, w_empty [SW]; a_full, a_empty [SA];
-  // t_full, t_empty, drain
-  static constexpr int kNumBars = 2 * kW8SX + 2 * kW8SW + 2 * kW8SA + 3;
+  // t_full[2], t_empty[2], drain
+  static constexpr int kNumBars = 2 * kW8SX + 2 * kW8SW + 2 * kW8SA + 5;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kBytes = kOffMisc + 16;
   static constexpr int kAlloc = kBytes + 1024;
@@ -93,7 +95,7 @@ __global__ void __launch_bounds__(kW8Threads, 1)
     gemm_w8_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
                          const __grid_constant__ CUtensorMap tmW, const GemmArgs args) {
   using L = W8Smem;
-  // D[128 n x 256 m] += W^T (TMEM, K-major) . A^T (shared, K-major)
+  // D[128 n x 192 m] += W^T (TMEM, K-major) . A^T (shared, K-major)
   constexpr uint32_t kIdesc = make_idesc_f16(kW8BN, kW8BM, 0, 0);
 
   extern __shared__ uint8_t smem_raw[];
@@ -107,8 +109,8 @@ __global__ void __launch_bounds__(kW8Threads, 1)
   uint64_t* a_full = w_empty + kW8SW;
   uint64_t* a_empty = a_full + kW8SA;
   uint64_t* t_full = a_empty + kW8SA;
-  uint64_t* t_empty = t_full + 1;
-  uint64_t* drain = t_empty + 1;
+  uint64_t* t_empty = t_full + 2;
+  uint64_t* drain = t_empty + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 4);
 
@@ -122,8 +124,10 @@ __global__ void __launch_bounds__(kW8Threads, 1)
     for (int s = 0; s < kW8SX; ++s) { mbar_init(&x_full[s], 1); mbar_init(&x_empty[s], 1); }
     for (int s = 0; s < kW8SW; ++s) { mbar_init(&w_full[s], 1); mbar_init(&w_empty[s], kW8ConvWarps); }
     for (int s = 0; s < kW8SA; ++s) { mbar_init(&a_full[s], kW8ConvWarps); mbar_init(&a_empty[s], 1); }
-    mbar_init(t_full, 1);
-    mbar_init(t_empty, kW8EpiWarps);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&t_full[i], 1);
+      mbar_init(&t_empty[i], kW8EpiWarps);
+    }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -177,8 +181,10 @@ __global__ void __launch_bounds__(kW8Threads, 1)
       int tl = 0;
       bool ok = true, issued_any = false;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++tl) {
-        if (!mbar_wait(t_empty, (uint32_t)(tl & 1) ^ 1, fs)) { ok = false; break; }
+        const int acc = tl & 1;
+        if (!mbar_wait(&t_empty[acc], (uint32_t)((tl >> 1) & 1) ^ 1, fs)) { ok = false; break; }
         tc_fence_after();
+        const uint32_t d_tmem = tmem_base + kW8BM * acc;
         for (int kb = 0; kb < num_kb; ++kb) {
           const int sx = cx.slot, sa = ca.slot;
           if (!mbar_wait(&x_full[sx], cx.phase, fs) || !mbar_wait(&a_full[sa], ca.phase, fs)) {
@@ -187,11 +193,11 @@ __global__ void __launch_bounds__(kW8Threads, 1)
           }
           tc_fence_after();
           const uint32_t x_addr = smem_u32(smem + L::kOffX + sx * L::kXBytes);
-          const uint32_t a_tmem = tmem_base + 256 + 32 * sa;
+          const uint32_t a_tmem = tmem_base + kW8ACol + 32 * sa;
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k) {
             const uint64_t bdesc = make_smem_desc(x_addr + k * 32, 16, 1024, kLayoutSwizzle128);
-            umma_f16_ts(tmem_base, a_tmem + 8 * k, bdesc, kIdesc, (kb | k) != 0);
+            umma_f16_ts(d_tmem, a_tmem + 8 * k, bdesc, kIdesc, (kb | k) != 0);
           }
           issued_any = true;
           umma_commit(&x_empty[sx]);
@@ -199,7 +205,7 @@ __global__ void __launch_bounds__(kW8Threads, 1)
           cx.advance();
           ca.advance();
         }
-        if (ok) umma_commit(t_full);
+        if (ok) umma_commit(&t_full[acc]);
       }
       if (!ok && issued_any) {
         umma_commit(drain);
@@ -224,7 +230,7 @@ __global__ void __launch_bounds__(kW8Threads, 1)
         if (!__all_sync(0xffffffffu, ready)) { ok = false; break; }
         tc_fence_after();
         w8_chunk_to_tmem(smem_u32(smem + L::kOffW + sw * L::kWBytes), tmem_base, 16 * chunk,
-                         256 + 32 * sa, chunk, lane);
+                         kW8ACol + 32 * sa, chunk, lane);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
@@ -248,7 +254,8 @@ __global__ void __launch_bounds__(kW8Threads, 1)
     for (int tt = blockIdx.x; tt < num_tiles; tt += gridDim.x, ++tl) {
       int tm, tn;
       tile_coords(tt, args, tm, tn);
-      const bool ready = mbar_wait(t_full, (uint32_t)(tl & 1), fs);
+      const int acc = tl & 1;
+      const bool ready = mbar_wait(&t_full[acc], (uint32_t)((tl >> 1) & 1), fs);
       if (!__all_sync(0xffffffffu, ready)) break;
       tc_fence_after();
       const int m0 = tm * kW8BM;
@@ -262,7 +269,7 @@ __global__ void __launch_bounds__(kW8Threads, 1)
         __half* cbase = reinterpret_cast<__half*>(args.C) + n;
         const __half* rbase =
             args.C_init ? reinterpret_cast<const __half*>(args.C_init) + n : nullptr;
-        const uint32_t taddr = tmem_base + ((uint32_t)(16 * chunk) << 16);
+        const uint32_t taddr = tmem_base + ((uint32_t)(16 * chunk) << 16) + kW8BM * acc;
 #pragma unroll 1
         for (int c = 0; c < kW8BM / 32; ++c) {
           uint32_t r[16];
@@ -296,7 +303,7 @@ __global__ void __launch_bounds__(kW8Threads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(t_empty);
+      if (lane == 0) mbar_arrive(&t_empty[acc]);
     }
   }
 
