@@ -185,6 +185,110 @@ def run_reference(args, rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+SH_M, SH_K, SH_N = 16384, 8192, 28672
+
+
+def run_sharded(args, rank: int, world: int, local_rank: int) -> None:
+    """C[16384, 28672] = A[16384, 8192] . B, B split
+    along N over the ranks; one step = the fused GEMM + all-gather (every rank
+    ends with the full C). Also timed: the GEMM alone into the local shard
+    (compute-only scaling) and the NCCL all-gather baseline."""
+    import torch
+    import torch.distributed as dist
+    import __graft_entry__ as ge
+    from datetime import timedelta
+
+    pkg = ge.load_package()
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    steps = min(args.steps, 50)
+    g = torch.Generator(device=dev).manual_seed(0)
+    a = (torch.rand(SH_M, SH_K, device=dev, generator=g) * 2 - 1).half()
+    sm = pkg.sharded.ShardedMatmul(SH_M, SH_N, SH_K, device=dev)
+    n = sm.end - sm.begin
+    b = (torch.rand(SH_K, n, device=dev, generator=g) * 2 - 1).half()
+    shard = torch.empty(SH_M, n, dtype=torch.float16, device=dev)
+    gathered = torch.empty(world * SH_M, n, dtype=torch.float16, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / steps
+        if world > 1:
+            t = torch.tensor([ms], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    time.sleep(0.3)
+    fused_ms = timed(lambda: sm.fused(a, b))
+    clocks = sampler.stop()
+    compute_ms = timed(lambda: pkg.matmul(a, b, out=shard))
+    nccl_ms = timed(lambda: sm.nccl(a, b, shard_out=shard, gathered=gathered))
+    # e2e: the public call with A copied from pinned host memory and C read
+    # back to the host every step
+    a_h = torch.empty(SH_M, SH_K, dtype=torch.float16, pin_memory=True)
+    a_h.copy_(a.cpu())
+    c_h = torch.empty(SH_M, SH_N, dtype=torch.float16, pin_memory=True)
+
+    def e2e_step():
+        a.copy_(a_h, non_blocking=True)
+        out = sm.fused(a, b)
+        c_h.copy_(out, non_blocking=True)
+    e2e_ms = timed(e2e_step)
+    status = pkg.device_status()
+    sm.close()
+    del sm
+    flop = 2.0 * SH_M * SH_N * SH_K
+    peaks, peak_kind = _peaks()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    per_gpu_flop = flop / world
+    line = {
+        "metric": METRIC, "value": flop / (fused_ms / 1e3) / 1e12, "unit": "TFLOP/s",
+        "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": fused_ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f16->f32", "data": "synthetic",
+        "config": {"workload": "sharded_gemm_16384x8192x28672", "split": f"N over {world} ranks",
+                   "collective": "all-gather fused into the GEMM epilogue (NVLink peer stores)",
+                   "l2": "inputs (A 268 MB) larger than the 126 MB L2"},
+        "compute_only": {"value": flop / (compute_ms / 1e3) / 1e12, "unit": "TFLOP/s",
+                         "ms_per_step": compute_ms, "note": "GEMM into the local shard, C left sharded"},
+        "nccl_baseline": {"value": flop / (nccl_ms / 1e3) / 1e12, "unit": "TFLOP/s",
+                          "ms_per_step": nccl_ms,
+                          "note": "GEMM + NCCL all_gather_into_tensor + layout step"},
+        "roofline": {"bound": "tensor" if world == 1 else "tensor+nvlink",
+                     "achieved": per_gpu_flop / (compute_ms / 1e3) / 1e12,
+                     "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": per_gpu_flop / (compute_ms / 1e3) / 1e12 / peaks["bf16_tflops"],
+                     "traffic": None, "peak_source": f"{peak_kind} bf16 dense (burst)",
+                     "kernel": "gemm_sm100_kernel (per-GPU shard)",
+                     "nvlink_floor_ms": (world - 1) / world * SH_M * SH_N * 2 / 770e9 * 1e3},
+        "e2e": {"value": flop / (e2e_ms / 1e3) / 1e12, "unit": "TFLOP/s",
+                "h2d_bytes_per_step": SH_M * SH_K * 2, "d2h_bytes_per_step": SH_M * SH_N * 2},
+        "gpu_launches": steps * (1 + (2 if world > 1 else 0)),
+        "clocks": clocks, "device_status": status,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -192,6 +296,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["w8a16_gemm", "sharded_gemm"], default="w8a16_gemm",
+                    help="w8a16_gemm: BASELINE configuration 2 (the metric's config, default); "
+                         "sharded_gemm: configuration 5 split along N over the ranks")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -201,6 +308,9 @@ def main():
 
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.workload == "sharded_gemm":
+        run_sharded(args, rank, world, local_rank)
         return
 
     import torch

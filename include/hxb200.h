@@ -162,6 +162,34 @@ hxb_status_t hxb_attention_f16_bshd(const void* Q, int64_t ldq, const void* K,
                                     int64_t D, float scale, int causal,
                                     void* stream);
 
+/* ---- N-sharded f16 matmul across GPUs --------
+ * The reference has no collectives (plugins/runtime/hexagon/channel.c:55-56
+ * returns IREE_STATUS_UNIMPLEMENTED); these entries serve the multi-GPU split
+ * of one large matmul along N, each rank computing C[:, its columns]. */
+
+/* f16 matmul whose epilogue also writes every output tile into the other
+ * ranks' copies of C over NVLink: an all-gather fused into the GEMM.
+ *   C         this rank's column block of its own full [M, ldc] output
+ *             (i.e. full_output + column offset of the shard)
+ *   replicas  nreplicas (0..7) peer pointers to the same column offset in
+ *             the other ranks' full outputs (peer memory, e.g. CUDA IPC)
+ * A is [M, K] (lda), B the rank's shard [K, N] or [N, K] (ldb), both with
+ * 16-byte aligned rows. The caller orders this call after the peers stopped
+ * reading their outputs and synchronises the ranks after it (e.g. a
+ * stream-ordered collective) before reading the gathered C. */
+hxb_status_t hxb_matmul_f16_allgather(const void* A, int64_t lda, const void* B,
+                                      int64_t ldb, int transpose_b, void* C,
+                                      void* const* replicas, int nreplicas,
+                                      int64_t ldc, int64_t M, int64_t N,
+                                      int64_t K, void* stream);
+
+/* dst[m, g*n + j] = src[g, m, j]: the [G, M, n] result of an NCCL all-gather
+ * of column shards laid out as the [M, G*n] matrix (row pitch ldd).
+ * n % 8 == 0, 16-byte aligned buffers. */
+hxb_status_t hxb_gather_column_blocks_f16(const void* src, void* dst, int64_t G,
+                                          int64_t M, int64_t n, int64_t ldd,
+                                          void* stream);
+
 /* ---- Llama-style decoder block ----------------
  * The reference has no decoder kernels of its own; its decoder models are
  * Hugging Face Llama checkpoints run through torch

@@ -8,8 +8,9 @@ identifier it is imported as `iree_hexagon_plugins_b200` through
 """
 from . import _native
 from ._native import HxbError
+from . import sharded
 from .dispatch import (DecoderBlockW8, attention, attention_bshd, device_status, matmul,
                        matmul_w8a16, rmsnorm, rope_, swiglu)
 
-__all__ = ["HxbError", "DecoderBlockW8", "attention", "attention_bshd", "device_status",
+__all__ = ["sharded", "HxbError", "DecoderBlockW8", "attention", "attention_bshd", "device_status",
            "matmul", "matmul_w8a16", "rmsnorm", "rope_", "swiglu", "_native"]

@@ -41,6 +41,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "hxb_rmsnorm_f16": (c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_float, c_vp]),
     "hxb_rope_f16": (c_int, [c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_float, c_vp]),
     "hxb_swiglu_f16": (c_int, [c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_vp]),
+    "hxb_matmul_f16_allgather": (c_int, [c_vp, c_i64, c_vp, c_i64, c_int, c_vp, c_vp, c_int,
+                                         c_i64, c_i64, c_i64, c_i64, c_vp]),
+    "hxb_gather_column_blocks_f16": (c_int, [c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp]),
     "hxb_decoder_block_workspace_bytes": (c_size, [c_vp, c_i64, c_i64]),
     "hxb_decoder_block_w8a16": (c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp,
                                         c_size, c_vp]),

@@ -65,11 +65,11 @@ hxb_status_t make_a_map(CUtensorMap* m, const void* A, int64_t lda, int64_t M,
 
 }  // namespace
 
-hxb_status_t gemm_f16_impl(const void* A, int64_t lda, const void* B,
-                           int64_t ldb, int transpose_b, const void* C_init,
-                           void* C, int64_t ldc, hxb_dtype_t c_dtype, int64_t M,
-                           int64_t N, int64_t K, void* workspace,
-                           size_t workspace_bytes, cudaStream_t stream) {
+hxb_status_t gemm_f16_launch(const void* A, int64_t lda, const void* B, int64_t ldb,
+                             int transpose_b, const void* C_init, void* C, int64_t ldc,
+                             hxb_dtype_t c_dtype, int64_t M, int64_t N, int64_t K,
+                             void* workspace, size_t workspace_bytes, void* const* replicas,
+                             int nreplicas, cudaStream_t stream) {
   if (M < 1 || N < 1 || K < 1)
     return fail(HXB_STATUS_INVALID_ARGUMENT, "matmul: M, N, K must be >= 1 (got %lld, %lld, %lld)",
                 (long long)M, (long long)N, (long long)K);
@@ -154,6 +154,12 @@ hxb_status_t gemm_f16_impl(const void* A, int64_t lda, const void* B,
   const int esz = c_dtype == HXB_DTYPE_F16 ? 2 : 4;
   args.vec_ok = aligned16(C) && (ldc * esz) % 16 == 0 &&
                 (!C_init || aligned16(C_init));
+  args.ndests = nreplicas > 0 ? nreplicas + 1 : 0;
+  args.dests[0] = C;
+  for (int i = 0; i < nreplicas; ++i) {
+    args.dests[i + 1] = const_cast<void*>(replicas[i]);
+    args.vec_ok = args.vec_ok && aligned16(replicas[i]);
+  }
 
   if (c_dtype == HXB_DTYPE_F16) {
     return transpose_b
@@ -180,6 +186,35 @@ hxb_status_t launch_gemv(const DeviceInfo& dev, const GemvArgs& p, cudaStream_t 
   kernel<<<grid, kGemvThreads, GemvSmem::kBytes, stream>>>(p);
   return cuda_status(cudaGetLastError(), "gemv_w8 launch");
 }
+
+hxb_status_t gemm_f16_impl(const void* A, int64_t lda, const void* B,
+                           int64_t ldb, int transpose_b, const void* C_init,
+                           void* C, int64_t ldc, hxb_dtype_t c_dtype, int64_t M,
+                           int64_t N, int64_t K, void* workspace,
+                           size_t workspace_bytes, cudaStream_t stream) {
+  return gemm_f16_launch(A, lda, B, ldb, transpose_b, C_init, C, ldc, c_dtype, M, N, K,
+                         workspace, workspace_bytes, nullptr, 0, stream);
+}
+
+namespace {
+
+// [G, M, n] -> [M, G*n] (column block g of the destination = source block g),
+// 16-byte vectors; the layout step after an NCCL all-gather of column shards.
+__global__ void gather_column_blocks_kernel(const uint4* __restrict__ src, __half* __restrict__ dst,
+                                            long long M, int n, int G, long long ldd) {
+  const long long vec_per_row = n / 8;
+  const long long total = (long long)G * M * vec_per_row;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long v = i % vec_per_row;
+    const long long gm = i / vec_per_row;
+    const long long m = gm % M;
+    const int g = (int)(gm / M);
+    *reinterpret_cast<uint4*>(dst + m * ldd + (long long)g * n + v * 8) = src[i];
+  }
+}
+
+}  // namespace
 
 hxb_status_t gemv_w8_impl(const void* A, int64_t lda, const void* W, int64_t ldw,
                           const void* scale, const void* R, void* C, int64_t ldc, int64_t M,
@@ -311,4 +346,42 @@ extern "C" hxb_status_t hxb_matmul_w8a16_residual(const void* A, int64_t lda, co
   if (!R) return hxb::fail(HXB_STATUS_INVALID_ARGUMENT, "matmul_w8a16_residual: null residual");
   return hxb::matmul_w8a16_impl(A, lda, W, ldw, scale, R, C, ldc, M, N, K,
                                 static_cast<cudaStream_t>(stream));
+}
+
+extern "C" hxb_status_t hxb_matmul_f16_allgather(const void* A, int64_t lda, const void* B,
+                                                 int64_t ldb, int transpose_b, void* C,
+                                                 void* const* replicas, int nreplicas,
+                                                 int64_t ldc, int64_t M, int64_t N, int64_t K,
+                                                 void* stream) {
+  using namespace hxb;
+  if (nreplicas < 0 || nreplicas > kMaxDests - 1)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "matmul_f16_allgather: 0..%d replicas",
+                kMaxDests - 1);
+  if (nreplicas > 0 && !replicas)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "matmul_f16_allgather: null replica list");
+  for (int i = 0; i < nreplicas; ++i)
+    if (!replicas[i])
+      return fail(HXB_STATUS_INVALID_ARGUMENT, "matmul_f16_allgather: null replica %d", i);
+  if (!aligned16(A) || !aligned16(B) || (lda * 2) % 16 || (ldb * 2) % 16)
+    return fail(HXB_STATUS_INVALID_ARGUMENT,
+                "matmul_f16_allgather: A and B need 16-byte aligned rows (no re-pitching)");
+  return gemm_f16_launch(A, lda, B, ldb, transpose_b, nullptr, C, ldc, HXB_DTYPE_F16, M, N, K,
+                         nullptr, 0, replicas, nreplicas, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" hxb_status_t hxb_gather_column_blocks_f16(const void* src, void* dst, int64_t G,
+                                                     int64_t M, int64_t n, int64_t ldd,
+                                                     void* stream) {
+  using namespace hxb;
+  if (!src || !dst || G < 1 || M < 1 || n < 8 || n % 8 || ldd < G * n || ldd % 8 ||
+      !aligned16(src) || !aligned16(dst))
+    return fail(HXB_STATUS_INVALID_ARGUMENT,
+                "gather_column_blocks: need n %% 8 == 0, ldd >= G*n, 16-byte alignment");
+  DeviceInfo* dev = nullptr;
+  hxb_status_t s = current_device(&dev);
+  if (s != HXB_OK) return s;
+  const unsigned grid = (unsigned)(dev->num_sms * 8);
+  gather_column_blocks_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(src), static_cast<__half*>(dst), M, (int)n, (int)G, ldd);
+  return cuda_status(cudaGetLastError(), "gather_column_blocks launch");
 }

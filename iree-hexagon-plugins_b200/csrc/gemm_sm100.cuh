@@ -31,6 +31,8 @@ enum BMode : int {
 
 enum OutMode : int { kOutF16 = 0, kOutF32 = 1 };
 
+constexpr int kMaxDests = 8;  // all-gather epilogue: output replicas (one per rank)
+
 struct GemmArgs {
   int M, N, K;
   void* C;             // output, row-major with leading dimension ldc
@@ -41,6 +43,11 @@ struct GemmArgs {
   int tiles_m, tiles_n;
   int group_m;         // L2 raster: tiles walk GROUP_M rows of tiles at a time
   int vec_ok;          // 1 if C/C_init rows allow 16-byte vector access
+  // All-gather epilogue (f16 output only): when ndests > 0 every output tile
+  // is also written to dests[1..ndests) -- other ranks' copies of the output,
+  // reached over NVLink through peer pointers -- at the same row and column.
+  int ndests;
+  void* dests[kMaxDests];
 };
 
 constexpr int kBM = 128;
@@ -100,7 +107,7 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& args, int row,
       if (irow) {
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          uint4 i4 = *reinterpret_cast<const uint4*>(irow + col0 + u * 8);
+          const uint4 i4 = *reinterpret_cast<const uint4*>(irow + col0 + u * 8);
           const __half2* h = reinterpret_cast<const __half2*>(&i4);
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
@@ -110,14 +117,20 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& args, int row,
           }
         }
       }
+      uint4 o[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        uint4 o;
-        o.x = pack_half2(v[u * 8 + 0], v[u * 8 + 1]);
-        o.y = pack_half2(v[u * 8 + 2], v[u * 8 + 3]);
-        o.z = pack_half2(v[u * 8 + 4], v[u * 8 + 5]);
-        o.w = pack_half2(v[u * 8 + 6], v[u * 8 + 7]);
-        *reinterpret_cast<uint4*>(crow + col0 + u * 8) = o;
+        o[u].x = pack_half2(v[u * 8 + 0], v[u * 8 + 1]);
+        o[u].y = pack_half2(v[u * 8 + 2], v[u * 8 + 3]);
+        o[u].z = pack_half2(v[u * 8 + 4], v[u * 8 + 5]);
+        o[u].w = pack_half2(v[u * 8 + 6], v[u * 8 + 7]);
+        *reinterpret_cast<uint4*>(crow + col0 + u * 8) = o[u];
+      }
+      // replicas on the other ranks: the same 64 bytes at the same offset
+      for (int d = 1; d < args.ndests; ++d) {
+        __half* prow = reinterpret_cast<__half*>(args.dests[d]) + (long long)row * args.ldc;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) *reinterpret_cast<uint4*>(prow + col0 + u * 8) = o[u];
       }
     } else {
 #pragma unroll
@@ -125,7 +138,10 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& args, int row,
         if (col0 + j < args.N) {
           float x = v[j];
           if (irow) x += __half2float(irow[col0 + j]);
-          crow[col0 + j] = __float2half_rn(x);
+          const __half hx = __float2half_rn(x);
+          crow[col0 + j] = hx;
+          for (int d = 1; d < args.ndests; ++d)
+            reinterpret_cast<__half*>(args.dests[d])[(long long)row * args.ldc + col0 + j] = hx;
         }
       }
     }

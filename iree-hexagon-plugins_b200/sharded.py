@@ -1,0 +1,140 @@
+"""Multi-GPU split of one large f16 matmul along N (
+A [16384, 8192] x B [8192, 28672], split across 1/2/4/8 GPUs).
+
+One process per GPU, torch.distributed for the plumbing. Rank r of G holds A
+(replicated) and the column shard B[:, cols_r] and computes C[:, cols_r] with
+the tcgen05 GEMM. The gathered C is produced one of two ways:
+
+  * "fused" (the product path): every rank keeps a full [M, N] output buffer;
+    the ranks exchange CUDA IPC handles of these buffers once, and the GEMM's
+    epilogue writes each output tile into all G buffers -- its own and, over
+    NVLink, the peers' -- at the shard's columns
+    (hxb_matmul_f16_allgather). A stream-ordered collective after the GEMM
+    tells every rank that all peers' tiles have landed. No gather copy and no
+    layout fix-up remain.
+  * "nccl" (the baseline it is measured against): GEMM into a local shard,
+    NCCL all-gather of the shards into [G, M, N/G], then the [G, M, n] ->
+    [M, N] layout step (hxb_gather_column_blocks_f16).
+
+The reference itself has no collectives (plugins/runtime/hexagon/channel.c:
+55-56 returns IREE_STATUS_UNIMPLEMENTED). Peer memory here is plain CUDA IPC
+(no NVLink multicast objects), and the TMA loads of the GEMM only ever read
+this rank's own A and B.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _native
+from ._native import check
+
+
+def shard_columns(N: int, world: int, rank: int, align: int = 8) -> tuple[int, int]:
+    """[begin, end) of rank's column shard: N split into `world` contiguous
+    blocks whose sizes are multiples of `align` (the last block takes the
+    remainder), so every block starts on a 16-byte boundary."""
+    if N % align:
+        raise ValueError(f"N={N} must be a multiple of {align}")
+    units = N // align
+    base, extra = divmod(units, world)
+    begin = (rank * base + min(rank, extra)) * align
+    size = (base + (1 if rank < extra else 0)) * align
+    return begin, begin + size
+
+
+def exchange_peer_payloads(payload, *, group=None) -> list:
+    """All-gathers one picklable payload per rank over `group` and returns the
+    other ranks' payloads in rank order (this rank's own left out)."""
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    infos = [None] * world
+    dist.all_gather_object(infos, (rank, payload), group=group)
+    assert [r for r, _ in infos] == list(range(world)), "ranks out of order"
+    return [p for r, p in infos if r != rank]
+
+
+def _stream_ptr(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+class ShardedMatmul:
+    """C = A @ B for B split along N across the ranks of `group` (one GPU
+    per rank). Holds this rank's full output buffer and the peers' buffers
+    opened through CUDA IPC."""
+
+    def __init__(self, M: int, N: int, K: int, *, group=None, device=None):
+        import torch.distributed as dist
+        self.dist = dist
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if self.world > 8:
+            raise ValueError("at most 8 ranks (one replica per peer in the epilogue)")
+        self.M, self.N, self.K = M, N, K
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        self.cols = [shard_columns(N, self.world, r) for r in range(self.world)]
+        self.begin, self.end = self.cols[self.rank]
+        self.out = torch.empty((M, N), dtype=torch.float16, device=self.device)
+        self._peer_storages: list = []
+        self.peer_ptrs: list[int] = []
+        if self.world > 1:
+            self._open_peers()
+        self._flag = torch.zeros(1, dtype=torch.float32, device=self.device)
+
+    def _open_peers(self) -> None:
+        # CUDA IPC through torch's storage sharing: (handle, offset) of this
+        # rank's output, exchanged once over the process group
+        storage = self.out.untyped_storage()
+        payload = (storage._share_cuda_(), self.out.storage_offset())
+        ptrs = []
+        for meta, off in exchange_peer_payloads(payload, group=self.group):
+            peer = torch.UntypedStorage._new_shared_cuda(*meta)
+            self._peer_storages.append(peer)  # keeps the mapping open
+            ptrs.append(peer.data_ptr() + off * 2)
+        self.peer_ptrs = ptrs
+
+    def _sync(self) -> None:
+        # stream-ordered: every rank's GEMM (and its remote stores) is done
+        # before any rank continues past this point on its stream
+        if self.world > 1:
+            self.dist.all_reduce(self._flag, group=self.group)
+
+    def fused(self, a: torch.Tensor, b_shard: torch.Tensor) -> torch.Tensor:
+        """GEMM with the all-gather in its epilogue; returns the full C."""
+        lib = _native.load()
+        n = self.end - self.begin
+        assert b_shard.shape == (self.K, n) and a.shape == (self.M, self.K)
+        # peers may still be reading the previous result out of their buffers
+        self._sync()
+        reps = (ctypes.c_void_p * max(1, len(self.peer_ptrs)))(
+            *[p + self.begin * 2 for p in self.peer_ptrs] or [0])
+        check(lib.hxb_matmul_f16_allgather(
+            a.data_ptr(), a.stride(0), b_shard.data_ptr(), b_shard.stride(0), 0,
+            self.out.data_ptr() + self.begin * 2, reps if self.peer_ptrs else None,
+            len(self.peer_ptrs), self.out.stride(0), self.M, n, self.K, _stream_ptr(a)))
+        self._sync()
+        return self.out
+
+    def nccl(self, a: torch.Tensor, b_shard: torch.Tensor, *, shard_out: torch.Tensor,
+             gathered: torch.Tensor) -> torch.Tensor:
+        """Baseline: GEMM into the local shard, NCCL all-gather, layout step.
+        Needs equal shards (N divisible by 8 * world)."""
+        from .dispatch import matmul
+        lib = _native.load()
+        n = self.end - self.begin
+        matmul(a, b_shard, out=shard_out)
+        if self.world > 1:
+            self.dist.all_gather_into_tensor(gathered, shard_out, group=self.group)
+            src = gathered
+        else:
+            src = shard_out
+        check(lib.hxb_gather_column_blocks_f16(src.data_ptr(), self.out.data_ptr(), self.world,
+                                               self.M, n, self.out.stride(0), _stream_ptr(a)))
+        return self.out
+
+    def close(self) -> None:
+        self._peer_storages.clear()
+        self.peer_ptrs = []
