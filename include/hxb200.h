@@ -183,6 +183,17 @@ hxb_status_t hxb_matmul_f16_allgather(const void* A, int64_t lda, const void* B,
                                       int64_t ldc, int64_t M, int64_t N,
                                       int64_t K, void* stream);
 
+/* CUDA IPC for the replicas of hxb_matmul_f16_allgather. get_handle fills
+ * HXB_IPC_HANDLE_BYTES bytes naming the allocation that holds `ptr` and the
+ * byte offset of `ptr` inside it; open maps a peer's allocation into the
+ * CURRENT device's context with peer access enabled (so kernels on this
+ * device can store into it) and returns the pointer at `offset`; close
+ * unmaps it. */
+#define HXB_IPC_HANDLE_BYTES 64
+hxb_status_t hxb_ipc_get_handle(const void* ptr, void* handle, int64_t* offset);
+hxb_status_t hxb_ipc_open(const void* handle, int64_t offset, void** ptr);
+hxb_status_t hxb_ipc_close(void* ptr, int64_t offset);
+
 /* dst[m, g*n + j] = src[g, m, j]: the [G, M, n] result of an NCCL all-gather
  * of column shards laid out as the [M, G*n] matrix (row pitch ldd).
  * n % 8 == 0, 16-byte aligned buffers. */

@@ -44,6 +44,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "hxb_matmul_f16_allgather": (c_int, [c_vp, c_i64, c_vp, c_i64, c_int, c_vp, c_vp, c_int,
                                          c_i64, c_i64, c_i64, c_i64, c_vp]),
     "hxb_gather_column_blocks_f16": (c_int, [c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp]),
+    "hxb_ipc_get_handle": (c_int, [c_vp, c_vp, ctypes.POINTER(c_i64)]),
+    "hxb_ipc_open": (c_int, [c_vp, c_i64, ctypes.POINTER(c_vp)]),
+    "hxb_ipc_close": (c_int, [c_vp, c_i64]),
     "hxb_decoder_block_workspace_bytes": (c_size, [c_vp, c_i64, c_i64]),
     "hxb_decoder_block_w8a16": (c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp,
                                         c_size, c_vp]),

@@ -141,3 +141,74 @@ extern "C" hxb_status_t hxb_device_status(int clear, int* out_bits) {
 }
 
 extern "C" int hxb_abi_version(void) { return HXB_ABI_VERSION; }
+
+// ---------------------------------------------------------------- CUDA IPC
+// Peer buffers for the all-gather epilogue: a rank maps the other ranks'
+// output buffers into ITS OWN device's context (the current device), with
+// peer access enabled, so kernels running on that device can store into them
+// over NVLink. Plain IPC mappings; no NVLink multicast objects.
+
+extern "C" hxb_status_t hxb_ipc_get_handle(const void* ptr, void* handle, int64_t* offset) {
+  if (!ptr || !handle || !offset)
+    return hxb::fail(HXB_STATUS_INVALID_ARGUMENT, "ipc_get_handle: null argument");
+  // the handle names the whole allocation; report where ptr sits inside it
+  typedef CUresult (*RangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+  static RangeFn range = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &p, 12000, cudaEnableDefault,
+                                         &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<RangeFn>(p);
+  }();
+  if (!range) return hxb::fail(HXB_STATUS_CUDA_ERROR, "ipc_get_handle: cuMemGetAddressRange missing");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+    return hxb::fail(HXB_STATUS_INVALID_ARGUMENT, "ipc_get_handle: not a device allocation");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return hxb::cuda_status(e, "cudaIpcGetMemHandle");
+  memcpy(handle, &h, sizeof(h));
+  *offset = (int64_t)(reinterpret_cast<CUdeviceptr>(ptr) - base);
+  return HXB_OK;
+}
+
+extern "C" hxb_status_t hxb_ipc_open(const void* handle, int64_t offset, void** ptr) {
+  if (!handle || !ptr || offset < 0)
+    return hxb::fail(HXB_STATUS_INVALID_ARGUMENT, "ipc_open: bad argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return hxb::cuda_status(e, "cudaIpcOpenMemHandle");
+  // make sure the current device may access the owner's memory
+  int cur = 0;
+  cudaPointerAttributes attr;
+  if (cudaGetDevice(&cur) == cudaSuccess && cudaPointerGetAttributes(&attr, base) == cudaSuccess &&
+      attr.device != cur) {
+    int can = 0;
+    cudaDeviceCanAccessPeer(&can, cur, attr.device);
+    if (!can) {
+      cudaIpcCloseMemHandle(base);
+      return hxb::fail(HXB_STATUS_UNSUPPORTED, "ipc_open: device %d cannot access device %d",
+                       cur, attr.device);
+    }
+    e = cudaDeviceEnablePeerAccess(attr.device, 0);
+    if (e == cudaErrorPeerAccessAlreadyEnabled) {
+      cudaGetLastError();
+    } else if (e != cudaSuccess) {
+      cudaIpcCloseMemHandle(base);
+      return hxb::cuda_status(e, "cudaDeviceEnablePeerAccess");
+    }
+  }
+  *ptr = static_cast<uint8_t*>(base) + offset;
+  return HXB_OK;
+}
+
+extern "C" hxb_status_t hxb_ipc_close(void* ptr, int64_t offset) {
+  if (!ptr || offset < 0) return hxb::fail(HXB_STATUS_INVALID_ARGUMENT, "ipc_close: bad argument");
+  return hxb::cuda_status(cudaIpcCloseMemHandle(static_cast<uint8_t*>(ptr) - offset),
+                          "cudaIpcCloseMemHandle");
+}

@@ -78,22 +78,27 @@ class ShardedMatmul:
         self.cols = [shard_columns(N, self.world, r) for r in range(self.world)]
         self.begin, self.end = self.cols[self.rank]
         self.out = torch.empty((M, N), dtype=torch.float16, device=self.device)
-        self._peer_storages: list = []
+        self._peer_storages: list = []  # (mapped pointer, offset) of opened peers
         self.peer_ptrs: list[int] = []
         if self.world > 1:
             self._open_peers()
         self._flag = torch.zeros(1, dtype=torch.float32, device=self.device)
 
     def _open_peers(self) -> None:
-        # CUDA IPC through torch's storage sharing: (handle, offset) of this
-        # rank's output, exchanged once over the process group
-        storage = self.out.untyped_storage()
-        payload = (storage._share_cuda_(), self.out.storage_offset())
+        # CUDA IPC: (handle, offset) of this rank's output, exchanged once over
+        # the process group; each peer buffer is mapped into THIS rank's
+        # device context (hxb_ipc_open), where the GEMM epilogue runs
+        lib = _native.load()
+        handle = ctypes.create_string_buffer(64)
+        offset = ctypes.c_int64(0)
+        check(lib.hxb_ipc_get_handle(self.out.data_ptr(), handle, ctypes.byref(offset)))
+        payload = (bytes(handle.raw), offset.value)
         ptrs = []
-        for meta, off in exchange_peer_payloads(payload, group=self.group):
-            peer = torch.UntypedStorage._new_shared_cuda(*meta)
-            self._peer_storages.append(peer)  # keeps the mapping open
-            ptrs.append(peer.data_ptr() + off * 2)
+        for h, off in exchange_peer_payloads(payload, group=self.group):
+            p = ctypes.c_void_p(0)
+            check(lib.hxb_ipc_open(h, off, ctypes.byref(p)))
+            self._peer_storages.append((p.value, off))
+            ptrs.append(p.value)
         self.peer_ptrs = ptrs
 
     def _sync(self) -> None:
@@ -136,5 +141,8 @@ class ShardedMatmul:
         return self.out
 
     def close(self) -> None:
+        lib = _native.load()
+        for p, off in self._peer_storages:
+            check(lib.hxb_ipc_close(p, off))
         self._peer_storages.clear()
         self.peer_ptrs = []
