@@ -69,7 +69,7 @@ hxb_status_t gemm_f16_launch(const void* A, int64_t lda, const void* B, int64_t 
                              int transpose_b, const void* C_init, void* C, int64_t ldc,
                              hxb_dtype_t c_dtype, int64_t M, int64_t N, int64_t K,
                              void* workspace, size_t workspace_bytes, void* const* replicas,
-                             int nreplicas, cudaStream_t stream) {
+                             int nreplicas, cudaStream_t stream, const GemmPlan* forced = nullptr) {
   if (M < 1 || N < 1 || K < 1)
     return fail(HXB_STATUS_INVALID_ARGUMENT, "matmul: M, N, K must be >= 1 (got %lld, %lld, %lld)",
                 (long long)M, (long long)N, (long long)K);
@@ -120,7 +120,10 @@ hxb_status_t gemm_f16_launch(const void* A, int64_t lda, const void* B, int64_t 
   }
 
   const int bmode = transpose_b ? kBF16RowMajorNK : kBF16RowMajorKN;
-  const GemmPlan plan = plan_gemm((int)M, (int)N, (int)K, bmode, dev->num_sms);
+  GemmPlan plan = forced ? *forced : plan_gemm((int)M, (int)N, (int)K, bmode, dev->num_sms);
+  const int64_t tiles_m = (M + kBM - 1) / kBM;
+  if (plan.group_m < 1) plan.group_m = 1;
+  if (plan.group_m > tiles_m) plan.group_m = (int)tiles_m;
 
   CUtensorMap tmA, tmB;
   if ((s = make_a_map(&tmA, A, lda, M, K)) != HXB_OK) return s;
@@ -384,4 +387,32 @@ extern "C" hxb_status_t hxb_gather_column_blocks_f16(const void* src, void* dst,
   gather_column_blocks_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint4*>(src), static_cast<__half*>(dst), M, (int)n, (int)G, ldd);
   return cuda_status(cudaGetLastError(), "gather_column_blocks launch");
+}
+
+extern "C" hxb_status_t hxb_matmul_f16_tiled(const void* A, int64_t lda, const void* B,
+                                             int64_t ldb, int transpose_b, void* C, int64_t ldc,
+                                             hxb_dtype_t c_dtype, int64_t M, int64_t N, int64_t K,
+                                             int block_n, int group_m, void* stream) {
+  using namespace hxb;
+  if (block_n != 64 && block_n != 128 && block_n != 256)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "matmul_f16_tiled: block_n must be 64, 128 or 256");
+  if (!aligned16(A) || !aligned16(B) || (lda * 2) % 16 || (ldb * 2) % 16)
+    return fail(HXB_STATUS_INVALID_ARGUMENT,
+                "matmul_f16_tiled: A and B need 16-byte aligned rows (no re-pitching)");
+  const GemmPlan plan{block_n, group_m};
+  return gemm_f16_launch(A, lda, B, ldb, transpose_b, nullptr, C, ldc, c_dtype, M, N, K,
+                         nullptr, 0, nullptr, 0, static_cast<cudaStream_t>(stream), &plan);
+}
+
+extern "C" hxb_status_t hxb_plan_matmul_f16(int64_t M, int64_t N, int64_t K, int transpose_b,
+                                            int num_sms, int* block_n, int* group_m) {
+  using namespace hxb;
+  if (M < 1 || N < 1 || K < 1 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX ||
+      num_sms < 1 || !block_n || !group_m)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "plan_matmul_f16: bad arguments");
+  const GemmPlan p = plan_gemm((int)M, (int)N, (int)K,
+                               transpose_b ? kBF16RowMajorNK : kBF16RowMajorKN, num_sms);
+  *block_n = p.block_n;
+  *group_m = p.group_m;
+  return HXB_OK;
 }

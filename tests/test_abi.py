@@ -83,3 +83,20 @@ def test_workspace_query_is_host_only(pkg):
 def test_no_cpu_fallback_when_library_missing(pkg, tmp_path):
     with pytest.raises(OSError, match="no fallback"):
         pkg._native.load(tmp_path / "libhxb200.so")
+
+
+def test_planner_uses_the_baked_sweep_table(pkg):
+    """Shapes measured by the offline tile sweep (csrc/tile_table.inc) are
+    answered from the table, before the cost model."""
+    import ctypes
+    import re
+    lib = pkg._native.load()
+    table = (Path(__file__).resolve().parent.parent / "iree-hexagon-plugins_b200" / "csrc" /
+             "tile_table.inc").read_text()
+    rows = [tuple(int(v) for v in m.groups())
+            for m in re.finditer(r"\{(\d+), (\d+), (\d+), (\d+), (\d+), (\d+)\}", table)]
+    assert len(rows) >= 64
+    for M, N, K, bmode, bn, gm in rows:
+        b, g = ctypes.c_int(0), ctypes.c_int(0)
+        assert lib.hxb_plan_matmul_f16(M, N, K, bmode, 148, ctypes.byref(b), ctypes.byref(g)) == 0
+        assert (b.value, g.value) == (bn, gm), (M, N, K)
