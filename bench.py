@@ -185,6 +185,211 @@ def run_reference(args, rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------------
+# The other BASELINE configurations, one dispatch per step. Each spec builds
+# enough rotating input sets that the sets together exceed the 126 MB L2, so
+# every step reads its inputs from HBM; K steps run back to back between two
+# CUDA events on the launching stream (launch gaps included).
+
+def _spec_f16_gemm(torch, pkg, dev):
+    M = N = K = 1024
+    sets = 24  # 24 x 6.3 MB
+    g = torch.Generator(device=dev).manual_seed(0)
+    a = [(torch.rand(M, K, device=dev, generator=g) * 2 - 1).half() for _ in range(sets)]
+    b = [(torch.rand(K, N, device=dev, generator=g) * 2 - 1).half() for _ in range(sets)]
+    c = [torch.empty(M, N, dtype=torch.float16, device=dev) for _ in range(sets)]
+    return {"step": lambda i: pkg.matmul(a[i % sets], b[i % sets], out=c[i % sets]),
+            "in": a[0], "out": c[0], "sets": sets}
+
+
+def _spec_gemv(m):
+    def make(torch, pkg, dev):
+        K, N = 4096, 11008
+        sets = 4  # 4 x 45 MB of weights
+        g = torch.Generator(device=dev).manual_seed(0)
+        a = torch.randn(m, K, device=dev, generator=g).half()
+        w = [torch.randint(-127, 128, (K, N), device=dev, dtype=torch.int8, generator=g)
+             for _ in range(sets)]
+        s = (torch.rand(N, device=dev, generator=g) * 0.019 + 0.001).half()
+        c = torch.empty(m, N, dtype=torch.float16, device=dev)
+        return {"step": lambda i: pkg.matmul_w8a16(a, w[i % sets], s, out=c), "in": a, "out": c,
+                "sets": sets}
+    return make
+
+
+def _spec_attention(torch, pkg, dev):
+    B, H, S, D = 4, 32, 2048, 128
+    sets = 2  # 2 x 201 MB of q, k, v
+    g = torch.Generator(device=dev).manual_seed(0)
+    qkv = [[torch.randn(B, H, S, D, device=dev, generator=g).half() for _ in range(3)]
+           for _ in range(sets)]
+    o = torch.empty_like(qkv[0][0])
+    return {"step": lambda i: pkg.attention(*qkv[i % sets], out=o), "in": qkv[0][0], "out": o,
+            "sets": sets}
+
+
+def _spec_decoder(torch, pkg, dev):
+    H, F, S, NH = 4096, 11008, 512, 32
+    g = torch.Generator(device=dev).manual_seed(0)
+
+    def w8(k, n):
+        return torch.randint(-127, 128, (k, n), device=dev, dtype=torch.int8, generator=g)
+
+    def sc(n):  # int8 quantisation of a 0.02-std random init
+        return (torch.rand(n, device=dev, generator=g) * 2.5e-4 + 1.5e-4).half()
+    ones = torch.ones(H, device=dev, dtype=torch.float16)
+    blk = pkg.DecoderBlockW8(heads=NH, attn_norm=ones, ffn_norm=ones.clone(),
+                             w_qkv=w8(H, 3 * H), s_qkv=sc(3 * H), w_o=w8(H, H), s_o=sc(H),
+                             w_gate_up=w8(H, 2 * F), s_gate_up=sc(2 * F), w_down=w8(F, H),
+                             s_down=sc(H))
+    x = torch.randn(S, H, device=dev, generator=g).half()
+    out = torch.empty_like(x)
+    # one set: the block streams 202 MB of weights per step
+    return {"step": lambda i: blk(x, out=out), "in": x, "out": out, "sets": 1}
+
+
+SPECS = {
+    "f16_gemm_1024": {
+        "make": _spec_f16_gemm, "flop": 2.0 * 1024 ** 3, "bound": "tensor",
+        "kernel": "gemm_sm100_kernel", "dtype": "f16->f32",
+        "config": {"workload": "f16_gemm_1024x1024x1024", "cfg": 1,
+                   "inputs": "A, B ~ U[-1, 1] f16, f16 out"}},
+    "gemv_w8_m1": {
+        "make": _spec_gemv(1), "bytes": 4096 * 11008 + 2 * 4096 + 2 * 11008 + 2 * 11008,
+        "flop": 2.0 * 4096 * 11008, "bound": "hbm", "kernel": "gemv_w8_kernel",
+        "dtype": "f16xi8->f32",
+        "config": {"workload": "w8a16_gemv_1x4096x11008", "cfg": "2b"}},
+    "gemv_w8_m16": {
+        "make": _spec_gemv(16), "bytes": 4096 * 11008 + 2 * 16 * 4096 + 2 * 11008 + 2 * 16 * 11008,
+        "flop": 2.0 * 16 * 4096 * 11008, "bound": "hbm", "kernel": "gemv_w8_kernel",
+        "dtype": "f16xi8->f32",
+        "config": {"workload": "w8a16_gemv_16x4096x11008", "cfg": "2b"}},
+    "attention": {
+        "make": _spec_attention, "flop": 4.0 * 4 * 32 * 2048 * 2048 * 128, "bound": "tensor",
+        "kernel": "attention_fwd_kernel", "dtype": "f16->f32",
+        "config": {"workload": "attention_4x32x2048x128_noncausal", "cfg": 3}},
+    "decoder_block": {
+        "make": _spec_decoder,
+        "flop": 2.0 * 512 * (4 * 4096 * 4096 + 3 * 4096 * 11008) + 2.0 * 32 * 512 * 512 * 128,
+        "bound": "tensor", "kernel": "gemm_w8_sm100_kernel (+ attention, norms)", "launches": 9,
+        "dtype": "f16xi8->f32",
+        "config": {"workload": "llama_decoder_block_w8_s512", "cfg": 4,
+                   "scales": "U[1.5e-4, 4e-4] (int8 of a 0.02-std init)"}},
+}
+
+
+def run_spec(args, spec: dict, rank: int, world: int, local_rank: int) -> None:
+    """One spec'd configuration; with N ranks each runs its own replica
+    (weak scaling, no collective)."""
+    import torch
+    import torch.distributed as dist
+    import __graft_entry__ as ge
+    from datetime import timedelta
+
+    pkg = ge.load_package()
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    st = spec["make"](torch, pkg, dev)
+    stream = torch.cuda.current_stream(dev)
+    steps = min(args.steps, 200)
+    # The K dispatches are captured once into a CUDA graph, so a step costs its
+    # kernels' device time and not the Python launch path (a 1024^3 GEMM runs in
+    # a few microseconds, less than one ctypes call).
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        for i in range(args.warmup):
+            st["step"](i)
+    stream.wait_stream(side)
+    torch.cuda.synchronize(dev)
+    assert pkg.device_status() == 0, "a kernel wait timed out during warm-up"
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(steps):
+            st["step"](i)
+    graph.replay()
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    time.sleep(0.3)
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    e0.record(stream)
+    graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    total_ms = e0.elapsed_time(e1)
+    del graph
+    if world > 1:
+        t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    ms = total_ms / steps
+    # e2e: the same call with its main input copied from pinned host memory and
+    # its output read back, inside the timed region
+    inp, out = st["in"], st["out"]
+    in_h = torch.empty(inp.shape, dtype=inp.dtype, pin_memory=True)
+    in_h.copy_(inp.cpu())
+    out_h = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+
+    def e2e_step(i):
+        inp.copy_(in_h, non_blocking=True)
+        st["step"](i)
+        out_h.copy_(out, non_blocking=True)
+    for i in range(3):
+        e2e_step(i)
+    torch.cuda.synchronize(dev)
+    e_steps = max(3, min(20, steps))
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record(stream)
+    for i in range(e_steps):
+        e2e_step(i)
+    a1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = a0.elapsed_time(a1) / e_steps
+    status = pkg.device_status()
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    peaks, peak_kind = _peaks()
+    if spec["bound"] == "hbm":
+        unit, work = "GB/s", spec["bytes"] / 1e9
+        peak, peak_label = peaks["hbm_gbs"], f"{peak_kind} HBM copy"
+    else:
+        unit, work = "TFLOP/s", spec["flop"] / 1e12
+        peak, peak_label = peaks["bf16_tflops"], f"{peak_kind} bf16 dense (burst)"
+    achieved = work / (ms / 1e3)
+    line = {
+        "metric": METRIC, "value": work * world / (ms / 1e3), "unit": unit, "n_gpus": world,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": spec["dtype"], "data": "synthetic",
+        "config": dict(spec["config"], parallelism=f"{world} replicas",
+                       l2=f"{st['sets']} rotating input set(s), together larger than the 126 MB L2",
+                       timing="K dispatches in one CUDA graph, one replay between two events"),
+        "roofline": {"bound": spec["bound"], "achieved": achieved, "peak": peak, "unit": unit,
+                     "frac": achieved / peak, "traffic": _profile_traffic(spec["config"]["workload"]),
+                     "peak_source": peak_label, "kernel": spec["kernel"], "kernel_ms": ms},
+        "e2e": {"value": work * world / (e2e_ms / 1e3), "unit": unit,
+                "h2d_bytes_per_step": inp.numel() * inp.element_size(),
+                "d2h_bytes_per_step": out.numel() * out.element_size()},
+        "gpu_launches": steps * spec.get("launches", 1), "clocks": clocks,
+        "device_status": status,
+    }
+    if "flop" in spec and unit != "TFLOP/s":
+        line["tflops"] = spec["flop"] / (ms / 1e3) / 1e12
+    print(json.dumps(line), flush=True)
+
+
 SH_M, SH_K, SH_N = 16384, 8192, 28672
 
 
@@ -296,9 +501,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["w8a16_gemm", "sharded_gemm"], default="w8a16_gemm",
+    ap.add_argument("--workload", choices=["w8a16_gemm", "sharded_gemm"] + sorted(SPECS),
+                    default="w8a16_gemm",
                     help="w8a16_gemm: BASELINE configuration 2 (the metric's config, default); "
-                         "sharded_gemm: configuration 5 split along N over the ranks")
+                         "sharded_gemm: configuration 5 split along N over the ranks; the "
+                         "others: the remaining configurations, one dispatch per step")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -311,6 +518,9 @@ def main():
         return
     if args.workload == "sharded_gemm":
         run_sharded(args, rank, world, local_rank)
+        return
+    if args.workload in SPECS:
+        run_spec(args, SPECS[args.workload], rank, world, local_rank)
         return
 
     import torch
