@@ -156,6 +156,29 @@ hxb_status_t hxb_matmul_w8a16_residual(const void* A, int64_t lda, const void* W
                                        int64_t M, int64_t N, int64_t K,
                                        void* stream);
 
+/* Device scratch hxb_matmul_w8a16_streamk needs on the current device (the
+ * same for every shape): 4096 bytes of flags, then one 96 KB f32 partial
+ * accumulator per SM. */
+size_t hxb_matmul_w8a16_workspace_bytes(int64_t M, int64_t N, int64_t K);
+
+/* hxb_matmul_w8a16 (R optional, may be NULL) that may split K across CTAs
+ * (stream-K) when whole output tiles would leave SMs idle in the last wave,
+ * e.g. the M = 512 projections of the decoder block. Tiles cut between CTAs
+ * are summed in a fixed CTA order, so results are deterministic; they may
+ * differ from hxb_matmul_w8a16 in the last f32 bit of a sum.
+ * `workspace` (16-byte aligned, >= hxb_matmul_w8a16_workspace_bytes) is
+ * owned by the caller; its first 4096 bytes must be zero before the first
+ * call and every successful call leaves them zero. Calls sharing a workspace
+ * must be ordered (one stream). After a call that set hxb_device_status, zero
+ * those bytes again. No counterpart in the reference (its HMX path has no
+ * int8 weights, ContractionStrategy.cpp:141). */
+hxb_status_t hxb_matmul_w8a16_streamk(const void* A, int64_t lda, const void* W,
+                                      int64_t ldw, const void* scale,
+                                      const void* R, void* C, int64_t ldc,
+                                      int64_t M, int64_t N, int64_t K,
+                                      void* workspace, size_t workspace_bytes,
+                                      void* stream);
+
 /* Fused attention dispatch: O = softmax(scale * Q.K^T [+ causal mask]) . V,
  * f32 softmax statistics, f16 in/out. Replaces the decomposed f32 dispatches
  * of examples/attention_layer/attention_layer.mlir:17-111 (which scale Q and

@@ -10,7 +10,8 @@ from . import _native
 from ._native import HxbError
 from . import sharded
 from .dispatch import (DecoderBlockW8, attention, attention_bshd, device_status, matmul,
-                       matmul_w8a16, rmsnorm, rope_, swiglu)
+                       matmul_w8a16, rmsnorm, rope_, swiglu, w8a16_workspace)
 
 __all__ = ["sharded", "HxbError", "DecoderBlockW8", "attention", "attention_bshd", "device_status",
-           "matmul", "matmul_w8a16", "rmsnorm", "rope_", "swiglu", "_native"]
+           "matmul", "matmul_w8a16", "rmsnorm", "rope_", "swiglu", "w8a16_workspace",
+           "_native"]

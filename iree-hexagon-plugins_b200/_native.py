@@ -39,6 +39,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                   c_i64, c_float, c_int, c_vp]),
     "hxb_matmul_w8a16_residual": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp,
                                           c_i64, c_i64, c_i64, c_i64, c_vp]),
+    "hxb_matmul_w8a16_workspace_bytes": (c_size, [c_i64, c_i64, c_i64]),
+    "hxb_matmul_w8a16_streamk": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_i64,
+                                         c_i64, c_i64, c_i64, c_vp, c_size, c_vp]),
     "hxb_attention_f16_bshd": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64,
                                        c_i64, c_i64, c_i64, c_i64, c_i64, c_float, c_int,
                                        c_vp]),

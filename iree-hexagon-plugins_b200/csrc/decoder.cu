@@ -29,7 +29,10 @@ namespace hxb {
 
 hxb_status_t matmul_w8a16_impl(const void* A, int64_t lda, const void* W, int64_t ldw,
                                const void* scale, const void* R, void* C, int64_t ldc,
-                               int64_t M, int64_t N, int64_t K, cudaStream_t stream);
+                               int64_t M, int64_t N, int64_t K, void* sk_ws,
+                               size_t sk_ws_bytes, cudaStream_t stream);
+size_t w8_streamk_workspace_bytes(int ctas);
+int w8_streamk_flag_ints();
 hxb_status_t attention_launch(const void* Q, int64_t ldq, const void* K, int64_t ldk,
                               const void* V, int64_t ldv, void* O, int64_t ldo, int64_t B,
                               int64_t H, int64_t hpr, int64_t Sq, int64_t Skv, int64_t D,
@@ -38,9 +41,14 @@ hxb_status_t attention_launch(const void* Q, int64_t ldq, const void* K, int64_t
 namespace {
 
 // One warp per row; 16-byte vector loads (cols % 8 == 0).
+// `clear` (optional, nclear ints) is zeroed by block 0: the decoder block's
+// first kernel resets the stream-K flags its W8 GEMMs use.
 __global__ void rmsnorm_kernel(const __half* __restrict__ x, long long ldx,
                                const __half* __restrict__ gamma, __half* __restrict__ y,
-                               long long ldy, int rows, int cols, float eps) {
+                               long long ldy, int rows, int cols, float eps, int* clear,
+                               int nclear) {
+  if (clear && blockIdx.x == 0)
+    for (int i = threadIdx.x; i < nclear; i += blockDim.x) clear[i] = 0;
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= rows) return;
@@ -123,12 +131,13 @@ __global__ void swiglu_kernel(const __half* __restrict__ gu, long long ldgu, __h
 }
 
 hxb_status_t launch_rmsnorm(const void* x, int64_t ldx, const void* gamma, void* y, int64_t ldy,
-                            int64_t rows, int64_t cols, float eps, cudaStream_t stream) {
+                            int64_t rows, int64_t cols, float eps, cudaStream_t stream,
+                            int* clear = nullptr, int nclear = 0) {
   const int threads = 256;
   const long long blocks = (rows * 32 + threads - 1) / threads;
   rmsnorm_kernel<<<(unsigned)blocks, threads, 0, stream>>>(
       static_cast<const __half*>(x), ldx, static_cast<const __half*>(gamma),
-      static_cast<__half*>(y), ldy, (int)rows, (int)cols, eps);
+      static_cast<__half*>(y), ldy, (int)rows, (int)cols, eps, clear, nclear);
   return cuda_status(cudaGetLastError(), "rmsnorm launch");
 }
 
@@ -155,12 +164,17 @@ hxb_status_t launch_swiglu(const void* gu, int64_t ldgu, void* a, int64_t lda, i
 size_t round256(size_t b) { return (b + 255) & ~size_t(255); }
 
 struct DecoderBuffers {
-  size_t h, qkv, att, h2, gu, a, total;
+  size_t sk, sk_bytes, h, qkv, att, h2, gu, a, total;
 };
 
+// Stream-K scratch of the W8 GEMMs (flags, then partial accumulators) first,
+// then the activations.
 DecoderBuffers decoder_layout(const hxb_decoder_w8_t* w, int64_t rows) {
   DecoderBuffers b{};
   size_t off = 0;
+  DeviceInfo* dev = nullptr;
+  b.sk_bytes = current_device(&dev) == HXB_OK ? w8_streamk_workspace_bytes(dev->num_sms) : 0;
+  b.sk = off;  off += round256(b.sk_bytes);
   b.h = off;   off += round256((size_t)rows * w->hidden * 2);
   b.qkv = off; off += round256((size_t)rows * 3 * w->hidden * 2);
   b.att = off; off += round256((size_t)rows * w->hidden * 2);
@@ -255,9 +269,14 @@ extern "C" hxb_status_t hxb_decoder_block_w8a16(const hxb_decoder_w8_t* w, const
   __half* a = reinterpret_cast<__half*>(ws + b.a);
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
 
-  if ((s = launch_rmsnorm(x, H, w->attn_norm, h, H, rows, H, w->rms_eps, stream)) != HXB_OK) return s;
+  void* sk = b.sk_bytes ? ws + b.sk : nullptr;
+  const size_t skb = b.sk_bytes;
+
+  if ((s = launch_rmsnorm(x, H, w->attn_norm, h, H, rows, H, w->rms_eps, stream,
+                          static_cast<int*>(sk), sk ? w8_streamk_flag_ints() : 0)) != HXB_OK)
+    return s;
   if ((s = matmul_w8a16_impl(h, H, w->w_qkv, 3 * H, w->s_qkv, nullptr, qkv, 3 * H, rows, 3 * H, H,
-                             stream)) != HXB_OK)
+                             sk, skb, stream)) != HXB_OK)
     return s;
   // q and k are the first 2 * heads heads of every qkv row
   if ((s = launch_rope(qkv, 3 * H, rows, 2 * w->heads, seq, pos0, w->rope_theta, stream)) != HXB_OK)
@@ -266,12 +285,13 @@ extern "C" hxb_status_t hxb_decoder_block_w8a16(const hxb_decoder_w8_t* w, const
                             w->heads, w->heads, seq, seq, w->head_dim,
                             1.0f / sqrtf((float)w->head_dim), 1, stream)) != HXB_OK)
     return s;
-  if ((s = matmul_w8a16_impl(att, H, w->w_o, H, w->s_o, x, h2, H, rows, H, H, stream)) != HXB_OK)
+  if ((s = matmul_w8a16_impl(att, H, w->w_o, H, w->s_o, x, h2, H, rows, H, H, sk, skb, stream)) !=
+      HXB_OK)
     return s;
   if ((s = launch_rmsnorm(h2, H, w->ffn_norm, h, H, rows, H, w->rms_eps, stream)) != HXB_OK) return s;
   if ((s = matmul_w8a16_impl(h, H, w->w_gate_up, 2 * F, w->s_gate_up, nullptr, gu, 2 * F, rows,
-                             2 * F, H, stream)) != HXB_OK)
+                             2 * F, H, sk, skb, stream)) != HXB_OK)
     return s;
   if ((s = launch_swiglu(gu, 2 * F, a, F, rows, F, stream)) != HXB_OK) return s;
-  return matmul_w8a16_impl(a, F, w->w_down, H, w->s_down, h2, out, H, rows, H, F, stream);
+  return matmul_w8a16_impl(a, F, w->w_down, H, w->s_down, h2, out, H, rows, H, F, sk, skb, stream);
 }

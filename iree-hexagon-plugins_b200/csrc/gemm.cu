@@ -240,9 +240,17 @@ hxb_status_t gemv_w8_impl(const void* A, int64_t lda, const void* W, int64_t ldw
   return M <= 8 ? launch_gemv<8>(*dev, p, stream) : launch_gemv<16>(*dev, p, stream);
 }
 
+// Stream-K workspace of the int8-weight GEMM for `ctas` CTAs: flags, then one
+// f32 partial accumulator per CTA.
+size_t w8_streamk_workspace_bytes(int ctas) {
+  return kW8FlagBytes + (size_t)ctas * kW8PartialFloats * sizeof(float);
+}
+int w8_streamk_flag_ints() { return (int)(kW8FlagBytes / sizeof(int)); }
+
 hxb_status_t gemm_w8_impl(const void* A, int64_t lda, const void* W,
                           int64_t ldw, const void* scale, const void* R, void* C, int64_t ldc,
-                          int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
+                          int64_t M, int64_t N, int64_t K, void* sk_ws, size_t sk_ws_bytes,
+                          cudaStream_t stream) {
   DeviceInfo* dev = nullptr;
   hxb_status_t s = current_device(&dev);
   if (s != HXB_OK) return s;
@@ -286,7 +294,26 @@ hxb_status_t gemm_w8_impl(const void* A, int64_t lda, const void* W,
     configured[dev->ordinal] = true;
   }
   const int tiles = args.tiles_m * args.tiles_n;
-  const int grid = tiles < dev->num_sms ? tiles : dev->num_sms;
+  int grid = tiles < dev->num_sms ? tiles : dev->num_sms;
+  // Stream-K when whole tiles leave SMs idle in the last wave (and the caller
+  // gave the workspace): every SM then gets the same share of K-blocks.
+  const int sms = dev->num_sms;
+  if (sk_ws && sms <= kW8MaxStreamKCtas && sk_ws_bytes >= w8_streamk_workspace_bytes(sms)) {
+    const long long num_kb = (K + kBK - 1) / kBK;
+    const long long total = (long long)tiles * num_kb;
+    const int waves = (tiles + sms - 1) / sms;
+    const double fill = (double)tiles / ((double)waves * sms);
+    const long long g = total / kW8MinShare < sms ? total / kW8MinShare : sms;
+    // fewer tiles than SMs: spread them over more CTAs; several waves: even
+    // out the last one over all SMs
+    if (fill < 0.92 && (g > tiles || (tiles > sms && g == sms))) {
+      grid = (int)g;
+      args.streamk = 1;
+      args.sk_flags = static_cast<int*>(sk_ws);
+      args.sk_partials =
+          reinterpret_cast<float*>(static_cast<uint8_t*>(sk_ws) + kW8FlagBytes);
+    }
+  }
   gemm_w8_sm100_kernel<<<grid, kW8Threads, W8Smem::kAlloc, stream>>>(tmA, tmW, args);
   return cuda_status(cudaGetLastError(), "gemm_w8 launch");
 }
@@ -315,7 +342,8 @@ extern "C" hxb_status_t hxb_matmul_f16(const void* A, int64_t lda, const void* B
 namespace hxb {
 hxb_status_t matmul_w8a16_impl(const void* A, int64_t lda, const void* W, int64_t ldw,
                                const void* scale, const void* R, void* C, int64_t ldc,
-                               int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
+                               int64_t M, int64_t N, int64_t K, void* sk_ws,
+                               size_t sk_ws_bytes, cudaStream_t stream) {
   if (M < 1 || N < 1 || K < 1)
     return fail(HXB_STATUS_INVALID_ARGUMENT, "matmul_w8a16: M, N, K must be >= 1");
   if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX)
@@ -330,7 +358,9 @@ hxb_status_t matmul_w8a16_impl(const void* A, int64_t lda, const void* W, int64_
                 "matmul_w8a16: A/W/C/scale/R must be 16-byte aligned with lda%%8 == 0, "
                 "ldw%%16 == 0, ldc%%8 == 0");
   if (M <= kGemvRows) return gemv_w8_impl(A, lda, W, ldw, scale, R, C, ldc, M, N, K, stream);
-  return gemm_w8_impl(A, lda, W, ldw, scale, R, C, ldc, M, N, K, stream);
+  if (sk_ws && !aligned16(sk_ws))
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "matmul_w8a16: workspace must be 16-byte aligned");
+  return gemm_w8_impl(A, lda, W, ldw, scale, R, C, ldc, M, N, K, sk_ws, sk_ws_bytes, stream);
 }
 }  // namespace hxb
 
@@ -338,7 +368,7 @@ extern "C" hxb_status_t hxb_matmul_w8a16(const void* A, int64_t lda, const void*
                                          int64_t ldw, const void* scale, void* C,
                                          int64_t ldc, int64_t M, int64_t N, int64_t K,
                                          void* stream) {
-  return hxb::matmul_w8a16_impl(A, lda, W, ldw, scale, nullptr, C, ldc, M, N, K,
+  return hxb::matmul_w8a16_impl(A, lda, W, ldw, scale, nullptr, C, ldc, M, N, K, nullptr, 0,
                                 static_cast<cudaStream_t>(stream));
 }
 
@@ -347,8 +377,28 @@ extern "C" hxb_status_t hxb_matmul_w8a16_residual(const void* A, int64_t lda, co
                                                   void* C, int64_t ldc, int64_t M, int64_t N,
                                                   int64_t K, void* stream) {
   if (!R) return hxb::fail(HXB_STATUS_INVALID_ARGUMENT, "matmul_w8a16_residual: null residual");
-  return hxb::matmul_w8a16_impl(A, lda, W, ldw, scale, R, C, ldc, M, N, K,
+  return hxb::matmul_w8a16_impl(A, lda, W, ldw, scale, R, C, ldc, M, N, K, nullptr, 0,
                                 static_cast<cudaStream_t>(stream));
+}
+
+extern "C" size_t hxb_matmul_w8a16_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+  (void)M;
+  (void)N;
+  (void)K;
+  hxb::DeviceInfo* dev = nullptr;
+  if (hxb::current_device(&dev) != HXB_OK) return 0;
+  return hxb::w8_streamk_workspace_bytes(dev->num_sms);
+}
+
+extern "C" hxb_status_t hxb_matmul_w8a16_streamk(const void* A, int64_t lda, const void* W,
+                                                 int64_t ldw, const void* scale, const void* R,
+                                                 void* C, int64_t ldc, int64_t M, int64_t N,
+                                                 int64_t K, void* workspace,
+                                                 size_t workspace_bytes, void* stream) {
+  if (!workspace)
+    return hxb::fail(HXB_STATUS_INVALID_ARGUMENT, "matmul_w8a16_streamk: null workspace");
+  return hxb::matmul_w8a16_impl(A, lda, W, ldw, scale, R, C, ldc, M, N, K, workspace,
+                                workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" hxb_status_t hxb_matmul_f16_allgather(const void* A, int64_t lda, const void* B,

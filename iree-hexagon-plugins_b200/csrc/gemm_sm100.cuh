@@ -48,6 +48,12 @@ struct GemmArgs {
   // reached over NVLink through peer pointers -- at the same row and column.
   int ndests;
   void* dests[kMaxDests];
+  // Stream-K (int8-weight GEMM only): when streamk != 0 every CTA owns a
+  // contiguous share of the tiles x K-blocks iteration space; tiles split
+  // between CTAs are summed through sk_partials (f32) under sk_flags.
+  int streamk;
+  int* sk_flags;
+  float* sk_partials;
 };
 
 constexpr int kBM = 128;

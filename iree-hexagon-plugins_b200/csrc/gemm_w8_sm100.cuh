@@ -1,31 +1,49 @@
-// Int8-weight GEMM for sm_100a: C[M,N] f16 = (A[M,K] f16 . W[K,N] int8) * scale[N].
+// Int8-weight GEMM for sm_100a: C[M,N] f16 = (A[M,K] f16 . W[K,N] int8) * scale[N] (+ R).
 //
 // The kernel computes the transposed product D[n, m] = sum_k W[k, n] A[m, k]
 // on the tensor core so that the dequantised weights never pass through
 // shared memory a second time:
 //   * TMA lands the raw int8 weight tile [64 k][128 n] (8 KB, 128-byte
-//     swizzle) and the activation tile [256 m][64 k] f16 (32 KB) in two
+//     swizzle) and the activation tile [192 m][64 k] f16 (24 KB) in two
 //     independent rings;
 //   * eight converter warps transpose the int8 tile on its way out of shared
 //     memory (ldmatrix.trans), convert it exactly to f16 (|w| <= 127) in
 //     registers and write it into TMEM with tcgen05.st, where it is the A
-//     operand (M = 128 weight columns) of tcgen05.mma;
+//     operand (M = 128 weight columns) of tcgen05.mma. The converters form two
+//     groups of four that take alternate K-blocks, so two blocks are in
+//     conversion at once and the latency of one (shared-memory load, TMEM
+//     store, wait) is hidden behind the other;
 //   * one thread issues tcgen05.mma (A from TMEM, B = activations from shared
 //     memory, N = 192 activation rows) into one of two 192-column f32 TMEM
 //     accumulators, so the epilogue of tile t overlaps the main loop of t+1;
 //   * four epilogue warps read the accumulator back, apply the per-column
 //     scale once (it factors out of the K sum), add the optional residual and
-//     store C transposed.
+//     store C transposed. Scales are fetched before the accumulator is ready;
+//     residual and partial-sum loads are issued ahead of the TMEM reads they
+//     pair with, two 32-column chunks at a time.
 // Shared-memory traffic per k-block is the int8 tile (written by TMA, read
 // once by the converters) plus the activation tile (written by TMA, read by
 // the tensor core); the f16 weights live only in registers and TMEM.
 //
-// Roles (512 threads, one CTA per SM, persistent over output tiles):
+// Work split. Data-parallel: CTA b owns whole output tiles b, b + grid, ...
+// Stream-K (args.streamk): the tiles x K-blocks iteration space is cut into
+// `grid` equal contiguous shares, so every SM gets the same number of MMAs
+// whatever the tile count. A tile cut between CTAs is summed as follows: the
+// CTA holding the tile's first K-block (it processes that piece LAST, at the
+// end of its share) finalises it; every other CTA holding a piece of the
+// tile holds it FIRST, writes its f32 partial accumulator to
+// args.sk_partials[cta] and raises args.sk_flags[cta][quarter]. The finaliser
+// adds the partials in CTA order (deterministic), stores C and clears the
+// flags, so the flag array is all zero again when the kernel ends. No CTA
+// waits on a lower-numbered CTA, and every wait is bounded.
+//
+// Roles (512 threads, one CTA per SM, persistent):
 //   warp 0        TMA producer (one lane)
 //   warp 1        TMEM owner + MMA issuer (one lane)
 //   warps 2-3     idle
-//   warps 4-11    int8 -> f16 converters (two per TMEM lane quarter, each one
-//                 16-column chunk of the block)
+//   warps 4-11    int8 -> f16 converters: warp 4 + 4 g + q converts TMEM lane
+//                 quarter q (16-column chunks 2q, 2q + 1) of the CTA's
+//                 K-blocks g, g + 2, g + 4, ...
 //   warps 12-15   epilogue
 // TMEM: accumulators in columns [0, 192) and [192, 384), kW8SA converted
 // weight stages of 32 columns from column 384.
@@ -43,8 +61,18 @@ constexpr int kW8SW = 8;    // int8 weight stages
 constexpr int kW8SA = 4;    // TMEM weight stages
 constexpr int kW8ACol = 2 * kW8BM;  // first TMEM column of the weight stages
 constexpr int kW8Threads = 16 * 32;
-constexpr int kW8ConvWarps = 8;
+constexpr int kW8ConvGroups = 2;    // converter groups (alternate K-blocks)
+constexpr int kW8ConvWarps = 4 * kW8ConvGroups;
 constexpr int kW8EpiWarps = 4;
+// f32 partial accumulator of one tile: 128 x 192 floats
+constexpr int kW8PartialFloats = kW8BN * kW8BM;
+// Stream-K workspace: flags [CTA][quarter] (int, up to 256 CTAs) in the first
+// kW8FlagBytes, then one partial accumulator per CTA.
+constexpr size_t kW8FlagBytes = 4096;
+constexpr int kW8MaxStreamKCtas = (int)(kW8FlagBytes / 16);
+// Smallest stream-K share, in K-blocks: a shorter share costs more in partial
+// traffic than it gains in balance.
+constexpr int kW8MinShare = 8;
 
 struct W8Smem {
   static constexpr int kXBytes = kW8BM * kBK * 2;  // 24 KB
@@ -91,6 +119,90 @@ __device__ __forceinline__ void drain_ring(uint64_t* full, RingCursor<S> c, int 
   }
 }
 
+// One piece of work: K-blocks [k0, k1) of output tile `tile`.
+struct W8Seg {
+  int tile, k0, k1;
+};
+
+// The sequence of pieces one CTA processes (the same for all its roles).
+struct W8Work {
+  int num_kb, num_tiles, streamk;
+  long long total, it0, it1;
+
+  // First iteration of CTA c's stream-K share (total >= gridDim.x, so no
+  // share is empty).
+  __device__ __forceinline__ long long share_begin(int c) const {
+    return total * c / gridDim.x;
+  }
+  __device__ __forceinline__ void init(const GemmArgs& a) {
+    num_kb = (a.K + kBK - 1) / kBK;
+    num_tiles = a.tiles_m * a.tiles_n;
+    streamk = a.streamk;
+    total = (long long)num_tiles * num_kb;
+    it0 = share_begin(blockIdx.x);
+    it1 = share_begin(blockIdx.x + 1);
+  }
+  __device__ __forceinline__ long long first() const { return streamk ? it0 : blockIdx.x; }
+  // K-blocks this CTA processes in all.
+  __device__ __forceinline__ long long kb_count() const {
+    if (streamk) return it1 - it0;
+    const int b = blockIdx.x, g = gridDim.x;
+    const long long nt = b < num_tiles ? (num_tiles - 1 - b) / g + 1 : 0;
+    return nt * num_kb;
+  }
+  __device__ __forceinline__ bool next(long long& pos, W8Seg& s) const {
+    if (!streamk) {
+      if (pos >= num_tiles) return false;
+      s.tile = (int)pos;
+      s.k0 = 0;
+      s.k1 = num_kb;
+      pos += gridDim.x;
+      return true;
+    }
+    if (pos >= it1) return false;
+    s.tile = (int)(pos / num_kb);
+    s.k0 = (int)(pos - (long long)s.tile * num_kb);
+    const long long k1 = s.k0 + (it1 - pos);
+    s.k1 = k1 < num_kb ? (int)k1 : num_kb;
+    pos += s.k1 - s.k0;
+    return true;
+  }
+};
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_gpu(int* p, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Bounded wait until *flag == 1 (raised by another CTA of this grid).
+__device__ __forceinline__ bool wait_flag(const int* flag, const FailState& fs) {
+  if (ld_acquire_gpu(flag) == 1) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 16; ++i) {
+      if (ld_acquire_gpu(flag) == 1) return true;
+      __nanosleep(64);
+    }
+    if (*fs.abort) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      raise_failure(fs);
+      return false;
+    }
+  }
+}
+
+// float4 index of (epilogue quarter q, half h, 32-column chunk c, rep r, lane)
+// inside one CTA's partial accumulator image: the float4 a thread writes for
+// one tcgen05.ld repetition, so each warp access is 512 contiguous bytes.
+__device__ __forceinline__ int w8_partial_index(int q, int h, int c, int r, int lane) {
+  return (((q * 2 + h) * (kW8BM / 32) + c) * 4 + r) * 32 + lane;
+}
+
 __global__ void __launch_bounds__(kW8Threads, 1)
     gemm_w8_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
                          const __grid_constant__ CUtensorMap tmW, const GemmArgs args) {
@@ -116,14 +228,14 @@ __global__ void __launch_bounds__(kW8Threads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int num_tiles = args.tiles_m * args.tiles_n;
-  const int num_kb = (args.K + kBK - 1) / kBK;
+  W8Work work;
+  work.init(args);
   const FailState fs{abort_flag, args.status};
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kW8SX; ++s) { mbar_init(&x_full[s], 1); mbar_init(&x_empty[s], 1); }
-    for (int s = 0; s < kW8SW; ++s) { mbar_init(&w_full[s], 1); mbar_init(&w_empty[s], kW8ConvWarps); }
-    for (int s = 0; s < kW8SA; ++s) { mbar_init(&a_full[s], kW8ConvWarps); mbar_init(&a_empty[s], 1); }
+    for (int s = 0; s < kW8SW; ++s) { mbar_init(&w_full[s], 1); mbar_init(&w_empty[s], 4); }
+    for (int s = 0; s < kW8SA; ++s) { mbar_init(&a_full[s], 4); mbar_init(&a_empty[s], 1); }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&t_full[i], 1);
       mbar_init(&t_empty[i], kW8EpiWarps);
@@ -152,10 +264,12 @@ __global__ void __launch_bounds__(kW8Threads, 1)
       RingCursor<kW8SW> cw;
       int issued_x = 0, issued_w = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      long long pos = work.first();
+      W8Seg sg;
+      while (ok && work.next(pos, sg)) {
         int tm, tn;
-        tile_coords(t, args, tm, tn);
-        for (int kb = 0; kb < num_kb; ++kb) {
+        tile_coords(sg.tile, args, tm, tn);
+        for (int kb = sg.k0; kb < sg.k1; ++kb) {
           if (!mbar_wait(&w_empty[cw.slot], cw.phase ^ 1, fs)) { ok = false; break; }
           mbar_arrive_expect_tx(&w_full[cw.slot], L::kWBytes);
           tma_load_2d(smem + L::kOffW + cw.slot * L::kWBytes, &tmW, &w_full[cw.slot],
@@ -180,12 +294,14 @@ __global__ void __launch_bounds__(kW8Threads, 1)
       RingCursor<kW8SA> ca;
       int tl = 0;
       bool ok = true, issued_any = false;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++tl) {
+      long long pos = work.first();
+      W8Seg sg;
+      while (ok && work.next(pos, sg)) {
         const int acc = tl & 1;
         if (!mbar_wait(&t_empty[acc], (uint32_t)((tl >> 1) & 1) ^ 1, fs)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + kW8BM * acc;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = sg.k0; kb < sg.k1; ++kb) {
           const int sx = cx.slot, sa = ca.slot;
           if (!mbar_wait(&x_full[sx], cx.phase, fs) || !mbar_wait(&a_full[sa], ca.phase, fs)) {
             ok = false;
@@ -197,7 +313,7 @@ __global__ void __launch_bounds__(kW8Threads, 1)
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k) {
             const uint64_t bdesc = make_smem_desc(x_addr + k * 32, 16, 1024, kLayoutSwizzle128);
-            umma_f16_ts(d_tmem, a_tmem + 8 * k, bdesc, kIdesc, (kb | k) != 0);
+            umma_f16_ts(d_tmem, a_tmem + 8 * k, bdesc, kIdesc, (kb != sg.k0) || (k != 0));
           }
           issued_any = true;
           umma_commit(&x_empty[sx]);
@@ -206,6 +322,7 @@ __global__ void __launch_bounds__(kW8Threads, 1)
           ca.advance();
         }
         if (ok) umma_commit(&t_full[acc]);
+        ++tl;
       }
       if (!ok && issued_any) {
         umma_commit(drain);
@@ -216,30 +333,26 @@ __global__ void __launch_bounds__(kW8Threads, 1)
     }
   } else if (warp >= 4 && warp < 4 + kW8ConvWarps) {
     // ------------------------------------------------------ int8 -> f16 -> TMEM
+    // The g-th K-block of this CTA (over all its pieces, in order) sits in
+    // weight stage g % SW and goes to TMEM stage g % SA; group `grp` converts
+    // the blocks g = grp, grp + 2, ...
     const int q = warp & 3;
-    const int h = (warp - 4) >> 2;  // the warp's 16-column chunk of the quarter
-    const int chunk = 2 * q + h;
-    RingCursor<kW8SW> cw;
-    RingCursor<kW8SA> ca;
-    bool ok = true;
-    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-      for (int kb = 0; kb < num_kb; ++kb) {
-        const int sw = cw.slot, sa = ca.slot;
-        const bool ready = mbar_wait(&w_full[sw], cw.phase, fs) &&
-                           mbar_wait(&a_empty[sa], ca.phase ^ 1, fs);
-        if (!__all_sync(0xffffffffu, ready)) { ok = false; break; }
-        tc_fence_after();
-        w8_chunk_to_tmem(smem_u32(smem + L::kOffW + sw * L::kWBytes), tmem_base, 16 * chunk,
-                         kW8ACol + 32 * sa, chunk, lane);
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&a_full[sa]);
-          mbar_arrive(&w_empty[sw]);
-        }
-        cw.advance();
-        ca.advance();
+    const int grp = (warp - 4) >> 2;
+    const long long nkb = work.kb_count();
+    for (long long g = grp; g < nkb; g += kW8ConvGroups) {
+      const int sw = (int)(g % kW8SW), sa = (int)(g % kW8SA);
+      const uint32_t pw = (uint32_t)((g / kW8SW) & 1), pa = (uint32_t)((g / kW8SA) & 1);
+      const bool ready = mbar_wait(&w_full[sw], pw, fs) && mbar_wait(&a_empty[sa], pa ^ 1, fs);
+      if (!__all_sync(0xffffffffu, ready)) break;
+      tc_fence_after();
+      w8_chunks_to_tmem<2>(smem_u32(smem + L::kOffW + sw * L::kWBytes), tmem_base, 32 * q,
+                           kW8ACol + 32 * sa, 2 * q, lane);
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&a_full[sa]);
+        mbar_arrive(&w_empty[sw]);
       }
     }
   } else if (warp >= 4 + kW8ConvWarps) {
@@ -251,59 +364,181 @@ __global__ void __launch_bounds__(kW8Threads, 1)
     const int q = warp & 3;
     const int t = lane;
     int tl = 0;
-    for (int tt = blockIdx.x; tt < num_tiles; tt += gridDim.x, ++tl) {
+    long long pos = work.first();
+    W8Seg sg;
+    while (work.next(pos, sg)) {
       int tm, tn;
-      tile_coords(tt, args, tm, tn);
+      tile_coords(sg.tile, args, tm, tn);
       const int acc = tl & 1;
-      const bool ready = mbar_wait(&t_full[acc], (uint32_t)((tl >> 1) & 1), fs);
+      const bool contributor = sg.k0 > 0;
+      // CTAs whose partial accumulators this (finalising) piece adds
+      int c_lo = blockIdx.x + 1, c_hi = blockIdx.x + 1;
+      if (!contributor && sg.k1 < work.num_kb) {
+        const long long tile_end = (long long)(sg.tile + 1) * work.num_kb;
+        while (c_hi < (int)gridDim.x && work.share_begin(c_hi) < tile_end) ++c_hi;
+      }
+      // scales of this thread's column pairs, fetched while the MMAs run
+      float sc[2][2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int n = tn * kW8BN + 16 * (2 * q + h) + 2 * (t >> 2);
+        sc[h][0] = (!contributor && n < args.N) ? __half2float(args.scale[n]) : 0.0f;
+        sc[h][1] = (!contributor && n + 1 < args.N) ? __half2float(args.scale[n + 1]) : 0.0f;
+      }
+      bool ready = mbar_wait(&t_full[acc], (uint32_t)((tl >> 1) & 1), fs);
+      for (int c2 = c_lo; c2 < c_hi && ready; ++c2)
+        ready = wait_flag(args.sk_flags + 4 * c2 + q, fs);
       if (!__all_sync(0xffffffffu, ready)) break;
       tc_fence_after();
       const int m0 = tm * kW8BM;
+
+      if (contributor) {
+        float4* part = reinterpret_cast<float4*>(args.sk_partials) +
+                       (size_t)blockIdx.x * (kW8PartialFloats / 4);
 #pragma unroll 1
-      for (int h = 0; h < 2; ++h) {
-        const int chunk = 2 * q + h;
-        const int n = tn * kW8BN + 16 * chunk + 2 * (t >> 2);
-        const bool n0_ok = n < args.N, n1_ok = n + 1 < args.N;
-        const float s0 = n0_ok ? __half2float(args.scale[n]) : 0.0f;
-        const float s1 = n1_ok ? __half2float(args.scale[n + 1]) : 0.0f;
-        __half* cbase = reinterpret_cast<__half*>(args.C) + n;
-        const __half* rbase =
-            args.C_init ? reinterpret_cast<const __half*>(args.C_init) + n : nullptr;
-        const uint32_t taddr = tmem_base + ((uint32_t)(16 * chunk) << 16) + kW8BM * acc;
+        for (int h = 0; h < 2; ++h) {
+          const uint32_t taddr =
+              tmem_base + ((uint32_t)(16 * (2 * q + h)) << 16) + kW8BM * acc;
 #pragma unroll 1
-        for (int c = 0; c < kW8BM / 32; ++c) {
-          uint32_t r[16];
-          tmem_ld_16x256b_x4(taddr + 32 * c, r);
-          tmem_wait_ld();
-          if (!n0_ok) continue;
+          for (int c = 0; c < kW8BM / 32; c += 2) {
+            uint32_t r[2][16];
+            tmem_ld_16x256b_x4(taddr + 32 * c, r[0]);
+            tmem_ld_16x256b_x4(taddr + 32 * (c + 1), r[1]);
+            tmem_wait_ld();
 #pragma unroll
-          for (int rep = 0; rep < 4; ++rep) {
+            for (int u = 0; u < 2; ++u)
 #pragma unroll
-            for (int j = 0; j < 2; ++j) {
-              const int m = m0 + 32 * c + 8 * rep + 2 * (t & 3) + j;
-              if (m >= args.M) continue;
-              float v0 = __uint_as_float(r[4 * rep + j]) * s0;
-              float v1 = __uint_as_float(r[4 * rep + 2 + j]) * s1;
-              const long long off = (long long)m * args.ldc;
-              if (n1_ok) {
-                if (rbase) {
-                  const float2 rv =
-                      __half22float2(*reinterpret_cast<const __half2*>(rbase + off));
-                  v0 += rv.x;
-                  v1 += rv.y;
+              for (int rep = 0; rep < 4; ++rep)
+                __stcg(part + w8_partial_index(q, h, c + u, rep, t),
+                       make_float4(__uint_as_float(r[u][4 * rep]),
+                                   __uint_as_float(r[u][4 * rep + 1]),
+                                   __uint_as_float(r[u][4 * rep + 2]),
+                                   __uint_as_float(r[u][4 * rep + 3])));
+          }
+        }
+        // publish: every lane's stores, then the flag of this quarter
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) st_release_gpu(args.sk_flags + 4 * blockIdx.x + q, 1);
+      } else {
+        const bool rows_full = m0 + kW8BM <= args.M;
+        const __half* R = reinterpret_cast<const __half*>(args.C_init);
+#pragma unroll 1
+        for (int h = 0; h < 2; ++h) {
+          const int chunk = 2 * q + h;
+          const int n = tn * kW8BN + 16 * chunk + 2 * (t >> 2);
+          const bool n0_ok = n < args.N, n1_ok = n + 1 < args.N;
+          const bool fast = rows_full && n1_ok;
+          const float s0 = h ? sc[1][0] : sc[0][0], s1 = h ? sc[1][1] : sc[0][1];
+          const uint32_t taddr = tmem_base + ((uint32_t)(16 * chunk) << 16) + kW8BM * acc;
+          // row of (chunk c, rep, j) = row0 + 32 c + 8 rep + j
+          const int row0 = m0 + 2 * (t & 3);
+          __half* cbase = reinterpret_cast<__half*>(args.C) + (long long)row0 * args.ldc + n;
+          const __half* rbase = R ? R + (long long)row0 * args.ldc + n : nullptr;
+#pragma unroll 1
+          for (int c = 0; c < kW8BM / 32; c += 2) {
+            // residual pairs and partial sums of the two chunks, loaded ahead
+            // of the TMEM reads
+            uint32_t res[2][8];
+#pragma unroll
+            for (int u = 0; u < 2; ++u)
+#pragma unroll
+              for (int e = 0; e < 8; ++e) res[u][e] = 0u;
+            if (rbase && fast) {
+#pragma unroll
+              for (int u = 0; u < 2; ++u)
+#pragma unroll
+                for (int rep = 0; rep < 4; ++rep)
+#pragma unroll
+                  for (int j = 0; j < 2; ++j)
+                    res[u][2 * rep + j] = __ldg(reinterpret_cast<const unsigned int*>(
+                        rbase + (long long)(32 * (c + u) + 8 * rep + j) * args.ldc));
+            }
+            float v[2][16];
+#pragma unroll
+            for (int u = 0; u < 2; ++u)
+#pragma unroll
+              for (int e = 0; e < 16; ++e) v[u][e] = 0.0f;
+            for (int c2 = c_lo; c2 < c_hi; ++c2) {
+              const float4* part = reinterpret_cast<const float4*>(args.sk_partials) +
+                                   (size_t)c2 * (kW8PartialFloats / 4);
+#pragma unroll
+              for (int u = 0; u < 2; ++u)
+#pragma unroll
+                for (int rep = 0; rep < 4; ++rep) {
+                  const float4 p = __ldcg(part + w8_partial_index(q, h, c + u, rep, t));
+                  v[u][4 * rep] += p.x;
+                  v[u][4 * rep + 1] += p.y;
+                  v[u][4 * rep + 2] += p.z;
+                  v[u][4 * rep + 3] += p.w;
                 }
-                *reinterpret_cast<__half2*>(cbase + off) = __floats2half2_rn(v0, v1);
-              } else {
-                if (rbase) v0 += __half2float(rbase[off]);
-                cbase[off] = __float2half_rn(v0);
-              }
+            }
+            uint32_t r[2][16];
+            tmem_ld_16x256b_x4(taddr + 32 * c, r[0]);
+            tmem_ld_16x256b_x4(taddr + 32 * (c + 1), r[1]);
+            tmem_wait_ld();
+            // this CTA's accumulator plus the partials (summed in CTA order)
+#pragma unroll
+            for (int u = 0; u < 2; ++u)
+#pragma unroll
+              for (int e = 0; e < 16; ++e) v[u][e] = __uint_as_float(r[u][e]) + v[u][e];
+            if (fast) {
+#pragma unroll
+              for (int u = 0; u < 2; ++u)
+#pragma unroll
+                for (int rep = 0; rep < 4; ++rep)
+#pragma unroll
+                  for (int j = 0; j < 2; ++j) {
+                    float v0 = v[u][4 * rep + j] * s0;
+                    float v1 = v[u][4 * rep + 2 + j] * s1;
+                    if (rbase) {
+                      const float2 rv = __half22float2(
+                          *reinterpret_cast<const __half2*>(&res[u][2 * rep + j]));
+                      v0 += rv.x;
+                      v1 += rv.y;
+                    }
+                    *reinterpret_cast<__half2*>(
+                        cbase + (long long)(32 * (c + u) + 8 * rep + j) * args.ldc) =
+                        __floats2half2_rn(v0, v1);
+                  }
+            } else if (n0_ok) {
+              // ragged edge: rows past M, or the last column of an odd N
+#pragma unroll
+              for (int u = 0; u < 2; ++u)
+#pragma unroll
+                for (int rep = 0; rep < 4; ++rep)
+#pragma unroll
+                  for (int j = 0; j < 2; ++j) {
+                    const int dm = 32 * (c + u) + 8 * rep + j;
+                    if (row0 + dm >= args.M) continue;
+                    const long long off = (long long)dm * args.ldc;
+                    float v0 = v[u][4 * rep + j] * s0;
+                    float v1 = v[u][4 * rep + 2 + j] * s1;
+                    if (n1_ok) {
+                      if (rbase) {
+                        const float2 rv =
+                            __half22float2(*reinterpret_cast<const __half2*>(rbase + off));
+                        v0 += rv.x;
+                        v1 += rv.y;
+                      }
+                      *reinterpret_cast<__half2*>(cbase + off) = __floats2half2_rn(v0, v1);
+                    } else {
+                      if (rbase) v0 += __half2float(rbase[off]);
+                      cbase[off] = __float2half_rn(v0);
+                    }
+                  }
             }
           }
         }
+        // the partials of this tile are consumed: clear their flags for the
+        // next launch
+        if (lane == 0)
+          for (int c2 = c_lo; c2 < c_hi; ++c2) args.sk_flags[4 * c2 + q] = 0;
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&t_empty[acc]);
+      ++tl;
     }
   }
 

@@ -98,4 +98,38 @@ __device__ __forceinline__ void w8_chunk_to_tmem(uint32_t tile_s, uint32_t tmem_
   tmem_st_16x128b_x8(tmem_base + ((uint32_t)lane0 << 16) + tmem_col, out);
 }
 
+// Converts NC consecutive 16-column chunks (chunk0, chunk0 + 1, ...) of one
+// int8 tile into TMEM lanes lane0 + 16 c (c = 0 .. NC-1), columns [tmem_col,
+// tmem_col + 32). All shared-memory loads are issued before the arithmetic so
+// that their latencies overlap. Ends with the TMEM stores issued (the caller
+// waits with tmem_wait_st()).
+template <int NC>
+__device__ __forceinline__ void w8_chunks_to_tmem(uint32_t tile_s, uint32_t tmem_base, int lane0,
+                                                  uint32_t tmem_col, int chunk0, int lane) {
+  const int mrow = lane & 7, mat = lane >> 3;
+  uint32_t raw[NC][8];
+#pragma unroll
+  for (int c = 0; c < NC; ++c)
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+      const int k = 8 * (4 * s + mat) + mrow;
+      uint32_t r4[4];
+      ldsm_x4_trans(tile_s + k * 128 + (((chunk0 + c) ^ (k & 7)) << 4), r4);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) raw[c][4 * s + i] = r4[i];
+    }
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    uint32_t out[16];
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+      const uint32_t lo = (raw[c][g] & 0x00FF00FFu) ^ 0x64806480u;
+      const uint32_t hi = ((raw[c][g] >> 8) & 0x00FF00FFu) ^ 0x64806480u;
+      asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(out[2 * g]) : "r"(lo), "r"(0x64806480u));
+      asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(out[2 * g + 1]) : "r"(hi), "r"(0x64806480u));
+    }
+    tmem_st_16x128b_x8(tmem_base + ((uint32_t)(lane0 + 16 * c) << 16) + tmem_col, out);
+  }
+}
+
 }  // namespace hxb

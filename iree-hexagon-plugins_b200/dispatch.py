@@ -65,11 +65,23 @@ def matmul(a: torch.Tensor, b: torch.Tensor, *, transpose_b: bool = False,
     return out
 
 
+def w8a16_workspace(device: torch.device | str | None = None) -> torch.Tensor:
+    """A zeroed stream-K workspace for matmul_w8a16(..., workspace=) on
+    `device` (allocate once, reuse for calls ordered on one stream)."""
+    lib = _native.load()
+    dev = torch.device(device) if device is not None else torch.device("cuda")
+    with torch.cuda.device(dev):
+        nbytes = lib.hxb_matmul_w8a16_workspace_bytes(1, 1, 1)
+    return torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+
+
 def matmul_w8a16(a: torch.Tensor, w: torch.Tensor, scale: torch.Tensor,
                  out: torch.Tensor | None = None,
-                 residual: torch.Tensor | None = None) -> torch.Tensor:
+                 residual: torch.Tensor | None = None,
+                 workspace: torch.Tensor | None = None) -> torch.Tensor:
     """C[M,N] f16 = (a[M,K] f16 @ w[K,N] int8) * scale[N] f16 (+ residual),
-    f32 accumulation."""
+    f32 accumulation. With `workspace` (from w8a16_workspace) the dispatch may
+    split K across SMs (stream-K) when whole tiles would leave SMs idle."""
     lib = _native.load()
     _require(a.dtype == torch.float16 and w.dtype == torch.int8 and
              scale.dtype == torch.float16, "dtypes must be f16 / int8 / f16")
@@ -79,6 +91,17 @@ def matmul_w8a16(a: torch.Tensor, w: torch.Tensor, scale: torch.Tensor,
     if out is None:
         out = torch.empty((M, N), dtype=torch.float16, device=a.device)
     ldc = _rowmajor_ld(out, "out")
+    if workspace is not None:
+        _require(workspace.is_cuda and workspace.is_contiguous(), "workspace must be a CUDA buffer")
+        if residual is not None:
+            _require(residual.shape == out.shape and residual.stride() == out.stride() and
+                     residual.dtype == torch.float16, "residual must match out")
+        check(lib.hxb_matmul_w8a16_streamk(
+            a.data_ptr(), _rowmajor_ld(a, "a"), w.data_ptr(), _rowmajor_ld(w, "w"),
+            scale.data_ptr(), residual.data_ptr() if residual is not None else None,
+            out.data_ptr(), ldc, M, N, K, workspace.data_ptr(),
+            workspace.numel() * workspace.element_size(), _stream_ptr(a)))
+        return out
     if residual is None:
         check(lib.hxb_matmul_w8a16(a.data_ptr(), _rowmajor_ld(a, "a"), w.data_ptr(),
                                    _rowmajor_ld(w, "w"), scale.data_ptr(), out.data_ptr(),

@@ -1,0 +1,118 @@
+"""Parity of the stream-K schedule of the int8-weight GEMM
+(hxb_matmul_w8a16_streamk): K split across CTAs when whole tiles would leave
+SMs idle, partial sums added by the CTA that owns the tile's first K-block.
+
+Shapes are the decoder block's M = 512 projections (96 and 516 output tiles
+on 148 SMs) and small ragged cases where one tile is cut into many pieces."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from _support import baseline_check
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+FLAG_BYTES = 4096
+
+
+def _inputs(M, K, N, seed):
+    rng = np.random.default_rng(seed)
+    a = rng.standard_normal((M, K)).astype(np.float16)
+    w = rng.integers(-127, 128, (K, N), dtype=np.int8)
+    s = rng.uniform(0.001, 0.02, N).astype(np.float16)
+    r = rng.standard_normal((M, N)).astype(np.float16)
+    return a, w, s, r
+
+
+def _t(x):
+    return torch.from_numpy(x).to(DEV)
+
+
+@pytest.mark.parametrize("M,K,N,res", [
+    (512, 4096, 4096, True),     # decoder O projection: 96 tiles
+    (512, 11008, 4096, True),    # decoder down projection
+    (512, 4096, 22016, False),   # decoder gate|up: 516 tiles, 3.5 waves
+    (129, 1000, 272, True),      # ragged K and M, each tile cut in two
+    (100, 8192, 144, False),     # 2 tiles cut into 16 pieces each
+    (200, 320, 528, False),      # too little K to split: data-parallel
+])
+def test_streamk_vs_oracle(cuda_pkg, oracle, M, K, N, res):
+    a, w, s, r = _inputs(M, K, N, seed=M * 7 + N)
+    ws = cuda_pkg.w8a16_workspace(DEV)
+    ad, wd, sd, rd = _t(a), _t(w), _t(s), _t(r)
+    got = cuda_pkg.matmul_w8a16(ad, wd, sd, residual=rd if res else None, workspace=ws)
+    again = cuda_pkg.matmul_w8a16(ad, wd, sd, residual=rd if res else None, workspace=ws)
+    torch.cuda.synchronize()
+    assert cuda_pkg.device_status() == 0
+    # every finaliser cleared the flags it consumed; partial sums are added in
+    # a fixed order, so a second call is bit-identical
+    assert int(ws[:FLAG_BYTES].count_nonzero()) == 0
+    assert torch.equal(got, again)
+    rows = np.arange(M) if M * K * N <= 2**31 else np.array([0, 1, 190, 191, 192, 383, 384, 511])
+    ref = oracle.matmul_w8a16_f32(a[rows], w, s)
+    if res:
+        ref = ref + r[rows].astype(np.float32)
+    baseline_check(ref, got[torch.from_numpy(rows).to(DEV)].float().cpu().numpy(),
+                   f"w8 stream-K {M}x{K}x{N}")
+
+
+def test_streamk_matches_data_parallel(cuda_pkg):
+    """The split changes only the f32 summation order of the tensor-core
+    accumulation, so against the data-parallel schedule most f16 results are
+    bit-identical and the rest differ by rounding: within the BASELINE bar
+    (1e-2 + one f16 ulp), and within a few ulp where the scaled product and the
+    residual cancel."""
+    M, K, N = 512, 4096, 4096
+    a, w, s, r = _inputs(M, K, N, seed=5)
+    ad, wd, sd, rd = _t(a), _t(w), _t(s), _t(r)
+    sk = cuda_pkg.matmul_w8a16(ad, wd, sd, residual=rd, workspace=cuda_pkg.w8a16_workspace(DEV))
+    dp = cuda_pkg.matmul_w8a16(ad, wd, sd, residual=rd)
+    torch.cuda.synchronize()
+    sk, dp = sk.float().cpu().numpy(), dp.float().cpu().numpy()
+    big = np.maximum(np.abs(sk), np.abs(dp)).astype(np.float16)
+    ulp = np.spacing(big).astype(np.float64)
+    d = np.abs(sk.astype(np.float64) - dp)
+    assert (d <= 1e-2 + ulp).all(), float((d - ulp).max())
+    assert float((d == 0).mean()) > 0.5, float((d == 0).mean())
+
+
+def test_streamk_graph_replay(cuda_pkg):
+    """Captured once, replayed: the flags each replay raises are cleared by the
+    same replay, so every replay computes the same result."""
+    M, K, N = 512, 4096, 4096
+    a, w, s, r = _inputs(M, K, N, seed=6)
+    ad, wd, sd, rd = _t(a), _t(w), _t(s), _t(r)
+    ws = cuda_pkg.w8a16_workspace(DEV)
+    out = torch.empty(M, N, dtype=torch.float16, device=DEV)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        cuda_pkg.matmul_w8a16(ad, wd, sd, residual=rd, workspace=ws, out=out)
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    first = out.clone()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        cuda_pkg.matmul_w8a16(ad, wd, sd, residual=rd, workspace=ws, out=out)
+    for _ in range(3):
+        out.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, first)
+    assert int(ws[:FLAG_BYTES].count_nonzero()) == 0
+    assert cuda_pkg.device_status() == 0
+
+
+def test_streamk_rejects_missing_workspace(cuda_pkg):
+    lib = cuda_pkg._native.load()
+    a = torch.zeros(256, 256, dtype=torch.float16, device=DEV)
+    w = torch.zeros(256, 256, dtype=torch.int8, device=DEV)
+    s = torch.ones(256, dtype=torch.float16, device=DEV)
+    c = torch.empty(256, 256, dtype=torch.float16, device=DEV)
+    rc = lib.hxb_matmul_w8a16_streamk(a.data_ptr(), 256, w.data_ptr(), 256, s.data_ptr(), None,
+                                      c.data_ptr(), 256, 256, 256, 256, None, 0,
+                                      torch.cuda.current_stream().cuda_stream)
+    assert rc != 0
+    assert b"workspace" in lib.hxb_last_error_message()
