@@ -247,6 +247,20 @@ size_t w8_streamk_workspace_bytes(int ctas) {
 }
 int w8_streamk_flag_ints() { return (int)(kW8FlagBytes / sizeof(int)); }
 
+// Stream-K choice of the W8 GEMM: `units` CTAs can run at once, `tiles`
+// output tiles of `num_kb` K-blocks each. Returns the number of CTAs to
+// launch with stream-K, or 0 for the data-parallel schedule.
+int w8_streamk_units(int tiles, long long num_kb, int units) {
+  const long long total = (long long)tiles * num_kb;
+  const int waves = (tiles + units - 1) / units;
+  const double fill = (double)tiles / ((double)waves * units);
+  const long long g = total / kW8MinShare < units ? total / kW8MinShare : units;
+  // fewer tiles than units: spread them over more units; several waves: even
+  // out the last one over all units
+  if (fill < 0.92 && (g > tiles || (tiles > units && g == units))) return (int)g;
+  return 0;
+}
+
 hxb_status_t gemm_w8_impl(const void* A, int64_t lda, const void* W,
                           int64_t ldw, const void* scale, const void* R, void* C, int64_t ldc,
                           int64_t M, int64_t N, int64_t K, void* sk_ws, size_t sk_ws_bytes,
@@ -286,33 +300,28 @@ hxb_status_t gemm_w8_impl(const void* A, int64_t lda, const void* W,
   // CTAs running at the same time share that int8 block in L2
   args.group_m = args.tiles_m;
   args.vec_ok = 0;
-  static bool configured[64] = {};
-  if (!configured[dev->ordinal]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_w8_sm100_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, W8Smem::kAlloc);
-    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(gemm_w8)");
-    configured[dev->ordinal] = true;
-  }
   const int tiles = args.tiles_m * args.tiles_n;
-  int grid = tiles < dev->num_sms ? tiles : dev->num_sms;
-  // Stream-K when whole tiles leave SMs idle in the last wave (and the caller
-  // gave the workspace): every SM then gets the same share of K-blocks.
   const int sms = dev->num_sms;
+  int grid = tiles < sms ? tiles : sms;
+  // Stream-K (when the caller gave the workspace) if whole tiles would leave
+  // SMs idle in the last wave: every SM then gets the same share of K-blocks.
   if (sk_ws && sms <= kW8MaxStreamKCtas && sk_ws_bytes >= w8_streamk_workspace_bytes(sms)) {
-    const long long num_kb = (K + kBK - 1) / kBK;
-    const long long total = (long long)tiles * num_kb;
-    const int waves = (tiles + sms - 1) / sms;
-    const double fill = (double)tiles / ((double)waves * sms);
-    const long long g = total / kW8MinShare < sms ? total / kW8MinShare : sms;
-    // fewer tiles than SMs: spread them over more CTAs; several waves: even
-    // out the last one over all SMs
-    if (fill < 0.92 && (g > tiles || (tiles > sms && g == sms))) {
-      grid = (int)g;
+    const int g = w8_streamk_units(tiles, (K + kBK - 1) / kBK, sms);
+    if (g) {
+      grid = g;
       args.streamk = 1;
       args.sk_flags = static_cast<int*>(sk_ws);
       args.sk_partials =
           reinterpret_cast<float*>(static_cast<uint8_t*>(sk_ws) + kW8FlagBytes);
     }
+  }
+  static bool configured[64] = {};
+  if (!configured[dev->ordinal]) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_w8_sm100_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         W8Smem::kAlloc);
+    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(gemm_w8)");
+    configured[dev->ordinal] = true;
   }
   gemm_w8_sm100_kernel<<<grid, kW8Threads, W8Smem::kAlloc, stream>>>(tmA, tmW, args);
   return cuda_status(cudaGetLastError(), "gemm_w8 launch");

@@ -4,7 +4,7 @@
 // on the tensor core so that the dequantised weights never pass through
 // shared memory a second time:
 //   * TMA lands the raw int8 weight tile [64 k][128 n] (8 KB, 128-byte
-//     swizzle) and the activation tile [192 m][64 k] f16 (24 KB) in two
+//     swizzle) and the activation tile [256 m][64 k] f16 (32 KB) in two
 //     independent rings;
 //   * eight converter warps transpose the int8 tile on its way out of shared
 //     memory (ldmatrix.trans), convert it exactly to f16 (|w| <= 127) in
@@ -14,8 +14,14 @@
 //     conversion at once and the latency of one (shared-memory load, TMEM
 //     store, wait) is hidden behind the other;
 //   * one thread issues tcgen05.mma (A from TMEM, B = activations from shared
-//     memory, N = 192 activation rows) into one of two 192-column f32 TMEM
-//     accumulators, so the epilogue of tile t overlaps the main loop of t+1;
+//     memory, N = 256 activation rows) into a 256-column f32 TMEM
+//     accumulator. N = 256 amortises each converted weight block over the
+//     most activation rows one MMA takes; measured on B200 it beats two
+//     double-buffered 192-column accumulators (366 -> 317 us on the 4096 x
+//     4096 x 11008 dispatch). TMEM then has no room for a second accumulator,
+//     so the MMA waits while the epilogue drains the tile; the TMA and the
+//     converters keep running meanwhile and fill up to kW8SA converted
+//     K-blocks for the next tile;
 //   * four epilogue warps read the accumulator back, apply the per-column
 //     scale once (it factors out of the K sum), add the optional residual and
 //     store C transposed. Scales are fetched before the accumulator is ready;
@@ -45,8 +51,8 @@
 //                 quarter q (16-column chunks 2q, 2q + 1) of the CTA's
 //                 K-blocks g, g + 2, g + 4, ...
 //   warps 12-15   epilogue
-// TMEM: accumulators in columns [0, 192) and [192, 384), kW8SA converted
-// weight stages of 32 columns from column 384.
+// TMEM: the accumulator in columns [0, 256), kW8SA = 8 converted weight
+// stages of 32 columns from column 256.
 #pragma once
 
 #include "gemm_sm100.cuh"
@@ -55,16 +61,18 @@
 namespace hxb {
 
 constexpr int kW8BN = 128;  // weight columns per tile (MMA M, TMEM lanes)
-constexpr int kW8BM = 192;  // activation rows per tile (MMA N)
-constexpr int kW8SX = 6;    // activation stages
+constexpr int kW8BM = 256;  // activation rows per tile (MMA N)
+constexpr int kW8Acc = 1;   // TMEM accumulators (kW8Acc * kW8BM + 32 * kW8SA <= 512)
+constexpr int kW8SX = 5;    // activation stages
 constexpr int kW8SW = 8;    // int8 weight stages
-constexpr int kW8SA = 4;    // TMEM weight stages
-constexpr int kW8ACol = 2 * kW8BM;  // first TMEM column of the weight stages
+constexpr int kW8SA = 8;    // TMEM weight stages
+constexpr int kW8ACol = kW8Acc * kW8BM;  // first TMEM column of the weight stages
+static_assert(kW8ACol + 32 * kW8SA <= 512, "TMEM budget");
 constexpr int kW8Threads = 16 * 32;
 constexpr int kW8ConvGroups = 2;    // converter groups (alternate K-blocks)
 constexpr int kW8ConvWarps = 4 * kW8ConvGroups;
 constexpr int kW8EpiWarps = 4;
-// f32 partial accumulator of one tile: 128 x 192 floats
+// f32 partial accumulator of one tile: 128 x 256 floats
 constexpr int kW8PartialFloats = kW8BN * kW8BM;
 // Stream-K workspace: flags [CTA][quarter] (int, up to 256 CTAs) in the first
 // kW8FlagBytes, then one partial accumulator per CTA.
@@ -75,7 +83,7 @@ constexpr int kW8MaxStreamKCtas = (int)(kW8FlagBytes / 16);
 constexpr int kW8MinShare = 8;
 
 struct W8Smem {
-  static constexpr int kXBytes = kW8BM * kBK * 2;  // 24 KB
+  static constexpr int kXBytes = kW8BM * kBK * 2;  // 32 KB
   static constexpr int kWBytes = kW8BN * kBK;      // 8 KB
   static constexpr int kOffX = 0;
   static constexpr int kOffW = kOffX + kW8SX * kXBytes;
@@ -124,30 +132,30 @@ struct W8Seg {
   int tile, k0, k1;
 };
 
-// The sequence of pieces one CTA processes (the same for all its roles).
+// The sequence of pieces one work unit (a CTA) processes; the same for all
+// roles of the unit. Units are numbered 0 .. nunits-1.
 struct W8Work {
-  int num_kb, num_tiles, streamk;
+  int num_kb, num_tiles, streamk, unit, nunits;
   long long total, it0, it1;
 
-  // First iteration of CTA c's stream-K share (total >= gridDim.x, so no
-  // share is empty).
-  __device__ __forceinline__ long long share_begin(int c) const {
-    return total * c / gridDim.x;
-  }
-  __device__ __forceinline__ void init(const GemmArgs& a) {
+  // First iteration of unit c's stream-K share (total >= nunits, so no share
+  // is empty).
+  __device__ __forceinline__ long long share_begin(int c) const { return total * c / nunits; }
+  __device__ __forceinline__ void init(const GemmArgs& a, int unit_, int nunits_) {
+    unit = unit_;
+    nunits = nunits_;
     num_kb = (a.K + kBK - 1) / kBK;
     num_tiles = a.tiles_m * a.tiles_n;
     streamk = a.streamk;
     total = (long long)num_tiles * num_kb;
-    it0 = share_begin(blockIdx.x);
-    it1 = share_begin(blockIdx.x + 1);
+    it0 = share_begin(unit);
+    it1 = share_begin(unit + 1);
   }
-  __device__ __forceinline__ long long first() const { return streamk ? it0 : blockIdx.x; }
-  // K-blocks this CTA processes in all.
+  __device__ __forceinline__ long long first() const { return streamk ? it0 : unit; }
+  // K-blocks this unit processes in all.
   __device__ __forceinline__ long long kb_count() const {
     if (streamk) return it1 - it0;
-    const int b = blockIdx.x, g = gridDim.x;
-    const long long nt = b < num_tiles ? (num_tiles - 1 - b) / g + 1 : 0;
+    const long long nt = unit < num_tiles ? (num_tiles - 1 - unit) / nunits + 1 : 0;
     return nt * num_kb;
   }
   __device__ __forceinline__ bool next(long long& pos, W8Seg& s) const {
@@ -156,7 +164,7 @@ struct W8Work {
       s.tile = (int)pos;
       s.k0 = 0;
       s.k1 = num_kb;
-      pos += gridDim.x;
+      pos += nunits;
       return true;
     }
     if (pos >= it1) return false;
@@ -166,6 +174,15 @@ struct W8Work {
     s.k1 = k1 < num_kb ? (int)k1 : num_kb;
     pos += s.k1 - s.k0;
     return true;
+  }
+  // Units whose partial accumulators the finalising piece `sg` adds:
+  // [*lo, *hi) (empty unless sg is cut and holds the tile's first K-block).
+  __device__ __forceinline__ void contributors(const W8Seg& sg, int* lo, int* hi) const {
+    *lo = *hi = unit + 1;
+    if (sg.k0 == 0 && sg.k1 < num_kb) {
+      const long long tile_end = (long long)(sg.tile + 1) * num_kb;
+      while (*hi < nunits && share_begin(*hi) < tile_end) ++*hi;
+    }
   }
 };
 
@@ -203,11 +220,190 @@ __device__ __forceinline__ int w8_partial_index(int q, int h, int c, int r, int 
   return (((q * 2 + h) * (kW8BM / 32) + c) * 4 + r) * 32 + lane;
 }
 
+// Epilogue of one piece for epilogue warp q (lane t) of a CTA whose TMEM
+// accumulator at column `acc_tmem` holds weight columns n0 .. n0 + 127 (lane
+// order of w8_tmem.cuh) by activation rows m0 .. m0 + kW8BM - 1. Waits for the
+// accumulator (t_full, phase `parity`). A contributor piece writes the raw
+// accumulator to partial slot `self_slot` and raises that slot's flag; any
+// other piece adds the partials of slots c * slot_mul + slot_add for c in
+// [c_lo, c_hi) (waiting for their flags and clearing them afterwards), then
+// applies the scale and the optional residual and stores C.
+//
+// tcgen05.ld.16x256b gives lane t the TMEM lanes t/4 and t/4 + 8 of a 16-lane
+// group -- weight columns n and n + 1 -- at accumulator columns (activation
+// rows) m, m + 1: each pair (n, n + 1) of one row m is stored as one 4-byte
+// f16x2. Scales are fetched before the accumulator is ready; residual and
+// partial-sum loads are issued ahead of the TMEM reads they pair with, two
+// 32-column chunks at a time. Returns false after a timeout.
+__device__ __forceinline__ bool w8_epilogue_piece(const GemmArgs& args, const FailState& fs,
+                                                  uint64_t* t_full, uint32_t parity,
+                                                  uint32_t acc_tmem, int n0, int m0, int q,
+                                                  int t, bool contributor, int self_slot,
+                                                  int c_lo, int c_hi, int slot_mul,
+                                                  int slot_add) {
+  const int lane = t;
+  float sc[2][2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int n = n0 + 16 * (2 * q + h) + 2 * (t >> 2);
+    sc[h][0] = (!contributor && n < args.N) ? __half2float(args.scale[n]) : 0.0f;
+    sc[h][1] = (!contributor && n + 1 < args.N) ? __half2float(args.scale[n + 1]) : 0.0f;
+  }
+  bool ready = mbar_wait(t_full, parity, fs);
+  for (int c2 = c_lo; c2 < c_hi && ready; ++c2)
+    ready = wait_flag(args.sk_flags + 4 * (c2 * slot_mul + slot_add) + q, fs);
+  if (!__all_sync(0xffffffffu, ready)) return false;
+  tc_fence_after();
+
+  if (contributor) {
+    float4* part = reinterpret_cast<float4*>(args.sk_partials) +
+                   (size_t)self_slot * (kW8PartialFloats / 4);
+#pragma unroll 1
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t taddr = acc_tmem + ((uint32_t)(16 * (2 * q + h)) << 16);
+#pragma unroll 1
+      for (int c = 0; c < kW8BM / 32; c += 2) {
+        uint32_t r[2][16];
+        tmem_ld_16x256b_x4(taddr + 32 * c, r[0]);
+        tmem_ld_16x256b_x4(taddr + 32 * (c + 1), r[1]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+#pragma unroll
+          for (int rep = 0; rep < 4; ++rep)
+            __stcg(part + w8_partial_index(q, h, c + u, rep, t),
+                   make_float4(__uint_as_float(r[u][4 * rep]), __uint_as_float(r[u][4 * rep + 1]),
+                               __uint_as_float(r[u][4 * rep + 2]),
+                               __uint_as_float(r[u][4 * rep + 3])));
+      }
+    }
+    // publish: every lane's stores, then the flag of this quarter
+    __threadfence();
+    __syncwarp();
+    if (lane == 0) st_release_gpu(args.sk_flags + 4 * self_slot + q, 1);
+    return true;
+  }
+  const bool rows_full = m0 + kW8BM <= args.M;
+  const __half* R = reinterpret_cast<const __half*>(args.C_init);
+#pragma unroll 1
+  for (int h = 0; h < 2; ++h) {
+    const int chunk = 2 * q + h;
+    const int n = n0 + 16 * chunk + 2 * (t >> 2);
+    const bool n0_ok = n < args.N, n1_ok = n + 1 < args.N;
+    const bool fast = rows_full && n1_ok;
+    const float s0 = h ? sc[1][0] : sc[0][0], s1 = h ? sc[1][1] : sc[0][1];
+    const uint32_t taddr = acc_tmem + ((uint32_t)(16 * chunk) << 16);
+    // row of (chunk c, rep, j) = row0 + 32 c + 8 rep + j
+    const int row0 = m0 + 2 * (t & 3);
+    __half* cbase = reinterpret_cast<__half*>(args.C) + (long long)row0 * args.ldc + n;
+    const __half* rbase = R ? R + (long long)row0 * args.ldc + n : nullptr;
+#pragma unroll 1
+    for (int c = 0; c < kW8BM / 32; c += 2) {
+      // residual pairs and partial sums of the two chunks, loaded ahead
+      // of the TMEM reads
+      uint32_t res[2][8];
+#pragma unroll
+      for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) res[u][e] = 0u;
+      if (rbase && fast) {
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+#pragma unroll
+          for (int rep = 0; rep < 4; ++rep)
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+              res[u][2 * rep + j] = __ldg(reinterpret_cast<const unsigned int*>(
+                  rbase + (long long)(32 * (c + u) + 8 * rep + j) * args.ldc));
+      }
+      float v[2][16];
+#pragma unroll
+      for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int e = 0; e < 16; ++e) v[u][e] = 0.0f;
+      for (int c2 = c_lo; c2 < c_hi; ++c2) {
+        const float4* part = reinterpret_cast<const float4*>(args.sk_partials) +
+                             (size_t)(c2 * slot_mul + slot_add) * (kW8PartialFloats / 4);
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+#pragma unroll
+          for (int rep = 0; rep < 4; ++rep) {
+            const float4 p = __ldcg(part + w8_partial_index(q, h, c + u, rep, t));
+            v[u][4 * rep] += p.x;
+            v[u][4 * rep + 1] += p.y;
+            v[u][4 * rep + 2] += p.z;
+            v[u][4 * rep + 3] += p.w;
+          }
+      }
+      uint32_t r[2][16];
+      tmem_ld_16x256b_x4(taddr + 32 * c, r[0]);
+      tmem_ld_16x256b_x4(taddr + 32 * (c + 1), r[1]);
+      tmem_wait_ld();
+      // this CTA's accumulator plus the partials (summed in CTA order)
+#pragma unroll
+      for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int e = 0; e < 16; ++e) v[u][e] = __uint_as_float(r[u][e]) + v[u][e];
+      if (fast) {
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+#pragma unroll
+          for (int rep = 0; rep < 4; ++rep)
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              float v0 = v[u][4 * rep + j] * s0;
+              float v1 = v[u][4 * rep + 2 + j] * s1;
+              if (rbase) {
+                const float2 rv = __half22float2(
+                    *reinterpret_cast<const __half2*>(&res[u][2 * rep + j]));
+                v0 += rv.x;
+                v1 += rv.y;
+              }
+              *reinterpret_cast<__half2*>(
+                  cbase + (long long)(32 * (c + u) + 8 * rep + j) * args.ldc) =
+                  __floats2half2_rn(v0, v1);
+            }
+      } else if (n0_ok) {
+        // ragged edge: rows past M, or the last column of an odd N
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+#pragma unroll
+          for (int rep = 0; rep < 4; ++rep)
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              const int dm = 32 * (c + u) + 8 * rep + j;
+              if (row0 + dm >= args.M) continue;
+              const long long off = (long long)dm * args.ldc;
+              float v0 = v[u][4 * rep + j] * s0;
+              float v1 = v[u][4 * rep + 2 + j] * s1;
+              if (n1_ok) {
+                if (rbase) {
+                  const float2 rv =
+                      __half22float2(*reinterpret_cast<const __half2*>(rbase + off));
+                  v0 += rv.x;
+                  v1 += rv.y;
+                }
+                *reinterpret_cast<__half2*>(cbase + off) = __floats2half2_rn(v0, v1);
+              } else {
+                if (rbase) v0 += __half2float(rbase[off]);
+                cbase[off] = __float2half_rn(v0);
+              }
+            }
+      }
+    }
+  }
+  // the partials of this tile are consumed: clear their flags for the next
+  // launch
+  if (lane == 0)
+    for (int c2 = c_lo; c2 < c_hi; ++c2) args.sk_flags[4 * (c2 * slot_mul + slot_add) + q] = 0;
+  return true;
+}
+
 __global__ void __launch_bounds__(kW8Threads, 1)
     gemm_w8_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
                          const __grid_constant__ CUtensorMap tmW, const GemmArgs args) {
   using L = W8Smem;
-  // D[128 n x 192 m] += W^T (TMEM, K-major) . A^T (shared, K-major)
+  // D[128 n x 256 m] += W^T (TMEM, K-major) . A^T (shared, K-major)
   constexpr uint32_t kIdesc = make_idesc_f16(kW8BN, kW8BM, 0, 0);
 
   extern __shared__ uint8_t smem_raw[];
@@ -229,7 +425,7 @@ __global__ void __launch_bounds__(kW8Threads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   W8Work work;
-  work.init(args);
+  work.init(args, blockIdx.x, gridDim.x);
   const FailState fs{abort_flag, args.status};
 
   if (threadIdx.x == 0) {
@@ -297,8 +493,11 @@ __global__ void __launch_bounds__(kW8Threads, 1)
       long long pos = work.first();
       W8Seg sg;
       while (ok && work.next(pos, sg)) {
-        const int acc = tl & 1;
-        if (!mbar_wait(&t_empty[acc], (uint32_t)((tl >> 1) & 1) ^ 1, fs)) { ok = false; break; }
+        const int acc = tl % kW8Acc;
+        if (!mbar_wait(&t_empty[acc], (uint32_t)((tl / kW8Acc) & 1) ^ 1, fs)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + kW8BM * acc;
         for (int kb = sg.k0; kb < sg.k1; ++kb) {
@@ -357,184 +556,20 @@ __global__ void __launch_bounds__(kW8Threads, 1)
     }
   } else if (warp >= 4 + kW8ConvWarps) {
     // ------------------------------------------------------ epilogue
-    // tcgen05.ld.16x256b gives lane t the TMEM lanes t/4 and t/4 + 8 of a
-    // 16-lane group -- weight columns n and n + 1 (see w8_tmem.cuh) -- at
-    // accumulator columns (activation rows) m, m + 1: each pair (n, n + 1) of
-    // one row m is stored as one 4-byte f16x2.
     const int q = warp & 3;
-    const int t = lane;
     int tl = 0;
     long long pos = work.first();
     W8Seg sg;
     while (work.next(pos, sg)) {
       int tm, tn;
       tile_coords(sg.tile, args, tm, tn);
-      const int acc = tl & 1;
-      const bool contributor = sg.k0 > 0;
-      // CTAs whose partial accumulators this (finalising) piece adds
-      int c_lo = blockIdx.x + 1, c_hi = blockIdx.x + 1;
-      if (!contributor && sg.k1 < work.num_kb) {
-        const long long tile_end = (long long)(sg.tile + 1) * work.num_kb;
-        while (c_hi < (int)gridDim.x && work.share_begin(c_hi) < tile_end) ++c_hi;
-      }
-      // scales of this thread's column pairs, fetched while the MMAs run
-      float sc[2][2];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int n = tn * kW8BN + 16 * (2 * q + h) + 2 * (t >> 2);
-        sc[h][0] = (!contributor && n < args.N) ? __half2float(args.scale[n]) : 0.0f;
-        sc[h][1] = (!contributor && n + 1 < args.N) ? __half2float(args.scale[n + 1]) : 0.0f;
-      }
-      bool ready = mbar_wait(&t_full[acc], (uint32_t)((tl >> 1) & 1), fs);
-      for (int c2 = c_lo; c2 < c_hi && ready; ++c2)
-        ready = wait_flag(args.sk_flags + 4 * c2 + q, fs);
-      if (!__all_sync(0xffffffffu, ready)) break;
-      tc_fence_after();
-      const int m0 = tm * kW8BM;
-
-      if (contributor) {
-        float4* part = reinterpret_cast<float4*>(args.sk_partials) +
-                       (size_t)blockIdx.x * (kW8PartialFloats / 4);
-#pragma unroll 1
-        for (int h = 0; h < 2; ++h) {
-          const uint32_t taddr =
-              tmem_base + ((uint32_t)(16 * (2 * q + h)) << 16) + kW8BM * acc;
-#pragma unroll 1
-          for (int c = 0; c < kW8BM / 32; c += 2) {
-            uint32_t r[2][16];
-            tmem_ld_16x256b_x4(taddr + 32 * c, r[0]);
-            tmem_ld_16x256b_x4(taddr + 32 * (c + 1), r[1]);
-            tmem_wait_ld();
-#pragma unroll
-            for (int u = 0; u < 2; ++u)
-#pragma unroll
-              for (int rep = 0; rep < 4; ++rep)
-                __stcg(part + w8_partial_index(q, h, c + u, rep, t),
-                       make_float4(__uint_as_float(r[u][4 * rep]),
-                                   __uint_as_float(r[u][4 * rep + 1]),
-                                   __uint_as_float(r[u][4 * rep + 2]),
-                                   __uint_as_float(r[u][4 * rep + 3])));
-          }
-        }
-        // publish: every lane's stores, then the flag of this quarter
-        __threadfence();
-        __syncwarp();
-        if (lane == 0) st_release_gpu(args.sk_flags + 4 * blockIdx.x + q, 1);
-      } else {
-        const bool rows_full = m0 + kW8BM <= args.M;
-        const __half* R = reinterpret_cast<const __half*>(args.C_init);
-#pragma unroll 1
-        for (int h = 0; h < 2; ++h) {
-          const int chunk = 2 * q + h;
-          const int n = tn * kW8BN + 16 * chunk + 2 * (t >> 2);
-          const bool n0_ok = n < args.N, n1_ok = n + 1 < args.N;
-          const bool fast = rows_full && n1_ok;
-          const float s0 = h ? sc[1][0] : sc[0][0], s1 = h ? sc[1][1] : sc[0][1];
-          const uint32_t taddr = tmem_base + ((uint32_t)(16 * chunk) << 16) + kW8BM * acc;
-          // row of (chunk c, rep, j) = row0 + 32 c + 8 rep + j
-          const int row0 = m0 + 2 * (t & 3);
-          __half* cbase = reinterpret_cast<__half*>(args.C) + (long long)row0 * args.ldc + n;
-          const __half* rbase = R ? R + (long long)row0 * args.ldc + n : nullptr;
-#pragma unroll 1
-          for (int c = 0; c < kW8BM / 32; c += 2) {
-            // residual pairs and partial sums of the two chunks, loaded ahead
-            // of the TMEM reads
-            uint32_t res[2][8];
-#pragma unroll
-            for (int u = 0; u < 2; ++u)
-#pragma unroll
-              for (int e = 0; e < 8; ++e) res[u][e] = 0u;
-            if (rbase && fast) {
-#pragma unroll
-              for (int u = 0; u < 2; ++u)
-#pragma unroll
-                for (int rep = 0; rep < 4; ++rep)
-#pragma unroll
-                  for (int j = 0; j < 2; ++j)
-                    res[u][2 * rep + j] = __ldg(reinterpret_cast<const unsigned int*>(
-                        rbase + (long long)(32 * (c + u) + 8 * rep + j) * args.ldc));
-            }
-            float v[2][16];
-#pragma unroll
-            for (int u = 0; u < 2; ++u)
-#pragma unroll
-              for (int e = 0; e < 16; ++e) v[u][e] = 0.0f;
-            for (int c2 = c_lo; c2 < c_hi; ++c2) {
-              const float4* part = reinterpret_cast<const float4*>(args.sk_partials) +
-                                   (size_t)c2 * (kW8PartialFloats / 4);
-#pragma unroll
-              for (int u = 0; u < 2; ++u)
-#pragma unroll
-                for (int rep = 0; rep < 4; ++rep) {
-                  const float4 p = __ldcg(part + w8_partial_index(q, h, c + u, rep, t));
-                  v[u][4 * rep] += p.x;
-                  v[u][4 * rep + 1] += p.y;
-                  v[u][4 * rep + 2] += p.z;
-                  v[u][4 * rep + 3] += p.w;
-                }
-            }
-            uint32_t r[2][16];
-            tmem_ld_16x256b_x4(taddr + 32 * c, r[0]);
-            tmem_ld_16x256b_x4(taddr + 32 * (c + 1), r[1]);
-            tmem_wait_ld();
-            // this CTA's accumulator plus the partials (summed in CTA order)
-#pragma unroll
-            for (int u = 0; u < 2; ++u)
-#pragma unroll
-              for (int e = 0; e < 16; ++e) v[u][e] = __uint_as_float(r[u][e]) + v[u][e];
-            if (fast) {
-#pragma unroll
-              for (int u = 0; u < 2; ++u)
-#pragma unroll
-                for (int rep = 0; rep < 4; ++rep)
-#pragma unroll
-                  for (int j = 0; j < 2; ++j) {
-                    float v0 = v[u][4 * rep + j] * s0;
-                    float v1 = v[u][4 * rep + 2 + j] * s1;
-                    if (rbase) {
-                      const float2 rv = __half22float2(
-                          *reinterpret_cast<const __half2*>(&res[u][2 * rep + j]));
-                      v0 += rv.x;
-                      v1 += rv.y;
-                    }
-                    *reinterpret_cast<__half2*>(
-                        cbase + (long long)(32 * (c + u) + 8 * rep + j) * args.ldc) =
-                        __floats2half2_rn(v0, v1);
-                  }
-            } else if (n0_ok) {
-              // ragged edge: rows past M, or the last column of an odd N
-#pragma unroll
-              for (int u = 0; u < 2; ++u)
-#pragma unroll
-                for (int rep = 0; rep < 4; ++rep)
-#pragma unroll
-                  for (int j = 0; j < 2; ++j) {
-                    const int dm = 32 * (c + u) + 8 * rep + j;
-                    if (row0 + dm >= args.M) continue;
-                    const long long off = (long long)dm * args.ldc;
-                    float v0 = v[u][4 * rep + j] * s0;
-                    float v1 = v[u][4 * rep + 2 + j] * s1;
-                    if (n1_ok) {
-                      if (rbase) {
-                        const float2 rv =
-                            __half22float2(*reinterpret_cast<const __half2*>(rbase + off));
-                        v0 += rv.x;
-                        v1 += rv.y;
-                      }
-                      *reinterpret_cast<__half2*>(cbase + off) = __floats2half2_rn(v0, v1);
-                    } else {
-                      if (rbase) v0 += __half2float(rbase[off]);
-                      cbase[off] = __float2half_rn(v0);
-                    }
-                  }
-            }
-          }
-        }
-        // the partials of this tile are consumed: clear their flags for the
-        // next launch
-        if (lane == 0)
-          for (int c2 = c_lo; c2 < c_hi; ++c2) args.sk_flags[4 * c2 + q] = 0;
-      }
+      const int acc = tl % kW8Acc;
+      int c_lo, c_hi;
+      work.contributors(sg, &c_lo, &c_hi);
+      if (!w8_epilogue_piece(args, fs, &t_full[acc], (uint32_t)((tl / kW8Acc) & 1),
+                             tmem_base + kW8BM * acc, tn * kW8BN, tm * kW8BM, q, lane,
+                             sg.k0 > 0, blockIdx.x, c_lo, c_hi, 1, 0))
+        break;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&t_empty[acc]);

@@ -324,4 +324,5 @@ __device__ __forceinline__ uint32_t pack_half2(float x, float y) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+
 }  // namespace hxb

@@ -23,7 +23,9 @@ def _inputs(M, K, N, seed=0):
 
 @pytest.mark.parametrize("M,K,N", [(256, 4096, 11008), (1, 4096, 11008), (16, 4096, 11008),
                                    (200, 320, 528), (5, 64, 48), (129, 1000, 272),
-                                   (16, 200, 4112), (3, 4104, 96)])
+                                   (16, 200, 4112), (3, 4104, 96),
+                                   # N <= 128: the one-CTA kernel (one weight block)
+                                   (300, 512, 128), (40, 2048, 112)])
 def test_w8a16_vs_oracle(cuda_pkg, oracle, M, K, N):
     a, w, s = _inputs(M, K, N, seed=M + N)
     c = cuda_pkg.matmul_w8a16(torch.from_numpy(a).to(DEV), torch.from_numpy(w).to(DEV),
