@@ -285,6 +285,15 @@ hxb_status_t gemm_w8_impl(const void* A, int64_t lda, const void* W,
                                CU_TENSOR_MAP_SWIZZLE_128B)) != HXB_OK)
       return s;
   }
+  CUtensorMap tmC;
+  {
+    const uint64_t dims[2] = {(uint64_t)N, (uint64_t)M};
+    const uint64_t strides[1] = {(uint64_t)ldc * 2};
+    const uint32_t box[2] = {64, (uint32_t)kW8BM};
+    if ((s = encode_tensor_map(&tmC, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, C, dims, strides, box,
+                               CU_TENSOR_MAP_SWIZZLE_128B)) != HXB_OK)
+      return s;
+  }
   GemmArgs args{};
   args.M = (int)M;
   args.N = (int)N;
@@ -323,7 +332,7 @@ hxb_status_t gemm_w8_impl(const void* A, int64_t lda, const void* W,
     if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(gemm_w8)");
     configured[dev->ordinal] = true;
   }
-  gemm_w8_sm100_kernel<<<grid, kW8Threads, W8Smem::kAlloc, stream>>>(tmA, tmW, args);
+  gemm_w8_sm100_kernel<<<grid, kW8Threads, W8Smem::kAlloc, stream>>>(tmA, tmW, tmC, args);
   return cuda_status(cudaGetLastError(), "gemm_w8 launch");
 }
 

@@ -37,9 +37,9 @@ namespace hxb {
 constexpr int kGemvRows = 16;           // largest M served by this kernel
 constexpr int kGemvSub = 3;             // 32-column sub-tiles per CTA
 constexpr int kGemvBN = 32 * kGemvSub;  // weight columns per CTA
-constexpr int kGemvWarps = 8;           // warps per CTA, each a slice of K
+constexpr int kGemvWarps = 12;          // warps per CTA, each a slice of K
 constexpr int kGemvSlotRows = 32;       // K rows per ring slot (two 16-row MMA groups)
-constexpr int kGemvStages = 6;          // ring slots per warp
+constexpr int kGemvStages = 4;          // ring slots per warp
 constexpr int kGemvThreads = kGemvWarps * 32;
 
 struct GemvSmem {
