@@ -8,10 +8,10 @@ identifier it is imported as `iree_hexagon_plugins_b200` through
 """
 from . import _native
 from ._native import HxbError
-from . import sharded
+from . import hal, sharded
 from .dispatch import (DecoderBlockW8, attention, attention_bshd, device_status, matmul,
                        matmul_w8a16, rmsnorm, rope_, swiglu, w8a16_workspace)
 
-__all__ = ["sharded", "HxbError", "DecoderBlockW8", "attention", "attention_bshd", "device_status",
+__all__ = ["hal", "sharded", "HxbError", "DecoderBlockW8", "attention", "attention_bshd", "device_status",
            "matmul", "matmul_w8a16", "rmsnorm", "rope_", "swiglu", "w8a16_workspace",
            "_native"]

@@ -15,6 +15,7 @@ c_i64 = ctypes.c_int64
 c_int = ctypes.c_int
 c_vp = ctypes.c_void_p
 c_size = ctypes.c_size_t
+c_u64 = ctypes.c_uint64
 c_float = ctypes.c_float
 
 # name -> (restype, argtypes). Kept 1:1 with include/*.h; a test checks that
@@ -57,7 +58,92 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "hxb_decoder_block_workspace_bytes": (c_size, [c_vp, c_i64, c_i64]),
     "hxb_decoder_block_w8a16": (c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp,
                                         c_size, c_vp]),
+    # include/hxb200_hal.h: executable library
+    "hxb_executable_library_query": (c_vp, [ctypes.c_uint32, c_vp]),
+    # include/hxb200_hal.h: HAL runtime
+    "hxb_hal_device_options_initialize": (None, [c_vp]),
+    "hxb_hal_driver_options_initialize": (None, [c_vp]),
+    "hxb_hal_driver_create": (c_int, [ctypes.c_char_p, c_vp, ctypes.POINTER(c_vp)]),
+    "hxb_hal_driver_query_device_count": (c_int, [c_vp, ctypes.POINTER(ctypes.c_int32)]),
+    "hxb_hal_driver_release": (None, [c_vp]),
+    "hxb_hal_device_create": (c_int, [c_vp, ctypes.c_char_p, c_vp, ctypes.POINTER(c_vp)]),
+    "hxb_hal_device_release": (None, [c_vp]),
+    "hxb_hal_device_queue_stream": (c_vp, [c_vp]),
+    "hxb_hal_buffer_allocate": (c_int, [c_vp, c_u64, ctypes.POINTER(c_vp)]),
+    "hxb_hal_buffer_device_pointer": (c_vp, [c_vp]),
+    "hxb_hal_buffer_byte_length": (c_u64, [c_vp]),
+    "hxb_hal_buffer_write": (c_int, [c_vp, c_u64, c_vp, c_u64]),
+    "hxb_hal_buffer_read": (c_int, [c_vp, c_u64, c_vp, c_u64]),
+    "hxb_hal_buffer_release": (None, [c_vp]),
+    "hxb_hal_semaphore_create": (c_int, [c_vp, c_u64, ctypes.POINTER(c_vp)]),
+    "hxb_hal_semaphore_query": (c_int, [c_vp, ctypes.POINTER(c_u64)]),
+    "hxb_hal_semaphore_signal": (c_int, [c_vp, c_u64]),
+    "hxb_hal_semaphore_wait": (c_int, [c_vp, c_u64, c_u64]),
+    "hxb_hal_semaphore_release": (None, [c_vp]),
+    "hxb_hal_command_buffer_create": (c_int, [c_vp, ctypes.POINTER(c_vp)]),
+    "hxb_hal_command_buffer_begin": (c_int, [c_vp]),
+    "hxb_hal_command_buffer_dispatch": (c_int, [c_vp, ctypes.c_uint32,
+                                                ctypes.POINTER(ctypes.c_uint32), ctypes.c_uint32,
+                                                c_vp, ctypes.c_uint32]),
+    "hxb_hal_command_buffer_end": (c_int, [c_vp]),
+    "hxb_hal_command_buffer_release": (None, [c_vp]),
+    "hxb_hal_device_queue_execute": (c_int, [c_vp, c_vp, c_u64, c_vp, c_vp, c_u64]),
 }
+
+
+# ----------------------------------------------- include/hxb200_hal.h structs
+
+EXECUTABLE_LIBRARY_VERSION_1 = 0x48420001
+
+
+class ExecutableEnvironment(ctypes.Structure):
+    _fields_ = [("constants", c_vp), ("stream", c_vp), ("scratch", c_vp),
+                ("scratch_bytes", c_u64)]
+
+
+class DispatchState(ctypes.Structure):
+    _fields_ = [("workgroup_size_x", ctypes.c_uint32), ("workgroup_size_y", ctypes.c_uint32),
+                ("workgroup_size_z", ctypes.c_uint16), ("workgroup_count_x", ctypes.c_uint32),
+                ("workgroup_count_y", ctypes.c_uint32), ("workgroup_count_z", ctypes.c_uint16),
+                ("binding_count", ctypes.c_uint8), ("constants", c_vp),
+                ("binding_ptrs", c_vp), ("binding_lengths", c_vp), ("reserved", c_vp)]
+
+
+DispatchFn = ctypes.CFUNCTYPE(c_int, c_vp, c_vp, c_vp)
+
+
+class DispatchAttrs(ctypes.Structure):
+    _fields_ = [("flags", c_u64), ("smem_bytes", c_u64), ("threads", c_u64)]
+
+
+class ExportTable(ctypes.Structure):
+    _fields_ = [("count", ctypes.c_uint32), ("ptrs", c_vp), ("attrs", ctypes.POINTER(DispatchAttrs)),
+                ("names", ctypes.POINTER(ctypes.c_char_p))]
+
+
+class ImportTable(ctypes.Structure):
+    _fields_ = [("count", ctypes.c_uint32), ("symbols", c_vp)]
+
+
+class LibraryHeader(ctypes.Structure):
+    _fields_ = [("version", ctypes.c_uint32)]
+
+
+class ExecutableLibrary(ctypes.Structure):
+    _fields_ = [("header", ctypes.POINTER(LibraryHeader)), ("imports", ImportTable),
+                ("exports", ExportTable)]
+
+
+class DeviceOptions(ctypes.Structure):
+    _fields_ = [("ordinal", ctypes.c_int32), ("scratch_bytes", c_u64)]
+
+
+class DriverOptions(ctypes.Structure):
+    _fields_ = [("default_device_options", DeviceOptions)]
+
+
+class BufferRef(ctypes.Structure):
+    _fields_ = [("buffer", c_vp), ("offset", c_u64), ("length", c_u64)]
 
 
 class DecoderW8(ctypes.Structure):

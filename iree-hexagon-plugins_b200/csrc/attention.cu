@@ -420,6 +420,11 @@ hxb_status_t make_rows_map(CUtensorMap* m, const void* base, int64_t rows, int64
 
 }  // namespace
 
+// Dynamic shared memory (bytes) and threads per CTA of the attention kernel
+// (the executable library's export attributes).
+size_t attention_smem_bytes() { return AttSmem::kAlloc; }
+int attention_threads() { return kAttThreads; }
+
 // Shared launcher: B batches x H heads; hpr heads per matrix row (see AttArgs).
 hxb_status_t attention_launch(const void* Q, int64_t ldq, const void* K, int64_t ldk,
                               const void* V, int64_t ldv, void* O, int64_t ldo, int64_t B,

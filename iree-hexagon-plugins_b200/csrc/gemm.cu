@@ -240,6 +240,21 @@ hxb_status_t gemv_w8_impl(const void* A, int64_t lda, const void* W, int64_t ldw
   return M <= 8 ? launch_gemv<8>(*dev, p, stream) : launch_gemv<16>(*dev, p, stream);
 }
 
+// Largest dynamic shared memory (bytes) and threads per CTA of the f16 GEMM
+// and the int8-weight matmul kernels (the executable library's export
+// attributes).
+size_t gemm_f16_max_smem_bytes() {
+  size_t m = GemmSmem<256, 4, kBF16RowMajorKN>::kAlloc;
+  if (GemmSmem<128, 6, kBF16RowMajorKN>::kAlloc > m) m = GemmSmem<128, 6, kBF16RowMajorKN>::kAlloc;
+  if (GemmSmem<64, 8, kBF16RowMajorKN>::kAlloc > m) m = GemmSmem<64, 8, kBF16RowMajorKN>::kAlloc;
+  return m;
+}
+int gemm_f16_threads() { return GemmShape<256, kBF16RowMajorKN>::kThreads; }
+size_t w8_max_smem_bytes() {
+  return W8Smem::kAlloc > GemvSmem::kBytes ? (size_t)W8Smem::kAlloc : (size_t)GemvSmem::kBytes;
+}
+int w8_threads() { return kW8Threads; }
+
 // Stream-K workspace of the int8-weight GEMM for `ctas` CTAs: flags, then one
 // f32 partial accumulator per CTA.
 size_t w8_streamk_workspace_bytes(int ctas) {

@@ -1,0 +1,186 @@
+"""Python mirror of the executable-library and HAL-runtime ABI
+(include/hxb200_hal.h), the shapes of the reference's runtime plugin
+(plugins/runtime/hexagon/api.h:55-114; dsp/rt/executable_library.h:40-250):
+a driver creates devices, a device owns buffers, timeline semaphores and
+command buffers of dispatches of the library's exports, and queue execution
+orders them.
+
+Every call goes to libhxb200.so; errors raise HxbError with the library's
+message.
+"""
+from __future__ import annotations
+
+import ctypes
+import struct
+
+from . import _native
+from ._native import check
+
+EXPORTS = {"matmul_f16": 0, "matmul_w8a16": 1, "attention_f16": 2, "decoder_block_w8a16": 3}
+
+
+def f32_bits(x: float) -> int:
+    """A float as the u32 push constant the exports read."""
+    return struct.unpack("<I", struct.pack("<f", float(x)))[0]
+
+
+def library(version: int = _native.EXECUTABLE_LIBRARY_VERSION_1) -> dict | None:
+    """The executable library's header and export table, or None when
+    `version` is not the one it was built with."""
+    lib = _native.load()
+    p = lib.hxb_executable_library_query(version, None)
+    if not p:
+        return None
+    libs = ctypes.cast(p, ctypes.POINTER(_native.ExecutableLibrary)).contents
+    ex = libs.exports
+    exports = []
+    for i in range(ex.count):
+        a = ex.attrs[i]
+        exports.append({"name": ex.names[i].decode(), "flags": a.flags,
+                        "smem_bytes": a.smem_bytes, "threads": a.threads})
+    return {"version": libs.header.contents.version, "imports": libs.imports.count,
+            "exports": exports}
+
+
+class Driver:
+    def __init__(self, identifier: str = "b200"):
+        self._lib = _native.load()
+        h = ctypes.c_void_p()
+        check(self._lib.hxb_hal_driver_create(identifier.encode(), None, ctypes.byref(h)))
+        self.handle = h
+
+    def device_count(self) -> int:
+        n = ctypes.c_int32()
+        check(self._lib.hxb_hal_driver_query_device_count(self.handle, ctypes.byref(n)))
+        return n.value
+
+    def create_device(self, ordinal: int = 0, scratch_bytes: int = 0) -> "Device":
+        return Device(self, ordinal, scratch_bytes)
+
+    def close(self) -> None:
+        if self.handle:
+            self._lib.hxb_hal_driver_release(self.handle)
+            self.handle = None
+
+
+class Device:
+    def __init__(self, driver: Driver, ordinal: int, scratch_bytes: int):
+        self._lib = driver._lib
+        o = _native.DeviceOptions(ordinal, scratch_bytes)
+        h = ctypes.c_void_p()
+        check(self._lib.hxb_hal_device_create(driver.handle, b"b200", ctypes.byref(o),
+                                              ctypes.byref(h)))
+        self.handle = h
+
+    @property
+    def stream(self) -> int:
+        return self._lib.hxb_hal_device_queue_stream(self.handle) or 0
+
+    def allocate(self, nbytes: int) -> "Buffer":
+        return Buffer(self, nbytes)
+
+    def semaphore(self, initial: int = 0) -> "Semaphore":
+        return Semaphore(self, initial)
+
+    def command_buffer(self) -> "CommandBuffer":
+        return CommandBuffer(self)
+
+    def execute(self, command_buffer: "CommandBuffer | None", wait=None, signal=None) -> None:
+        """Queue `command_buffer` after `wait` = (semaphore, value) is reached;
+        then set `signal` = (semaphore, value). Does not block."""
+        ws, wv = (wait[0].handle, wait[1]) if wait else (None, 0)
+        ss, sv = (signal[0].handle, signal[1]) if signal else (None, 0)
+        check(self._lib.hxb_hal_device_queue_execute(
+            self.handle, ws, wv, command_buffer.handle if command_buffer else None, ss, sv))
+
+    def close(self) -> None:
+        if self.handle:
+            self._lib.hxb_hal_device_release(self.handle)
+            self.handle = None
+
+
+class Buffer:
+    def __init__(self, device: Device, nbytes: int):
+        self._lib = device._lib
+        h = ctypes.c_void_p()
+        check(self._lib.hxb_hal_buffer_allocate(device.handle, nbytes, ctypes.byref(h)))
+        self.handle = h
+        self.nbytes = nbytes
+
+    @property
+    def device_pointer(self) -> int:
+        return self._lib.hxb_hal_buffer_device_pointer(self.handle) or 0
+
+    def write(self, data, offset: int = 0) -> None:
+        """Copies a host buffer (bytes or a contiguous numpy array) in."""
+        mv = memoryview(data).cast("B")
+        buf = (ctypes.c_char * len(mv)).from_buffer_copy(mv)
+        check(self._lib.hxb_hal_buffer_write(self.handle, offset, buf, len(mv)))
+
+    def read(self, nbytes: int | None = None, offset: int = 0) -> bytes:
+        n = self.nbytes - offset if nbytes is None else nbytes
+        buf = (ctypes.c_char * n)()
+        check(self._lib.hxb_hal_buffer_read(self.handle, offset, buf, n))
+        return bytes(buf)
+
+    def ref(self, offset: int = 0, length: int | None = None) -> _native.BufferRef:
+        return _native.BufferRef(self.handle, offset,
+                                 self.nbytes - offset if length is None else length)
+
+    def close(self) -> None:
+        if self.handle:
+            self._lib.hxb_hal_buffer_release(self.handle)
+            self.handle = None
+
+
+class Semaphore:
+    def __init__(self, device: Device, initial: int):
+        self._lib = device._lib
+        h = ctypes.c_void_p()
+        check(self._lib.hxb_hal_semaphore_create(device.handle, initial, ctypes.byref(h)))
+        self.handle = h
+
+    @property
+    def value(self) -> int:
+        v = ctypes.c_uint64()
+        check(self._lib.hxb_hal_semaphore_query(self.handle, ctypes.byref(v)))
+        return v.value
+
+    def signal(self, value: int) -> None:
+        check(self._lib.hxb_hal_semaphore_signal(self.handle, value))
+
+    def wait(self, value: int, timeout_s: float = 10.0) -> None:
+        check(self._lib.hxb_hal_semaphore_wait(self.handle, value, int(timeout_s * 1e9)))
+
+    def close(self) -> None:
+        if self.handle:
+            self._lib.hxb_hal_semaphore_release(self.handle)
+            self.handle = None
+
+
+class CommandBuffer:
+    def __init__(self, device: Device):
+        self._lib = device._lib
+        h = ctypes.c_void_p()
+        check(self._lib.hxb_hal_command_buffer_create(device.handle, ctypes.byref(h)))
+        self.handle = h
+
+    def begin(self) -> None:
+        check(self._lib.hxb_hal_command_buffer_begin(self.handle))
+
+    def dispatch(self, export: str | int, constants, bindings) -> None:
+        """Records one dispatch: `bindings` are Buffers or BufferRefs."""
+        ordinal = EXPORTS[export] if isinstance(export, str) else int(export)
+        c = (ctypes.c_uint32 * max(1, len(constants)))(*[int(x) & 0xFFFFFFFF for x in constants])
+        refs = [b.ref() if isinstance(b, Buffer) else b for b in bindings]
+        arr = (_native.BufferRef * max(1, len(refs)))(*refs)
+        check(self._lib.hxb_hal_command_buffer_dispatch(self.handle, ordinal, c, len(constants),
+                                                        arr, len(refs)))
+
+    def end(self) -> None:
+        check(self._lib.hxb_hal_command_buffer_end(self.handle))
+
+    def close(self) -> None:
+        if self.handle:
+            self._lib.hxb_hal_command_buffer_release(self.handle)
+            self.handle = None

@@ -1,0 +1,187 @@
+"""The HAL-shaped runtime on the GPU: a command buffer of the executable
+library's dispatches, recorded once and replayed, ordered by timeline
+semaphores, gives the same bits as the direct C-ABI calls of the same
+kernels (and the oracle's values)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from _support import baseline_check
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+@pytest.fixture()
+def device(cuda_pkg):
+    drv = cuda_pkg.hal.Driver()
+    assert drv.device_count() >= 1
+    dev = drv.create_device(0)
+    yield dev
+    dev.close()
+    drv.close()
+
+
+def _upload(dev, arr: np.ndarray):
+    b = dev.allocate(arr.nbytes)
+    b.write(np.ascontiguousarray(arr))
+    return b
+
+
+def test_command_buffer_matches_direct_calls(cuda_pkg, oracle, device):
+    hal = cuda_pkg.hal
+    rng = np.random.default_rng(11)
+    # f16 matmul with a DPS init (f32 out), 320 x 256 x 192
+    M, N, K = 320, 256, 192
+    a = (rng.random((M, K)) * 2 - 1).astype(np.float16)
+    b = (rng.random((K, N)) * 2 - 1).astype(np.float16)
+    init = rng.standard_normal((M, N)).astype(np.float32)
+    # int8-weight matmul at a decoder shape (stream-K through the device scratch)
+    M8, K8, N8 = 512, 4096, 4096
+    x8 = rng.standard_normal((M8, K8)).astype(np.float16)
+    w8 = rng.integers(-127, 128, (K8, N8), dtype=np.int8)
+    s8 = rng.uniform(0.001, 0.02, N8).astype(np.float16)
+    # attention [2 heads, 256 queries, 384 keys, 128], causal
+    BH, Sq, Skv = 2, 256, 384
+    q = rng.standard_normal((BH, Sq, 128)).astype(np.float16)
+    k = rng.standard_normal((BH, Skv, 128)).astype(np.float16)
+    v = rng.standard_normal((BH, Skv, 128)).astype(np.float16)
+
+    bufs = {n: _upload(device, x) for n, x in
+            [("a", a), ("b", b), ("init", init), ("x8", x8), ("w8", w8), ("s8", s8),
+             ("q", q), ("k", k), ("v", v)]}
+    c = device.allocate(M * N * 4)
+    c8 = device.allocate(M8 * N8 * 2)
+    o = device.allocate(BH * Sq * 128 * 2)
+
+    cb = device.command_buffer()
+    cb.begin()
+    cb.dispatch("matmul_f16", [M, N, K, 2], [bufs["a"], bufs["b"], c, bufs["init"]])
+    cb.dispatch("matmul_w8a16", [M8, N8, K8], [bufs["x8"], bufs["w8"], bufs["s8"], c8])
+    cb.dispatch("attention_f16", [BH, Sq, Skv, 128, 1, 0], [bufs["q"], bufs["k"], bufs["v"], o])
+    cb.end()
+
+    done = device.semaphore(0)
+    device.execute(cb, signal=(done, 1))
+    done.wait(1)
+    got_c = np.frombuffer(c.read(), np.float32).reshape(M, N)
+    got_c8 = np.frombuffer(c8.read(), np.float16).reshape(M8, N8)
+    got_o = np.frombuffer(o.read(), np.float16).reshape(BH, Sq, 128)
+
+    # the same kernels through the direct calls give the same bits
+    t = lambda x: torch.from_numpy(x).to(DEV)
+    want_c = cuda_pkg.matmul(t(a), t(b), out_dtype=torch.float32, init=t(init))
+    want_c8 = cuda_pkg.matmul_w8a16(t(x8), t(w8), t(s8), workspace=cuda_pkg.w8a16_workspace(DEV))
+    want_o = cuda_pkg.attention(t(q), t(k), t(v), causal=True)
+    torch.cuda.synchronize()
+    assert np.array_equal(got_c, want_c.cpu().numpy())
+    assert np.array_equal(got_c8, want_c8.cpu().numpy())
+    assert np.array_equal(got_o, want_o.cpu().numpy())
+    # and the oracle's values
+    baseline_check(oracle.matmul_f32(a, b, init=init), got_c, "hal matmul_f16")
+    rows = np.array([0, 1, 255, 256, 511])
+    baseline_check(oracle.matmul_w8a16_f32(x8[rows], w8, s8), got_c8[rows].astype(np.float32),
+                   "hal matmul_w8a16")
+
+    # replay: the captured graph runs again, ordered by the semaphore
+    c8.write(np.zeros(M8 * N8, np.float16))
+    device.execute(cb, wait=(done, 1), signal=(done, 2))
+    done.wait(2)
+    assert np.array_equal(np.frombuffer(c8.read(), np.float16).reshape(M8, N8), got_c8)
+    assert cuda_pkg.device_status() == 0
+    cb.close()
+    done.close()
+    for buf in list(bufs.values()) + [c, c8, o]:
+        buf.close()
+
+
+def test_queue_waits_for_host_signal(cuda_pkg, device):
+    """A submission whose wait value the host has not signalled yet does not
+    run until the host signals it."""
+    rng = np.random.default_rng(12)
+    M = N = K = 256
+    a = (rng.random((M, K)) * 2 - 1).astype(np.float16)
+    b = (rng.random((K, N)) * 2 - 1).astype(np.float16)
+    ab, bb = _upload(device, a), _upload(device, b)
+    c = device.allocate(M * N * 2)
+    c.write(np.zeros(M * N, np.float16))
+    cb = device.command_buffer()
+    cb.begin()
+    cb.dispatch("matmul_f16", [M, N, K, 0], [ab, bb, c])
+    cb.end()
+    go, done = device.semaphore(0), device.semaphore(0)
+    device.execute(cb, wait=(go, 5), signal=(done, 1))
+    with pytest.raises(cuda_pkg.HxbError, match="not reached"):
+        done.wait(1, timeout_s=0.2)
+    assert done.value == 0
+    go.signal(5)
+    done.wait(1, timeout_s=10)
+    want = cuda_pkg.matmul(torch.from_numpy(a).to(DEV), torch.from_numpy(b).to(DEV))
+    torch.cuda.synchronize()
+    assert np.array_equal(np.frombuffer(c.read(), np.float16).reshape(M, N),
+                          want.cpu().numpy())
+    # a host signal below the current value is refused
+    with pytest.raises(cuda_pkg.HxbError, match="below"):
+        go.signal(4)
+    for o in (cb, go, done, ab, bb, c):
+        o.close()
+
+
+def test_decoder_block_dispatch(cuda_pkg, device):
+    hal = cuda_pkg.hal
+    H, NH, F, S = 1024, 8, 2816, 64
+    rng = np.random.default_rng(13)
+    w = {
+        "attn_norm": np.ones(H, np.float16), "ffn_norm": np.ones(H, np.float16),
+        "w_qkv": rng.integers(-127, 128, (H, 3 * H), dtype=np.int8),
+        "s_qkv": rng.uniform(1.5e-4, 4e-4, 3 * H).astype(np.float16),
+        "w_o": rng.integers(-127, 128, (H, H), dtype=np.int8),
+        "s_o": rng.uniform(1.5e-4, 4e-4, H).astype(np.float16),
+        "w_gate_up": rng.integers(-127, 128, (H, 2 * F), dtype=np.int8),
+        "s_gate_up": rng.uniform(1.5e-4, 4e-4, 2 * F).astype(np.float16),
+        "w_down": rng.integers(-127, 128, (F, H), dtype=np.int8),
+        "s_down": rng.uniform(1.5e-4, 4e-4, H).astype(np.float16),
+    }
+    x = rng.standard_normal((S, H)).astype(np.float16)
+    t = {n: torch.from_numpy(v).to(DEV) for n, v in w.items()}
+    blk = cuda_pkg.DecoderBlockW8(heads=NH, **t)
+    want = blk(torch.from_numpy(x).to(DEV))
+    torch.cuda.synchronize()
+    ws_bytes = blk.workspace_bytes(1, S)
+    order = ["attn_norm", "w_qkv", "s_qkv", "w_o", "s_o", "ffn_norm", "w_gate_up", "s_gate_up",
+             "w_down", "s_down"]
+    xb = _upload(device, x)
+    out = device.allocate(S * H * 2)
+    wb = [_upload(device, w[n]) for n in order]
+    ws = device.allocate(ws_bytes)
+    cb = device.command_buffer()
+    cb.begin()
+    cb.dispatch("decoder_block_w8a16",
+                [1, S, 0, H, NH, 128, F, hal.f32_bits(1e-5), hal.f32_bits(1e4)],
+                [xb, out] + wb + [ws])
+    cb.end()
+    done = device.semaphore(0)
+    device.execute(cb, signal=(done, 1))
+    done.wait(1)
+    got = np.frombuffer(out.read(), np.float16).reshape(S, H)
+    assert np.array_equal(got, want.cpu().numpy())
+    for o in [cb, done, xb, out, ws] + wb:
+        o.close()
+
+
+def test_end_reports_bad_dispatch(cuda_pkg, device):
+    a = device.allocate(64 * 64 * 2)
+    cb = device.command_buffer()
+    cb.begin()
+    # C binding too short for 64 x 64 f16
+    cb.dispatch("matmul_f16", [64, 64, 64, 0], [a, a, a.ref(0, 1024)])
+    with pytest.raises(cuda_pkg.HxbError, match="needs 8192"):
+        cb.end()
+    # the command buffer can be recorded again after the failure
+    cb.begin()
+    cb.dispatch("matmul_f16", [64, 64, 64, 0], [a, a, a])
+    cb.end()
+    cb.close()
+    a.close()
