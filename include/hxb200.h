@@ -186,7 +186,7 @@ hxb_status_t hxb_matmul_w8a16_streamk(const void* A, int64_t lda, const void* W,
  * fully-masked-row rule (rows whose scores are all -inf produce 0,
  * :86-103).
  *   Q [BH, Sq, D], K/V [BH, Skv, D], O [BH, Sq, D], all contiguous f16.
- * D must be 128. causal != 0 masks key j > query i + (Skv - Sq). */
+ * D must be 64 or 128. causal != 0 masks key j > query i + (Skv - Sq). */
 hxb_status_t hxb_attention_f16(const void* Q, const void* K, const void* V,
                                void* O, int64_t BH, int64_t Sq, int64_t Skv,
                                int64_t D, float scale, int causal,
@@ -204,6 +204,35 @@ hxb_status_t hxb_attention_f16_bshd(const void* Q, int64_t ldq, const void* K,
                                     int64_t heads, int64_t Sq, int64_t Skv,
                                     int64_t D, float scale, int causal,
                                     void* stream);
+
+/* Output layouts of hxb_attention_gqa_f16. */
+#define HXB_ATTN_OUT_BHSD 0 /* [batch, q_heads, q_len, D] */
+#define HXB_ATTN_OUT_BSHD 1 /* [batch, q_len, q_heads, D] */
+
+/* Grouped-query attention over the first kv_len rows of a KV cache, the
+ * SlicedCacheAttention of integration_tests/models/micro/
+ * attention-cache-slice-f16/model.py:17-31 (SmolLM2's attention against its
+ * static cache) and the grouped_query_attention of the KV-cache LMs
+ * (integration_tests/models/kv_cache.py:46-86): query head h reads KV head
+ * h / (q_heads / kv_heads).
+ *   Q    [batch, q_heads, q_len, D] contiguous f16
+ *   K, V [batch, kv_heads, kv_rows, D] contiguous f16; rows [0, kv_len)
+ *        of each head are attended (kv_len <= kv_rows)
+ *   O    out_layout HXB_ATTN_OUT_BHSD or HXB_ATTN_OUT_BSHD (the models'
+ *        permute(0, 3, 1, 2, 4) output)
+ * q_heads must be a multiple of kv_heads; D 64 or 128; scale > 0 (the models
+ * use D^-0.5). causal != 0 masks key j > q_pos0 + i for query i, q_pos0
+ * being the cache position of the first query: kv_len - q_len when the
+ * queries are the last cached rows (decode, chunked prefill), 0 for a
+ * padded prefill whose keys past the last real token are cut by kv_len.
+ * Rows that see no key are 0. The query heads of one group share one pass
+ * over their KV head's keys. */
+hxb_status_t hxb_attention_gqa_f16(const void* Q, const void* K, const void* V,
+                                   void* O, int64_t batch, int64_t q_heads,
+                                   int64_t kv_heads, int64_t q_len,
+                                   int64_t q_pos0, int64_t kv_len,
+                                   int64_t kv_rows, int64_t D, float scale,
+                                   int causal, int out_layout, void* stream);
 
 /* ---- N-sharded f16 matmul across GPUs --------
  * The reference has no collectives (plugins/runtime/hexagon/channel.c:55-56

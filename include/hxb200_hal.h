@@ -162,13 +162,22 @@ const hxb_executable_library_header_t** hxb_executable_library_query(
  *             [11] s_down, [12] workspace
  *             (hxb_decoder_block_workspace_bytes)
  *   constants: batch, seq, pos0, hidden, heads, head_dim, ffn,
- *              rms_eps as f32 bits, rope_theta as f32 bits */
+ *              rms_eps as f32 bits, rope_theta as f32 bits
+ * HXB_EXPORT_ATTENTION_GQA_F16 "attention_gqa_f16"
+ *   bindings: [0] Q [B,Hq,q_len,D], [1] K cache [B,Hkv,kv_rows,D],
+ *             [2] V cache [B,Hkv,kv_rows,D], [3] O ([B,Hq,q_len,D] or
+ *             [B,q_len,Hq,D] by out_layout), all f16
+ *   constants: batch, q_heads, kv_heads, q_len, q_pos0 (i32), kv_len,
+ *              kv_rows, D, causal, out_layout (HXB_ATTN_OUT_*), scale as
+ *              f32 bits (0 = 1/sqrt(D)); the arguments of
+ *              hxb_attention_gqa_f16 in its order */
 enum hxb_export_ordinal_e {
   HXB_EXPORT_MATMUL_F16 = 0,
   HXB_EXPORT_MATMUL_W8A16 = 1,
   HXB_EXPORT_ATTENTION_F16 = 2,
   HXB_EXPORT_DECODER_BLOCK_W8A16 = 3,
-  HXB_EXPORT_COUNT = 4,
+  HXB_EXPORT_ATTENTION_GQA_F16 = 4,
+  HXB_EXPORT_COUNT = 5,
 };
 
 /* ===================================================== HAL runtime */

@@ -9,9 +9,9 @@ identifier it is imported as `iree_hexagon_plugins_b200` through
 from . import _native
 from ._native import HxbError
 from . import hal, sharded
-from .dispatch import (DecoderBlockW8, attention, attention_bshd, device_status, matmul,
-                       matmul_w8a16, rmsnorm, rope_, swiglu, w8a16_workspace)
+from .dispatch import (DecoderBlockW8, attention, attention_bshd, attention_gqa, device_status,
+                       matmul, matmul_w8a16, rmsnorm, rope_, swiglu, w8a16_workspace)
 
-__all__ = ["hal", "sharded", "HxbError", "DecoderBlockW8", "attention", "attention_bshd", "device_status",
-           "matmul", "matmul_w8a16", "rmsnorm", "rope_", "swiglu", "w8a16_workspace",
+__all__ = ["hal", "sharded", "HxbError", "DecoderBlockW8", "attention", "attention_bshd",
+           "attention_gqa", "device_status", "matmul", "matmul_w8a16", "rmsnorm", "rope_", "swiglu", "w8a16_workspace",
            "_native"]

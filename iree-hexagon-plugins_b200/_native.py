@@ -46,6 +46,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "hxb_attention_f16_bshd": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64,
                                        c_i64, c_i64, c_i64, c_i64, c_i64, c_float, c_int,
                                        c_vp]),
+    "hxb_attention_gqa_f16": (c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64,
+                                      c_i64, c_i64, c_i64, c_i64, c_float, c_int, c_int, c_vp]),
     "hxb_rmsnorm_f16": (c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_float, c_vp]),
     "hxb_rope_f16": (c_int, [c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_float, c_vp]),
     "hxb_swiglu_f16": (c_int, [c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_vp]),

@@ -44,41 +44,57 @@
 namespace hxb {
 namespace {
 
-constexpr int kAttD = 128;       // head dimension
 constexpr int kAttBM = 128;      // query rows per tile
 constexpr int kAttTiles = 2;     // query tiles per CTA
 constexpr int kAttBN = 128;      // keys per block
-constexpr int kAttSlots = 4;     // K/V ring slots
-constexpr int kAttTileBytes = 128 * kAttD * 2;  // one [128 x 128] f16 tile
 constexpr int kAttBoxBytes = 128 * 64 * 2;      // one TMA box: 128 rows x 64 f16
 constexpr float kRescaleLog2 = 8.0f;
 constexpr int kAttThreads = 384;
 
+// Shared-memory plan for head dimension D (64 or 128): a Q, K or V tile is
+// D/64 boxes of [128 rows x 64] f16; the K/V ring keeps 128 KB of tiles
+// (4 slots at D = 128, 8 at D = 64).
+template <int D>
 struct AttSmem {
+  static_assert(D == 64 || D == 128, "head dimension 64 or 128");
+  static constexpr int kBoxes = D / 64;
+  static constexpr int kTileBytes = 128 * D * 2;
+  static constexpr int kSlots = D == 64 ? 8 : 4;
   static constexpr int kOffQ = 0;
-  static constexpr int kOffKV = kOffQ + kAttTiles * kAttTileBytes;
-  static constexpr int kOffBar = kOffKV + kAttSlots * kAttTileBytes;
+  static constexpr int kOffKV = kOffQ + kAttTiles * kTileBytes;
+  static constexpr int kOffBar = kOffKV + kSlots * kTileBytes;
   // q_full, kv_full[slots], kv_empty[slots], s_full[2], p_full[2], o_full, drain
-  static constexpr int kNumBars = 1 + 2 * kAttSlots + 2 * kAttTiles + 2;
+  static constexpr int kNumBars = 1 + 2 * kSlots + 2 * kAttTiles + 2;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kBytes = kOffMisc + 16;
   static constexpr int kAlloc = kBytes + 1024;
 };
 
-// Q, K, V and O are row-major matrices of B*S rows; head h of batch b
-// occupies rows [b*S, (b+1)*S) and columns [(h % hpr) * 128, +128) with
-// hpr heads per row: hpr = 1 is the contiguous [B*H, S, D] layout,
-// hpr = H the [B, S, H*D] layout (e.g. the Q/K/V column blocks of a fused QKV
-// projection output). Rows of a tile past S belong to the next head or batch
-// (or lie outside the matrix and read as zeros): their keys are masked and
-// their query rows are not stored.
+// Q, K, V are row-major matrices; a CTA head bh (one KV head) reads
+//   Q rows [hb*Sq, hb*Sq + Sq)        columns [(bh % hpr) * D, +D)
+//   K, V rows [hb*kv_stride, +Skv)    columns [(bh % hpr) * D, +D)
+// with hb = bh / hpr and hpr heads per matrix row: hpr = 1 is the contiguous
+// [B*H, S, D] layout, hpr = H the [B, S, H*D] layout (e.g. the Q/K/V column
+// blocks of a fused QKV projection output). kv_stride >= Skv lets K/V be the
+// first Skv rows of a longer cache. Grouped-query attention packs the `group`
+// query heads that share KV head bh into one CTA head of Sq = group * q_len
+// rows (hpr = 1): packed row r is position r % q_len of query head
+// bh * group + r / q_len. Output query head g (global index over batch x query
+// heads) position s goes to O row (g / o_hpr) * q_len + s, columns
+// [(g % o_hpr) * D, +D). Rows of a tile past Sq (or keys past Skv) belong to
+// the next head or batch, or lie outside the matrix and read as zeros: their
+// keys are masked and their query rows are not stored.
 struct AttArgs {
   int Sq, Skv;
-  int hpr;            // heads per row
+  int hpr;            // Q/K/V heads per row
+  int q_len;          // query positions per query head (Sq / group)
+  int group;          // query heads per CTA head
+  int o_hpr;          // O heads per row
+  long long kv_stride;  // K/V rows per head
   long long ldo;      // O row pitch (elements)
   int q_blocks;       // CTAs per head: ceil(Sq / 256)
   int causal;
-  int causal_offset;  // Skv - Sq: key j is visible to query i iff j <= i + offset
+  int causal_offset;  // key j is visible to query position i iff j <= i + offset
   float c;            // scale * log2(e)
   __half* O;
   int* status;
@@ -89,7 +105,10 @@ __device__ __forceinline__ int kv_blocks_for(const AttArgs& a, int q0) {
   int last_key = a.Skv - 1;
   if (a.causal) {
     const int last_row = min(q0 + kAttTiles * kAttBM, a.Sq) - 1;
-    last_key = min(last_key, last_row + a.causal_offset);
+    // the largest query position among the rows: a CTA spanning two query
+    // heads holds the last position of the first one
+    const int last_pos = last_row / a.q_len != q0 / a.q_len ? a.q_len - 1 : last_row % a.q_len;
+    last_key = min(last_key, last_pos + a.causal_offset);
   }
   return last_key < 0 ? 0 : last_key / kAttBN + 1;
 }
@@ -119,13 +138,16 @@ struct Cursor {
   }
 };
 
+template <int D>
 __global__ void __launch_bounds__(kAttThreads, 1)
     attention_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                          const __grid_constant__ CUtensorMap tmK,
                          const __grid_constant__ CUtensorMap tmV, const AttArgs args) {
-  using L = AttSmem;
+  using L = AttSmem<D>;
+  constexpr int kAttSlots = L::kSlots;
+  constexpr int kAttTileBytes = L::kTileBytes;
   constexpr uint32_t kIdescQK = make_idesc_f16(kAttBM, kAttBN, 0, 0);
-  constexpr uint32_t kIdescPV = make_idesc_f16(kAttBM, kAttD, 0, 1);
+  constexpr uint32_t kIdescPV = make_idesc_f16(kAttBM, D, 0, 1);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -145,8 +167,8 @@ __global__ void __launch_bounds__(kAttThreads, 1)
   const int lane = threadIdx.x & 31;
   const int qb = blockIdx.x % args.q_blocks;
   const int bh = blockIdx.x / args.q_blocks;
-  const int hx = (bh % args.hpr) * kAttD;  // column of this head
-  const int hb = bh / args.hpr;            // row block (batch) of this head
+  const int hx = (bh % args.hpr) * D;  // column of this head
+  const int hb = bh / args.hpr;        // row block (batch) of this head
   const int q0 = qb * kAttTiles * kAttBM;
   const int n_kv = kv_blocks_for(args, q0);
   const FailState fs{abort_flag, args.status};
@@ -185,7 +207,7 @@ __global__ void __launch_bounds__(kAttThreads, 1)
     if (lane == 0 && n_kv > 0) {
       mbar_arrive_expect_tx(q_full, kAttTiles * kAttTileBytes);
       for (int t = 0; t < kAttTiles; ++t)
-        for (int b = 0; b < 2; ++b)
+        for (int b = 0; b < L::kBoxes; ++b)
           tma_load_2d(smem + L::kOffQ + t * kAttTileBytes + b * kAttBoxBytes, &tmQ, q_full,
                       hx + 64 * b, hb * args.Sq + q0 + t * kAttBM);
       Cursor<kAttSlots> c;
@@ -199,9 +221,9 @@ __global__ void __launch_bounds__(kAttThreads, 1)
           }
           mbar_arrive_expect_tx(&kv_full[c.slot], kAttTileBytes);
           const CUtensorMap* map = which ? &tmV : &tmK;
-          for (int b = 0; b < 2; ++b)
+          for (int b = 0; b < L::kBoxes; ++b)
             tma_load_2d(smem + L::kOffKV + c.slot * kAttTileBytes + b * kAttBoxBytes, map,
-                        &kv_full[c.slot], hx + 64 * b, hb * args.Skv + j * kAttBN);
+                        &kv_full[c.slot], hx + 64 * b, (int)(hb * args.kv_stride) + j * kAttBN);
           c.advance();
           ++issued;
         }
@@ -239,7 +261,7 @@ __global__ void __launch_bounds__(kAttThreads, 1)
         tc_fence_after();
         for (int t = 0; t < kAttTiles; ++t) {
 #pragma unroll
-          for (int kk = 0; kk < kAttD / 16; ++kk)
+          for (int kk = 0; kk < D / 16; ++kk)
             umma_f16_ss(tmem_base + t * 128, kmajor_desc(q_addr + t * kAttTileBytes, kk),
                         kmajor_desc(kv_addr + kslot * kAttTileBytes, kk), kIdescQK, kk != 0);
           umma_commit(&s_full[t]);
@@ -260,7 +282,7 @@ __global__ void __launch_bounds__(kAttThreads, 1)
         for (int t = 0; t < kAttTiles && ok; ++t) {
           if (!mbar_wait(&p_full[t], (uint32_t)(j & 1), fs)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t o_tmem = tmem_base + 256 + t * 128;
+          const uint32_t o_tmem = tmem_base + 256 + t * D;
           const uint32_t p_tmem = tmem_base + t * 128 + 64;
 #pragma unroll
           for (int kk = 0; kk < kAttBN / 16; ++kk)
@@ -268,7 +290,7 @@ __global__ void __launch_bounds__(kAttThreads, 1)
                         kIdescPV, (j | kk) != 0);
           if (has_next) {
 #pragma unroll
-            for (int kk = 0; kk < kAttD / 16; ++kk)
+            for (int kk = 0; kk < D / 16; ++kk)
               umma_f16_ss(tmem_base + t * 128, kmajor_desc(q_addr + t * kAttTileBytes, kk),
                           kmajor_desc(kv_addr + kslot * kAttTileBytes, kk), kIdescQK, kk != 0);
             umma_commit(&s_full[t]);
@@ -292,9 +314,10 @@ __global__ void __launch_bounds__(kAttThreads, 1)
     const int t = (warp - 4) >> 2;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
-    const int qrow = q0 + t * kAttBM + r;
+    const int qrow = q0 + t * kAttBM + r;  // packed row of the CTA head
+    const int qpos = qrow % args.q_len;     // its query position
     const uint32_t lane_base = tmem_base + ((uint32_t)(quarter * 32) << 16);
-    const uint32_t s_col = t * 128, p_col = t * 128 + 64, o_col = 256 + t * 128;
+    const uint32_t s_col = t * 128, p_col = t * 128 + 64, o_col = 256 + t * D;
     const float c = args.c;
     float m_run = -INFINITY;  // running max of S*c (log2 domain)
     float l_run = 0.0f;       // running sum of P against m_run
@@ -314,7 +337,7 @@ __global__ void __launch_bounds__(kAttThreads, 1)
       tmem_wait_ld();
       const int key0 = j * kAttBN;
       if (key0 + kAttBN > args.Skv || args.causal) {
-        const int lim = args.causal ? min(args.Skv - 1, qrow + args.causal_offset) : args.Skv - 1;
+        const int lim = args.causal ? min(args.Skv - 1, qpos + args.causal_offset) : args.Skv - 1;
 #pragma unroll
         for (int e = 0; e < kAttBN; ++e)
           if (key0 + e > lim) s[e] = -INFINITY;
@@ -339,7 +362,7 @@ __global__ void __launch_bounds__(kAttThreads, 1)
           m_run = m_new;
         }
 #pragma unroll 1
-        for (int ch = 0; ch < 4; ++ch) {
+        for (int ch = 0; ch < D / 32; ++ch) {
           uint32_t u[32];
           tmem_ld_32x32b_x32(lane_base + o_col + ch * 32, u);
           tmem_wait_ld();
@@ -373,10 +396,12 @@ __global__ void __launch_bounds__(kAttThreads, 1)
     const bool all_have = __all_sync(0xffffffffu, have);
     if (all_have) tc_fence_after();
     const float inv = (all_have && l_run > 0.0f) ? 1.0f / l_run : 0.0f;
-    __half* orow = args.O + ((long long)hb * args.Sq + qrow) * args.ldo + hx;
+    const long long qhead = (long long)bh * args.group + qrow / args.q_len;
+    __half* orow = args.O + (qhead / args.o_hpr * args.q_len + qpos) * args.ldo +
+                   qhead % args.o_hpr * D;
     const bool write = (ok || n_kv == 0) && qrow < args.Sq;
 #pragma unroll 1
-    for (int ch = 0; ch < 4; ++ch) {
+    for (int ch = 0; ch < D / 32; ++ch) {
       uint32_t u[32];
       if (all_have) {
         tmem_ld_32x32b_x32(lane_base + o_col + ch * 32, u);
@@ -418,11 +443,110 @@ hxb_status_t make_rows_map(CUtensorMap* m, const void* base, int64_t rows, int64
                            CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+// Operand layout of one attention launch (see AttArgs for the mapping).
+struct AttLayout {
+  const void *Q, *K, *V;
+  void* O;
+  int64_t ldq, ldk, ldv, ldo;  // row pitches (elements)
+  int64_t heads;               // CTA heads: batch x KV heads
+  int64_t hpr;                 // Q/K/V heads per row
+  int64_t group;               // query heads per KV head
+  int64_t q_len;               // query positions per query head
+  int64_t Skv;                 // keys attended per head
+  int64_t kv_stride;           // K/V rows per head (>= Skv)
+  int64_t o_hpr;               // O heads per row
+  int64_t D;
+  int64_t q_pos0;              // causal: key j is visible to position i iff j <= q_pos0 + i
+};
+
+template <int D>
+hxb_status_t launch_d(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
+                      const AttArgs& args, int64_t ctas, int ordinal, cudaStream_t stream) {
+  static bool configured[64] = {};
+  if (!configured[ordinal]) {
+    cudaError_t e = cudaFuncSetAttribute(attention_fwd_kernel<D>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         AttSmem<D>::kAlloc);
+    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(attention)");
+    configured[ordinal] = true;
+  }
+  attention_fwd_kernel<D><<<(unsigned)ctas, kAttThreads, AttSmem<D>::kAlloc, stream>>>(
+      tmQ, tmK, tmV, args);
+  return cuda_status(cudaGetLastError(), "attention launch");
+}
+
+hxb_status_t attention_run(const AttLayout& a, float scale, int causal, cudaStream_t stream) {
+  const int64_t D = a.D;
+  if (a.heads < 1 || a.q_len < 1 || a.Skv < 1 || a.group < 1 || a.hpr < 1 || a.o_hpr < 1)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: batch, heads, Sq, Skv must be >= 1");
+  if (D != 64 && D != 128)
+    return fail(HXB_STATUS_UNSUPPORTED,
+                "attention: head dim %lld not supported (D = 64 or 128)", (long long)D);
+  if (!a.Q || !a.K || !a.V || !a.O)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: null operand");
+  if (!aligned16(a.Q) || !aligned16(a.K) || !aligned16(a.V) || !aligned16(a.O))
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: Q/K/V/O must be 16-byte aligned");
+  if (a.ldq % 8 || a.ldk % 8 || a.ldv % 8 || a.ldo % 8)
+    return fail(HXB_STATUS_INVALID_ARGUMENT,
+                "attention: row pitches must be multiples of 8 elements (16 bytes)");
+  if (a.ldq < a.hpr * D || a.ldk < a.hpr * D || a.ldv < a.hpr * D || a.ldo < a.o_hpr * D)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: row pitch smaller than the heads it holds");
+  if (causal && (a.q_pos0 < -(int64_t)(1 << 30) || a.q_pos0 > (int64_t)(1 << 30)))
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: query position out of range");
+  if (a.kv_stride < a.Skv)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: kv_len %lld exceeds the %lld cache rows",
+                (long long)a.Skv, (long long)a.kv_stride);
+  if (a.heads % a.hpr || (a.heads * a.group) % a.o_hpr || (a.group > 1 && a.hpr != 1))
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: inconsistent head layout");
+  if (!(scale > 0.0f) || !isfinite(scale))
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: scale must be finite and > 0");
+  if (a.q_len > (1 << 30) || a.Skv > (1 << 30) || a.group > (1 << 20) ||
+      a.group * a.q_len > (1 << 30))
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: extent too large");
+  const int64_t Sq = a.group * a.q_len;
+  const int64_t rows_q = a.heads / a.hpr * Sq, rows_kv = a.heads / a.hpr * a.kv_stride;
+  if (rows_q > INT32_MAX || rows_kv > INT32_MAX)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: extent too large");
+  const int64_t q_blocks = (Sq + kAttTiles * kAttBM - 1) / (kAttTiles * kAttBM);
+  if (q_blocks * a.heads > INT32_MAX)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: too many query tiles");
+
+  DeviceInfo* dev = nullptr;
+  hxb_status_t s = current_device(&dev);
+  if (s != HXB_OK) return s;
+  CUtensorMap tmQ, tmK, tmV;
+  if ((s = make_rows_map(&tmQ, a.Q, rows_q, a.ldq)) != HXB_OK) return s;
+  if ((s = make_rows_map(&tmK, a.K, rows_kv, a.ldk)) != HXB_OK) return s;
+  if ((s = make_rows_map(&tmV, a.V, rows_kv, a.ldv)) != HXB_OK) return s;
+
+  AttArgs args{};
+  args.Sq = (int)Sq;
+  args.Skv = (int)a.Skv;
+  args.hpr = (int)a.hpr;
+  args.q_len = (int)a.q_len;
+  args.group = (int)a.group;
+  args.o_hpr = (int)a.o_hpr;
+  args.kv_stride = a.kv_stride;
+  args.ldo = a.ldo;
+  args.q_blocks = (int)q_blocks;
+  args.causal = causal ? 1 : 0;
+  args.causal_offset = (int)a.q_pos0;
+  args.c = (float)((double)scale * 1.4426950408889634);  // scale * log2(e)
+  args.O = static_cast<__half*>(a.O);
+  args.status = dev->status_word;
+  const int64_t ctas = q_blocks * a.heads;
+  return D == 64 ? launch_d<64>(tmQ, tmK, tmV, args, ctas, dev->ordinal, stream)
+                 : launch_d<128>(tmQ, tmK, tmV, args, ctas, dev->ordinal, stream);
+}
+
 }  // namespace
 
 // Dynamic shared memory (bytes) and threads per CTA of the attention kernel
-// (the executable library's export attributes).
-size_t attention_smem_bytes() { return AttSmem::kAlloc; }
+// (the executable library's export attributes): the larger of the two
+// head-dimension instances.
+size_t attention_smem_bytes() {
+  return AttSmem<128>::kAlloc > AttSmem<64>::kAlloc ? AttSmem<128>::kAlloc : AttSmem<64>::kAlloc;
+}
 int attention_threads() { return kAttThreads; }
 
 // Shared launcher: B batches x H heads; hpr heads per matrix row (see AttArgs).
@@ -430,61 +554,32 @@ hxb_status_t attention_launch(const void* Q, int64_t ldq, const void* K, int64_t
                               const void* V, int64_t ldv, void* O, int64_t ldo, int64_t B,
                               int64_t H, int64_t hpr, int64_t Sq, int64_t Skv, int64_t D,
                               float scale, int causal, cudaStream_t stream) {
-  if (B < 1 || H < 1 || Sq < 1 || Skv < 1)
+  if (B < 1 || H < 1)
     return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: batch, heads, Sq, Skv must be >= 1");
-  if (D != kAttD)
-    return fail(HXB_STATUS_UNSUPPORTED, "attention: head dim %lld not supported (D = 128 only)",
-                (long long)D);
-  if (!Q || !K || !V || !O)
-    return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: null operand");
-  if (!aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(O))
-    return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: Q/K/V/O must be 16-byte aligned");
-  if (ldq % 8 || ldk % 8 || ldv % 8 || ldo % 8)
+  AttLayout a{Q, K, V, O, ldq, ldk, ldv, ldo, B * H, hpr, 1, Sq, Skv, Skv, hpr, D, Skv - Sq};
+  return attention_run(a, scale, causal, stream);
+}
+
+// Grouped-query attention over the first kv_len rows of a KV cache.
+hxb_status_t attention_gqa_launch(const void* Q, const void* K, const void* V, void* O,
+                                  int64_t batch, int64_t q_heads, int64_t kv_heads,
+                                  int64_t q_len, int64_t q_pos0, int64_t kv_len,
+                                  int64_t kv_rows, int64_t D, float scale, int causal,
+                                  int out_layout, cudaStream_t stream) {
+  if (batch < 1 || q_heads < 1 || kv_heads < 1)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: batch and heads must be >= 1");
+  if (q_heads % kv_heads)
     return fail(HXB_STATUS_INVALID_ARGUMENT,
-                "attention: row pitches must be multiples of 8 elements (16 bytes)");
-  if (ldq < hpr * D || ldk < hpr * D || ldv < hpr * D || ldo < hpr * D)
-    return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: row pitch smaller than the heads it holds");
-  if (!(scale > 0.0f) || !isfinite(scale))
-    return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: scale must be finite and > 0");
-  const int64_t BH = B * H;
-  const int64_t rows_q = BH / hpr * Sq, rows_kv = BH / hpr * Skv;
-  if (Sq > (1 << 30) || Skv > (1 << 30) || rows_q > INT32_MAX || rows_kv > INT32_MAX)
+                "attention: %lld query heads are not a multiple of %lld KV heads",
+                (long long)q_heads, (long long)kv_heads);
+  if (out_layout != HXB_ATTN_OUT_BHSD && out_layout != HXB_ATTN_OUT_BSHD)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: unknown output layout %d", out_layout);
+  if (batch > INT32_MAX || q_heads > INT32_MAX)
     return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: extent too large");
-  const int64_t q_blocks = (Sq + kAttTiles * kAttBM - 1) / (kAttTiles * kAttBM);
-  if (q_blocks * BH > INT32_MAX)
-    return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: too many query tiles");
-
-  DeviceInfo* dev = nullptr;
-  hxb_status_t s = current_device(&dev);
-  if (s != HXB_OK) return s;
-  CUtensorMap tmQ, tmK, tmV;
-  if ((s = make_rows_map(&tmQ, Q, rows_q, ldq)) != HXB_OK) return s;
-  if ((s = make_rows_map(&tmK, K, rows_kv, ldk)) != HXB_OK) return s;
-  if ((s = make_rows_map(&tmV, V, rows_kv, ldv)) != HXB_OK) return s;
-
-  AttArgs args{};
-  args.Sq = (int)Sq;
-  args.Skv = (int)Skv;
-  args.hpr = (int)hpr;
-  args.ldo = ldo;
-  args.q_blocks = (int)q_blocks;
-  args.causal = causal ? 1 : 0;
-  args.causal_offset = (int)(Skv - Sq);
-  args.c = (float)((double)scale * 1.4426950408889634);  // scale * log2(e)
-  args.O = static_cast<__half*>(O);
-  args.status = dev->status_word;
-
-  static bool configured[64] = {};
-  if (!configured[dev->ordinal]) {
-    cudaError_t e = cudaFuncSetAttribute(attention_fwd_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         AttSmem::kAlloc);
-    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(attention)");
-    configured[dev->ordinal] = true;
-  }
-  attention_fwd_kernel<<<(unsigned)(q_blocks * BH), kAttThreads, AttSmem::kAlloc, stream>>>(
-      tmQ, tmK, tmV, args);
-  return cuda_status(cudaGetLastError(), "attention launch");
+  const bool bshd = out_layout == HXB_ATTN_OUT_BSHD;
+  AttLayout a{Q, K, V, O, D, D, D, bshd ? q_heads * D : D, batch * kv_heads, 1,
+              q_heads / kv_heads, q_len, kv_len, kv_rows, bshd ? q_heads : 1, D, q_pos0};
+  return attention_run(a, scale, causal, stream);
 }
 
 }  // namespace hxb
@@ -504,4 +599,15 @@ extern "C" hxb_status_t hxb_attention_f16_bshd(const void* Q, int64_t ldq, const
                                                int causal, void* stream) {
   return hxb::attention_launch(Q, ldq, K, ldk, V, ldv, O, ldo, batch, heads, heads, Sq, Skv, D,
                                scale, causal, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" hxb_status_t hxb_attention_gqa_f16(const void* Q, const void* K, const void* V,
+                                              void* O, int64_t batch, int64_t q_heads,
+                                              int64_t kv_heads, int64_t q_len, int64_t q_pos0,
+                                              int64_t kv_len, int64_t kv_rows, int64_t D,
+                                              float scale, int causal, int out_layout,
+                                              void* stream) {
+  return hxb::attention_gqa_launch(Q, K, V, O, batch, q_heads, kv_heads, q_len, q_pos0, kv_len,
+                                   kv_rows, D, scale, causal, out_layout,
+                                   static_cast<cudaStream_t>(stream));
 }

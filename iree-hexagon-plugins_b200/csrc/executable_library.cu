@@ -160,6 +160,35 @@ int dispatch_attention_f16(const hxb_executable_environment_t* env,
                            (int64_t)D, scale, causal, env->stream);
 }
 
+// bindings: Q, K cache, V cache, O; constants: batch, q_heads, kv_heads, q_len,
+// q_pos0 (i32), kv_len, kv_rows, D, causal, out_layout, scale bits
+int dispatch_attention_gqa_f16(const hxb_executable_environment_t* env,
+                               const hxb_executable_dispatch_state_t* ds,
+                               const hxb_executable_workgroup_state_t*) {
+  hxb_status_t s = check_state(env, ds, 4, 4, "attention_gqa_f16");
+  if (s != HXB_OK) return s;
+  const uint32_t* c = ds->constants;
+  const uint64_t B = c[0], Hq = c[1], Hkv = c[2], q_len = c[3], kv_len = c[5], kv_rows = c[6],
+                 D = c[7];
+  const int32_t q_pos0 = (int32_t)c[4];
+  float scale = f32_bits(c[10]);
+  if (c[10] == 0u && D > 0) scale = 1.0f / sqrtf((float)D);
+  bool ok = true;
+  const uint64_t q_bytes = mulc(mulc(mulc(mulc(B, Hq, &ok), q_len, &ok), D, &ok), 2, &ok);
+  const uint64_t kv_bytes = mulc(mulc(mulc(mulc(B, Hkv, &ok), kv_rows, &ok), D, &ok), 2, &ok);
+  if (!ok) return fail(HXB_STATUS_INVALID_ARGUMENT, "attention_gqa_f16: extents overflow");
+  if ((s = need(ds, 0, q_bytes, "attention_gqa_f16")) != HXB_OK ||
+      (s = need(ds, 1, kv_bytes, "attention_gqa_f16")) != HXB_OK ||
+      (s = need(ds, 2, kv_bytes, "attention_gqa_f16")) != HXB_OK ||
+      (s = need(ds, 3, q_bytes, "attention_gqa_f16")) != HXB_OK)
+    return s;
+  void* const* p = ds->binding_ptrs;
+  return hxb_attention_gqa_f16(p[0], p[1], p[2], p[3], (int64_t)B, (int64_t)Hq, (int64_t)Hkv,
+                               (int64_t)q_len, (int64_t)q_pos0, (int64_t)kv_len,
+                               (int64_t)kv_rows, (int64_t)D, scale, c[8] != 0, (int)c[9],
+                               env->stream);
+}
+
 // bindings: x, out, attn_norm, w_qkv, s_qkv, w_o, s_o, ffn_norm, w_gate_up,
 // s_gate_up, w_down, s_down, workspace; constants: batch, seq, pos0, hidden,
 // heads, head_dim, ffn, rms_eps bits, rope_theta bits
@@ -217,10 +246,10 @@ const hxb_executable_library_header_t kHeader = {HXB_EXECUTABLE_LIBRARY_VERSION_
 
 const hxb_executable_dispatch_fn_t kPtrs[HXB_EXPORT_COUNT] = {
     dispatch_matmul_f16, dispatch_matmul_w8a16, dispatch_attention_f16,
-    dispatch_decoder_block_w8a16};
+    dispatch_decoder_block_w8a16, dispatch_attention_gqa_f16};
 
 const char* const kNames[HXB_EXPORT_COUNT] = {"matmul_f16", "matmul_w8a16", "attention_f16",
-                                              "decoder_block_w8a16"};
+                                              "decoder_block_w8a16", "attention_gqa_f16"};
 
 struct Library {
   const hxb_executable_library_header_t* header;
@@ -242,6 +271,7 @@ Library* library() {
                                       (uint64_t)gemm_f16_threads()};
     l.attrs[HXB_EXPORT_MATMUL_W8A16] = {tc, w8, (uint64_t)w8_threads()};
     l.attrs[HXB_EXPORT_ATTENTION_F16] = {tc, att, (uint64_t)attention_threads()};
+    l.attrs[HXB_EXPORT_ATTENTION_GQA_F16] = {tc, att, (uint64_t)attention_threads()};
     l.attrs[HXB_EXPORT_DECODER_BLOCK_W8A16] = {
         tc, w8 > att ? w8 : att,
         (uint64_t)(w8_threads() > attention_threads() ? w8_threads() : attention_threads())};

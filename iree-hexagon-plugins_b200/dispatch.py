@@ -139,11 +139,11 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
 
 def attention_bshd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, batch: int,
                    heads: int, scale: float | None = None, causal: bool = False,
-                   out: torch.Tensor | None = None) -> torch.Tensor:
-    """Attention over [batch * S, heads * 128] row-major matrices (views with
-    unit inner stride, e.g. column blocks of a fused QKV output)."""
+                   out: torch.Tensor | None = None, head_dim: int = 128) -> torch.Tensor:
+    """Attention over [batch * S, heads * head_dim] row-major matrices (views
+    with unit inner stride, e.g. column blocks of a fused QKV output)."""
     lib = _native.load()
-    D = 128
+    D = head_dim
     Sq, Skv = q.shape[0] // batch, k.shape[0] // batch
     if scale is None:
         scale = D ** -0.5
@@ -153,6 +153,47 @@ def attention_bshd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, batch: 
         q.data_ptr(), _rowmajor_ld(q, "q"), k.data_ptr(), _rowmajor_ld(k, "k"),
         v.data_ptr(), _rowmajor_ld(v, "v"), out.data_ptr(), _rowmajor_ld(out, "out"),
         batch, heads, Sq, Skv, D, float(scale), int(causal), _stream_ptr(q)))
+    return out
+
+
+ATTN_OUT_LAYOUTS = {"bhsd": 0, "bshd": 1}
+
+
+def attention_gqa(query: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, *,
+                  kv_len: int | None = None, scale: float | None = None, causal: bool = False,
+                  q_pos0: int | None = None, out_layout: str = "bhsd",
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """Grouped-query attention of `query` [B, Hq, q_len, D] over the first
+    `kv_len` rows of `k_cache` / `v_cache` [B, Hkv, kv_rows, D]: query head h
+    reads KV head h // (Hq // Hkv). The reference's SlicedCacheAttention
+    (integration_tests/models/micro/attention-cache-slice-f16/model.py:17-31)
+    is attention_gqa(q, k, v, kv_len=context, out_layout="bshd").
+    causal masks key j > q_pos0 + i for query i (q_pos0 = the cache position
+    of the first query, by default kv_len - q_len).
+    out_layout "bhsd" gives [B, Hq, q_len, D], "bshd" [B, q_len, Hq, D]."""
+    lib = _native.load()
+    _require(query.dtype == k_cache.dtype == v_cache.dtype == torch.float16,
+             "query/k_cache/v_cache must be f16")
+    _require(query.dim() == 4 and k_cache.dim() == 4 and v_cache.shape == k_cache.shape,
+             "query [B, Hq, q_len, D] and caches [B, Hkv, rows, D] expected")
+    _require(query.is_contiguous() and k_cache.is_contiguous() and v_cache.is_contiguous(),
+             "query/k_cache/v_cache must be contiguous")
+    B, Hq, q_len, D = query.shape
+    _require(k_cache.shape[0] == B and k_cache.shape[3] == D, "shape mismatch")
+    Hkv, kv_rows = k_cache.shape[1], k_cache.shape[2]
+    kv_len = kv_rows if kv_len is None else int(kv_len)
+    q_pos0 = kv_len - q_len if q_pos0 is None else int(q_pos0)
+    _require(out_layout in ATTN_OUT_LAYOUTS, f"out_layout must be one of {list(ATTN_OUT_LAYOUTS)}")
+    if scale is None:
+        scale = D ** -0.5
+    if out is None:
+        shape = (B, Hq, q_len, D) if out_layout == "bhsd" else (B, q_len, Hq, D)
+        out = torch.empty(shape, dtype=torch.float16, device=query.device)
+    _require(out.is_contiguous() and out.numel() == query.numel(), "out shape mismatch")
+    check(lib.hxb_attention_gqa_f16(query.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                                    out.data_ptr(), B, Hq, Hkv, q_len, q_pos0, kv_len, kv_rows, D,
+                                    float(scale), int(causal), ATTN_OUT_LAYOUTS[out_layout],
+                                    _stream_ptr(query)))
     return out
 
 

@@ -16,7 +16,8 @@ import struct
 from . import _native
 from ._native import check
 
-EXPORTS = {"matmul_f16": 0, "matmul_w8a16": 1, "attention_f16": 2, "decoder_block_w8a16": 3}
+EXPORTS = {"matmul_f16": 0, "matmul_w8a16": 1, "attention_f16": 2, "decoder_block_w8a16": 3,
+           "attention_gqa_f16": 4}
 
 
 def f32_bits(x: float) -> int:

@@ -99,6 +99,53 @@ def attention_f32(q: np.ndarray, k: np.ndarray, v: np.ndarray, *,
     return o
 
 
+def attention_gqa_f32(q: np.ndarray, k_cache: np.ndarray, v_cache: np.ndarray, *,
+                      kv_len: int | None = None, scale: float | None = None,
+                      causal: bool = False, q_pos0: int | None = None,
+                      out_layout: str = "bhsd", round_scores: bool = True) -> np.ndarray:
+    """Grouped-query attention over the first kv_len rows of a KV cache,
+    restating SlicedCacheAttention.forward
+    (integration_tests/models/micro/attention-cache-slice-f16/model.py:17-31):
+    the `group` query heads of one KV head are the rows of one f16 matmul
+    (:24-25), whose f16 result is widened and scaled in f32 (:26), softmax in
+    f32, weights rounded to f16 (:27), weights . V (:28), output
+    [B, Hq, q_len, D] ("bhsd") or permuted to [B, q_len, Hq, D] ("bshd",
+    :29-30). q [B, Hq, q_len, D], caches [B, Hkv, rows, D], all f16. The f16
+    matmuls accumulate in f64 and round once. causal (not in the sliced-cache
+    model; the additive causal mask of the KV-cache LMs,
+    integration_tests/models/kv_cache.py:72-79) masks key j > q_pos0 + i for
+    query i, q_pos0 defaulting to kv_len - q_len; a row with every key masked
+    is 0. round_scores=False keeps the scores in f32 (the arithmetic of a fused
+    kernel that never materialises them). Returns f32 (the model's last matmul
+    output before its f16 rounding)."""
+    B, Hq, q_len, D = q.shape
+    Hkv, rows = k_cache.shape[1], k_cache.shape[2]
+    kv_len = rows if kv_len is None else kv_len
+    group = Hq // Hkv
+    if scale is None:
+        scale = D ** -0.5
+    k = k_cache[:, :, :kv_len].astype(np.float64)
+    v = v_cache[:, :, :kv_len].astype(np.float64)
+    qg = q.reshape(B, Hkv, group * q_len, D).astype(np.float64)
+    s = np.matmul(qg, k.transpose(0, 1, 3, 2))
+    s = (s.astype(np.float16) if round_scores else s).astype(np.float32) * np.float32(scale)
+    if causal:
+        q_pos0 = kv_len - q_len if q_pos0 is None else q_pos0
+        pos = np.arange(group * q_len) % q_len
+        masked = np.arange(kv_len)[None, :] > pos[:, None] + q_pos0
+        s = np.where(masked[None, None], np.float32(-np.inf), s)
+    m = s.max(axis=-1, keepdims=True)
+    dead = ~np.isfinite(m)
+    e = np.exp(s - np.where(dead, np.float32(0), m), dtype=np.float32)
+    with np.errstate(invalid="ignore"):
+        w = e / e.sum(axis=-1, keepdims=True, dtype=np.float32)
+    w = np.where(dead, np.float32(0), w).astype(np.float16).astype(np.float64)
+    o = np.matmul(w, v).astype(np.float32).reshape(B, Hkv, group, q_len, D)
+    if out_layout == "bshd":
+        return np.ascontiguousarray(o.transpose(0, 3, 1, 2, 4).reshape(B, q_len, Hq, D))
+    return np.ascontiguousarray(o.reshape(B, Hq, q_len, D))
+
+
 def hmx_known_answer(accumulations: int = 1):
     """(activation, weight, expected) of the reference's HMX accumulator test."""
     act = np.empty((32, 32), dtype=np.float16)

@@ -37,6 +37,7 @@ OUT_JSON = HERE / "micro_models.json"
 MODELS = [
     "micro/matmul-1024x1024x1024-f16",
     "micro/attention-4x1024x128-f16",
+    "micro/attention-cache-slice-f16",
     "micro/hmx/matmul-small-prime-17x19x23-f16",
     "micro/hmx/matmul-square-32x32x32-f16",
     "micro/hmx/matmul-ragged-k-64x64x65-f16",

@@ -108,6 +108,85 @@ def test_attention_baseline_config_heads(cuda_pkg, oracle):
 
 
 def test_attention_rejects_unsupported_head_dim(cuda_pkg):
-    q = torch.zeros(1, 16, 64, dtype=torch.float16, device=DEV)
+    q = torch.zeros(1, 16, 96, dtype=torch.float16, device=DEV)
     with pytest.raises(cuda_pkg.HxbError, match="head dim"):
         cuda_pkg.attention(q, q, q)
+
+
+@pytest.mark.parametrize("BH,Sq,Skv,causal", [(3, 256, 256, False), (2, 200, 333, True),
+                                              (1, 1, 700, False), (4, 513, 129, True)])
+def test_attention_head_dim_64(cuda_pkg, oracle, BH, Sq, Skv, causal):
+    q, k, v = _qkv(BH, Sq, Skv, seed=64 + Sq + Skv, D=64)
+    got = _run(cuda_pkg, q, k, v, causal=causal)
+    baseline_check(oracle.attention_f32(q, k, v, causal=causal), got,
+                   f"attention D=64 {BH}x{Sq}x{Skv} causal={causal}")
+
+
+# ----------------------------------------------- grouped-query, sliced cache
+def _gqa_inputs(B, Hq, Hkv, q_len, rows, D, seed):
+    rng = np.random.default_rng(seed)
+    q = rng.standard_normal((B, Hq, q_len, D)).astype(np.float16)
+    k = rng.standard_normal((B, Hkv, rows, D)).astype(np.float16)
+    v = rng.standard_normal((B, Hkv, rows, D)).astype(np.float16)
+    return q, k, v
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,q_len,q_pos0,kv_len,rows,D,causal,layout", [
+    (1, 9, 3, 64, None, 64, 128, 64, False, "bshd"),   # the sliced-cache micro model
+    (2, 8, 2, 1, None, 300, 512, 128, False, "bhsd"),  # decode, group 4
+    (1, 32, 8, 1, None, 1000, 1024, 64, True, "bshd"), # decode against a long cache
+    (2, 12, 4, 100, None, 250, 256, 64, True, "bhsd"), # a group spans two CTAs
+    (1, 4, 4, 130, None, 130, 200, 128, True, "bshd"), # no grouping, cache rows > kv_len
+    (3, 6, 1, 50, None, 77, 77, 64, False, "bhsd"),    # one KV head for all (MQA)
+    (1, 16, 2, 40, None, 30, 64, 128, True, "bhsd"),   # q_len > kv_len: masked rows
+    (1, 9, 3, 96, 0, 70, 128, 64, True, "bshd"),       # padded prefill: keys cut at 70
+    (2, 15, 5, 32, 200, 232, 256, 64, True, "bshd"),   # chunked prefill after 200 tokens
+])
+def test_attention_gqa_vs_oracle(cuda_pkg, oracle, B, Hq, Hkv, q_len, q_pos0, kv_len, rows, D,
+                                 causal, layout):
+    q, k, v = _gqa_inputs(B, Hq, Hkv, q_len, rows, D, seed=Hq * 100 + q_len + kv_len)
+    qd, kd, vd = (torch.from_numpy(x).to(DEV) for x in (q, k, v))
+    got = cuda_pkg.attention_gqa(qd, kd, vd, kv_len=kv_len, causal=causal, q_pos0=q_pos0,
+                                 out_layout=layout)
+    torch.cuda.synchronize()
+    got = got.float().cpu().numpy()
+    kw = dict(kv_len=kv_len, causal=causal, q_pos0=q_pos0, out_layout=layout)
+    # the fused arithmetic (f32 scores) within the baseline bar
+    want = oracle.attention_gqa_f32(q, k, v, round_scores=False, **kw)
+    what = f"gqa {B}x{Hq}/{Hkv}x{q_len}@{q_pos0}x{kv_len}/{rows}x{D} {causal} {layout}"
+    baseline_check(want, got, what)
+    if causal and q_pos0 is None and q_len > kv_len:
+        dead = q_len - kv_len  # positions that see no key
+        assert not got.reshape(B, Hq, q_len, D)[:, :, :dead].any()
+    # and the model's own roundings within its tolerance
+    c = compare(oracle.attention_gqa_f32(q, k, v, **kw), got, 5e-2, 5e-2)
+    assert c.close and c.rel_l2_percent <= 1.0, str(c)
+    assert cuda_pkg.device_status() == 0
+
+
+def test_attention_gqa_vs_reference_golden(cuda_pkg, oracle):
+    """integration_tests/models/micro/attention-cache-slice-f16: the
+    reference's own torch-eager output of SlicedCacheAttention(context=64)
+    under its model.yaml tolerances."""
+    key = "micro__attention-cache-slice-f16"
+    entry = golden_manifest()[key]
+    q, k, v = (t.to(DEV) for t in golden_inputs(key))
+    got = cuda_pkg.attention_gqa(q, k, v, kv_len=64, out_layout="bshd")
+    torch.cuda.synchronize()
+    got = got.cpu().numpy()
+    exp, rows = golden_expected(key)
+    tol = entry["tolerances"]
+    c = compare(exp, got, tol["atol"], tol["rtol"])
+    assert c.close and c.rel_l2_percent <= tol["relative_l2_percent"], str(c)
+    assert math.isclose(float(got.astype(np.float64).sum()), entry["out_sum"],
+                        rel_tol=1e-2, abs_tol=0.5)
+
+
+def test_attention_gqa_rejects_bad_layouts(cuda_pkg):
+    q = torch.zeros(1, 9, 8, 64, dtype=torch.float16, device=DEV)
+    kv = torch.zeros(1, 2, 16, 64, dtype=torch.float16, device=DEV)
+    with pytest.raises(cuda_pkg.HxbError, match="multiple"):
+        cuda_pkg.attention_gqa(q, kv, kv)            # 9 query heads over 2 KV heads
+    kv = torch.zeros(1, 3, 16, 64, dtype=torch.float16, device=DEV)
+    with pytest.raises(cuda_pkg.HxbError, match="exceeds"):
+        cuda_pkg.attention_gqa(q, kv, kv, kv_len=17)  # more keys than cache rows

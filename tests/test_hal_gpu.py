@@ -185,3 +185,29 @@ def test_end_reports_bad_dispatch(cuda_pkg, device):
     cb.end()
     cb.close()
     a.close()
+
+
+def test_gqa_attention_dispatch(cuda_pkg, device):
+    """The sliced-cache GQA export gives the direct call's bits."""
+    rng = np.random.default_rng(14)
+    B, Hq, Hkv, q_len, kv_len, rows, D = 1, 9, 3, 64, 64, 128, 64
+    q = rng.standard_normal((B, Hq, q_len, D)).astype(np.float16)
+    k = rng.standard_normal((B, Hkv, rows, D)).astype(np.float16)
+    v = rng.standard_normal((B, Hkv, rows, D)).astype(np.float16)
+    qb, kb, vb = _upload(device, q), _upload(device, k), _upload(device, v)
+    o = device.allocate(q.nbytes)
+    cb = device.command_buffer()
+    cb.begin()
+    cb.dispatch("attention_gqa_f16", [B, Hq, Hkv, q_len, 0, kv_len, rows, D, 0, 1, 0],
+                [qb, kb, vb, o])
+    cb.end()
+    done = device.semaphore(0)
+    device.execute(cb, signal=(done, 1))
+    done.wait(1)
+    got = np.frombuffer(o.read(), np.float16).reshape(B, q_len, Hq, D)
+    t = lambda x: torch.from_numpy(x).to(DEV)
+    want = cuda_pkg.attention_gqa(t(q), t(k), t(v), kv_len=kv_len, out_layout="bshd")
+    torch.cuda.synchronize()
+    assert np.array_equal(got, want.cpu().numpy())
+    for x in (cb, done, qb, kb, vb, o):
+        x.close()

@@ -38,7 +38,8 @@ def test_library_query_and_exports(pkg):
     assert info["version"] == 0x48420001
     assert info["imports"] == 0
     assert [e["name"] for e in info["exports"]] == [
-        "matmul_f16", "matmul_w8a16", "attention_f16", "decoder_block_w8a16"]
+        "matmul_f16", "matmul_w8a16", "attention_f16", "decoder_block_w8a16",
+        "attention_gqa_f16"]
     for e in info["exports"]:
         assert e["flags"] & 0x1 and e["flags"] & 0x2      # resources valid, tensor core
         assert 100_000 < e["smem_bytes"] <= 232_448       # one CTA per SM
@@ -67,6 +68,10 @@ def test_dispatch_functions_check_bindings_before_device_access(pkg):
     assert b"null" in lib.hxb_last_error_message()
     # decoder block: 12 bindings (needs 13)
     assert _call(pkg, 3, [1, 8, 0, 128, 1, 128, 256, 0, 0], fake[:12], [1 << 24] * 12) == 1
+    # GQA attention: K cache binding shorter than B * Hkv * kv_rows * D * 2
+    gqa = [1, 9, 3, 64, 0, 64, 128, 64, 0, 1, 0]
+    assert _call(pkg, 4, gqa, fake[:4], [1 << 20, 3 * 128 * 64 * 2 - 2, 1 << 20, 1 << 20]) == 1
+    assert b"binding 1" in lib.hxb_last_error_message()
     # extents whose byte count overflows 64 bits
     assert _call(pkg, 0, [0xFFFFFFFF] * 3 + [0], fake[:3], [1 << 20] * 3) in (1,)
 

@@ -87,6 +87,68 @@ def test_oracle_matches_reference_golden_attention(oracle):
     assert c.close and c.rel_l2_percent <= tol["relative_l2_percent"], str(c)
 
 
+def test_oracle_matches_reference_golden_gqa_attention(oracle):
+    """integration_tests/models/micro/attention-cache-slice-f16: 9 query heads
+    over 3 KV heads, the first 64 of 128 cache rows, output permuted to
+    [batch, q_len, heads, D]."""
+    key = "micro__attention-cache-slice-f16"
+    entry = golden_manifest()[key]
+    q, k, v = (t.numpy() for t in golden_inputs(key))
+    got = oracle.attention_gqa_f32(q, k, v, kv_len=64, out_layout="bshd").astype(np.float16)
+    exp, rows = golden_expected(key)
+    assert rows is None and exp.shape == got.shape == (1, 64, 9, 64)
+    tol = entry["tolerances"]
+    c = compare(exp, got, tol["atol"], tol["rtol"])
+    assert c.close and c.rel_l2_percent <= tol["relative_l2_percent"], str(c)
+    # the restatement follows the model's roundings: nearly every element is
+    # bit-identical to the eager output, the rest differ by accumulation order
+    # (100x inside the model's atol)
+    assert (got == exp).mean() > 0.99
+    assert np.abs(got.astype(np.float32) - exp.astype(np.float32)).max() <= 5e-4
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_oracle_gqa_equals_attention_on_repeated_heads(oracle, causal):
+    """GQA over a cache slice is plain attention with each KV head repeated
+    for its query heads (up to the f16 rounding of the scores that the
+    sliced-cache model does and the attention layer does not)."""
+    rng = np.random.default_rng(3)
+    B, Hq, Hkv, q_len, kv_len, rows, D = 2, 6, 2, 20, 45, 64, 64
+    q = rng.standard_normal((B, Hq, q_len, D)).astype(np.float16)
+    k = rng.standard_normal((B, Hkv, rows, D)).astype(np.float16)
+    v = rng.standard_normal((B, Hkv, rows, D)).astype(np.float16)
+    got = oracle.attention_gqa_f32(q, k, v, kv_len=kv_len, causal=causal)
+    rep = lambda t: np.repeat(t[:, :, :kv_len], Hq // Hkv, axis=1).reshape(B * Hq, kv_len, D)
+    want = oracle.attention_f32(q.reshape(B * Hq, q_len, D), rep(k), rep(v), causal=causal)
+    assert np.abs(got.reshape(want.shape) - want).max() < 5e-3
+    bshd = oracle.attention_gqa_f32(q, k, v, kv_len=kv_len, causal=causal, out_layout="bshd")
+    assert np.array_equal(bshd, got.transpose(0, 2, 1, 3))
+    # with f32 scores only the f16 weights (model.py:27) remain as a difference
+    exact = oracle.attention_gqa_f32(q, k, v, kv_len=kv_len, causal=causal, round_scores=False)
+    assert np.abs(exact.reshape(want.shape) - want).max() < 1e-3
+
+
+def test_oracle_gqa_padded_prefill_mask(oracle):
+    """q_pos0 = 0 with kv_len cut at the last real token: the prefill mask of
+    integration_tests/models/kv_cache.py:160-171 (causal, and no key past
+    input_length), against a direct additive-mask softmax."""
+    rng = np.random.default_rng(4)
+    B, Hq, Hkv, n, last, D = 1, 4, 2, 12, 8, 64
+    q = rng.standard_normal((B, Hq, n, D)).astype(np.float16)
+    k = rng.standard_normal((B, Hkv, 16, D)).astype(np.float16)
+    v = rng.standard_normal((B, Hkv, 16, D)).astype(np.float16)
+    got = oracle.attention_gqa_f32(q, k, v, kv_len=last + 1, causal=True, q_pos0=0,
+                                   round_scores=False)
+    kk = np.repeat(k[:, :, :n], 2, axis=1).astype(np.float64)
+    vv = np.repeat(v[:, :, :n], 2, axis=1).astype(np.float64)
+    s = q.astype(np.float64) @ kk.transpose(0, 1, 3, 2) * D ** -0.5
+    i, j = np.arange(n)[:, None], np.arange(n)[None, :]
+    s = s + np.where((j <= i) & (j <= last), 0.0, -np.inf)
+    w = np.exp(s - s.max(-1, keepdims=True))
+    w = (w / w.sum(-1, keepdims=True)).astype(np.float16).astype(np.float64)
+    assert np.abs(got - w @ vv).max() < 1e-4
+
+
 def test_attention_split_scale_constant(oracle):
     # attention_layer.mlir:12 holds s = 0.29730177875068026 for head_dim 128
     assert oracle.split_scale(128 ** -0.5) == float(np.float32(0.29730177875068026))
