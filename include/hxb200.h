@@ -226,13 +226,26 @@ hxb_status_t hxb_attention_f16_bshd(const void* Q, int64_t ldq, const void* K,
  * queries are the last cached rows (decode, chunked prefill), 0 for a
  * padded prefill whose keys past the last real token are cut by kv_len.
  * Rows that see no key are 0. The query heads of one group share one pass
- * over their KV head's keys. */
+ * over their KV head's keys.
+ * When the query blocks alone would not fill the SMs (decode: a handful of
+ * rows per KV head against a long cache) the keys are split across CTAs and
+ * the partial results merged by a second kernel; that needs `workspace` of
+ * hxb_attention_gqa_workspace_bytes(...) bytes (16-byte aligned, no
+ * initial contents). A null or smaller workspace runs without the split.
+ * Calls sharing a workspace must be ordered (one stream). */
 hxb_status_t hxb_attention_gqa_f16(const void* Q, const void* K, const void* V,
                                    void* O, int64_t batch, int64_t q_heads,
                                    int64_t kv_heads, int64_t q_len,
                                    int64_t q_pos0, int64_t kv_len,
                                    int64_t kv_rows, int64_t D, float scale,
-                                   int causal, int out_layout, void* stream);
+                                   int causal, int out_layout, void* workspace,
+                                   size_t workspace_bytes, void* stream);
+
+/* Workspace hxb_attention_gqa_f16 uses for its key split on the current
+ * device; 0 when that shape runs without a split (or is invalid). */
+size_t hxb_attention_gqa_workspace_bytes(int64_t batch, int64_t q_heads,
+                                         int64_t kv_heads, int64_t q_len,
+                                         int64_t kv_len, int64_t D);
 
 /* ---- N-sharded f16 matmul across GPUs --------
  * The reference has no collectives (plugins/runtime/hexagon/channel.c:55-56
@@ -330,6 +343,41 @@ hxb_status_t hxb_decoder_block_w8a16(const hxb_decoder_w8_t* w, const void* x,
                                      void* out, int64_t batch, int64_t seq,
                                      int64_t pos0, void* workspace,
                                      size_t workspace_bytes, void* stream);
+
+/* KV-cache update (SliceUpdateKvCache.update,
+ * integration_tests/models/kv_cache.py:101-112):
+ *   k_cache[b, h, begin + t, :] = k_src[b * n + t, h*D : (h+1)*D]
+ *   v_cache[b, h, begin + t, :] = v_src[b * n + t, h*D : (h+1)*D]
+ * for t < n. Sources are row-major [batch * n, ld_src] f16 (e.g. the K and V
+ * column blocks of a fused QKV output, ld_src = 3 * hidden); caches are
+ * [batch, kv_heads, cache_rows, D] f16. begin + n <= cache_rows. */
+hxb_status_t hxb_kv_cache_write_f16(const void* k_src, const void* v_src,
+                                    int64_t ld_src, void* k_cache, void* v_cache,
+                                    int64_t batch, int64_t kv_heads, int64_t n,
+                                    int64_t begin, int64_t cache_rows,
+                                    int64_t head_dim, void* stream);
+
+/* Device workspace hxb_decoder_block_w8a16_cached needs for batch * seq new
+ * rows (0 if the weights description is invalid). */
+size_t hxb_decoder_block_cached_workspace_bytes(const hxb_decoder_w8_t* w,
+                                                int64_t batch, int64_t seq);
+
+/* The decoder block against a KV cache, the prefill / decode steps of the
+ * reference's KV-cache LMs (integration_tests/models/kv_cache.py:145-186):
+ * the seq new rows of each batch are at positions pos0 .. pos0 + seq - 1;
+ * their rotated K and their V are written into k_cache / v_cache
+ * ([batch, heads, cache_rows, head_dim] f16) at rows pos0 .., and attention
+ * reads keys [0, pos0 + seq) from the caches, causally. pos0 = 0 with the
+ * whole prompt is the prefill (same result as hxb_decoder_block_w8a16);
+ * seq = 1 at pos0 = the tokens so far is one decode step. Short steps split
+ * the keys across SMs. */
+hxb_status_t hxb_decoder_block_w8a16_cached(const hxb_decoder_w8_t* w,
+                                            const void* x, void* out,
+                                            int64_t batch, int64_t seq,
+                                            int64_t pos0, void* k_cache,
+                                            void* v_cache, int64_t cache_rows,
+                                            void* workspace,
+                                            size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

@@ -54,7 +54,8 @@ typedef struct hxb_executable_library_header_t {
  * launches on. `scratch` (may be NULL) is device memory the runtime owns for
  * the dispatches of one queue: with it the int8-weight exports use the
  * stream-K schedule (hxb_matmul_w8a16_streamk; its first 4096 bytes must be
- * zero when the runtime creates it). */
+ * zero when the runtime creates it) and the GQA attention export splits the
+ * keys of short queries across SMs (its partials go past those 4096 bytes). */
 typedef struct hxb_executable_environment_t {
   const uint32_t* constants;
   void* stream;
@@ -189,8 +190,9 @@ typedef struct hxb_hal_semaphore_s hxb_hal_semaphore_t;
 typedef struct hxb_hal_command_buffer_s hxb_hal_command_buffer_t;
 
 /* Device options (api.h:40-63): which GPU, and the size of the device's
- * scratch arena (stream-K partials of the int8-weight dispatches; 0 = the
- * size the device needs). */
+ * scratch arena (stream-K partials of the int8-weight dispatches and the
+ * key-split partials of GQA attention; 0 = the stream-K size, which also
+ * covers a decode step's key split). */
 typedef struct hxb_hal_device_options_t {
   int32_t ordinal;
   uint64_t scratch_bytes;

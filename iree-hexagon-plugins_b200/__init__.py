@@ -9,9 +9,11 @@ identifier it is imported as `iree_hexagon_plugins_b200` through
 from . import _native
 from ._native import HxbError
 from . import hal, sharded
-from .dispatch import (DecoderBlockW8, attention, attention_bshd, attention_gqa, device_status,
-                       matmul, matmul_w8a16, rmsnorm, rope_, swiglu, w8a16_workspace)
+from .dispatch import (DecoderBlockW8, attention, attention_bshd, attention_gqa,
+                       attention_gqa_workspace_bytes, device_status, kv_cache_write, matmul,
+                       matmul_w8a16, rmsnorm, rope_, swiglu, w8a16_workspace)
 
 __all__ = ["hal", "sharded", "HxbError", "DecoderBlockW8", "attention", "attention_bshd",
-           "attention_gqa", "device_status", "matmul", "matmul_w8a16", "rmsnorm", "rope_", "swiglu", "w8a16_workspace",
-           "_native"]
+           "attention_gqa", "attention_gqa_workspace_bytes", "device_status",
+           "kv_cache_write", "matmul", "matmul_w8a16", "rmsnorm", "rope_", "swiglu",
+           "w8a16_workspace", "_native"]

@@ -47,7 +47,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                        c_i64, c_i64, c_i64, c_i64, c_i64, c_float, c_int,
                                        c_vp]),
     "hxb_attention_gqa_f16": (c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64,
-                                      c_i64, c_i64, c_i64, c_i64, c_float, c_int, c_int, c_vp]),
+                                      c_i64, c_i64, c_i64, c_i64, c_float, c_int, c_int, c_vp,
+                                      c_size, c_vp]),
+    "hxb_attention_gqa_workspace_bytes": (c_size, [c_i64, c_i64, c_i64, c_i64, c_i64, c_i64]),
     "hxb_rmsnorm_f16": (c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_float, c_vp]),
     "hxb_rope_f16": (c_int, [c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_float, c_vp]),
     "hxb_swiglu_f16": (c_int, [c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_vp]),
@@ -58,6 +60,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "hxb_ipc_open": (c_int, [c_vp, c_i64, ctypes.POINTER(c_vp)]),
     "hxb_ipc_close": (c_int, [c_vp, c_i64]),
     "hxb_decoder_block_workspace_bytes": (c_size, [c_vp, c_i64, c_i64]),
+    "hxb_decoder_block_cached_workspace_bytes": (c_size, [c_vp, c_i64, c_i64]),
+    "hxb_decoder_block_w8a16_cached": (c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp,
+                                               c_i64, c_vp, c_size, c_vp]),
+    "hxb_kv_cache_write_f16": (c_int, [c_vp, c_vp, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64,
+                                       c_i64, c_i64, c_vp]),
     "hxb_decoder_block_w8a16": (c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp,
                                         c_size, c_vp]),
     # include/hxb200_hal.h: executable library

@@ -38,6 +38,8 @@
 //   warps 8-11    softmax + epilogue of query tile 1
 #include <math.h>
 
+#include <algorithm>
+
 #include "runtime_common.h"
 #include "sm100.cuh"
 
@@ -71,14 +73,14 @@ struct AttSmem {
 };
 
 // Q, K, V are row-major matrices; a CTA head bh (one KV head) reads
-//   Q rows [hb*Sq, hb*Sq + Sq)        columns [(bh % hpr) * D, +D)
-//   K, V rows [hb*kv_stride, +Skv)    columns [(bh % hpr) * D, +D)
-// with hb = bh / hpr and hpr heads per matrix row: hpr = 1 is the contiguous
-// [B*H, S, D] layout, hpr = H the [B, S, H*D] layout (e.g. the Q/K/V column
-// blocks of a fused QKV projection output). kv_stride >= Skv lets K/V be the
-// first Skv rows of a longer cache. Grouped-query attention packs the `group`
-// query heads that share KV head bh into one CTA head of Sq = group * q_len
-// rows (hpr = 1): packed row r is position r % q_len of query head
+//   Q rows [(bh / q_hpr) * Sq, +Sq)              columns [(bh % q_hpr) * D, +D)
+//   K, V rows [(bh / kv_hpr) * kv_stride, +Skv)  columns [(bh % kv_hpr) * D, +D)
+// with q_hpr / kv_hpr heads per matrix row: 1 is the contiguous [B*H, S, D]
+// layout, H the [B, S, H*D] layout (e.g. the Q/K/V column blocks of a fused
+// QKV projection output). kv_stride >= Skv lets K/V be the first Skv rows of
+// a longer cache. Grouped-query attention packs the `group` query heads that
+// share KV head bh into one CTA head of Sq = group * q_len rows
+// (q_hpr = 1): packed row r is position r % q_len of query head
 // bh * group + r / q_len. Output query head g (global index over batch x query
 // heads) position s goes to O row (g / o_hpr) * q_len + s, columns
 // [(g % o_hpr) * D, +D). Rows of a tile past Sq (or keys past Skv) belong to
@@ -86,13 +88,19 @@ struct AttSmem {
 // keys are masked and their query rows are not stored.
 struct AttArgs {
   int Sq, Skv;
-  int hpr;            // Q/K/V heads per row
+  int q_hpr, kv_hpr;  // Q and K/V heads per row
   int q_len;          // query positions per query head (Sq / group)
   int group;          // query heads per CTA head
   int o_hpr;          // O heads per row
   long long kv_stride;  // K/V rows per head
   long long ldo;      // O row pitch (elements)
-  int q_blocks;       // CTAs per head: ceil(Sq / 256)
+  int q_blocks;       // query blocks per head: ceil(Sq / 256)
+  int q_box;          // Q rows one TMA box brings (min(128, Sq rounded up to 8))
+  int kv_splits;      // CTAs sharing one query block's keys (1: no split)
+  int split_blocks;   // key blocks per split
+  float* part_o;      // kv_splits > 1: normalised partial O, f32 [CTA][part_rows][D]
+  float* part_lse;    // and its log2-sum-exp2, [CTA][part_rows]
+  int part_rows;      // rows kept per CTA: min(256, Sq)
   int causal;
   int causal_offset;  // key j is visible to query position i iff j <= i + offset
   float c;            // scale * log2(e)
@@ -165,12 +173,20 @@ __global__ void __launch_bounds__(kAttThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int qb = blockIdx.x % args.q_blocks;
-  const int bh = blockIdx.x / args.q_blocks;
-  const int hx = (bh % args.hpr) * D;  // column of this head
-  const int hb = bh / args.hpr;        // row block (batch) of this head
+  const int split = blockIdx.x % args.kv_splits;
+  const int qb = blockIdx.x / args.kv_splits % args.q_blocks;
+  const int bh = blockIdx.x / args.kv_splits / args.q_blocks;
+  const int qx = (bh % args.q_hpr) * D;   // Q column of this head
+  const int qy = bh / args.q_hpr;         // Q row block of this head
+  const int kx = (bh % args.kv_hpr) * D;  // K/V column
+  const int ky = bh / args.kv_hpr;        // K/V row block
   const int q0 = qb * kAttTiles * kAttBM;
-  const int n_kv = kv_blocks_for(args, q0);
+  // this CTA's key blocks: [j0, j0 + n_kv) of the query block's visible ones
+  const int visible = kv_blocks_for(args, q0);
+  const int j0 = split * args.split_blocks;
+  const int n_kv = args.kv_splits == 1 ? visible : max(0, min(visible - j0, args.split_blocks));
+  // a second query tile only when the rows reach into it
+  const int n_tiles = args.Sq - q0 > kAttBM ? kAttTiles : 1;
   const FailState fs{abort_flag, args.status};
 
   if (threadIdx.x == 0) {
@@ -205,11 +221,13 @@ __global__ void __launch_bounds__(kAttThreads, 1)
   if (warp == 0) {
     // -------------------------------------------------------- TMA producer
     if (lane == 0 && n_kv > 0) {
-      mbar_arrive_expect_tx(q_full, kAttTiles * kAttTileBytes);
-      for (int t = 0; t < kAttTiles; ++t)
+      // a short Q (decode: a group's few rows) loads only q_box rows; the
+      // rest of the tile keeps stale bytes, which reach only rows not stored
+      mbar_arrive_expect_tx(q_full, n_tiles * L::kBoxes * args.q_box * 128);
+      for (int t = 0; t < n_tiles; ++t)
         for (int b = 0; b < L::kBoxes; ++b)
           tma_load_2d(smem + L::kOffQ + t * kAttTileBytes + b * kAttBoxBytes, &tmQ, q_full,
-                      hx + 64 * b, hb * args.Sq + q0 + t * kAttBM);
+                      qx + 64 * b, qy * args.Sq + q0 + t * kAttBM);
       Cursor<kAttSlots> c;
       int issued = 0;
       bool ok = true;
@@ -223,7 +241,8 @@ __global__ void __launch_bounds__(kAttThreads, 1)
           const CUtensorMap* map = which ? &tmV : &tmK;
           for (int b = 0; b < L::kBoxes; ++b)
             tma_load_2d(smem + L::kOffKV + c.slot * kAttTileBytes + b * kAttBoxBytes, map,
-                        &kv_full[c.slot], hx + 64 * b, (int)(hb * args.kv_stride) + j * kAttBN);
+                        &kv_full[c.slot], kx + 64 * b,
+                        (int)(ky * args.kv_stride) + (j0 + j) * kAttBN);
           c.advance();
           ++issued;
         }
@@ -259,7 +278,7 @@ __global__ void __launch_bounds__(kAttThreads, 1)
       c.advance();
       if (ok) {
         tc_fence_after();
-        for (int t = 0; t < kAttTiles; ++t) {
+        for (int t = 0; t < n_tiles; ++t) {
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk)
             umma_f16_ss(tmem_base + t * 128, kmajor_desc(q_addr + t * kAttTileBytes, kk),
@@ -279,7 +298,7 @@ __global__ void __launch_bounds__(kAttThreads, 1)
           if (!mbar_wait(&kv_full[kslot], c.phase, fs)) { ok = false; break; }
           c.advance();
         }
-        for (int t = 0; t < kAttTiles && ok; ++t) {
+        for (int t = 0; t < n_tiles && ok; ++t) {
           if (!mbar_wait(&p_full[t], (uint32_t)(j & 1), fs)) { ok = false; break; }
           tc_fence_after();
           const uint32_t o_tmem = tmem_base + 256 + t * D;
@@ -322,7 +341,8 @@ __global__ void __launch_bounds__(kAttThreads, 1)
     float m_run = -INFINITY;  // running max of S*c (log2 domain)
     float l_run = 0.0f;       // running sum of P against m_run
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
+    const int my_kv = t < n_tiles ? n_kv : 0;
+    for (int j = 0; j < my_kv; ++j) {
       const bool ready = mbar_wait(&s_full[t], (uint32_t)(j & 1), fs);
       if (!__all_sync(0xffffffffu, ready)) { ok = false; break; }
       tc_fence_after();
@@ -335,7 +355,7 @@ __global__ void __launch_bounds__(kAttThreads, 1)
         for (int e = 0; e < 32; ++e) s[ch * 32 + e] = __uint_as_float(u[e]);
       }
       tmem_wait_ld();
-      const int key0 = j * kAttBN;
+      const int key0 = (j0 + j) * kAttBN;
       if (key0 + kAttBN > args.Skv || args.causal) {
         const int lim = args.causal ? min(args.Skv - 1, qpos + args.causal_offset) : args.Skv - 1;
 #pragma unroll
@@ -400,6 +420,11 @@ __global__ void __launch_bounds__(kAttThreads, 1)
     __half* orow = args.O + (qhead / args.o_hpr * args.q_len + qpos) * args.ldo +
                    qhead % args.o_hpr * D;
     const bool write = (ok || n_kv == 0) && qrow < args.Sq;
+    const bool partial = args.kv_splits > 1;
+    // split keys: this CTA's normalised O and log2-sum-exp2 of its row
+    const size_t pidx = (size_t)blockIdx.x * args.part_rows + (t * kAttBM + r);
+    if (partial && write)
+      args.part_lse[pidx] = (all_have && l_run > 0.0f) ? m_run + log2f(l_run) : -INFINITY;
 #pragma unroll 1
     for (int ch = 0; ch < D / 32; ++ch) {
       uint32_t u[32];
@@ -410,7 +435,17 @@ __global__ void __launch_bounds__(kAttThreads, 1)
 #pragma unroll
         for (int e = 0; e < 32; ++e) u[e] = 0u;
       }
-      if (write) {
+      if (partial) {
+        if (write) {
+          float4* po = reinterpret_cast<float4*>(args.part_o + pidx * D + ch * 32);
+#pragma unroll
+          for (int v = 0; v < 8; ++v)
+            po[v] = make_float4(__uint_as_float(u[v * 4 + 0]) * inv,
+                                __uint_as_float(u[v * 4 + 1]) * inv,
+                                __uint_as_float(u[v * 4 + 2]) * inv,
+                                __uint_as_float(u[v * 4 + 3]) * inv);
+        }
+      } else if (write) {
 #pragma unroll
         for (int v = 0; v < 4; ++v) {
           uint4 o;
@@ -433,12 +468,69 @@ __global__ void __launch_bounds__(kAttThreads, 1)
   }
 }
 
-// 2-D map over a row-major [rows, ld] f16 matrix read in [128 rows x 64]
+// Split keys: one warp per (CTA head, query row) merges the kv_splits
+// partial results of the row, each a normalised O_i with its log2-sum-exp2
+// L_i: O = sum_i 2^(L_i - M) O_i / sum_i 2^(L_i - M), M = max_i L_i. A row
+// whose partials are all -inf (no visible key) is 0.
+template <int D>
+__global__ void __launch_bounds__(256)
+    attention_combine_kernel(const AttArgs args, int heads) {
+  constexpr int kPer = D / 32;  // O elements per lane
+  const long long gw = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gw >= (long long)heads * args.Sq) return;
+  const int bh = (int)(gw / args.Sq), qrow = (int)(gw % args.Sq);
+  const int qb = qrow / (kAttTiles * kAttBM), prow = qrow % (kAttTiles * kAttBM);
+  const size_t unit0 = ((size_t)bh * args.q_blocks + qb) * args.kv_splits;
+  float mx = -INFINITY;
+  for (int sp = lane; sp < args.kv_splits; sp += 32)
+    mx = fmaxf(mx, args.part_lse[(unit0 + sp) * args.part_rows + prow]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  float acc[kPer];
+#pragma unroll
+  for (int e = 0; e < kPer; ++e) acc[e] = 0.0f;
+  float wsum = 0.0f;
+  if (mx != -INFINITY) {
+    for (int sp = 0; sp < args.kv_splits; ++sp) {
+      const size_t idx = (unit0 + sp) * args.part_rows + prow;
+      const float w = ex2_approx(args.part_lse[idx] - mx);  // 0 for -inf
+      wsum += w;
+      const float* po = args.part_o + idx * D + lane * kPer;
+      if constexpr (kPer == 4) {
+        const float4 o = *reinterpret_cast<const float4*>(po);
+        acc[0] = fmaf(w, o.x, acc[0]);
+        acc[1] = fmaf(w, o.y, acc[1]);
+        acc[2] = fmaf(w, o.z, acc[2]);
+        acc[3] = fmaf(w, o.w, acc[3]);
+      } else {
+        const float2 o = *reinterpret_cast<const float2*>(po);
+        acc[0] = fmaf(w, o.x, acc[0]);
+        acc[1] = fmaf(w, o.y, acc[1]);
+      }
+    }
+  }
+  const float inv = wsum > 0.0f ? 1.0f / wsum : 0.0f;
+  const long long qhead = (long long)bh * args.group + qrow / args.q_len;
+  __half* orow = args.O + (qhead / args.o_hpr * args.q_len + qrow % args.q_len) * args.ldo +
+                 qhead % args.o_hpr * D + lane * kPer;
+  if constexpr (kPer == 4) {
+    uint2 v;
+    v.x = pack_half2(acc[0] * inv, acc[1] * inv);
+    v.y = pack_half2(acc[2] * inv, acc[3] * inv);
+    *reinterpret_cast<uint2*>(orow) = v;
+  } else {
+    *reinterpret_cast<uint32_t*>(orow) = pack_half2(acc[0] * inv, acc[1] * inv);
+  }
+}
+
+// 2-D map over a row-major [rows, ld] f16 matrix read in [box_rows x 64]
 // boxes (128-byte swizzle).
-hxb_status_t make_rows_map(CUtensorMap* m, const void* base, int64_t rows, int64_t ld) {
+hxb_status_t make_rows_map(CUtensorMap* m, const void* base, int64_t rows, int64_t ld,
+                           uint32_t box_rows = 128) {
   const uint64_t dims[2] = {(uint64_t)ld, (uint64_t)rows};
   const uint64_t strides[1] = {(uint64_t)ld * 2};
-  const uint32_t box[2] = {64, 128};
+  const uint32_t box[2] = {64, box_rows};
   return encode_tensor_map(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, dims, strides, box,
                            CU_TENSOR_MAP_SWIZZLE_128B);
 }
@@ -449,7 +541,7 @@ struct AttLayout {
   void* O;
   int64_t ldq, ldk, ldv, ldo;  // row pitches (elements)
   int64_t heads;               // CTA heads: batch x KV heads
-  int64_t hpr;                 // Q/K/V heads per row
+  int64_t q_hpr, kv_hpr;       // Q and K/V heads per row
   int64_t group;               // query heads per KV head
   int64_t q_len;               // query positions per query head
   int64_t Skv;                 // keys attended per head
@@ -457,11 +549,39 @@ struct AttLayout {
   int64_t o_hpr;               // O heads per row
   int64_t D;
   int64_t q_pos0;              // causal: key j is visible to position i iff j <= q_pos0 + i
+  void* workspace;             // split-key partials (null: no split)
+  size_t workspace_bytes;
 };
+
+// How the keys of one query block are split across CTAs: for short queries
+// (one query tile per CTA: decode, speculative or chunked steps) enough
+// splits to fill one wave of the SMs when the query blocks alone do not, with
+// at least one key block per split. Longer queries run unsplit.
+struct SplitPlan {
+  int splits = 1, split_blocks = 0, part_rows = 0;
+  size_t bytes = 0;  // workspace the partials need (0 without a split)
+};
+
+SplitPlan plan_splits(int64_t ctas, int64_t Sq, int64_t Skv, int64_t D, int num_sms) {
+  SplitPlan p;
+  const int64_t blocks = (Skv + kAttBN - 1) / kAttBN;
+  p.split_blocks = (int)blocks;
+  const int64_t want = ctas > 0 ? num_sms / ctas : 0;
+  if (want < 2 || blocks < 2 || Sq > kAttBM) return p;
+  const int64_t per = (blocks + std::min(want, blocks) - 1) / std::min(want, blocks);
+  const int64_t splits = (blocks + per - 1) / per;
+  if (splits < 2) return p;
+  p.splits = (int)splits;
+  p.split_blocks = (int)per;
+  p.part_rows = (int)std::min<int64_t>(kAttTiles * kAttBM, Sq);
+  const size_t rows = (size_t)(ctas * splits) * (size_t)p.part_rows;
+  p.bytes = (rows * sizeof(float) + 15) / 16 * 16 + rows * (size_t)D * sizeof(float);
+  return p;
+}
 
 template <int D>
 hxb_status_t launch_d(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
-                      const AttArgs& args, int64_t ctas, int ordinal, cudaStream_t stream) {
+                      const AttArgs& args, int64_t heads, int ordinal, cudaStream_t stream) {
   static bool configured[64] = {};
   if (!configured[ordinal]) {
     cudaError_t e = cudaFuncSetAttribute(attention_fwd_kernel<D>,
@@ -470,14 +590,20 @@ hxb_status_t launch_d(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUte
     if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(attention)");
     configured[ordinal] = true;
   }
+  const int64_t ctas = heads * args.q_blocks * args.kv_splits;
   attention_fwd_kernel<D><<<(unsigned)ctas, kAttThreads, AttSmem<D>::kAlloc, stream>>>(
       tmQ, tmK, tmV, args);
-  return cuda_status(cudaGetLastError(), "attention launch");
+  hxb_status_t s = cuda_status(cudaGetLastError(), "attention launch");
+  if (s != HXB_OK || args.kv_splits == 1) return s;
+  const int64_t warps = heads * args.Sq;
+  attention_combine_kernel<D><<<(unsigned)((warps + 7) / 8), 256, 0, stream>>>(args, (int)heads);
+  return cuda_status(cudaGetLastError(), "attention combine launch");
 }
 
 hxb_status_t attention_run(const AttLayout& a, float scale, int causal, cudaStream_t stream) {
   const int64_t D = a.D;
-  if (a.heads < 1 || a.q_len < 1 || a.Skv < 1 || a.group < 1 || a.hpr < 1 || a.o_hpr < 1)
+  if (a.heads < 1 || a.q_len < 1 || a.Skv < 1 || a.group < 1 || a.q_hpr < 1 || a.kv_hpr < 1 ||
+      a.o_hpr < 1)
     return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: batch, heads, Sq, Skv must be >= 1");
   if (D != 64 && D != 128)
     return fail(HXB_STATUS_UNSUPPORTED,
@@ -489,14 +615,16 @@ hxb_status_t attention_run(const AttLayout& a, float scale, int causal, cudaStre
   if (a.ldq % 8 || a.ldk % 8 || a.ldv % 8 || a.ldo % 8)
     return fail(HXB_STATUS_INVALID_ARGUMENT,
                 "attention: row pitches must be multiples of 8 elements (16 bytes)");
-  if (a.ldq < a.hpr * D || a.ldk < a.hpr * D || a.ldv < a.hpr * D || a.ldo < a.o_hpr * D)
+  if (a.ldq < a.q_hpr * D || a.ldk < a.kv_hpr * D || a.ldv < a.kv_hpr * D ||
+      a.ldo < a.o_hpr * D)
     return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: row pitch smaller than the heads it holds");
   if (causal && (a.q_pos0 < -(int64_t)(1 << 30) || a.q_pos0 > (int64_t)(1 << 30)))
     return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: query position out of range");
   if (a.kv_stride < a.Skv)
     return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: kv_len %lld exceeds the %lld cache rows",
                 (long long)a.Skv, (long long)a.kv_stride);
-  if (a.heads % a.hpr || (a.heads * a.group) % a.o_hpr || (a.group > 1 && a.hpr != 1))
+  if (a.heads % a.q_hpr || a.heads % a.kv_hpr || (a.heads * a.group) % a.o_hpr ||
+      (a.group > 1 && a.q_hpr != 1))
     return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: inconsistent head layout");
   if (!(scale > 0.0f) || !isfinite(scale))
     return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: scale must be finite and > 0");
@@ -504,39 +632,56 @@ hxb_status_t attention_run(const AttLayout& a, float scale, int causal, cudaStre
       a.group * a.q_len > (1 << 30))
     return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: extent too large");
   const int64_t Sq = a.group * a.q_len;
-  const int64_t rows_q = a.heads / a.hpr * Sq, rows_kv = a.heads / a.hpr * a.kv_stride;
+  const int64_t rows_q = a.heads / a.q_hpr * Sq, rows_kv = a.heads / a.kv_hpr * a.kv_stride;
   if (rows_q > INT32_MAX || rows_kv > INT32_MAX)
     return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: extent too large");
   const int64_t q_blocks = (Sq + kAttTiles * kAttBM - 1) / (kAttTiles * kAttBM);
-  if (q_blocks * a.heads > INT32_MAX)
+  if (q_blocks * a.heads > INT32_MAX / 1024)
     return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: too many query tiles");
 
   DeviceInfo* dev = nullptr;
   hxb_status_t s = current_device(&dev);
   if (s != HXB_OK) return s;
+  SplitPlan plan = plan_splits(q_blocks * a.heads, Sq, a.Skv, D, dev->num_sms);
+  if (plan.splits > 1 && (!a.workspace || a.workspace_bytes < plan.bytes ||
+                          (reinterpret_cast<uintptr_t>(a.workspace) & 15u))) {
+    plan = SplitPlan{};  // no room for partials: one CTA walks all the keys
+    plan.split_blocks = (int)((a.Skv + kAttBN - 1) / kAttBN);
+  }
+  const int q_box = (int)std::min<int64_t>(kAttBM, (Sq + 7) / 8 * 8);
   CUtensorMap tmQ, tmK, tmV;
-  if ((s = make_rows_map(&tmQ, a.Q, rows_q, a.ldq)) != HXB_OK) return s;
+  if ((s = make_rows_map(&tmQ, a.Q, rows_q, a.ldq, (uint32_t)q_box)) != HXB_OK) return s;
   if ((s = make_rows_map(&tmK, a.K, rows_kv, a.ldk)) != HXB_OK) return s;
   if ((s = make_rows_map(&tmV, a.V, rows_kv, a.ldv)) != HXB_OK) return s;
 
   AttArgs args{};
   args.Sq = (int)Sq;
   args.Skv = (int)a.Skv;
-  args.hpr = (int)a.hpr;
+  args.q_hpr = (int)a.q_hpr;
+  args.kv_hpr = (int)a.kv_hpr;
   args.q_len = (int)a.q_len;
   args.group = (int)a.group;
   args.o_hpr = (int)a.o_hpr;
   args.kv_stride = a.kv_stride;
   args.ldo = a.ldo;
   args.q_blocks = (int)q_blocks;
+  args.q_box = q_box;
+  args.kv_splits = plan.splits;
+  args.split_blocks = plan.split_blocks;
+  args.part_rows = plan.part_rows;
+  if (plan.splits > 1) {
+    args.part_lse = static_cast<float*>(a.workspace);
+    const size_t lse_bytes = ((size_t)q_blocks * a.heads * plan.splits * plan.part_rows *
+                                  sizeof(float) + 15) / 16 * 16;
+    args.part_o = reinterpret_cast<float*>(static_cast<char*>(a.workspace) + lse_bytes);
+  }
   args.causal = causal ? 1 : 0;
   args.causal_offset = (int)a.q_pos0;
   args.c = (float)((double)scale * 1.4426950408889634);  // scale * log2(e)
   args.O = static_cast<__half*>(a.O);
   args.status = dev->status_word;
-  const int64_t ctas = q_blocks * a.heads;
-  return D == 64 ? launch_d<64>(tmQ, tmK, tmV, args, ctas, dev->ordinal, stream)
-                 : launch_d<128>(tmQ, tmK, tmV, args, ctas, dev->ordinal, stream);
+  return D == 64 ? launch_d<64>(tmQ, tmK, tmV, args, a.heads, dev->ordinal, stream)
+                 : launch_d<128>(tmQ, tmK, tmV, args, a.heads, dev->ordinal, stream);
 }
 
 }  // namespace
@@ -556,7 +701,16 @@ hxb_status_t attention_launch(const void* Q, int64_t ldq, const void* K, int64_t
                               float scale, int causal, cudaStream_t stream) {
   if (B < 1 || H < 1)
     return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: batch, heads, Sq, Skv must be >= 1");
-  AttLayout a{Q, K, V, O, ldq, ldk, ldv, ldo, B * H, hpr, 1, Sq, Skv, Skv, hpr, D, Skv - Sq};
+  AttLayout a{};
+  a.Q = Q, a.K = K, a.V = V, a.O = O;
+  a.ldq = ldq, a.ldk = ldk, a.ldv = ldv, a.ldo = ldo;
+  a.heads = B * H;
+  a.q_hpr = a.kv_hpr = a.o_hpr = hpr;
+  a.group = 1;
+  a.q_len = Sq;
+  a.Skv = a.kv_stride = Skv;
+  a.D = D;
+  a.q_pos0 = Skv - Sq;
   return attention_run(a, scale, causal, stream);
 }
 
@@ -565,7 +719,8 @@ hxb_status_t attention_gqa_launch(const void* Q, const void* K, const void* V, v
                                   int64_t batch, int64_t q_heads, int64_t kv_heads,
                                   int64_t q_len, int64_t q_pos0, int64_t kv_len,
                                   int64_t kv_rows, int64_t D, float scale, int causal,
-                                  int out_layout, cudaStream_t stream) {
+                                  int out_layout, void* workspace, size_t workspace_bytes,
+                                  cudaStream_t stream) {
   if (batch < 1 || q_heads < 1 || kv_heads < 1)
     return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: batch and heads must be >= 1");
   if (q_heads % kv_heads)
@@ -577,9 +732,76 @@ hxb_status_t attention_gqa_launch(const void* Q, const void* K, const void* V, v
   if (batch > INT32_MAX || q_heads > INT32_MAX)
     return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: extent too large");
   const bool bshd = out_layout == HXB_ATTN_OUT_BSHD;
-  AttLayout a{Q, K, V, O, D, D, D, bshd ? q_heads * D : D, batch * kv_heads, 1,
-              q_heads / kv_heads, q_len, kv_len, kv_rows, bshd ? q_heads : 1, D, q_pos0};
+  AttLayout a{};
+  a.Q = Q, a.K = K, a.V = V, a.O = O;
+  a.ldq = a.ldk = a.ldv = D;
+  a.ldo = bshd ? q_heads * D : D;
+  a.heads = batch * kv_heads;
+  a.q_hpr = a.kv_hpr = 1;
+  a.o_hpr = bshd ? q_heads : 1;
+  a.group = q_heads / kv_heads;
+  a.q_len = q_len;
+  a.Skv = kv_len;
+  a.kv_stride = kv_rows;
+  a.D = D;
+  a.q_pos0 = q_pos0;
+  a.workspace = workspace;
+  a.workspace_bytes = workspace_bytes;
   return attention_run(a, scale, causal, stream);
+}
+
+// Upper bound of the split-key workspace of any call with Sq query rows per
+// CTA head on the current device, whatever the number of keys: the splits
+// never make more CTAs than there are SMs.
+size_t attention_split_bound(int64_t Sq, int64_t D) {
+  DeviceInfo* dev = nullptr;
+  if (Sq < 1 || Sq > kAttBM || current_device(&dev) != HXB_OK) return 0;
+  const size_t rows = (size_t)dev->num_sms * (size_t)Sq;
+  return (rows * sizeof(float) + 15) / 16 * 16 + rows * (size_t)D * sizeof(float);
+}
+
+// Self-attention of new rows against a KV cache: Q is [batch * seq, ldq]
+// with head h at columns [h*D, +D) (a fused QKV output), K/V caches are
+// [batch, heads, cache_rows, D], keys [0, kv_len) attended causally from
+// position q_pos0; O is [batch * seq, ldo] in the layout of Q.
+hxb_status_t attention_cached_launch(const void* Q, int64_t ldq, const void* k_cache,
+                                     const void* v_cache, int64_t cache_rows, void* O,
+                                     int64_t ldo, int64_t batch, int64_t heads, int64_t seq,
+                                     int64_t kv_len, int64_t q_pos0, int64_t D, float scale,
+                                     void* workspace, size_t workspace_bytes,
+                                     cudaStream_t stream) {
+  if (batch < 1 || heads < 1)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: batch and heads must be >= 1");
+  AttLayout a{};
+  a.Q = Q, a.K = k_cache, a.V = v_cache, a.O = O;
+  a.ldq = ldq, a.ldk = a.ldv = D, a.ldo = ldo;
+  a.heads = batch * heads;
+  a.q_hpr = a.o_hpr = heads;
+  a.kv_hpr = 1;
+  a.group = 1;
+  a.q_len = seq;
+  a.Skv = kv_len;
+  a.kv_stride = cache_rows;
+  a.D = D;
+  a.q_pos0 = q_pos0;
+  a.workspace = workspace;
+  a.workspace_bytes = workspace_bytes;
+  return attention_run(a, scale, 1, stream);
+}
+
+// Workspace the split-key plan of a GQA call needs on the current device (0:
+// the call does not split, or the shape or device is invalid).
+size_t attention_gqa_workspace(int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t q_len,
+                               int64_t kv_len, int64_t D) {
+  if (batch < 1 || q_heads < 1 || kv_heads < 1 || q_len < 1 || kv_len < 1 ||
+      q_heads % kv_heads || (D != 64 && D != 128) || batch > INT32_MAX || q_heads > INT32_MAX ||
+      q_len > (1 << 30) || kv_len > (1 << 30) || (q_heads / kv_heads) * q_len > (1 << 30))
+    return 0;
+  DeviceInfo* dev = nullptr;
+  if (current_device(&dev) != HXB_OK) return 0;
+  const int64_t Sq = q_heads / kv_heads * q_len;
+  const int64_t q_blocks = (Sq + kAttTiles * kAttBM - 1) / (kAttTiles * kAttBM);
+  return plan_splits(q_blocks * batch * kv_heads, Sq, kv_len, D, dev->num_sms).bytes;
 }
 
 }  // namespace hxb
@@ -606,8 +828,15 @@ extern "C" hxb_status_t hxb_attention_gqa_f16(const void* Q, const void* K, cons
                                               int64_t kv_heads, int64_t q_len, int64_t q_pos0,
                                               int64_t kv_len, int64_t kv_rows, int64_t D,
                                               float scale, int causal, int out_layout,
+                                              void* workspace, size_t workspace_bytes,
                                               void* stream) {
   return hxb::attention_gqa_launch(Q, K, V, O, batch, q_heads, kv_heads, q_len, q_pos0, kv_len,
-                                   kv_rows, D, scale, causal, out_layout,
-                                   static_cast<cudaStream_t>(stream));
+                                   kv_rows, D, scale, causal, out_layout, workspace,
+                                   workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" size_t hxb_attention_gqa_workspace_bytes(int64_t batch, int64_t q_heads,
+                                                    int64_t kv_heads, int64_t q_len,
+                                                    int64_t kv_len, int64_t D) {
+  return hxb::attention_gqa_workspace(batch, q_heads, kv_heads, q_len, kv_len, D);
 }

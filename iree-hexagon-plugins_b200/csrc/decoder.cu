@@ -37,6 +37,13 @@ hxb_status_t attention_launch(const void* Q, int64_t ldq, const void* K, int64_t
                               const void* V, int64_t ldv, void* O, int64_t ldo, int64_t B,
                               int64_t H, int64_t hpr, int64_t Sq, int64_t Skv, int64_t D,
                               float scale, int causal, cudaStream_t stream);
+hxb_status_t attention_cached_launch(const void* Q, int64_t ldq, const void* k_cache,
+                                     const void* v_cache, int64_t cache_rows, void* O,
+                                     int64_t ldo, int64_t batch, int64_t heads, int64_t seq,
+                                     int64_t kv_len, int64_t q_pos0, int64_t D, float scale,
+                                     void* workspace, size_t workspace_bytes,
+                                     cudaStream_t stream);
+size_t attention_split_bound(int64_t Sq, int64_t D);
 
 namespace {
 
@@ -130,6 +137,63 @@ __global__ void swiglu_kernel(const __half* __restrict__ gu, long long ldgu, __h
   *reinterpret_cast<uint4*>(a + (long long)r * lda + c) = o;
 }
 
+// KV-cache update: cache[b, h, begin + t, :] = src[b * n + t, h*D : (h+1)*D]
+// for the K (blockIdx.y 0) and V (1) blocks of a fused projection output;
+// one thread per 8 halves, coalesced on both sides.
+__global__ void kv_cache_write_kernel(const __half* __restrict__ k_src,
+                                      const __half* __restrict__ v_src, long long ld_src,
+                                      __half* __restrict__ k_cache, __half* __restrict__ v_cache,
+                                      int n, int heads, int D, int begin, long long cache_rows,
+                                      long long vectors) {
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= vectors) return;
+  const __half* src = blockIdx.y ? v_src : k_src;
+  __half* cache = blockIdx.y ? v_cache : k_cache;
+  const int per_row = heads * D / 8;
+  const long long r = idx / per_row;  // source row b * n + t
+  const int c = (int)(idx - r * per_row) * 8;
+  const int h = c / D, d = c - h * D;
+  const long long b = r / n, t = r - b * n;
+  const uint4 v = *reinterpret_cast<const uint4*>(src + r * ld_src + c);
+  *reinterpret_cast<uint4*>(cache + ((b * heads + h) * cache_rows + begin + t) * D + d) = v;
+}
+
+hxb_status_t launch_kv_cache_write(const void* k_src, const void* v_src, int64_t ld_src,
+                                   void* k_cache, void* v_cache, int64_t batch, int64_t heads,
+                                   int64_t n, int64_t begin, int64_t cache_rows, int64_t D,
+                                   cudaStream_t stream) {
+  const long long vectors = (long long)batch * n * heads * D / 8;
+  const int threads = 256;
+  const dim3 grid((unsigned)((vectors + threads - 1) / threads), 2);
+  kv_cache_write_kernel<<<grid, threads, 0, stream>>>(
+      static_cast<const __half*>(k_src), static_cast<const __half*>(v_src), ld_src,
+      static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), (int)n, (int)heads, (int)D,
+      (int)begin, cache_rows, vectors);
+  return cuda_status(cudaGetLastError(), "kv cache write launch");
+}
+
+hxb_status_t check_kv_cache_write(const void* k_src, const void* v_src, int64_t ld_src,
+                                  const void* k_cache, const void* v_cache, int64_t batch,
+                                  int64_t heads, int64_t n, int64_t begin, int64_t cache_rows,
+                                  int64_t D) {
+  if (!k_src || !v_src || !k_cache || !v_cache)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "kv cache write: null pointer");
+  if (!aligned16(k_src) || !aligned16(v_src) || !aligned16(k_cache) || !aligned16(v_cache) ||
+      ld_src % 8 || D % 8 || D < 8)
+    return fail(HXB_STATUS_INVALID_ARGUMENT,
+                "kv cache write: 16-byte aligned rows and head_dim %% 8 == 0 required");
+  if (batch < 1 || heads < 1 || n < 1 || begin < 0 || ld_src < heads * D)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "kv cache write: bad extents");
+  if (begin + n > cache_rows)
+    return fail(HXB_STATUS_INVALID_ARGUMENT,
+                "kv cache write: rows [%lld, %lld) exceed the %lld cache rows", (long long)begin,
+                (long long)(begin + n), (long long)cache_rows);
+  if (batch * n * heads * D / 8 > ((int64_t)1 << 40) || n > INT32_MAX || begin > INT32_MAX ||
+      heads * D > INT32_MAX)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "kv cache write: extent too large");
+  return HXB_OK;
+}
+
 hxb_status_t launch_rmsnorm(const void* x, int64_t ldx, const void* gamma, void* y, int64_t ldy,
                             int64_t rows, int64_t cols, float eps, cudaStream_t stream,
                             int* clear = nullptr, int nclear = 0) {
@@ -164,17 +228,20 @@ hxb_status_t launch_swiglu(const void* gu, int64_t ldgu, void* a, int64_t lda, i
 size_t round256(size_t b) { return (b + 255) & ~size_t(255); }
 
 struct DecoderBuffers {
-  size_t sk, sk_bytes, h, qkv, att, h2, gu, a, total;
+  size_t sk, sk_bytes, att_ws, att_ws_bytes, h, qkv, att, h2, gu, a, total;
 };
 
 // Stream-K scratch of the W8 GEMMs (flags, then partial accumulators) first,
-// then the activations.
-DecoderBuffers decoder_layout(const hxb_decoder_w8_t* w, int64_t rows) {
+// then (with a KV cache) the key-split partials of the attention, then the
+// activations.
+DecoderBuffers decoder_layout(const hxb_decoder_w8_t* w, int64_t rows, int64_t seq = 0) {
   DecoderBuffers b{};
   size_t off = 0;
   DeviceInfo* dev = nullptr;
   b.sk_bytes = current_device(&dev) == HXB_OK ? w8_streamk_workspace_bytes(dev->num_sms) : 0;
   b.sk = off;  off += round256(b.sk_bytes);
+  b.att_ws_bytes = seq > 0 ? attention_split_bound(seq, w->head_dim) : 0;
+  b.att_ws = off; off += round256(b.att_ws_bytes);
   b.h = off;   off += round256((size_t)rows * w->hidden * 2);
   b.qkv = off; off += round256((size_t)rows * 3 * w->hidden * 2);
   b.att = off; off += round256((size_t)rows * w->hidden * 2);
@@ -239,26 +306,35 @@ extern "C" hxb_status_t hxb_swiglu_f16(const void* gu, int64_t ldgu, void* a, in
   return launch_swiglu(gu, ldgu, a, lda, rows, ffn, static_cast<cudaStream_t>(stream));
 }
 
-extern "C" size_t hxb_decoder_block_workspace_bytes(const hxb_decoder_w8_t* w, int64_t batch,
-                                                    int64_t seq) {
-  if (hxb::check_decoder(w, batch, seq) != HXB_OK) return 0;
-  return hxb::decoder_layout(w, batch * seq).total;
-}
+namespace hxb {
+namespace {
 
-extern "C" hxb_status_t hxb_decoder_block_w8a16(const hxb_decoder_w8_t* w, const void* x,
-                                                void* out, int64_t batch, int64_t seq,
-                                                int64_t pos0, void* workspace,
-                                                size_t workspace_bytes, void* stream_ptr) {
-  using namespace hxb;
+struct KvCache {
+  void *k, *v;
+  int64_t rows;
+};
+
+// The block's dispatch sequence; with `cache` the new K/V rows go into the
+// cache at pos0 and attention reads keys [0, pos0 + seq) from it.
+hxb_status_t decoder_run(const hxb_decoder_w8_t* w, const void* x, void* out, int64_t batch,
+                         int64_t seq, int64_t pos0, const KvCache* cache, void* workspace,
+                         size_t workspace_bytes, cudaStream_t stream) {
   hxb_status_t s = check_decoder(w, batch, seq);
   if (s != HXB_OK) return s;
   if (!x || !out || !aligned16(x) || !aligned16(out))
     return fail(HXB_STATUS_INVALID_ARGUMENT, "decoder: x / out must be 16-byte aligned");
+  if (pos0 < 0 || pos0 + seq > (1 << 24))
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "decoder: positions out of range");
   const int64_t rows = batch * seq, H = w->hidden, F = w->ffn;
-  const DecoderBuffers b = decoder_layout(w, rows);
+  const DecoderBuffers b = decoder_layout(w, rows, cache ? seq : 0);
   if (!workspace || workspace_bytes < b.total)
     return fail(HXB_STATUS_INVALID_ARGUMENT, "decoder: workspace needs %zu bytes, got %zu",
                 b.total, workspace_bytes);
+  // the cache side of the K/V write (its sources are this block's own qkv rows,
+  // aligned like x)
+  if (cache && (s = check_kv_cache_write(x, x, 3 * H, cache->k, cache->v, batch, w->heads, seq,
+                                         pos0, cache->rows, w->head_dim)) != HXB_OK)
+    return s;
   uint8_t* ws = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
   __half* h = reinterpret_cast<__half*>(ws + b.h);
@@ -267,10 +343,10 @@ extern "C" hxb_status_t hxb_decoder_block_w8a16(const hxb_decoder_w8_t* w, const
   __half* h2 = reinterpret_cast<__half*>(ws + b.h2);
   __half* gu = reinterpret_cast<__half*>(ws + b.gu);
   __half* a = reinterpret_cast<__half*>(ws + b.a);
-  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
 
   void* sk = b.sk_bytes ? ws + b.sk : nullptr;
   const size_t skb = b.sk_bytes;
+  const float scale = 1.0f / sqrtf((float)w->head_dim);
 
   if ((s = launch_rmsnorm(x, H, w->attn_norm, h, H, rows, H, w->rms_eps, stream,
                           static_cast<int*>(sk), sk ? w8_streamk_flag_ints() : 0)) != HXB_OK)
@@ -281,10 +357,21 @@ extern "C" hxb_status_t hxb_decoder_block_w8a16(const hxb_decoder_w8_t* w, const
   // q and k are the first 2 * heads heads of every qkv row
   if ((s = launch_rope(qkv, 3 * H, rows, 2 * w->heads, seq, pos0, w->rope_theta, stream)) != HXB_OK)
     return s;
-  if ((s = attention_launch(qkv, 3 * H, qkv + H, 3 * H, qkv + 2 * H, 3 * H, att, H, batch,
-                            w->heads, w->heads, seq, seq, w->head_dim,
-                            1.0f / sqrtf((float)w->head_dim), 1, stream)) != HXB_OK)
+  if (cache) {
+    if ((s = launch_kv_cache_write(qkv + H, qkv + 2 * H, 3 * H, cache->k, cache->v, batch,
+                                   w->heads, seq, pos0, cache->rows, w->head_dim, stream)) !=
+        HXB_OK)
+      return s;
+    if ((s = attention_cached_launch(qkv, 3 * H, cache->k, cache->v, cache->rows, att, H, batch,
+                                     w->heads, seq, pos0 + seq, pos0, w->head_dim, scale,
+                                     b.att_ws_bytes ? ws + b.att_ws : nullptr, b.att_ws_bytes,
+                                     stream)) != HXB_OK)
+      return s;
+  } else if ((s = attention_launch(qkv, 3 * H, qkv + H, 3 * H, qkv + 2 * H, 3 * H, att, H, batch,
+                                   w->heads, w->heads, seq, seq, w->head_dim, scale, 1,
+                                   stream)) != HXB_OK) {
     return s;
+  }
   if ((s = matmul_w8a16_impl(att, H, w->w_o, H, w->s_o, x, h2, H, rows, H, H, sk, skb, stream)) !=
       HXB_OK)
     return s;
@@ -294,4 +381,51 @@ extern "C" hxb_status_t hxb_decoder_block_w8a16(const hxb_decoder_w8_t* w, const
     return s;
   if ((s = launch_swiglu(gu, 2 * F, a, F, rows, F, stream)) != HXB_OK) return s;
   return matmul_w8a16_impl(a, F, w->w_down, H, w->s_down, h2, out, H, rows, H, F, sk, skb, stream);
+}
+
+}  // namespace
+}  // namespace hxb
+
+extern "C" size_t hxb_decoder_block_workspace_bytes(const hxb_decoder_w8_t* w, int64_t batch,
+                                                    int64_t seq) {
+  if (hxb::check_decoder(w, batch, seq) != HXB_OK) return 0;
+  return hxb::decoder_layout(w, batch * seq).total;
+}
+
+extern "C" hxb_status_t hxb_decoder_block_w8a16(const hxb_decoder_w8_t* w, const void* x,
+                                                void* out, int64_t batch, int64_t seq,
+                                                int64_t pos0, void* workspace,
+                                                size_t workspace_bytes, void* stream) {
+  return hxb::decoder_run(w, x, out, batch, seq, pos0, nullptr, workspace, workspace_bytes,
+                          static_cast<cudaStream_t>(stream));
+}
+
+extern "C" size_t hxb_decoder_block_cached_workspace_bytes(const hxb_decoder_w8_t* w,
+                                                           int64_t batch, int64_t seq) {
+  if (hxb::check_decoder(w, batch, seq) != HXB_OK) return 0;
+  return hxb::decoder_layout(w, batch * seq, seq).total;
+}
+
+extern "C" hxb_status_t hxb_decoder_block_w8a16_cached(const hxb_decoder_w8_t* w, const void* x,
+                                                       void* out, int64_t batch, int64_t seq,
+                                                       int64_t pos0, void* k_cache,
+                                                       void* v_cache, int64_t cache_rows,
+                                                       void* workspace, size_t workspace_bytes,
+                                                       void* stream) {
+  const hxb::KvCache c{k_cache, v_cache, cache_rows};
+  return hxb::decoder_run(w, x, out, batch, seq, pos0, &c, workspace, workspace_bytes,
+                          static_cast<cudaStream_t>(stream));
+}
+
+extern "C" hxb_status_t hxb_kv_cache_write_f16(const void* k_src, const void* v_src,
+                                               int64_t ld_src, void* k_cache, void* v_cache,
+                                               int64_t batch, int64_t kv_heads, int64_t n,
+                                               int64_t begin, int64_t cache_rows,
+                                               int64_t head_dim, void* stream) {
+  using namespace hxb;
+  hxb_status_t s = check_kv_cache_write(k_src, v_src, ld_src, k_cache, v_cache, batch, kv_heads,
+                                        n, begin, cache_rows, head_dim);
+  if (s != HXB_OK) return s;
+  return launch_kv_cache_write(k_src, v_src, ld_src, k_cache, v_cache, batch, kv_heads, n, begin,
+                               cache_rows, head_dim, static_cast<cudaStream_t>(stream));
 }

@@ -23,6 +23,9 @@ int attention_threads();
 
 namespace {
 
+// Leading bytes of the environment's scratch that hold the stream-K flags.
+constexpr uint64_t kScratchFlagBytes = 4096;
+
 // a * b (+ overflow check into *ok)
 uint64_t mulc(uint64_t a, uint64_t b, bool* ok) {
   if (a != 0 && b > UINT64_MAX / a) {
@@ -183,10 +186,18 @@ int dispatch_attention_gqa_f16(const hxb_executable_environment_t* env,
       (s = need(ds, 3, q_bytes, "attention_gqa_f16")) != HXB_OK)
     return s;
   void* const* p = ds->binding_ptrs;
+  // the key split's partials go to the device scratch past the stream-K
+  // flags, which they must not touch
+  char* ws = nullptr;
+  size_t ws_bytes = 0;
+  if (env->scratch && env->scratch_bytes > kScratchFlagBytes) {
+    ws = static_cast<char*>(env->scratch) + kScratchFlagBytes;
+    ws_bytes = env->scratch_bytes - kScratchFlagBytes;
+  }
   return hxb_attention_gqa_f16(p[0], p[1], p[2], p[3], (int64_t)B, (int64_t)Hq, (int64_t)Hkv,
                                (int64_t)q_len, (int64_t)q_pos0, (int64_t)kv_len,
-                               (int64_t)kv_rows, (int64_t)D, scale, c[8] != 0, (int)c[9],
-                               env->stream);
+                               (int64_t)kv_rows, (int64_t)D, scale, c[8] != 0, (int)c[9], ws,
+                               ws_bytes, env->stream);
 }
 
 // bindings: x, out, attn_norm, w_qkv, s_qkv, w_o, s_o, ffn_norm, w_gate_up,

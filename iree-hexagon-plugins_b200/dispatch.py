@@ -162,7 +162,8 @@ ATTN_OUT_LAYOUTS = {"bhsd": 0, "bshd": 1}
 def attention_gqa(query: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, *,
                   kv_len: int | None = None, scale: float | None = None, causal: bool = False,
                   q_pos0: int | None = None, out_layout: str = "bhsd",
-                  out: torch.Tensor | None = None) -> torch.Tensor:
+                  out: torch.Tensor | None = None,
+                  workspace: torch.Tensor | None | bool = True) -> torch.Tensor:
     """Grouped-query attention of `query` [B, Hq, q_len, D] over the first
     `kv_len` rows of `k_cache` / `v_cache` [B, Hkv, kv_rows, D]: query head h
     reads KV head h // (Hq // Hkv). The reference's SlicedCacheAttention
@@ -170,7 +171,10 @@ def attention_gqa(query: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Ten
     is attention_gqa(q, k, v, kv_len=context, out_layout="bshd").
     causal masks key j > q_pos0 + i for query i (q_pos0 = the cache position
     of the first query, by default kv_len - q_len).
-    out_layout "bhsd" gives [B, Hq, q_len, D], "bshd" [B, q_len, Hq, D]."""
+    out_layout "bhsd" gives [B, Hq, q_len, D], "bshd" [B, q_len, Hq, D].
+    workspace: a device tensor for the key split (see
+    attention_gqa_workspace_bytes), True to allocate one when the shape
+    splits, or None/False to run without the split."""
     lib = _native.load()
     _require(query.dtype == k_cache.dtype == v_cache.dtype == torch.float16,
              "query/k_cache/v_cache must be f16")
@@ -190,11 +194,24 @@ def attention_gqa(query: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Ten
         shape = (B, Hq, q_len, D) if out_layout == "bhsd" else (B, q_len, Hq, D)
         out = torch.empty(shape, dtype=torch.float16, device=query.device)
     _require(out.is_contiguous() and out.numel() == query.numel(), "out shape mismatch")
+    if workspace is True:
+        n = attention_gqa_workspace_bytes(B, Hq, Hkv, q_len, kv_len, D)
+        workspace = torch.empty(n, dtype=torch.uint8, device=query.device) if n else None
+    ws_ptr, ws_bytes = (workspace.data_ptr(), workspace.numel() * workspace.element_size()) \
+        if isinstance(workspace, torch.Tensor) else (None, 0)
     check(lib.hxb_attention_gqa_f16(query.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
                                     out.data_ptr(), B, Hq, Hkv, q_len, q_pos0, kv_len, kv_rows, D,
                                     float(scale), int(causal), ATTN_OUT_LAYOUTS[out_layout],
-                                    _stream_ptr(query)))
+                                    ws_ptr, ws_bytes, _stream_ptr(query)))
     return out
+
+
+def attention_gqa_workspace_bytes(batch: int, q_heads: int, kv_heads: int, q_len: int,
+                                  kv_len: int, head_dim: int) -> int:
+    """Bytes of the key-split workspace attention_gqa uses for this shape on
+    the current device (0: it does not split)."""
+    return int(_native.load().hxb_attention_gqa_workspace_bytes(batch, q_heads, kv_heads, q_len,
+                                                                kv_len, head_dim))
 
 
 def rmsnorm(x: torch.Tensor, gamma: torch.Tensor, eps: float = 1e-5,
@@ -269,6 +286,60 @@ class DecoderBlockW8:
                                           batch, seq, pos0, self._ws.data_ptr(),
                                           self._ws.numel(), _stream_ptr(x)))
         return out
+
+    def new_cache(self, batch: int, cache_rows: int, device=None) -> tuple[torch.Tensor, torch.Tensor]:
+        """Zeroed K and V caches [batch, heads, cache_rows, head_dim] f16 (the
+        registered buffers of the reference's SliceUpdateKvCache,
+        integration_tests/models/kv_cache.py:91-99)."""
+        d = self.desc
+        shape = (batch, d.heads, cache_rows, d.head_dim)
+        dev = device or self.tensors["w_qkv"].device
+        return (torch.zeros(shape, dtype=torch.float16, device=dev),
+                torch.zeros(shape, dtype=torch.float16, device=dev))
+
+    def step(self, x: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, *, pos0: int,
+             batch: int = 1, out: torch.Tensor | None = None) -> torch.Tensor:
+        """The block on x [batch * seq, hidden] at positions pos0 .. against a
+        KV cache: writes the new rows' K/V into the caches and attends to
+        cache rows [0, pos0 + seq) (hxb_decoder_block_w8a16_cached). A prompt
+        at pos0 = 0 is the prefill; one row per batch at pos0 = tokens so far
+        is a decode step."""
+        import ctypes
+        lib = _native.load()
+        rows = x.shape[0]
+        seq = rows // batch
+        _require(k_cache.shape == v_cache.shape and k_cache.dim() == 4 and
+                 k_cache.shape[0] == batch and k_cache.dtype == torch.float16 and
+                 k_cache.is_contiguous() and v_cache.is_contiguous(),
+                 "k_cache / v_cache must be contiguous f16 [batch, heads, rows, head_dim]")
+        need = lib.hxb_decoder_block_cached_workspace_bytes(ctypes.byref(self.desc), batch, seq)
+        _require(need > 0, "invalid decoder description")
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = torch.empty(need, dtype=torch.uint8, device=x.device)
+        if out is None:
+            out = torch.empty_like(x)
+        check(lib.hxb_decoder_block_w8a16_cached(
+            ctypes.byref(self.desc), x.data_ptr(), out.data_ptr(), batch, seq, pos0,
+            k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[2], self._ws.data_ptr(),
+            self._ws.numel(), _stream_ptr(x)))
+        return out
+
+
+def kv_cache_write(k_src: torch.Tensor, v_src: torch.Tensor, k_cache: torch.Tensor,
+                   v_cache: torch.Tensor, *, begin: int, batch: int = 1) -> None:
+    """k_cache[b, h, begin + t] = k_src[b * n + t, h*D:(h+1)*D] (and V), the
+    in-place cache update of SliceUpdateKvCache.update
+    (integration_tests/models/kv_cache.py:101-112). Sources are [batch * n,
+    >= heads * D] row-major views (unit inner stride), caches contiguous
+    [batch, heads, rows, D] f16."""
+    lib = _native.load()
+    _require(k_cache.shape == v_cache.shape and k_cache.dim() == 4 and
+             k_cache.is_contiguous() and v_cache.is_contiguous(), "bad cache tensors")
+    _require(k_src.stride() == v_src.stride(), "k_src / v_src must share a layout")
+    B, H, rows, D = k_cache.shape
+    check(lib.hxb_kv_cache_write_f16(k_src.data_ptr(), v_src.data_ptr(), _rowmajor_ld(k_src, "k_src"),
+                                     k_cache.data_ptr(), v_cache.data_ptr(), batch, H,
+                                     k_src.shape[0] // batch, begin, rows, D, _stream_ptr(k_src)))
 
 
 def device_status(clear: bool = True) -> int:

@@ -279,17 +279,48 @@ def attention_bshd_f16(qkv_or_q: np.ndarray, *, heads: int, seq: int, batch: int
                                 .reshape(batch * seq, HD))
 
 
+def kv_cache_write(k_src: np.ndarray, v_src: np.ndarray, k_cache: np.ndarray,
+                   v_cache: np.ndarray, *, begin: int, batch: int = 1) -> None:
+    """SliceUpdateKvCache.update (integration_tests/models/kv_cache.py:101-112)
+    on [batch * n, heads * D] source rows: cache[b, h, begin + t] = the head-h
+    columns of row b * n + t. Updates the caches in place."""
+    B, H, rows, D = k_cache.shape
+    n = k_src.shape[0] // batch
+    for src, cache in ((k_src, k_cache), (v_src, v_cache)):
+        cache[:, :, begin:begin + n] = (src[:, :H * D].reshape(batch, n, H, D)
+                                        .transpose(0, 2, 1, 3))
+
+
 def decoder_block_w8(x: np.ndarray, wt: dict, *, heads: int, batch: int = 1, pos0: int = 0,
-                     eps: float = 1e-5, theta: float = 10000.0) -> dict:
+                     eps: float = 1e-5, theta: float = 10000.0,
+                     k_cache: np.ndarray | None = None,
+                     v_cache: np.ndarray | None = None) -> dict:
     """Every intermediate of the decoder block for
     x [batch*seq, hidden] f16; wt holds attn_norm, w_qkv, s_qkv, w_o, s_o,
-    ffn_norm, w_gate_up, s_gate_up, w_down, s_down as numpy arrays."""
+    ffn_norm, w_gate_up, s_gate_up, w_down, s_down as numpy arrays. With
+    k_cache / v_cache ([batch, heads, rows, 128] f16, updated in place) the
+    rotated K and V of the new rows are written at rows pos0 .. and attention
+    reads keys [0, pos0 + seq) from the caches (kv_cache.py:101-112,
+    grouped_query_attention :46-86 with one query head per KV head)."""
     seq = x.shape[0] // batch
     r = {}
     r["h"] = rmsnorm_f16(x, wt["attn_norm"], eps)
     r["qkv_raw"] = linear_w8_f16(r["h"], wt["w_qkv"], wt["s_qkv"])
     r["qkv"] = rope_f16(r["qkv_raw"], 2 * heads, seq, pos0, theta)
-    r["att"] = attention_bshd_f16(r["qkv"], heads=heads, seq=seq, batch=batch)
+    if k_cache is None:
+        r["att"] = attention_bshd_f16(r["qkv"], heads=heads, seq=seq, batch=batch)
+    else:
+        HD = heads * 128
+        kv_cache_write(r["qkv"][:, HD:2 * HD], r["qkv"][:, 2 * HD:], k_cache, v_cache,
+                       begin=pos0, batch=batch)
+        kv_len = pos0 + seq
+        q = np.ascontiguousarray(r["qkv"][:, :HD].reshape(batch, seq, heads, 128)
+                                 .transpose(0, 2, 1, 3).reshape(batch * heads, seq, 128))
+        kk = np.ascontiguousarray(k_cache[:, :, :kv_len]).reshape(batch * heads, kv_len, 128)
+        vv = np.ascontiguousarray(v_cache[:, :, :kv_len]).reshape(batch * heads, kv_len, 128)
+        o = attention_f32(q, kk, vv, causal=True).astype(np.float16)
+        r["att"] = np.ascontiguousarray(o.reshape(batch, heads, seq, 128).transpose(0, 2, 1, 3)
+                                        .reshape(batch * seq, HD))
     r["h2"] = linear_w8_f16(r["att"], wt["w_o"], wt["s_o"], residual=x)
     r["n2"] = rmsnorm_f16(r["h2"], wt["ffn_norm"], eps)
     r["gu"] = linear_w8_f16(r["n2"], wt["w_gate_up"], wt["s_gate_up"])

@@ -190,3 +190,42 @@ def test_attention_gqa_rejects_bad_layouts(cuda_pkg):
     kv = torch.zeros(1, 3, 16, 64, dtype=torch.float16, device=DEV)
     with pytest.raises(cuda_pkg.HxbError, match="exceeds"):
         cuda_pkg.attention_gqa(q, kv, kv, kv_len=17)  # more keys than cache rows
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,q_len,q_pos0,kv_len,rows,D,causal", [
+    (1, 32, 8, 1, None, 4000, 4096, 128, False),  # decode, long cache: 8 heads x 16 splits
+    (4, 32, 8, 1, None, 8192, 8192, 128, True),   # batched decode
+    (1, 9, 3, 1, None, 700, 1024, 64, True),      # SmolLM2-like heads, D = 64
+    (1, 8, 8, 100, 0, 1000, 1024, 128, True),     # most splits see no visible key
+    (2, 28, 4, 4, None, 1500, 2048, 128, True),   # a 4-token step, group 7
+])
+def test_attention_gqa_split_keys(cuda_pkg, oracle, B, Hq, Hkv, q_len, q_pos0, kv_len, rows, D,
+                                  causal):
+    """Short queries against a long cache split the keys across SMs; the
+    merged result matches the oracle and the unsplit kernel."""
+    n = cuda_pkg.attention_gqa_workspace_bytes(B, Hq, Hkv, q_len, kv_len, D)
+    assert n > 0, "this shape is expected to split"
+    q, k, v = _gqa_inputs(B, Hq, Hkv, q_len, rows, D, seed=kv_len + q_len)
+    qd, kd, vd = (torch.from_numpy(x).to(DEV) for x in (q, k, v))
+    kw = dict(kv_len=kv_len, causal=causal, q_pos0=q_pos0)
+    ws = torch.empty(n, dtype=torch.uint8, device=DEV)
+    split = cuda_pkg.attention_gqa(qd, kd, vd, workspace=ws, **kw)
+    whole = cuda_pkg.attention_gqa(qd, kd, vd, workspace=None, **kw)
+    torch.cuda.synchronize()
+    split, whole = split.float().cpu().numpy(), whole.float().cpu().numpy()
+    want = oracle.attention_gqa_f32(q, k, v, round_scores=False, **kw)
+    baseline_check(want, split, f"split gqa {B}x{Hq}/{Hkv}x{q_len}x{kv_len}")
+    baseline_check(want, whole, f"unsplit gqa {B}x{Hq}/{Hkv}x{q_len}x{kv_len}")
+    assert np.abs(split - whole).max() < 4e-3
+    assert cuda_pkg.device_status() == 0
+
+
+def test_attention_gqa_workspace_query(cuda_pkg):
+    # long prefill fills the SMs by itself: no split, no workspace
+    assert cuda_pkg.attention_gqa_workspace_bytes(4, 32, 8, 2048, 2048, 128) == 0
+    # a single key block cannot split
+    assert cuda_pkg.attention_gqa_workspace_bytes(1, 32, 8, 1, 100, 128) == 0
+    assert cuda_pkg.attention_gqa_workspace_bytes(1, 9, 2, 1, 100, 64) == 0  # invalid heads
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    n = cuda_pkg.attention_gqa_workspace_bytes(1, 32, 8, 1, 4096, 128)
+    assert 0 < n <= (sms * 4 * 129 * 4 + 16)

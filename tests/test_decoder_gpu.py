@@ -163,3 +163,90 @@ def test_decoder_block_baseline_config4(cuda_pkg, oracle):
     rel = np.linalg.norm(d) / np.linalg.norm(ref.astype(np.float64))
     assert rel <= 2e-3, f"relative L2 {rel:.3g}"
     assert (d <= 2e-2 + 4 * f16_ulp(ref.astype(np.float32))).all(), f"max |d| {d.max():.4g}"
+
+
+# ------------------------------------------------------------- KV cache
+def test_kv_cache_write(cuda_pkg, oracle):
+    """SliceUpdateKvCache.update: the K and V column blocks of fused QKV rows
+    land in the caches at rows [begin, begin + n) of every batch and head;
+    every other row is untouched (bit-exact copy)."""
+    rng = np.random.default_rng(21)
+    batch, n, heads, rows, begin = 2, 37, 3, 96, 50
+    qkv = rng.standard_normal((batch * n, 3 * heads * 128)).astype(np.float16)
+    kc = rng.standard_normal((batch, heads, rows, 128)).astype(np.float16)
+    vc = rng.standard_normal((batch, heads, rows, 128)).astype(np.float16)
+    d, kd, vd = _t(qkv), _t(kc), _t(vc)
+    HD = heads * 128
+    cuda_pkg.kv_cache_write(d[:, HD:2 * HD], d[:, 2 * HD:], kd, vd, begin=begin, batch=batch)
+    oracle.kv_cache_write(qkv[:, HD:2 * HD], qkv[:, 2 * HD:], kc, vc, begin=begin, batch=batch)
+    torch.cuda.synchronize()
+    assert np.array_equal(kd.cpu().numpy(), kc) and np.array_equal(vd.cpu().numpy(), vc)
+    with pytest.raises(cuda_pkg.HxbError, match="exceed"):
+        cuda_pkg.kv_cache_write(d[:, HD:2 * HD], d[:, 2 * HD:], kd, vd, begin=60, batch=batch)
+
+
+def _block(cuda_pkg, wt, heads):
+    return cuda_pkg.DecoderBlockW8(heads=heads, **{k: _t(v) for k, v in wt.items()})
+
+
+@pytest.mark.parametrize("batch,S", [(1, 160), (2, 300)])
+def test_cached_prefill_equals_block(cuda_pkg, oracle, batch, S):
+    """A prefill through the KV cache (pos0 = 0, the whole prompt) gives the
+    uncached block's bits (the same GEMMs; attention reads the same K/V
+    values from the cache), and leaves the prompt's rotated K and V in it."""
+    rng = np.random.default_rng(22 + S)
+    hidden, heads, ffn, rows = 512, 4, 1376, 512
+    wt = _weights(rng, hidden, ffn, 2e-4, 8e-4, gamma_random=True)
+    x = rng.standard_normal((batch * S, hidden)).astype(np.float16)
+    blk = _block(cuda_pkg, wt, heads)
+    want = blk(_t(x), batch=batch)
+    kc, vc = blk.new_cache(batch, rows)
+    got = blk.step(_t(x), kc, vc, pos0=0, batch=batch)
+    torch.cuda.synchronize()
+    assert np.array_equal(got.cpu().numpy(), want.cpu().numpy())
+    ref = oracle.decoder_block_w8(x, wt, heads=heads, batch=batch)
+    HD = heads * 128
+    k_ref = ref["qkv"][:, HD:2 * HD].reshape(batch, S, heads, 128).transpose(0, 2, 1, 3)
+    v_ref = ref["qkv"][:, 2 * HD:].reshape(batch, S, heads, 128).transpose(0, 2, 1, 3)
+    kg, vg = kc.cpu().numpy(), vc.cpu().numpy()
+    assert not kg[:, :, S:].any() and not vg[:, :, S:].any()
+    # rotated K within the RoPE kernel's angle error, V within the GEMM's
+    assert np.abs(kg[:, :, :S].astype(np.float32) - k_ref).max() < 3e-2
+    assert np.abs(vg[:, :, :S].astype(np.float32) - v_ref).max() < 3e-2
+    assert cuda_pkg.device_status() == 0
+
+
+@pytest.mark.parametrize("batch,prompt,steps,hidden,heads,ffn",
+                         [(1, 300, 3, 512, 4, 1376), (2, 257, 2, 1024, 8, 2752)])
+def test_cached_decode_steps_vs_oracle(cuda_pkg, oracle, batch, prompt, steps, hidden, heads,
+                                       ffn):
+    """Prefill, then single-row decode steps against the cache (the keys
+    split across SMs), each compared with the oracle's cached block run on
+    its own copy of the cache."""
+    rng = np.random.default_rng(23 + prompt)
+    wt = _weights(rng, hidden, ffn, 2e-4, 8e-4, gamma_random=True)
+    rows = prompt + steps + 5
+    blk = _block(cuda_pkg, wt, heads)
+    kc, vc = blk.new_cache(batch, rows)
+    k_ref = np.zeros((batch, heads, rows, 128), np.float16)
+    v_ref = np.zeros_like(k_ref)
+    x = rng.standard_normal((batch * prompt, hidden)).astype(np.float16)
+    blk.step(_t(x), kc, vc, pos0=0, batch=batch)
+    oracle.decoder_block_w8(x, wt, heads=heads, batch=batch, k_cache=k_ref, v_cache=v_ref)
+    for i in range(steps):
+        xt = rng.standard_normal((batch, hidden)).astype(np.float16)
+        got = blk.step(_t(xt), kc, vc, pos0=prompt + i, batch=batch)
+        torch.cuda.synchronize()
+        ref = oracle.decoder_block_w8(xt, wt, heads=heads, batch=batch, pos0=prompt + i,
+                                      k_cache=k_ref, v_cache=v_ref)["out"]
+        g = got.cpu().numpy().astype(np.float64)
+        d = np.abs(g - ref.astype(np.float64))
+        rel = np.linalg.norm(d) / np.linalg.norm(ref.astype(np.float64))
+        assert np.isfinite(g).all()
+        assert rel <= 2e-3, f"step {i}: relative L2 {rel:.3g}"
+        assert (d <= 2e-2 + 4 * f16_ulp(ref.astype(np.float32))).all(), f"step {i}: {d.max():.4g}"
+    # the caches hold every row written so far and nothing past it
+    n = prompt + steps
+    assert not kc[:, :, n:].any() and not vc[:, :, n:].any()
+    assert np.abs(kc[:, :, :n].float().cpu().numpy() - k_ref[:, :, :n]).max() < 3e-2
+    assert cuda_pkg.device_status() == 0

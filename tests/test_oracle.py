@@ -215,3 +215,30 @@ def test_oracle_w8a16_vs_float64(oracle):
     got = oracle.matmul_w8a16_f32(a, w, s)
     want = a.astype(np.float64) @ (w.astype(np.float64) * s.astype(np.float64))
     assert np.abs(got - want).max() < 1e-3
+
+
+def test_oracle_cached_decoder_matches_uncached(oracle):
+    """The oracle's KV-cache block: a prefill of S rows then a decode step at
+    position S give the bits of the uncached block on S + 1 rows (the linears
+    and RoPE are row-wise, the attention row sees the same keys)."""
+    rng = np.random.default_rng(5)
+    hidden, heads, ffn, S = 256, 2, 512, 20
+
+    def s(n):
+        return rng.uniform(2e-4, 8e-4, n).astype(np.float16)
+    wt = {"attn_norm": np.ones(hidden, np.float16), "ffn_norm": np.ones(hidden, np.float16),
+          "w_qkv": rng.integers(-127, 128, (hidden, 3 * hidden), dtype=np.int8),
+          "s_qkv": s(3 * hidden),
+          "w_o": rng.integers(-127, 128, (hidden, hidden), dtype=np.int8), "s_o": s(hidden),
+          "w_gate_up": rng.integers(-127, 128, (hidden, 2 * ffn), dtype=np.int8),
+          "s_gate_up": s(2 * ffn),
+          "w_down": rng.integers(-127, 128, (ffn, hidden), dtype=np.int8), "s_down": s(hidden)}
+    x = rng.standard_normal((S + 1, hidden)).astype(np.float16)
+    full = oracle.decoder_block_w8(x, wt, heads=heads)["out"]
+    kc = np.zeros((1, heads, S + 4, 128), np.float16)
+    vc = np.zeros_like(kc)
+    pre = oracle.decoder_block_w8(x[:S], wt, heads=heads, k_cache=kc, v_cache=vc)["out"]
+    assert np.array_equal(pre, oracle.decoder_block_w8(x[:S], wt, heads=heads)["out"])
+    step = oracle.decoder_block_w8(x[S:], wt, heads=heads, pos0=S, k_cache=kc, v_cache=vc)["out"]
+    assert np.array_equal(step, full[S:])
+    assert not kc[:, :, S + 1:].any()
