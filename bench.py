@@ -212,8 +212,10 @@ def _spec_gemv(m):
              for _ in range(sets)]
         s = (torch.rand(N, device=dev, generator=g) * 0.019 + 0.001).half()
         c = torch.empty(m, N, dtype=torch.float16, device=dev)
-        return {"step": lambda i: pkg.matmul_w8a16(a, w[i % sets], s, out=c), "in": a, "out": c,
-                "sets": sets}
+        # with the stream-K workspace the dispatch spreads W over every SM
+        ws = pkg.w8a16_workspace(dev)
+        return {"step": lambda i: pkg.matmul_w8a16(a, w[i % sets], s, out=c, workspace=ws),
+                "in": a, "out": c, "sets": sets}
     return make
 
 
@@ -248,6 +250,60 @@ def _spec_decoder(torch, pkg, dev):
     return {"step": lambda i: blk(x, out=out), "in": x, "out": out, "sets": 1}
 
 
+GQA_B, GQA_HQ, GQA_HKV, GQA_CTX, GQA_D = 4, 32, 8, 8192, 128
+
+
+def _spec_gqa_decode(torch, pkg, dev):
+    """One decode step of grouped-query attention (32 query heads over 8 KV
+    heads, head dim 128) for 4 sequences against an 8192-row KV cache: the
+    keys are split across the SMs and merged."""
+    sets = 2  # 2 x 134 MB of K/V cache
+    g = torch.Generator(device=dev).manual_seed(0)
+    q = torch.randn(GQA_B, GQA_HQ, 1, GQA_D, device=dev, generator=g).half()
+    kv = [[torch.randn(GQA_B, GQA_HKV, GQA_CTX, GQA_D, device=dev, generator=g).half()
+           for _ in range(2)] for _ in range(sets)]
+    o = torch.empty(GQA_B, 1, GQA_HQ, GQA_D, dtype=torch.float16, device=dev)
+    n = pkg.attention_gqa_workspace_bytes(GQA_B, GQA_HQ, GQA_HKV, 1, GQA_CTX, GQA_D)
+    ws = torch.empty(max(n, 16), dtype=torch.uint8, device=dev)
+    return {"step": lambda i: pkg.attention_gqa(q, kv[i % sets][0], kv[i % sets][1],
+                                                out_layout="bshd", out=o, workspace=ws),
+            "in": q, "out": o, "sets": sets}
+
+
+DEC_CTX = 2048  # tokens in the cache before the decode step
+
+
+def _spec_decoder_decode(torch, pkg, dev):
+    """One decode step of the configuration-4 block against a KV cache of
+    2048 tokens (one new token, batch 1): GEMVs over 202 MB of int8 weights,
+    the cache write and split-key attention over 33.6 MB of K/V."""
+    H, F, NH = 4096, 11008, 32
+    g = torch.Generator(device=dev).manual_seed(0)
+
+    def w8(k, n):
+        return torch.randint(-127, 128, (k, n), device=dev, dtype=torch.int8, generator=g)
+
+    def sc(n):
+        return (torch.rand(n, device=dev, generator=g) * 2.5e-4 + 1.5e-4).half()
+    ones = torch.ones(H, device=dev, dtype=torch.float16)
+    blk = pkg.DecoderBlockW8(heads=NH, attn_norm=ones, ffn_norm=ones.clone(),
+                             w_qkv=w8(H, 3 * H), s_qkv=sc(3 * H), w_o=w8(H, H), s_o=sc(H),
+                             w_gate_up=w8(H, 2 * F), s_gate_up=sc(2 * F), w_down=w8(F, H),
+                             s_down=sc(H))
+    kc, vc = blk.new_cache(1, DEC_CTX + 64)
+    kc.normal_(generator=g)
+    vc.normal_(generator=g)
+    x = torch.randn(1, H, device=dev, generator=g).half()
+    out = torch.empty_like(x)
+    # the step rewrites cache row DEC_CTX each time and attends to rows
+    # [0, DEC_CTX]; weights and cache (236 MB) exceed the L2
+    return {"step": lambda i: blk.step(x, kc, vc, pos0=DEC_CTX, out=out), "in": x, "out": out,
+            "sets": 1}
+
+
+_W8_DEC_BYTES = 4096 * (3 * 4096 + 4096 + 2 * 11008) + 11008 * 4096
+_SC_DEC_BYTES = 2 * (3 * 4096 + 4096 + 2 * 11008 + 4096)
+
 SPECS = {
     "f16_gemm_1024": {
         "make": _spec_f16_gemm, "flop": 2.0 * 1024 ** 3, "bound": "tensor",
@@ -256,12 +312,12 @@ SPECS = {
                    "inputs": "A, B ~ U[-1, 1] f16, f16 out"}},
     "gemv_w8_m1": {
         "make": _spec_gemv(1), "bytes": 4096 * 11008 + 2 * 4096 + 2 * 11008 + 2 * 11008,
-        "flop": 2.0 * 4096 * 11008, "bound": "hbm", "kernel": "gemv_w8_kernel",
+        "flop": 2.0 * 4096 * 11008, "bound": "hbm", "kernel": "gemv_w8_sk_kernel",
         "dtype": "f16xi8->f32",
         "config": {"workload": "w8a16_gemv_1x4096x11008", "cfg": "2b"}},
     "gemv_w8_m16": {
         "make": _spec_gemv(16), "bytes": 4096 * 11008 + 2 * 16 * 4096 + 2 * 11008 + 2 * 16 * 11008,
-        "flop": 2.0 * 16 * 4096 * 11008, "bound": "hbm", "kernel": "gemv_w8_kernel",
+        "flop": 2.0 * 16 * 4096 * 11008, "bound": "hbm", "kernel": "gemv_w8_sk_kernel",
         "dtype": "f16xi8->f32",
         "config": {"workload": "w8a16_gemv_16x4096x11008", "cfg": "2b"}},
     "attention": {
@@ -275,6 +331,23 @@ SPECS = {
         "dtype": "f16xi8->f32",
         "config": {"workload": "llama_decoder_block_w8_s512", "cfg": 4,
                    "scales": "U[1.5e-4, 4e-4] (int8 of a 0.02-std init)"}},
+    "gqa_decode": {
+        "make": _spec_gqa_decode,
+        "bytes": 2 * GQA_B * GQA_HKV * GQA_CTX * GQA_D * 2 + 2 * 2 * GQA_B * GQA_HQ * GQA_D,
+        "flop": 4.0 * GQA_B * GQA_HQ * GQA_CTX * GQA_D, "bound": "hbm",
+        "kernel": "attention_fwd_kernel (split keys) + attention_combine_kernel", "launches": 2,
+        "dtype": "f16->f32",
+        "config": {"workload": "gqa_decode_b4_32q8kv_ctx8192_d128", "cfg": "f3",
+                   "shape": "q [4, 32, 1, 128], K/V cache [4, 8, 8192, 128], out [4, 1, 32, 128]"}},
+    "decoder_decode": {
+        "make": _spec_decoder_decode,
+        "bytes": _W8_DEC_BYTES + _SC_DEC_BYTES + 2 * 32 * (DEC_CTX + 1) * 128 * 2,
+        "flop": 2.0 * _W8_DEC_BYTES + 4.0 * 32 * (DEC_CTX + 1) * 128, "bound": "hbm",
+        "kernel": "gemv_w8_sk_kernel (+ split-key attention, norms)", "launches": 11,
+        "dtype": "f16xi8->f32",
+        "config": {"workload": "llama_decoder_block_w8_decode_ctx2048", "cfg": "4+f3",
+                   "scales": "U[1.5e-4, 4e-4] (int8 of a 0.02-std init)",
+                   "bytes": "int8 weights + scales + K/V rows [0, 2048] read"}},
 }
 
 

@@ -3,6 +3,7 @@
 
 #include "gemm_sm100.cuh"
 #include "gemm_w8_sm100.cuh"
+#include "gemv_w8_sk_sm100.cuh"
 #include "gemv_w8_sm100.cuh"
 #include "planner.h"
 #include "runtime_common.h"
@@ -240,6 +241,66 @@ hxb_status_t gemv_w8_impl(const void* A, int64_t lda, const void* W, int64_t ldw
   return M <= 8 ? launch_gemv<8>(*dev, p, stream) : launch_gemv<16>(*dev, p, stream);
 }
 
+// M <= 16 over every SM (gemv_w8_sk_sm100.cuh), with the stream-K workspace
+// for the cross-SM partial sums. Returns HXB_STATUS_UNSUPPORTED (nothing
+// launched) when the workspace is missing or too small.
+hxb_status_t gemv_w8_sk_impl(const void* A, int64_t lda, const void* W, int64_t ldw,
+                             const void* scale, const void* R, void* C, int64_t ldc, int64_t M,
+                             int64_t N, int64_t K, void* ws, size_t ws_bytes,
+                             cudaStream_t stream) {
+  DeviceInfo* dev = nullptr;
+  hxb_status_t s = current_device(&dev);
+  if (s != HXB_OK) return s;
+  const int64_t strips = (N + kGsBN - 1) / kGsBN, kc = (K + kGsBK - 1) / kGsBK;
+  const int64_t tiles = strips * kc;
+  const int ctas = (int)(tiles < dev->num_sms ? tiles : dev->num_sms);
+  if (!ws || !aligned16(ws) || tiles > INT32_MAX / 1024 || ctas > (int)(kW8FlagBytes / 4) ||
+      ws_bytes < kW8FlagBytes + (size_t)ctas * kGsPartialFloats * sizeof(float))
+    return HXB_STATUS_UNSUPPORTED;
+  CUtensorMap tmW, tmX;
+  {
+    const uint64_t dims[2] = {(uint64_t)N, (uint64_t)K};
+    const uint64_t strides[1] = {(uint64_t)ldw};
+    const uint32_t box[2] = {128, kGsBK};
+    if ((s = encode_tensor_map(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, W, dims, strides, box,
+                               CU_TENSOR_MAP_SWIZZLE_128B)) != HXB_OK)
+      return s;
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
+    const uint64_t strides[1] = {(uint64_t)lda * 2};
+    const uint32_t box[2] = {kGsBK, 16};
+    if ((s = encode_tensor_map(&tmX, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, A, dims, strides, box,
+                               CU_TENSOR_MAP_SWIZZLE_128B)) != HXB_OK)
+      return s;
+  }
+  GsArgs g{};
+  g.scale = static_cast<const __half*>(scale);
+  g.C = static_cast<__half*>(C);
+  g.R = static_cast<const __half*>(R);
+  g.ldc = ldc;
+  g.M = (int)M;
+  g.N = (int)N;
+  g.K = (int)K;
+  g.kc = (int)kc;
+  g.tiles = (int)tiles;
+  g.ctas = ctas;
+  g.flags = static_cast<int*>(ws);
+  g.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kW8FlagBytes);
+  g.status = dev->status_word;
+  auto kernel = M <= 8 ? gemv_w8_sk_kernel<1> : gemv_w8_sk_kernel<2>;
+  static bool configured[2][64] = {};
+  bool& done = configured[M <= 8 ? 0 : 1][dev->ordinal];
+  if (!done) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         GsSmem::kAlloc);
+    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(gemv_w8_sk)");
+    done = true;
+  }
+  kernel<<<ctas, kGsThreads, GsSmem::kAlloc, stream>>>(tmW, tmX, g);
+  return cuda_status(cudaGetLastError(), "gemv_w8_sk launch");
+}
+
 // Largest dynamic shared memory (bytes) and threads per CTA of the f16 GEMM
 // and the int8-weight matmul kernels (the executable library's export
 // attributes).
@@ -251,7 +312,10 @@ size_t gemm_f16_max_smem_bytes() {
 }
 int gemm_f16_threads() { return GemmShape<256, kBF16RowMajorKN>::kThreads; }
 size_t w8_max_smem_bytes() {
-  return W8Smem::kAlloc > GemvSmem::kBytes ? (size_t)W8Smem::kAlloc : (size_t)GemvSmem::kBytes;
+  size_t m = W8Smem::kAlloc;
+  if ((size_t)GemvSmem::kBytes > m) m = GemvSmem::kBytes;
+  if ((size_t)GsSmem::kAlloc > m) m = GsSmem::kAlloc;
+  return m;
 }
 int w8_threads() { return kW8Threads; }
 
@@ -390,7 +454,14 @@ hxb_status_t matmul_w8a16_impl(const void* A, int64_t lda, const void* W, int64_
     return fail(HXB_STATUS_INVALID_ARGUMENT,
                 "matmul_w8a16: A/W/C/scale/R must be 16-byte aligned with lda%%8 == 0, "
                 "ldw%%16 == 0, ldc%%8 == 0");
-  if (M <= kGemvRows) return gemv_w8_impl(A, lda, W, ldw, scale, R, C, ldc, M, N, K, stream);
+  if (M <= kGemvRows) {
+    if (sk_ws) {
+      const hxb_status_t s =
+          gemv_w8_sk_impl(A, lda, W, ldw, scale, R, C, ldc, M, N, K, sk_ws, sk_ws_bytes, stream);
+      if (s != HXB_STATUS_UNSUPPORTED) return s;
+    }
+    return gemv_w8_impl(A, lda, W, ldw, scale, R, C, ldc, M, N, K, stream);
+  }
   if (sk_ws && !aligned16(sk_ws))
     return fail(HXB_STATUS_INVALID_ARGUMENT, "matmul_w8a16: workspace must be 16-byte aligned");
   return gemm_w8_impl(A, lda, W, ldw, scale, R, C, ldc, M, N, K, sk_ws, sk_ws_bytes, stream);

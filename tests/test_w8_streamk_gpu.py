@@ -117,3 +117,55 @@ def test_streamk_rejects_missing_workspace(cuda_pkg):
                                       torch.cuda.current_stream().cuda_stream)
     assert rc != 0
     assert b"workspace" in lib.hxb_last_error_message()
+
+
+@pytest.mark.parametrize("M,K,N,res", [
+    (1, 4096, 11008, False),   # BASELINE configuration 2b, M = 1: 43 strips x 64 k tiles
+    (16, 4096, 11008, True),   # M = 16, the decoder residual form
+    (5, 1000, 1104, True),     # ragged K (a zero-filled tail tile), N not a strip multiple
+    (9, 64, 16, False),        # one tile: a single SM, no partial sums
+    (8, 8192, 272, False),     # 2 strips x 128 k tiles over every SM: many contributors
+    (12, 11008, 4096, True),   # decoder down projection at decode batch 12
+])
+def test_gemv_all_sms_vs_oracle(cuda_pkg, oracle, M, K, N, res):
+    """M <= 16 with the workspace: the GEMV that spreads the weight tiles over
+    every SM and adds the partial sums of strips shared between SMs."""
+    a, w, s, r = _inputs(M, K, N, seed=M * 11 + N + K)
+    ws = cuda_pkg.w8a16_workspace(DEV)
+    ad, wd, sd, rd = _t(a), _t(w), _t(s), _t(r)
+    got = cuda_pkg.matmul_w8a16(ad, wd, sd, residual=rd if res else None, workspace=ws)
+    again = cuda_pkg.matmul_w8a16(ad, wd, sd, residual=rd if res else None, workspace=ws)
+    plain = cuda_pkg.matmul_w8a16(ad, wd, sd, residual=rd if res else None)
+    torch.cuda.synchronize()
+    assert cuda_pkg.device_status() == 0
+    assert int(ws[:FLAG_BYTES].count_nonzero()) == 0
+    assert torch.equal(got, again)
+    ref = oracle.matmul_w8a16_f32(a, w, s)
+    if res:
+        ref = ref + r.astype(np.float32)
+    baseline_check(ref, got.float().cpu().numpy(), f"gemv all-SM {M}x{K}x{N}")
+    baseline_check(ref, plain.float().cpu().numpy(), f"gemv strip-per-SM {M}x{K}x{N}")
+
+
+def test_gemv_all_sms_graph_replay(cuda_pkg):
+    """Flags left zero by every launch: replays of a captured graph agree."""
+    a, w, s, _ = _inputs(1, 4096, 11008, seed=5)
+    ws = cuda_pkg.w8a16_workspace(DEV)
+    ad, wd, sd = _t(a), _t(w), _t(s)
+    out = torch.empty(1, 11008, dtype=torch.float16, device=DEV)
+    cuda_pkg.matmul_w8a16(ad, wd, sd, workspace=ws, out=out)
+    torch.cuda.synchronize()
+    first = out.clone()
+    g = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(g):
+            for _ in range(3):
+                cuda_pkg.matmul_w8a16(ad, wd, sd, workspace=ws, out=out)
+    for _ in range(5):
+        out.zero_()
+        g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, first)
+    assert int(ws[:FLAG_BYTES].count_nonzero()) == 0
+    assert cuda_pkg.device_status() == 0
