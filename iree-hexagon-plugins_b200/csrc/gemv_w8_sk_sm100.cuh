@@ -265,15 +265,38 @@ __global__ void __launch_bounds__(kGsThreads, 1)
   bool ok = true;
 
   // C = acc * scale (+ R) for strip s; D rows g / g + 8 are columns n0 /
-  // n0 + 1, columns 2 tq / 2 tq + 1 are activation rows
-  auto epilogue = [&](const float (&v)[2][MT][4], int s) {
+  // n0 + 1, columns 2 tq / 2 tq + 1 are activation rows. The scale and
+  // residual operands are loaded first (epi_load), so the finisher of a
+  // shared strip has them in registers before it waits for the partials.
+  struct EpiIn {
+    float sc[2][2];         // [chunk][column n0, n0 + 1]
+    float r[2][MT][2][2];   // [chunk][mt][e][column]
+  };
+  auto epi_load = [&](int s, EpiIn& in) {
+#pragma unroll
+    for (int ch = 0; ch < 2; ++ch) {
+      const int n0 = s * kGsBN + 32 * cw + 16 * ch + 2 * g;
+      const bool one = n0 < a.N, two = n0 + 1 < a.N;
+      in.sc[ch][0] = one ? __half2float(a.scale[n0]) : 0.0f;
+      in.sc[ch][1] = two ? __half2float(a.scale[n0 + 1]) : 0.0f;
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int m = 8 * mt + 2 * tq + e;
+          const long long off = (long long)m * a.ldc + n0;
+          const bool row = m < a.M && a.R;
+          in.r[ch][mt][e][0] = row && one ? __half2float(a.R[off]) : 0.0f;
+          in.r[ch][mt][e][1] = row && two ? __half2float(a.R[off + 1]) : 0.0f;
+        }
+    }
+  };
+  auto epi_store = [&](const float (&v)[2][MT][4], int s, const EpiIn& in) {
 #pragma unroll
     for (int ch = 0; ch < 2; ++ch) {
       const int n0 = s * kGsBN + 32 * cw + 16 * ch + 2 * g;
       if (n0 >= a.N) continue;
       const bool two = n0 + 1 < a.N;
-      const float s0 = __half2float(a.scale[n0]);
-      const float s1 = two ? __half2float(a.scale[n0 + 1]) : 0.0f;
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
@@ -281,11 +304,8 @@ __global__ void __launch_bounds__(kGsThreads, 1)
           const int m = 8 * mt + 2 * tq + e;
           if (m >= a.M) continue;
           const long long off = (long long)m * a.ldc + n0;
-          float v0 = v[ch][mt][e] * s0, v1 = v[ch][mt][2 + e] * s1;
-          if (a.R) {
-            v0 += __half2float(a.R[off]);
-            if (two) v1 += __half2float(a.R[off + 1]);
-          }
+          const float v0 = fmaf(v[ch][mt][e], in.sc[ch][0], in.r[ch][mt][e][0]);
+          const float v1 = fmaf(v[ch][mt][2 + e], in.sc[ch][1], in.r[ch][mt][e][1]);
           if (two && (off & 1) == 0) {
             *reinterpret_cast<__half2*>(a.C + off) = __floats2half2_rn(v0, v1);
           } else {
@@ -357,7 +377,9 @@ __global__ void __launch_bounds__(kGsThreads, 1)
       __syncwarp();
       if (lane == 0) red_or_release_gpu(a.flags + b, bit);
     } else if (j == a.kc - 1) {
-      epilogue(acc, s);  // a whole strip inside this run
+      EpiIn in;  // a whole strip inside this run
+      epi_load(s, in);
+      epi_store(acc, s, in);
     } else {
 #pragma unroll
       for (int ch = 0; ch < 2; ++ch)
@@ -370,6 +392,8 @@ __global__ void __launch_bounds__(kGsThreads, 1)
     clear();
   }
   if (!ok || held_s < 0) return;
+  EpiIn held_in;
+  epi_load(held_s, held_in);
 
   // finisher of strip held_s: add the partials of the SMs holding the rest of
   // it. The flags of up to 32 contributors are polled at once (lane i polls
@@ -413,7 +437,7 @@ __global__ void __launch_bounds__(kGsThreads, 1)
     __syncwarp();
     if (lane < nc) atomicAnd(a.flags + c0 + lane, ~bit);
   }
-  epilogue(held, held_s);
+  epi_store(held, held_s, held_in);
 }
 
 }  // namespace hxb
