@@ -217,6 +217,10 @@ __global__ void __launch_bounds__(kAttThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  // the set-up above overlaps the previous kernel of the stream; Q/K/V and O
+  // are touched only after it has finished
+  pdl_trigger();
+  pdl_wait();
 
   if (warp == 0) {
     // -------------------------------------------------------- TMA producer
@@ -475,6 +479,8 @@ __global__ void __launch_bounds__(kAttThreads, 1)
 template <int D>
 __global__ void __launch_bounds__(256)
     attention_combine_kernel(const AttArgs args, int heads) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int kPer = D / 32;  // O elements per lane
   const long long gw = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -591,13 +597,12 @@ hxb_status_t launch_d(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUte
     configured[ordinal] = true;
   }
   const int64_t ctas = heads * args.q_blocks * args.kv_splits;
-  attention_fwd_kernel<D><<<(unsigned)ctas, kAttThreads, AttSmem<D>::kAlloc, stream>>>(
-      tmQ, tmK, tmV, args);
-  hxb_status_t s = cuda_status(cudaGetLastError(), "attention launch");
+  hxb_status_t s = launch_pdl(attention_fwd_kernel<D>, dim3((unsigned)ctas), dim3(kAttThreads),
+                              AttSmem<D>::kAlloc, stream, "attention launch", tmQ, tmK, tmV, args);
   if (s != HXB_OK || args.kv_splits == 1) return s;
   const int64_t warps = heads * args.Sq;
-  attention_combine_kernel<D><<<(unsigned)((warps + 7) / 8), 256, 0, stream>>>(args, (int)heads);
-  return cuda_status(cudaGetLastError(), "attention combine launch");
+  return launch_pdl(attention_combine_kernel<D>, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0,
+                    stream, "attention combine launch", args, (int)heads);
 }
 
 hxb_status_t attention_run(const AttLayout& a, float scale, int causal, cudaStream_t stream) {

@@ -54,6 +54,8 @@ __global__ void rmsnorm_kernel(const __half* __restrict__ x, long long ldx,
                                const __half* __restrict__ gamma, __half* __restrict__ y,
                                long long ldy, int rows, int cols, float eps, int* clear,
                                int nclear) {
+  pdl_wait();
+  pdl_trigger();
   if (clear && blockIdx.x == 0)
     for (int i = threadIdx.x; i < nclear; i += blockDim.x) clear[i] = 0;
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -97,6 +99,8 @@ __global__ void rmsnorm_kernel(const __half* __restrict__ x, long long ldx,
 // (i + 32, i + 96). Row r has position pos0 + r % seq.
 __global__ void rope_kernel(__half* __restrict__ x, long long ldx, int rows, int heads, int seq,
                             int pos0, float log2_theta) {
+  pdl_wait();
+  pdl_trigger();
   const int wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (wid >= rows * heads) return;
@@ -118,6 +122,8 @@ __global__ void rope_kernel(__half* __restrict__ x, long long ldx, int rows, int
 // a[r, j] = silu(gu[r, j]) * gu[r, F + j], 8 columns per thread (F % 8 == 0).
 __global__ void swiglu_kernel(const __half* __restrict__ gu, long long ldgu, __half* __restrict__ a,
                               long long lda, int rows, int F) {
+  pdl_wait();
+  pdl_trigger();
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   const int per_row = F / 8;
   if (idx >= (long long)rows * per_row) return;
@@ -145,6 +151,8 @@ __global__ void kv_cache_write_kernel(const __half* __restrict__ k_src,
                                       __half* __restrict__ k_cache, __half* __restrict__ v_cache,
                                       int n, int heads, int D, int begin, long long cache_rows,
                                       long long vectors) {
+  pdl_wait();
+  pdl_trigger();
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= vectors) return;
   const __half* src = blockIdx.y ? v_src : k_src;
@@ -165,11 +173,11 @@ hxb_status_t launch_kv_cache_write(const void* k_src, const void* v_src, int64_t
   const long long vectors = (long long)batch * n * heads * D / 8;
   const int threads = 256;
   const dim3 grid((unsigned)((vectors + threads - 1) / threads), 2);
-  kv_cache_write_kernel<<<grid, threads, 0, stream>>>(
-      static_cast<const __half*>(k_src), static_cast<const __half*>(v_src), ld_src,
-      static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), (int)n, (int)heads, (int)D,
-      (int)begin, cache_rows, vectors);
-  return cuda_status(cudaGetLastError(), "kv cache write launch");
+  return launch_pdl(kv_cache_write_kernel, grid, dim3(threads), 0, stream,
+                    "kv cache write launch", static_cast<const __half*>(k_src),
+                    static_cast<const __half*>(v_src), (long long)ld_src,
+                    static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), (int)n,
+                    (int)heads, (int)D, (int)begin, (long long)cache_rows, vectors);
 }
 
 hxb_status_t check_kv_cache_write(const void* k_src, const void* v_src, int64_t ld_src,
@@ -199,30 +207,28 @@ hxb_status_t launch_rmsnorm(const void* x, int64_t ldx, const void* gamma, void*
                             int* clear = nullptr, int nclear = 0) {
   const int threads = 256;
   const long long blocks = (rows * 32 + threads - 1) / threads;
-  rmsnorm_kernel<<<(unsigned)blocks, threads, 0, stream>>>(
-      static_cast<const __half*>(x), ldx, static_cast<const __half*>(gamma),
-      static_cast<__half*>(y), ldy, (int)rows, (int)cols, eps, clear, nclear);
-  return cuda_status(cudaGetLastError(), "rmsnorm launch");
+  return launch_pdl(rmsnorm_kernel, dim3((unsigned)blocks), dim3(threads), 0, stream,
+                    "rmsnorm launch", static_cast<const __half*>(x), (long long)ldx,
+                    static_cast<const __half*>(gamma), static_cast<__half*>(y), (long long)ldy,
+                    (int)rows, (int)cols, eps, clear, nclear);
 }
 
 hxb_status_t launch_rope(void* x, int64_t ldx, int64_t rows, int64_t heads, int64_t seq,
                          int64_t pos0, float theta, cudaStream_t stream) {
   const int threads = 256;
   const long long blocks = (rows * heads * 32 + threads - 1) / threads;
-  rope_kernel<<<(unsigned)blocks, threads, 0, stream>>>(static_cast<__half*>(x), ldx, (int)rows,
-                                                        (int)heads, (int)seq, (int)pos0,
-                                                        log2f(theta));
-  return cuda_status(cudaGetLastError(), "rope launch");
+  return launch_pdl(rope_kernel, dim3((unsigned)blocks), dim3(threads), 0, stream, "rope launch",
+                    static_cast<__half*>(x), (long long)ldx, (int)rows, (int)heads, (int)seq,
+                    (int)pos0, log2f(theta));
 }
 
 hxb_status_t launch_swiglu(const void* gu, int64_t ldgu, void* a, int64_t lda, int64_t rows,
                            int64_t F, cudaStream_t stream) {
   const int threads = 256;
   const long long blocks = (rows * (F / 8) + threads - 1) / threads;
-  swiglu_kernel<<<(unsigned)blocks, threads, 0, stream>>>(static_cast<const __half*>(gu), ldgu,
-                                                          static_cast<__half*>(a), lda, (int)rows,
-                                                          (int)F);
-  return cuda_status(cudaGetLastError(), "swiglu launch");
+  return launch_pdl(swiglu_kernel, dim3((unsigned)blocks), dim3(threads), 0, stream,
+                    "swiglu launch", static_cast<const __half*>(gu), (long long)ldgu,
+                    static_cast<__half*>(a), (long long)lda, (int)rows, (int)F);
 }
 
 size_t round256(size_t b) { return (b + 255) & ~size_t(255); }

@@ -297,8 +297,8 @@ hxb_status_t gemv_w8_sk_impl(const void* A, int64_t lda, const void* W, int64_t 
     if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(gemv_w8_sk)");
     done = true;
   }
-  kernel<<<ctas, kGsThreads, GsSmem::kAlloc, stream>>>(tmW, tmX, g);
-  return cuda_status(cudaGetLastError(), "gemv_w8_sk launch");
+  return launch_pdl(kernel, dim3(ctas), dim3(kGsThreads), GsSmem::kAlloc, stream,
+                    "gemv_w8_sk launch", tmW, tmX, g);
 }
 
 // Largest dynamic shared memory (bytes) and threads per CTA of the f16 GEMM

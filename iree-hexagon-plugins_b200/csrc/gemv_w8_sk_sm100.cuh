@@ -180,15 +180,32 @@ __global__ void __launch_bounds__(kGsThreads, 1)
     fence_mbar_init();
   }
   __syncthreads();
+  pdl_trigger();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       tma_prefetch_desc(&tmW);
       tma_prefetch_desc(&tmX);
-      int stage = 0, issued = 0;
-      uint32_t phase = 0;
-      for (int i = 0; i < n; ++i) {
+      // The weights of the first stages are requested before waiting for the
+      // previous kernel of the stream (no dispatch of this library writes
+      // int8 weights); the activations, which that kernel may produce, after.
+      const int pre = min(n, kGsStages);
+      for (int i = 0; i < pre; ++i) {
+        const int u = order.tile(i);
+        const int s = u / a.kc, j = u - s * a.kc;
+        uint8_t* st = smem + i * kGsStageBytes;
+        mbar_arrive_expect_tx(&full[i], kGsStageBytes);
+        tma_load_2d(st, &tmW, &full[i], s * kGsBN, j * kGsBK);
+        tma_load_2d(st + kGsWBox, &tmW, &full[i], s * kGsBN + 128, j * kGsBK);
+      }
+      pdl_wait();
+      for (int i = 0; i < pre; ++i)
+        tma_load_2d(smem + i * kGsStageBytes + 2 * kGsWBox, &tmX, &full[i],
+                    order.tile(i) % a.kc * kGsBK, 0);
+      int stage = pre % kGsStages, issued = pre;
+      uint32_t phase = pre == kGsStages ? 1u : 0u;
+      for (int i = pre; i < n; ++i) {
         if (!mbar_wait(&empty[stage], phase ^ 1, fs)) break;
         const int u = order.tile(i);
         const int s = u / a.kc, j = u - s * a.kc;

@@ -17,6 +17,25 @@ namespace hxb {
 hxb_status_t cuda_status(cudaError_t e, const char* where);
 hxb_status_t fail(hxb_status_t code, const char* fmt, ...);
 
+// Launches `kernel` with programmatic stream serialization: it may start while
+// the previous kernel of `stream` runs, and must order its dependent accesses
+// with pdl_wait() (sm100.cuh).
+template <typename... KArgs, typename... Args>
+hxb_status_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                        cudaStream_t stream, const char* what, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...), what);
+}
+
 struct DeviceInfo {
   int ordinal;
   int num_sms;

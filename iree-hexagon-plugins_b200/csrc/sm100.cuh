@@ -33,6 +33,19 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
   return t;
 }
 
+// ------------------------------------------- programmatic dependent launch
+// A kernel launched with launch_pdl (programmatic stream serialization) may be
+// scheduled while the kernel before it in the stream still runs. It must call
+// pdl_wait() before it reads anything that kernel (or any earlier one) writes,
+// or writes anything they read; pdl_wait() returns once they have completed
+// and their memory is visible. pdl_trigger() lets the next such kernel be
+// scheduled as soon as every CTA of this grid has called it or exited; it
+// does not let that kernel pass its own pdl_wait() before this grid ends.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)),
