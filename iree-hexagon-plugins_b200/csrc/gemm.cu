@@ -28,8 +28,8 @@ hxb_status_t launch_gemm(const DeviceInfo& dev, const CUtensorMap& tmA,
   }
   const int tiles = args.tiles_m * args.tiles_n;
   const int grid = tiles < dev.num_sms ? tiles : dev.num_sms;
-  kernel<<<grid, GemmShape<BN, BMODE>::kThreads, L::kAlloc, stream>>>(tmA, tmB, args);
-  return cuda_status(cudaGetLastError(), "gemm launch");
+  return launch_pdl(kernel, dim3(grid), dim3(GemmShape<BN, BMODE>::kThreads), L::kAlloc, stream,
+                    "gemm launch", tmA, tmB, args);
 }
 
 template <int BMODE, int OUT>

@@ -234,10 +234,16 @@ __global__ void __launch_bounds__(GemmShape<BN, BMODE>::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  // The set-up above overlaps the previous kernel of the stream (programmatic
+  // dependent launch). Every global access below follows the producer's
+  // pdl_wait(): operand loads directly, the epilogue through the mbarrier
+  // chain of the tiles it drains.
+  pdl_trigger();
 
   if (warp == 0) {
     // ------------------------------------------------------ TMA producer
     if (lane == 0) {
+      pdl_wait();
       int stage = 0;
       uint32_t phase = 0;
       long long issued = 0;
