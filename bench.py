@@ -46,13 +46,16 @@ def _peaks():
     return dict(FALLBACK_PEAKS), "fallback"
 
 
-def _profile_traffic(kernel_tag: str):
-    """dram bytes per launch from the committed ncu summary, or None."""
-    f = REPO / "profiles" / f"{kernel_tag}.txt"
+def _profile_traffic(name: str):
+    """dram bytes per launch from the committed ncu summary
+    (profiles/<name>, or profiles/<name>.txt), or None."""
+    f = REPO / "profiles" / name
+    if not f.exists():
+        f = REPO / "profiles" / f"{name}.txt"
     if not f.exists():
         return None
     for line in f.read_text().splitlines():
-        if line.startswith("traffic_bytes_per_launch:"):
+        if line.strip().startswith("traffic_bytes_per_launch:"):
             return float(line.split(":", 1)[1].split()[0])
     return None
 
@@ -323,6 +326,7 @@ SPECS = {
     "attention": {
         "make": _spec_attention, "flop": 4.0 * 4 * 32 * 2048 * 2048 * 128, "bound": "tensor",
         "kernel": "attention_fwd_kernel", "dtype": "f16->f32",
+        "profile": "attention_4x32x2048x128.txt",
         "config": {"workload": "attention_4x32x2048x128_noncausal", "cfg": 3}},
     "decoder_block": {
         "make": _spec_decoder,
@@ -336,6 +340,7 @@ SPECS = {
         "bytes": 2 * GQA_B * GQA_HKV * GQA_CTX * GQA_D * 2 + 2 * 2 * GQA_B * GQA_HQ * GQA_D,
         "flop": 4.0 * GQA_B * GQA_HQ * GQA_CTX * GQA_D, "bound": "hbm",
         "kernel": "attention_fwd_kernel (split keys) + attention_combine_kernel", "launches": 2,
+        "profile": "attention_gqa_decode_b4_32q8kv_ctx8192_d128.md",
         "dtype": "f16->f32",
         "config": {"workload": "gqa_decode_b4_32q8kv_ctx8192_d128", "cfg": "f3",
                    "shape": "q [4, 32, 1, 128], K/V cache [4, 8, 8192, 128], out [4, 1, 32, 128]"}},
@@ -450,7 +455,8 @@ def run_spec(args, spec: dict, rank: int, world: int, local_rank: int) -> None:
                        l2=f"{st['sets']} rotating input set(s), together larger than the 126 MB L2",
                        timing="K dispatches in one CUDA graph, one replay between two events"),
         "roofline": {"bound": spec["bound"], "achieved": achieved, "peak": peak, "unit": unit,
-                     "frac": achieved / peak, "traffic": _profile_traffic(spec["config"]["workload"]),
+                     "frac": achieved / peak,
+                     "traffic": _profile_traffic(spec.get("profile", spec["config"]["workload"])),
                      "peak_source": peak_label, "kernel": spec["kernel"], "kernel_ms": ms},
         "e2e": {"value": work * world / (e2e_ms / 1e3), "unit": unit,
                 "h2d_bytes_per_step": inp.numel() * inp.element_size(),
