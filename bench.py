@@ -348,7 +348,7 @@ SPECS = {
         "make": _spec_decoder_decode,
         "bytes": _W8_DEC_BYTES + _SC_DEC_BYTES + 2 * 32 * (DEC_CTX + 1) * 128 * 2,
         "flop": 2.0 * _W8_DEC_BYTES + 4.0 * 32 * (DEC_CTX + 1) * 128, "bound": "hbm",
-        "kernel": "gemv_w8_sk_kernel (+ split-key attention, norms)", "launches": 11,
+        "kernel": "gemv_w8_sk_kernel (+ split-key attention, norms)", "launches": 10,
         "dtype": "f16xi8->f32",
         "config": {"workload": "llama_decoder_block_w8_decode_ctx2048", "cfg": "4+f3",
                    "scales": "U[1.5e-4, 4e-4] (int8 of a 0.02-std init)",

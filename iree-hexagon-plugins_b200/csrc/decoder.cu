@@ -4,6 +4,8 @@
 //   h   = RMSNorm(x) * attn_norm                          rmsnorm_kernel
 //   qkv = h . Wqkv * s_qkv                                W8 GEMM  [S, 3*hidden]
 //   q,k = RoPE(q), RoPE(k)   (in place inside qkv)        rope_kernel
+//        (with a KV cache: rope_cache_kernel, which also writes the new
+//        rows' k and v into the caches)
 //   att = causal softmax(q k^T / sqrt(d)) v               attention, [B,S,H*D]
 //   h2  = att . Wo * s_o + x                              W8 GEMM + residual
 //   g,u = RMSNorm(h2) * ffn_norm . Wgu * s_gu             rmsnorm + W8 GEMM
@@ -97,6 +99,28 @@ __global__ void rmsnorm_kernel(const __half* __restrict__ x, long long ldx,
 // start of every row (the q and k blocks of a fused QKV row). One warp per
 // (row, head); lane i handles the rotate-half pairs (i, i + 64) and
 // (i + 32, i + 96). Row r has position pos0 + r % seq.
+// Rotates one 128-wide head in place at position `pos` (lane i: the pairs
+// (i, i + 64) and (i + 32, i + 96)); `out`, if given, receives a copy of the
+// rotated head.
+__device__ __forceinline__ void rope_head(__half* v, float pos, float log2_theta, int lane,
+                                          __half* out) {
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int i = lane + 32 * k;
+    const float inv_freq = exp2f(-(2.0f * (float)i / 128.0f) * log2_theta);
+    float sn, cs;
+    sincosf(pos * inv_freq, &sn, &cs);
+    const float a = __half2float(v[i]), b = __half2float(v[i + 64]);
+    const __half ra = __float2half_rn(a * cs - b * sn), rb = __float2half_rn(b * cs + a * sn);
+    v[i] = ra;
+    v[i + 64] = rb;
+    if (out) {
+      out[i] = ra;
+      out[i + 64] = rb;
+    }
+  }
+}
+
 __global__ void rope_kernel(__half* __restrict__ x, long long ldx, int rows, int heads, int seq,
                             int pos0, float log2_theta) {
   pdl_wait();
@@ -105,17 +129,32 @@ __global__ void rope_kernel(__half* __restrict__ x, long long ldx, int rows, int
   const int lane = threadIdx.x & 31;
   if (wid >= rows * heads) return;
   const int row = wid / heads, head = wid - row * heads;
-  __half* v = x + (long long)row * ldx + head * 128;
-  const float pos = (float)(pos0 + row % seq);
-#pragma unroll
-  for (int k = 0; k < 2; ++k) {
-    const int i = lane + 32 * k;
-    const float inv_freq = exp2f(-(2.0f * (float)i / 128.0f) * log2_theta);
-    float sn, cs;
-    sincosf(pos * inv_freq, &sn, &cs);
-    const float a = __half2float(v[i]), b = __half2float(v[i + 64]);
-    v[i] = __float2half_rn(a * cs - b * sn);
-    v[i + 64] = __float2half_rn(b * cs + a * sn);
+  rope_head(x + (long long)row * ldx + head * 128, (float)(pos0 + row % seq), log2_theta, lane,
+            nullptr);
+}
+
+// RoPE of the q and k heads of fused QKV rows fused with the KV-cache update:
+// one warp per (row, slot); slots [0, heads) rotate q in place, [heads,
+// 2 heads) rotate k in place and copy it to k_cache, [2 heads, 3 heads) copy
+// v to v_cache (row b * seq + t goes to cache row pos0 + t of batch b).
+__global__ void rope_cache_kernel(__half* __restrict__ qkv, long long ld, int rows, int heads,
+                                  int seq, int pos0, float log2_theta, __half* __restrict__ k_cache,
+                                  __half* __restrict__ v_cache, long long cache_rows) {
+  pdl_wait();
+  pdl_trigger();
+  const long long wid = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (wid >= (long long)rows * 3 * heads) return;
+  const int row = (int)(wid / (3 * heads)), slot = (int)(wid - (long long)row * 3 * heads);
+  const int b = row / seq, t = row - b * seq;
+  __half* src = qkv + (long long)row * ld + slot * 128;
+  const int h = slot % heads;
+  const long long crow = (((long long)b * heads + h) * cache_rows + pos0 + t) * 128;
+  if (slot < 2 * heads) {
+    rope_head(src, (float)(pos0 + t), log2_theta, lane, slot < heads ? nullptr : k_cache + crow);
+  } else {
+    *reinterpret_cast<uint2*>(v_cache + crow + 4 * lane) =
+        *reinterpret_cast<const uint2*>(src + 4 * lane);
   }
 }
 
@@ -220,6 +259,17 @@ hxb_status_t launch_rope(void* x, int64_t ldx, int64_t rows, int64_t heads, int6
   return launch_pdl(rope_kernel, dim3((unsigned)blocks), dim3(threads), 0, stream, "rope launch",
                     static_cast<__half*>(x), (long long)ldx, (int)rows, (int)heads, (int)seq,
                     (int)pos0, log2f(theta));
+}
+
+hxb_status_t launch_rope_cache(void* qkv, int64_t ld, int64_t rows, int64_t heads, int64_t seq,
+                               int64_t pos0, float theta, void* k_cache, void* v_cache,
+                               int64_t cache_rows, cudaStream_t stream) {
+  const int threads = 256;
+  const long long blocks = (rows * 3 * heads * 32 + threads - 1) / threads;
+  return launch_pdl(rope_cache_kernel, dim3((unsigned)blocks), dim3(threads), 0, stream,
+                    "rope + kv cache launch", static_cast<__half*>(qkv), (long long)ld, (int)rows,
+                    (int)heads, (int)seq, (int)pos0, log2f(theta), static_cast<__half*>(k_cache),
+                    static_cast<__half*>(v_cache), (long long)cache_rows);
 }
 
 hxb_status_t launch_swiglu(const void* gu, int64_t ldgu, void* a, int64_t lda, int64_t rows,
@@ -360,23 +410,25 @@ hxb_status_t decoder_run(const hxb_decoder_w8_t* w, const void* x, void* out, in
   if ((s = matmul_w8a16_impl(h, H, w->w_qkv, 3 * H, w->s_qkv, nullptr, qkv, 3 * H, rows, 3 * H, H,
                              sk, skb, stream)) != HXB_OK)
     return s;
-  // q and k are the first 2 * heads heads of every qkv row
-  if ((s = launch_rope(qkv, 3 * H, rows, 2 * w->heads, seq, pos0, w->rope_theta, stream)) != HXB_OK)
-    return s;
   if (cache) {
-    if ((s = launch_kv_cache_write(qkv + H, qkv + 2 * H, 3 * H, cache->k, cache->v, batch,
-                                   w->heads, seq, pos0, cache->rows, w->head_dim, stream)) !=
-        HXB_OK)
+    // RoPE of q and k with the new rows' k and v written into the caches
+    if ((s = launch_rope_cache(qkv, 3 * H, rows, w->heads, seq, pos0, w->rope_theta, cache->k,
+                               cache->v, cache->rows, stream)) != HXB_OK)
       return s;
     if ((s = attention_cached_launch(qkv, 3 * H, cache->k, cache->v, cache->rows, att, H, batch,
                                      w->heads, seq, pos0 + seq, pos0, w->head_dim, scale,
                                      b.att_ws_bytes ? ws + b.att_ws : nullptr, b.att_ws_bytes,
                                      stream)) != HXB_OK)
       return s;
-  } else if ((s = attention_launch(qkv, 3 * H, qkv + H, 3 * H, qkv + 2 * H, 3 * H, att, H, batch,
-                                   w->heads, w->heads, seq, seq, w->head_dim, scale, 1,
-                                   stream)) != HXB_OK) {
-    return s;
+  } else {
+    // q and k are the first 2 * heads heads of every qkv row
+    if ((s = launch_rope(qkv, 3 * H, rows, 2 * w->heads, seq, pos0, w->rope_theta, stream)) !=
+        HXB_OK)
+      return s;
+    if ((s = attention_launch(qkv, 3 * H, qkv + H, 3 * H, qkv + 2 * H, 3 * H, att, H, batch,
+                              w->heads, w->heads, seq, seq, w->head_dim, scale, 1, stream)) !=
+        HXB_OK)
+      return s;
   }
   if ((s = matmul_w8a16_impl(att, H, w->w_o, H, w->s_o, x, h2, H, rows, H, H, sk, skb, stream)) !=
       HXB_OK)
