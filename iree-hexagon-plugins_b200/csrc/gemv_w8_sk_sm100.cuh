@@ -15,10 +15,10 @@
 //     are published when an SM is done streaming and every SM completes its
 //     shared strip after its own last tile;
 //   * one producer thread keeps a 4-stage TMA ring of weight tiles (and the
-//     matching 64-k slice of the activations) in flight, 72 KB per CTA: small
-//     enough that the next launch's CTA fits on the same SM and starts its
-//     weight stream while this one finishes (4 to 8 stages measured within
-//     2 % of each other; 8 stages, which keep one CTA per SM, 5 % slower);
+//     matching 64-k slice of the activations) in flight, 72 KB per CTA
+//     (4, 5 and 6 stages measured within 1 % of each other, 8 stages 5 %
+//     slower). One CTA per SM: its registers fill an SM sub-partition's
+//     share, so the next launch's CTAs start as this launch's CTAs exit;
 //   * eight consumer warps each own 32 columns of a strip and contract with
 //     warp-level MMAs in the swapped orientation D[n, m] = W^T[n, k] X^T[k, m]:
 //     one m16n8k16 consumes 256 weights, and ldmatrix.trans hands every lane
