@@ -339,7 +339,7 @@ SPECS = {
         "make": _spec_gqa_decode,
         "bytes": 2 * GQA_B * GQA_HKV * GQA_CTX * GQA_D * 2 + 2 * 2 * GQA_B * GQA_HQ * GQA_D,
         "flop": 4.0 * GQA_B * GQA_HQ * GQA_CTX * GQA_D, "bound": "hbm",
-        "kernel": "attention_fwd_kernel (split keys) + attention_combine_kernel", "launches": 2,
+        "kernel": "attention_decode_kernel (split keys) + attention_combine_kernel", "launches": 2,
         "profile": "attention_gqa_decode_b4_32q8kv_ctx8192_d128.md",
         "dtype": "f16->f32",
         "config": {"workload": "gqa_decode_b4_32q8kv_ctx8192_d128", "cfg": "f3",

@@ -141,6 +141,8 @@ def _gqa_inputs(B, Hq, Hkv, q_len, rows, D, seed):
     (1, 16, 2, 40, None, 30, 64, 128, True, "bhsd"),   # q_len > kv_len: masked rows
     (1, 9, 3, 96, 0, 70, 128, 64, True, "bshd"),       # padded prefill: keys cut at 70
     (2, 15, 5, 32, 200, 232, 256, 64, True, "bshd"),   # chunked prefill after 200 tokens
+    (2, 16, 4, 4, 100, 180, 256, 128, True, "bshd"),   # 16 rows per KV head, from position 100
+    (1, 6, 3, 1, None, 129, 200, 128, False, "bhsd"),  # 2 rows per KV head, a ragged key block
 ])
 def test_attention_gqa_vs_oracle(cuda_pkg, oracle, B, Hq, Hkv, q_len, q_pos0, kv_len, rows, D,
                                  causal, layout):
@@ -198,6 +200,8 @@ def test_attention_gqa_rejects_bad_layouts(cuda_pkg):
     (1, 9, 3, 1, None, 700, 1024, 64, True),      # SmolLM2-like heads, D = 64
     (1, 8, 8, 100, 0, 1000, 1024, 128, True),     # most splits see no visible key
     (2, 28, 4, 4, None, 1500, 2048, 128, True),   # a 4-token step, group 7
+    (1, 8, 2, 4, None, 600, 1024, 128, True),     # 16 rows per KV head, causal
+    (3, 16, 8, 1, None, 2000, 2048, 128, False),  # group 2
 ])
 def test_attention_gqa_split_keys(cuda_pkg, oracle, B, Hq, Hkv, q_len, q_pos0, kv_len, rows, D,
                                   causal):
