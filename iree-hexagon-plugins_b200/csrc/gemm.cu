@@ -326,6 +326,13 @@ size_t w8_streamk_workspace_bytes(int ctas) {
 }
 int w8_streamk_flag_ints() { return (int)(kW8FlagBytes / sizeof(int)); }
 
+// Cost of the stream-K fix-up in K-blocks of one CTA's main loop: writing a
+// contributor's partial tile and adding the partials at the tile's end keep
+// the single accumulator busy for about this long (measured on B200 with the
+// decoder-block projections at M = 512: 512 x 4096 x {4096, 12288, 22016}
+// and 512 x 11008 x 4096, data-parallel against stream-K).
+constexpr long long kW8StreamKFixupKb = 43;
+
 // Stream-K choice of the W8 GEMM: `units` CTAs can run at once, `tiles`
 // output tiles of `num_kb` K-blocks each. Returns the number of CTAs to
 // launch with stream-K, or 0 for the data-parallel schedule.
@@ -335,8 +342,11 @@ int w8_streamk_units(int tiles, long long num_kb, int units) {
   const double fill = (double)tiles / ((double)waves * units);
   const long long g = total / kW8MinShare < units ? total / kW8MinShare : units;
   // fewer tiles than units: spread them over more units; several waves: even
-  // out the last one over all units
-  if (fill < 0.92 && (g > tiles || (tiles > units && g == units))) return (int)g;
+  // out the last one over all units -- when the even shares plus the fix-up
+  // beat the data-parallel waves
+  if (fill < 0.92 && (g > tiles || (tiles > units && g == units)) && g > 0 &&
+      (total + g - 1) / g + kW8StreamKFixupKb < (long long)waves * num_kb)
+    return (int)g;
   return 0;
 }
 

@@ -32,10 +32,11 @@ def _t(x):
 
 
 @pytest.mark.parametrize("M,K,N,res", [
-    (512, 4096, 4096, True),     # decoder O projection: 64 tiles
-    (512, 11008, 4096, True),    # decoder down projection
-    (512, 4096, 22016, False),   # decoder gate|up: 344 tiles, 2.3 waves
-    (129, 1000, 272, True),      # ragged K and M, each tile cut in two
+    (512, 4096, 4096, True),     # decoder O projection: 64 tiles (data-parallel wins)
+    (512, 11008, 4096, True),    # decoder down projection: stream-K
+    (512, 4096, 12288, False),   # decoder qkv: 192 tiles, stream-K
+    (512, 4096, 22016, False),   # decoder gate|up: 344 tiles (data-parallel wins)
+    (129, 4000, 272, True),      # ragged K and M, stream-K over 3 tiles
     (100, 8192, 144, False),     # 2 tiles cut into 16 pieces each
     (200, 320, 528, False),      # too little K to split: data-parallel
 ])
