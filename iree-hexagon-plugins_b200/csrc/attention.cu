@@ -489,7 +489,7 @@ __global__ void __launch_bounds__(kAttThreads, 1)
 // stay per thread until the end. Partial results of split keys use the same
 // layout as attention_fwd_kernel, so attention_combine_kernel merges them.
 constexpr int kDecRows = 16;     // query rows per CTA head (MMA N)
-constexpr int kDecSlots = 6;     // K/V ring slots
+constexpr int kDecSlots = 3;     // K/V ring slots (two CTAs per SM)
 constexpr int kDecThreads = 256; // warp 0 TMA, warp 1 MMA + TMEM, warps 4-7 keys
 constexpr int kDecTmemCols = 32; // S^T in [0, 16), O^T in [16, 32)
 
@@ -516,7 +516,7 @@ __device__ __forceinline__ uint64_t rows16_desc(uint32_t base, int kk) {
                         kLayoutSwizzle128);
 }
 
-__global__ void __launch_bounds__(kDecThreads, 1)
+__global__ void __launch_bounds__(kDecThreads, 2)
     attention_decode_kernel(const __grid_constant__ CUtensorMap tmQ,
                             const __grid_constant__ CUtensorMap tmK,
                             const __grid_constant__ CUtensorMap tmV, const AttArgs args) {
@@ -948,6 +948,13 @@ struct SplitPlan {
   size_t bytes = 0;  // workspace the partials need (0 without a split)
 };
 
+// CTAs that run at once: the decode kernel (2-16 rows per head, D = 128)
+// fits two per SM, the others one.
+bool uses_decode_kernel(int64_t Sq, int64_t D) { return D == 128 && Sq >= 2 && Sq <= kDecRows; }
+int split_units(int64_t Sq, int64_t D, int num_sms) {
+  return uses_decode_kernel(Sq, D) ? 2 * num_sms : num_sms;
+}
+
 SplitPlan plan_splits(int64_t ctas, int64_t Sq, int64_t Skv, int64_t D, int num_sms) {
   SplitPlan p;
   const int64_t blocks = (Skv + kAttBN - 1) / kAttBN;
@@ -994,6 +1001,11 @@ hxb_status_t launch_decode(const CUtensorMap& tmQ, const CUtensorMap& tmK, const
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          DecSmem::kAlloc);
     if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(attention decode)");
+    // all of the unified L1 as shared memory: two CTAs per SM
+    e = cudaFuncSetAttribute(attention_decode_kernel,
+                             cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(attention decode carveout)");
     configured[ordinal] = true;
   }
   const int64_t ctas = heads * args.kv_splits;
@@ -1048,7 +1060,7 @@ hxb_status_t attention_run(const AttLayout& a, float scale, int causal, cudaStre
   DeviceInfo* dev = nullptr;
   hxb_status_t s = current_device(&dev);
   if (s != HXB_OK) return s;
-  SplitPlan plan = plan_splits(q_blocks * a.heads, Sq, a.Skv, D, dev->num_sms);
+  SplitPlan plan = plan_splits(q_blocks * a.heads, Sq, a.Skv, D, split_units(Sq, D, dev->num_sms));
   if (plan.splits > 1 && (!a.workspace || a.workspace_bytes < plan.bytes ||
                           (reinterpret_cast<uintptr_t>(a.workspace) & 15u))) {
     plan = SplitPlan{};  // no room for partials: one CTA walks all the keys
@@ -1057,7 +1069,7 @@ hxb_status_t attention_run(const AttLayout& a, float scale, int causal, cudaStre
   // 2 to 16 query rows per head (grouped-query decode, short steps): the
   // keys-on-lanes kernel. A single row per head (multi-head decode) measured
   // ~2 % faster on attention_fwd_kernel, whose Q arrives by TMA.
-  const bool decode = D == 128 && Sq >= 2 && Sq <= kDecRows;
+  const bool decode = uses_decode_kernel(Sq, D);
   const int q_box = (int)std::min<int64_t>(kAttBM, (Sq + 7) / 8 * 8);
   CUtensorMap tmQ, tmK, tmV;
   if ((s = make_rows_map(&tmQ, a.Q, rows_q, a.ldq, (uint32_t)q_box)) != HXB_OK) return s;
@@ -1165,11 +1177,11 @@ hxb_status_t attention_gqa_launch(const void* Q, const void* K, const void* V, v
 
 // Upper bound of the split-key workspace of any call with Sq query rows per
 // CTA head on the current device, whatever the number of keys: the splits
-// never make more CTAs than there are SMs.
+// never make more CTAs than can run at once.
 size_t attention_split_bound(int64_t Sq, int64_t D) {
   DeviceInfo* dev = nullptr;
   if (Sq < 1 || Sq > kAttBM || current_device(&dev) != HXB_OK) return 0;
-  const size_t rows = (size_t)dev->num_sms * (size_t)Sq;
+  const size_t rows = (size_t)split_units(Sq, D, dev->num_sms) * (size_t)Sq;
   return (rows * sizeof(float) + 15) / 16 * 16 + rows * (size_t)D * sizeof(float);
 }
 
@@ -1214,7 +1226,8 @@ size_t attention_gqa_workspace(int64_t batch, int64_t q_heads, int64_t kv_heads,
   if (current_device(&dev) != HXB_OK) return 0;
   const int64_t Sq = q_heads / kv_heads * q_len;
   const int64_t q_blocks = (Sq + kAttTiles * kAttBM - 1) / (kAttTiles * kAttBM);
-  return plan_splits(q_blocks * batch * kv_heads, Sq, kv_len, D, dev->num_sms).bytes;
+  return plan_splits(q_blocks * batch * kv_heads, Sq, kv_len, D,
+                     split_units(Sq, D, dev->num_sms)).bytes;
 }
 
 }  // namespace hxb
