@@ -326,12 +326,17 @@ size_t w8_streamk_workspace_bytes(int ctas) {
 }
 int w8_streamk_flag_ints() { return (int)(kW8FlagBytes / sizeof(int)); }
 
-// Cost of the stream-K fix-up in K-blocks of one CTA's main loop: writing a
-// contributor's partial tile and adding the partials at the tile's end keep
-// the single accumulator busy for about this long (measured on B200 with the
-// decoder-block projections at M = 512: 512 x 4096 x {4096, 12288, 22016}
-// and 512 x 11008 x 4096, data-parallel against stream-K).
-constexpr long long kW8StreamKFixupKb = 43;
+// Cost of the stream-K fix-up in K-blocks of one CTA's main loop: a
+// contributor's partial write holds the single accumulator (~3 us), the
+// finaliser adds the partials it waited for (~4 us for two) and the shares
+// walk tiles in an order that shares less L2 between the CTAs running at
+// once, which costs more the more tiles a share spans. Fitted on B200 against
+// the data-parallel schedule (us, data-parallel / stream-K): 512 x 4096 x
+// 4096 33.1 / 28.6, 512 x 11008 x 4096 76.0 / 49.1, 512 x 4096 x 12288
+// 62.4 / 52.4, 512 x 4096 x 22016 91.7 / 93.7, 1024 x 4096 x 4096
+// 32.4 / 37.3, 4096 x 4096 x 11008 313.6 / 333.9 (M x K x N).
+constexpr long long kW8StreamKFixupKb = 28;
+constexpr long long kW8StreamKFixupWaveKb = 8;
 
 // Stream-K choice of the W8 GEMM: `units` CTAs can run at once, `tiles`
 // output tiles of `num_kb` K-blocks each. Returns the number of CTAs to
@@ -341,11 +346,12 @@ int w8_streamk_units(int tiles, long long num_kb, int units) {
   const int waves = (tiles + units - 1) / units;
   const double fill = (double)tiles / ((double)waves * units);
   const long long g = total / kW8MinShare < units ? total / kW8MinShare : units;
+  const long long fixup = kW8StreamKFixupKb + kW8StreamKFixupWaveKb * (waves - 1);
   // fewer tiles than units: spread them over more units; several waves: even
   // out the last one over all units -- when the even shares plus the fix-up
   // beat the data-parallel waves
   if (fill < 0.92 && (g > tiles || (tiles > units && g == units)) && g > 0 &&
-      (total + g - 1) / g + kW8StreamKFixupKb < (long long)waves * num_kb)
+      (total + g - 1) / g + fixup < (long long)waves * num_kb)
     return (int)g;
   return 0;
 }
@@ -380,6 +386,17 @@ hxb_status_t gemm_w8_impl(const void* A, int64_t lda, const void* W,
     const uint64_t strides[1] = {(uint64_t)ldc * 2};
     const uint32_t box[2] = {64, (uint32_t)kW8BM};
     if ((s = encode_tensor_map(&tmC, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, C, dims, strides, box,
+                               CU_TENSOR_MAP_SWIZZLE_128B)) != HXB_OK)
+      return s;
+  }
+  // The residual (same shape and leading dimension as C, 16-byte aligned like
+  // it) comes in by TMA into the output staging tile.
+  CUtensorMap tmR = tmC;
+  if (R) {
+    const uint64_t dims[2] = {(uint64_t)N, (uint64_t)M};
+    const uint64_t strides[1] = {(uint64_t)ldc * 2};
+    const uint32_t box[2] = {64, (uint32_t)kW8BM};
+    if ((s = encode_tensor_map(&tmR, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, R, dims, strides, box,
                                CU_TENSOR_MAP_SWIZZLE_128B)) != HXB_OK)
       return s;
   }
@@ -421,7 +438,7 @@ hxb_status_t gemm_w8_impl(const void* A, int64_t lda, const void* W,
     if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(gemm_w8)");
     configured[dev->ordinal] = true;
   }
-  gemm_w8_sm100_kernel<<<grid, kW8Threads, W8Smem::kAlloc, stream>>>(tmA, tmW, tmC, args);
+  gemm_w8_sm100_kernel<<<grid, kW8Threads, W8Smem::kAlloc, stream>>>(tmA, tmW, tmC, tmR, args);
   return cuda_status(cudaGetLastError(), "gemm_w8 launch");
 }
 

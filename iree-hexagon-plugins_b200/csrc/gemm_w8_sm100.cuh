@@ -23,14 +23,14 @@
 //     converters keep running meanwhile and fill up to kW8SA converted
 //     K-blocks for the next tile;
 //   * four epilogue warps read the accumulator back and apply the
-//     per-column scale once (it factors out of the K sum). A whole tile
-//     without a residual is packed to f16 into a 64 KB shared-memory staging
-//     tile, the accumulator is released to the MMA as soon as it is read,
-//     and one thread writes C with two TMA stores that overlap the next
-//     tile's main loop. Stream-K pieces and residual tiles take a register
-//     path (scales fetched before the accumulator is ready, residual and
-//     partial-sum loads issued ahead of the TMEM reads, f16x2 column-pair
-//     stores, one f16 rounding of acc * s + r).
+//     per-column scale once (it factors out of the K sum). The tile is
+//     packed to f16 into a 64 KB shared-memory staging tile, the accumulator
+//     is released to the MMA as soon as it is read, and one thread writes C
+//     with two TMA stores that overlap the next tile's main loop. A residual
+//     is loaded by TMA into the same staging tile while the main loop runs
+//     (same boxes and swizzle as the output, so each thread reads its
+//     residual pair where it then writes its result: one f16 rounding of
+//     acc * s + r).
 //   * Measured decomposition of the 4096 x 4096 x 11008 dispatch on B200
 //     (307 us before the staging was sized as below): tensor pipe alone
 //     ~167 us; with TMA feeding but no conversion and no epilogue 234 us;
@@ -47,9 +47,11 @@
 // end of its share) finalises it; every other CTA holding a piece of the
 // tile holds it FIRST, writes its f32 partial accumulator to
 // args.sk_partials[cta] and raises args.sk_flags[cta][quarter]. The finaliser
-// adds the partials in CTA order (deterministic), stores C and clears the
-// flags, so the flag array is all zero again when the kernel ends. No CTA
-// waits on a lower-numbered CTA, and every wait is bounded.
+// brings the partials of each quarter into the (then idle) activation stages
+// with 1-D bulk copies and adds them into its TMEM accumulator in CTA order
+// (deterministic), then runs the normal epilogue and clears the flags, so the
+// flag array is all zero again when the kernel ends. No CTA waits on a
+// lower-numbered CTA, and every wait is bounded.
 //
 // Roles (512 threads, one CTA per SM, persistent):
 //   warp 0        TMA producer (one lane)
@@ -102,8 +104,10 @@ struct W8Smem {
   static constexpr int kOffStage = kOffW + kW8SW * kWBytes;
   static constexpr int kOffBar = kOffStage + 2 * kBoxBytes;
   // x_full, x_empty [SX]; w_full, w_empty [SW]; a_full, a_empty [SA];
-  // t_full[2], t_empty[2], drain
-  static constexpr int kNumBars = 2 * kW8SX + 2 * kW8SW + 2 * kW8SA + 5;
+  // t_full[2], t_empty[2], drain; fix_full[4 epilogue warps][2] (partial
+  // segments of a cut tile, landing in the activation stages once the last
+  // main loop is done); r_full (residual tile in the staging tile)
+  static constexpr int kNumBars = 2 * kW8SX + 2 * kW8SW + 2 * kW8SA + 5 + 2 * kW8EpiWarps + 1;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kBytes = kOffMisc + 16;
   static constexpr int kAlloc = kBytes + 1024;
@@ -233,189 +237,204 @@ __device__ __forceinline__ int w8_partial_index(int q, int h, int c, int r, int 
   return (((q * 2 + h) * (kW8BM / 32) + c) * 4 + r) * 32 + lane;
 }
 
-// Epilogue of one piece for epilogue warp q (lane t) of a CTA whose TMEM
-// accumulator at column `acc_tmem` holds weight columns n0 .. n0 + 127 (lane
-// order of w8_tmem.cuh) by activation rows m0 .. m0 + kW8BM - 1. Waits for the
-// accumulator (t_full, phase `parity`). A contributor piece writes the raw
-// accumulator to partial slot `self_slot` and raises that slot's flag; any
-// other piece adds the partials of slots c * slot_mul + slot_add for c in
-// [c_lo, c_hi) (waiting for their flags and clearing them afterwards), then
-// applies the scale and the optional residual and stores C.
-//
-// tcgen05.ld.16x256b gives lane t the TMEM lanes t/4 and t/4 + 8 of a 16-lane
-// group -- weight columns n and n + 1 -- at accumulator columns (activation
-// rows) m, m + 1: each pair (n, n + 1) of one row m is stored as one 4-byte
-// f16x2. Scales are fetched before the accumulator is ready; residual and
-// partial-sum loads are issued ahead of the TMEM reads they pair with, two
-// 32-column chunks at a time. Returns false after a timeout.
-__device__ __forceinline__ bool w8_epilogue_piece(const GemmArgs& args, const FailState& fs,
-                                                  uint64_t* t_full, uint32_t parity,
-                                                  uint32_t acc_tmem, int n0, int m0, int q,
-                                                  int t, bool contributor, int self_slot,
-                                                  int c_lo, int c_hi, int slot_mul,
-                                                  int slot_add) {
-  const int lane = t;
-  float sc[2][2];
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const int n = n0 + 16 * (2 * q + h) + 2 * (t >> 2);
-    sc[h][0] = (!contributor && n < args.N) ? __half2float(args.scale[n]) : 0.0f;
-    sc[h][1] = (!contributor && n + 1 < args.N) ? __half2float(args.scale[n + 1]) : 0.0f;
-  }
-  bool ready = mbar_wait(t_full, parity, fs);
-  for (int c2 = c_lo; c2 < c_hi && ready; ++c2)
-    ready = wait_flag(args.sk_flags + 4 * (c2 * slot_mul + slot_add) + q, fs);
+// Contributor epilogue (epilogue warp q, lane t): a piece that does not hold
+// its tile's first K-block writes its raw f32 accumulator (TMEM at
+// `acc_tmem`, waited for on t_full, phase `parity`) to partial slot
+// `self_slot` and raises that slot's flag for quarter q. tcgen05.ld.16x256b
+// gives lane t, for repetition r, the accumulator values of TMEM lanes t/4 and
+// t/4 + 8 of a 16-lane group at columns 8r + 2(t%4), +1; each warp store is
+// 512 contiguous bytes (w8_partial_index). Returns false after a timeout.
+__device__ __forceinline__ bool w8_write_partial(const GemmArgs& args, const FailState& fs,
+                                                 uint64_t* t_full, uint32_t parity,
+                                                 uint32_t acc_tmem, int q, int t, int self_slot) {
+  const bool ready = mbar_wait(t_full, parity, fs);
   if (!__all_sync(0xffffffffu, ready)) return false;
   tc_fence_after();
-
-  if (contributor) {
-    float4* part = reinterpret_cast<float4*>(args.sk_partials) +
-                   (size_t)self_slot * (kW8PartialFloats / 4);
-#pragma unroll 1
-    for (int h = 0; h < 2; ++h) {
-      const uint32_t taddr = acc_tmem + ((uint32_t)(16 * (2 * q + h)) << 16);
-#pragma unroll 1
-      for (int c = 0; c < kW8BM / 32; c += 2) {
-        uint32_t r[2][16];
-        tmem_ld_16x256b_x4(taddr + 32 * c, r[0]);
-        tmem_ld_16x256b_x4(taddr + 32 * (c + 1), r[1]);
-        tmem_wait_ld();
-#pragma unroll
-        for (int u = 0; u < 2; ++u)
-#pragma unroll
-          for (int rep = 0; rep < 4; ++rep)
-            __stcg(part + w8_partial_index(q, h, c + u, rep, t),
-                   make_float4(__uint_as_float(r[u][4 * rep]), __uint_as_float(r[u][4 * rep + 1]),
-                               __uint_as_float(r[u][4 * rep + 2]),
-                               __uint_as_float(r[u][4 * rep + 3])));
-      }
-    }
-    // publish: every lane's stores, then the flag of this quarter
-    __threadfence();
-    __syncwarp();
-    if (lane == 0) st_release_gpu(args.sk_flags + 4 * self_slot + q, 1);
-    return true;
-  }
-  const bool rows_full = m0 + kW8BM <= args.M;
-  const __half* R = reinterpret_cast<const __half*>(args.C_init);
+  float4* part =
+      reinterpret_cast<float4*>(args.sk_partials) + (size_t)self_slot * (kW8PartialFloats / 4);
 #pragma unroll 1
   for (int h = 0; h < 2; ++h) {
-    const int chunk = 2 * q + h;
-    const int n = n0 + 16 * chunk + 2 * (t >> 2);
-    const bool n0_ok = n < args.N, n1_ok = n + 1 < args.N;
-    const bool fast = rows_full && n1_ok;
-    const float s0 = h ? sc[1][0] : sc[0][0], s1 = h ? sc[1][1] : sc[0][1];
-    const uint32_t taddr = acc_tmem + ((uint32_t)(16 * chunk) << 16);
-    // row of (chunk c, rep, j) = row0 + 32 c + 8 rep + j
-    const int row0 = m0 + 2 * (t & 3);
-    __half* cbase = reinterpret_cast<__half*>(args.C) + (long long)row0 * args.ldc + n;
-    const __half* rbase = R ? R + (long long)row0 * args.ldc + n : nullptr;
+    const uint32_t taddr = acc_tmem + ((uint32_t)(16 * (2 * q + h)) << 16);
 #pragma unroll 1
-    for (int c = 0; c < kW8BM / 32; c += 2) {
-      // residual pairs and partial sums of the two chunks, loaded ahead
-      // of the TMEM reads
-      uint32_t res[2][8];
+    for (int c = 0; c < kW8BM / 32; c += 4) {
+      // four 32-column chunks per TMEM round trip
+      uint32_t r[4][16];
 #pragma unroll
-      for (int u = 0; u < 2; ++u)
-#pragma unroll
-        for (int e = 0; e < 8; ++e) res[u][e] = 0u;
-      if (rbase && fast) {
-#pragma unroll
-        for (int u = 0; u < 2; ++u)
-#pragma unroll
-          for (int rep = 0; rep < 4; ++rep)
-#pragma unroll
-            for (int j = 0; j < 2; ++j)
-              res[u][2 * rep + j] = __ldg(reinterpret_cast<const unsigned int*>(
-                  rbase + (long long)(32 * (c + u) + 8 * rep + j) * args.ldc));
-      }
-      float v[2][16];
-#pragma unroll
-      for (int u = 0; u < 2; ++u)
-#pragma unroll
-        for (int e = 0; e < 16; ++e) v[u][e] = 0.0f;
-      for (int c2 = c_lo; c2 < c_hi; ++c2) {
-        const float4* part = reinterpret_cast<const float4*>(args.sk_partials) +
-                             (size_t)(c2 * slot_mul + slot_add) * (kW8PartialFloats / 4);
-#pragma unroll
-        for (int u = 0; u < 2; ++u)
-#pragma unroll
-          for (int rep = 0; rep < 4; ++rep) {
-            const float4 p = __ldcg(part + w8_partial_index(q, h, c + u, rep, t));
-            v[u][4 * rep] += p.x;
-            v[u][4 * rep + 1] += p.y;
-            v[u][4 * rep + 2] += p.z;
-            v[u][4 * rep + 3] += p.w;
-          }
-      }
-      uint32_t r[2][16];
-      tmem_ld_16x256b_x4(taddr + 32 * c, r[0]);
-      tmem_ld_16x256b_x4(taddr + 32 * (c + 1), r[1]);
+      for (int u = 0; u < 4; ++u) tmem_ld_16x256b_x4(taddr + 32 * (c + u), r[u]);
       tmem_wait_ld();
-      // this CTA's accumulator plus the partials (summed in CTA order)
 #pragma unroll
-      for (int u = 0; u < 2; ++u)
+      for (int u = 0; u < 4; ++u)
 #pragma unroll
-        for (int e = 0; e < 16; ++e) v[u][e] = __uint_as_float(r[u][e]) + v[u][e];
-      if (fast) {
-#pragma unroll
-        for (int u = 0; u < 2; ++u)
-#pragma unroll
-          for (int rep = 0; rep < 4; ++rep)
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-              float v0 = v[u][4 * rep + j] * s0;
-              float v1 = v[u][4 * rep + 2 + j] * s1;
-              if (rbase) {
-                const float2 rv = __half22float2(
-                    *reinterpret_cast<const __half2*>(&res[u][2 * rep + j]));
-                v0 += rv.x;
-                v1 += rv.y;
-              }
-              *reinterpret_cast<__half2*>(
-                  cbase + (long long)(32 * (c + u) + 8 * rep + j) * args.ldc) =
-                  __floats2half2_rn(v0, v1);
-            }
-      } else if (n0_ok) {
-        // ragged edge: rows past M, or the last column of an odd N
-#pragma unroll
-        for (int u = 0; u < 2; ++u)
-#pragma unroll
-          for (int rep = 0; rep < 4; ++rep)
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-              const int dm = 32 * (c + u) + 8 * rep + j;
-              if (row0 + dm >= args.M) continue;
-              const long long off = (long long)dm * args.ldc;
-              float v0 = v[u][4 * rep + j] * s0;
-              float v1 = v[u][4 * rep + 2 + j] * s1;
-              if (n1_ok) {
-                if (rbase) {
-                  const float2 rv =
-                      __half22float2(*reinterpret_cast<const __half2*>(rbase + off));
-                  v0 += rv.x;
-                  v1 += rv.y;
-                }
-                *reinterpret_cast<__half2*>(cbase + off) = __floats2half2_rn(v0, v1);
-              } else {
-                if (rbase) v0 += __half2float(rbase[off]);
-                cbase[off] = __float2half_rn(v0);
-              }
-            }
-      }
+        for (int rep = 0; rep < 4; ++rep)
+          __stcg(part + w8_partial_index(q, h, c + u, rep, t),
+                 make_float4(__uint_as_float(r[u][4 * rep]), __uint_as_float(r[u][4 * rep + 1]),
+                             __uint_as_float(r[u][4 * rep + 2]),
+                             __uint_as_float(r[u][4 * rep + 3])));
     }
   }
-  // the partials of this tile are consumed: clear their flags for the next
-  // launch
-  if (lane == 0)
-    for (int c2 = c_lo; c2 < c_hi; ++c2) args.sk_flags[4 * (c2 * slot_mul + slot_add) + q] = 0;
+  // publish: every lane's stores, then the flag of this quarter
+  __threadfence();
+  __syncwarp();
+  if (t == 0) st_release_gpu(args.sk_flags + 4 * self_slot + q, 1);
   return true;
+}
+
+// Finaliser of a tile cut between CTAs (epilogue warp q, lane `lane`): adds
+// the f32 partial accumulators that CTAs c_lo .. c_hi - 1 wrote for this tile
+// into this CTA's TMEM accumulator at `acc_tmem`, lane quarter q, in CTA
+// order, then clears their flags. Called after the accumulator is complete.
+// The segments (CTA, half h) of the quarter, 16 KB each, come in by 1-D bulk
+// copies into the warp's two 16 KB buffers `buf` (shared memory that the
+// CTA's last main loop no longer uses) under bars[0..1], one segment ahead of
+// the one being added; each 32 accumulator columns cost a TMEM load, 32 adds
+// from shared memory and a TMEM store. Returns false (every lane agreeing)
+// after a timeout, once the copies it issued have landed.
+__device__ __forceinline__ bool w8_add_partials(const GemmArgs& args, const FailState& fs,
+                                                uint8_t* buf, uint64_t* bars, uint32_t acc_tmem,
+                                                int q, int lane, int c_lo, int c_hi) {
+  constexpr uint32_t kSegBytes = kW8PartialFloats / 8 * sizeof(float);
+  bool ready = true;
+  for (int c2 = c_lo; c2 < c_hi && ready; ++c2) ready = wait_flag(args.sk_flags + 4 * c2 + q, fs);
+  if (!__all_sync(0xffffffffu, ready)) return false;
+  tc_fence_after();
+  const int nc = c_hi - c_lo, S = 2 * nc;
+  const uint8_t* part = reinterpret_cast<const uint8_t*>(args.sk_partials);
+  // segment s: half s / nc of CTA c_lo + s % nc (partial layout of
+  // w8_partial_index: 8 segments (q, h) of 16 KB per CTA)
+  auto src = [&](int s) {
+    return part + ((size_t)(c_lo + s % nc) * 8 + (size_t)(2 * q + s / nc)) * kSegBytes;
+  };
+  if (lane == 0) {
+    fence_proxy_async_global();
+    for (int s = 0; s < 2 && s < S; ++s) {
+      mbar_arrive_expect_tx(&bars[s], kSegBytes);
+      bulk_load_1d(buf + s * kSegBytes, src(s), kSegBytes, &bars[s]);
+    }
+  }
+  int s = 0;
+  bool ok = true;
+  for (; s < S; ++s) {
+    const int b = s & 1;
+    ok = mbar_wait(&bars[b], (uint32_t)(s >> 1) & 1u, fs);
+    if (!__all_sync(0xffffffffu, ok)) {
+      ok = false;
+      break;
+    }
+    const float4* p = reinterpret_cast<const float4*>(buf + b * kSegBytes);
+    const uint32_t taddr = acc_tmem + ((uint32_t)(16 * (2 * q + s / nc)) << 16);
+#pragma unroll 1
+    for (int c = 0; c < kW8BM / 32; c += 4) {
+      // four 32-column chunks per TMEM round trip
+      uint32_t r[4][16];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) tmem_ld_16x256b_x4(taddr + 32 * (c + u), r[u]);
+      tmem_wait_ld();
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int rep = 0; rep < 4; ++rep) {
+          const float4 v = p[((c + u) * 4 + rep) * 32 + lane];
+          r[u][4 * rep] = __float_as_uint(__uint_as_float(r[u][4 * rep]) + v.x);
+          r[u][4 * rep + 1] = __float_as_uint(__uint_as_float(r[u][4 * rep + 1]) + v.y);
+          r[u][4 * rep + 2] = __float_as_uint(__uint_as_float(r[u][4 * rep + 2]) + v.z);
+          r[u][4 * rep + 3] = __float_as_uint(__uint_as_float(r[u][4 * rep + 3]) + v.w);
+        }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) tmem_st_16x256b_x4(taddr + 32 * (c + u), r[u]);
+    }
+    tmem_wait_st();
+    // every lane has read buffer b: refill it with segment s + 2
+    __syncwarp();
+    if (lane == 0 && s + 2 < S) {
+      mbar_arrive_expect_tx(&bars[b], kSegBytes);
+      bulk_load_1d(buf + b * kSegBytes, src(s + 2), kSegBytes, &bars[b]);
+    }
+  }
+  if (!ok) {
+    // segments s and s + 1 may still be landing in the buffers
+    if (lane == 0) {
+      const unsigned long long t0 = globaltimer_ns();
+      for (int s2 = s; s2 < S && s2 < s + 2; ++s2)
+        while (!mbar_try_wait(&bars[s2 & 1], (uint32_t)(s2 >> 1) & 1u) &&
+               globaltimer_ns() - t0 < kWaitLimitNs) {
+        }
+    }
+    __syncwarp();
+    return false;
+  }
+  tc_fence_before();
+  if (lane == 0)
+    for (int c2 = c_lo; c2 < c_hi; ++c2) args.sk_flags[4 * c2 + q] = 0;
+  return true;
+}
+
+// Staged epilogue of epilogue warp q (lane t): reads the warp's accumulator
+// quarter (TMEM at `acc_tmem`, lanes 32q .. 32q + 31) four 32-column chunks per
+// TMEM round trip (two with a residual, whose pairs take the registers of the
+// other two), applies the column scales (plus the residual pair that
+// sits at the same staging address when RESID: one f16 rounding of
+// acc * s + r) and writes f16 pairs into the staging box `box` of its quarter
+// pair. Lane t writes the pair (n, n + 1), n = 16 (2q + h) + 2 (t >> 2), of
+// row m = 32 c + 8 rep + 2 (t & 3) + j at 16-byte chunk
+// (4 (q & 1) + 2 h + (t >> 4)) ^ (m & 7), word (t >> 2) & 3 of the 128-byte
+// row m: the 32 lanes of each access hit 32 different banks.
+template <bool RESID>
+__device__ __forceinline__ void w8_stage_tile(uint32_t acc_tmem, uint8_t* box, int q, int lane,
+                                              const float (&sc)[2][2]) {
+  constexpr int CH = RESID ? 2 : 4;  // 32-column chunks per TMEM round trip
+#pragma unroll 1
+  for (int h = 0; h < 2; ++h) {
+    const uint32_t taddr = acc_tmem + ((uint32_t)(16 * (2 * q + h)) << 16);
+    const float s0 = h ? sc[1][0] : sc[0][0], s1 = h ? sc[1][1] : sc[0][1];
+    const int chunk0 = 4 * (q & 1) + 2 * h + (lane >> 4);
+    const int word = 4 * ((lane >> 2) & 3);
+#pragma unroll 1
+    for (int c = 0; c < kW8BM / 32; c += CH) {
+      uint32_t r[CH][16];
+#pragma unroll
+      for (int u = 0; u < CH; ++u) tmem_ld_16x256b_x4(taddr + 32 * (c + u), r[u]);
+      uint32_t res[CH][8];
+      if (RESID) {
+#pragma unroll
+        for (int u = 0; u < CH; ++u)
+#pragma unroll
+          for (int rep = 0; rep < 4; ++rep)
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              const int m = 32 * (c + u) + 8 * rep + 2 * (lane & 3) + j;
+              res[u][2 * rep + j] = *reinterpret_cast<const uint32_t*>(
+                  box + m * 128 + ((chunk0 ^ (m & 7)) << 4) + word);
+            }
+      }
+      tmem_wait_ld();
+#pragma unroll
+      for (int u = 0; u < CH; ++u)
+#pragma unroll
+        for (int rep = 0; rep < 4; ++rep)
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int m = 32 * (c + u) + 8 * rep + 2 * (lane & 3) + j;
+            const float a0 = __uint_as_float(r[u][4 * rep + j]);
+            const float a1 = __uint_as_float(r[u][4 * rep + 2 + j]);
+            uint32_t v;
+            if (RESID) {
+              const float2 rv =
+                  __half22float2(*reinterpret_cast<const __half2*>(&res[u][2 * rep + j]));
+              v = pack_half2(__fmaf_rn(a0, s0, rv.x), __fmaf_rn(a1, s1, rv.y));
+            } else {
+              v = pack_half2(a0 * s0, a1 * s1);
+            }
+            *reinterpret_cast<uint32_t*>(box + m * 128 + ((chunk0 ^ (m & 7)) << 4) + word) = v;
+          }
+    }
+  }
 }
 
 __global__ void __launch_bounds__(kW8Threads, 1)
     gemm_w8_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
                          const __grid_constant__ CUtensorMap tmW,
-                         const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
+                         const __grid_constant__ CUtensorMap tmC,
+                         const __grid_constant__ CUtensorMap tmR, const GemmArgs args) {
   using L = W8Smem;
   // D[128 n x 256 m] += W^T (TMEM, K-major) . A^T (shared, K-major)
   constexpr uint32_t kIdesc = make_idesc_f16(kW8BN, kW8BM, 0, 0);
@@ -433,6 +452,8 @@ __global__ void __launch_bounds__(kW8Threads, 1)
   uint64_t* t_full = a_empty + kW8SA;
   uint64_t* t_empty = t_full + 2;
   uint64_t* drain = t_empty + 2;
+  uint64_t* fix_full = drain + 1;
+  uint64_t* r_full = fix_full + 2 * kW8EpiWarps;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 4);
 
@@ -451,6 +472,8 @@ __global__ void __launch_bounds__(kW8Threads, 1)
       mbar_init(&t_empty[i], kW8EpiWarps);
     }
     mbar_init(drain, 1);
+    for (int i = 0; i < 2 * kW8EpiWarps; ++i) mbar_init(&fix_full[i], 1);
+    mbar_init(r_full, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -458,6 +481,7 @@ __global__ void __launch_bounds__(kW8Threads, 1)
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmW);
     tma_prefetch_desc(&tmC);
+    if (args.C_init) tma_prefetch_desc(&tmR);
   }
   if (warp == 1) {
     tmem_alloc(tmem_holder, 512);
@@ -571,17 +595,24 @@ __global__ void __launch_bounds__(kW8Threads, 1)
     }
   } else if (warp >= 4 + kW8ConvWarps) {
     // ------------------------------------------------------ epilogue
-    // Whole tiles without a residual leave through shared memory: the
-    // accumulator is read, scaled and packed to f16 into the staging tile,
-    // the accumulator is released to the MMA at once, and one thread writes
-    // the tile to C with two TMA stores that run while the next tile's main
-    // loop does. Cut (stream-K) pieces and tiles with a residual use
-    // w8_epilogue_piece (register path, one f16 rounding of acc * s + r).
+    // Every piece that ends a tile leaves through shared memory: a tile cut
+    // between CTAs first has the other CTAs' partial accumulators added into
+    // its TMEM accumulator (w8_add_partials); the residual, if any, is loaded
+    // by TMA into the staging tile while the main loop still runs; the
+    // accumulator is read, scaled (plus the residual: one f16 rounding of
+    // acc * s + r) and packed to f16 into the staging tile, released to the
+    // MMA at once, and one thread writes the tile to C with two TMA stores
+    // that run while the next tile's main loop does. Contributor pieces
+    // write their raw accumulator to the stream-K workspace instead
+    // (w8_write_partial).
     const int q = warp & 3;
     const bool issuer = warp == 4 + kW8ConvWarps && lane == 0;
     uint8_t* stage = smem + L::kOffStage;
-    const uint32_t stage_s = smem_u32(stage);
-    int tl = 0;
+    // the warp's two 16 KB partial buffers: activation stage q (free once the
+    // CTA's last main loop is done; a cut tile's finaliser is its last piece)
+    uint8_t* fix_buf = smem + L::kOffX + q * L::kXBytes;
+    const bool resid = args.C_init != nullptr;
+    int tl = 0, rl = 0, r_landed = 0;
     bool stores_pending = false;
     long long pos = work.first();
     W8Seg sg;
@@ -590,13 +621,11 @@ __global__ void __launch_bounds__(kW8Threads, 1)
       tile_coords(sg.tile, args, tm, tn);
       const int acc = tl % kW8Acc;
       const uint32_t parity = (uint32_t)((tl / kW8Acc) & 1);
+      const uint32_t acc_tmem = tmem_base + kW8BM * acc;
       int c_lo, c_hi;
       work.contributors(sg, &c_lo, &c_hi);
-      const bool staged = sg.k0 == 0 && c_lo == c_hi && args.C_init == nullptr;
-      if (!staged) {
-        if (!w8_epilogue_piece(args, fs, &t_full[acc], parity, tmem_base + kW8BM * acc,
-                               tn * kW8BN, tm * kW8BM, q, lane, sg.k0 > 0, blockIdx.x, c_lo,
-                               c_hi, 1, 0))
+      if (sg.k0 > 0) {
+        if (!w8_write_partial(args, fs, &t_full[acc], parity, acc_tmem, q, lane, blockIdx.x))
           break;
         tc_fence_before();
         __syncwarp();
@@ -611,46 +640,31 @@ __global__ void __launch_bounds__(kW8Threads, 1)
         sc[h][0] = n < args.N ? __half2float(args.scale[n]) : 0.0f;
         sc[h][1] = n + 1 < args.N ? __half2float(args.scale[n + 1]) : 0.0f;
       }
+      if (issuer) {
+        // the previous tile's stores must have read the staging tile before
+        // the residual lands in it (or the warps write it)
+        if (stores_pending) bulk_wait_read_all();
+        if (resid) {
+          mbar_arrive_expect_tx(r_full, 2 * L::kBoxBytes);
+          tma_load_2d(stage, &tmR, r_full, tn * kW8BN, tm * kW8BM);
+          tma_load_2d(stage + L::kBoxBytes, &tmR, r_full, tn * kW8BN + 64, tm * kW8BM);
+        }
+      }
       // (a failed wait raises the CTA's abort flag before the barrier, so all
       // four warps leave together after it)
-      mbar_wait(&t_full[acc], parity, fs);
-      // the previous tile's stores must have read the staging tile
-      if (issuer && stores_pending) bulk_wait_read_all();
+      bool ok = mbar_wait(&t_full[acc], parity, fs);
+      if (ok && c_hi > c_lo)
+        ok = w8_add_partials(args, fs, fix_buf, fix_full + 2 * q, acc_tmem, q, lane, c_lo, c_hi);
+      if (ok && resid && mbar_wait(r_full, (uint32_t)(rl & 1), fs)) ++r_landed;
+      if (resid) ++rl;
       named_barrier_sync(1, 32 * kW8EpiWarps);
       if (*abort_flag) break;
       tc_fence_after();
-      // lane t writes f16 pairs (n, n + 1), n = 16 (2q + h) + 2 (t >> 2), of
-      // rows m = 32 c + 8 rep + 2 (t & 3) + j into box q >> 1 at 16-byte
-      // chunk (4 (q & 1) + 2 h + (t >> 4)) ^ (m & 7), word (t >> 2) & 3: the 32
-      // lanes of each store hit 32 different banks.
-      const uint32_t box_s = stage_s + (uint32_t)((q >> 1) * L::kBoxBytes);
-#pragma unroll 1
-      for (int h = 0; h < 2; ++h) {
-        const uint32_t taddr = tmem_base + ((uint32_t)(16 * (2 * q + h)) << 16) + kW8BM * acc;
-        const float s0 = h ? sc[1][0] : sc[0][0], s1 = h ? sc[1][1] : sc[0][1];
-        const int chunk0 = 4 * (q & 1) + 2 * h + (lane >> 4);
-        const uint32_t word = 4u * (uint32_t)((lane >> 2) & 3);
-#pragma unroll 1
-        for (int c = 0; c < kW8BM / 32; c += 2) {
-          uint32_t r[2][16];
-          tmem_ld_16x256b_x4(taddr + 32 * c, r[0]);
-          tmem_ld_16x256b_x4(taddr + 32 * (c + 1), r[1]);
-          tmem_wait_ld();
-#pragma unroll
-          for (int u = 0; u < 2; ++u)
-#pragma unroll
-            for (int rep = 0; rep < 4; ++rep)
-#pragma unroll
-              for (int j = 0; j < 2; ++j) {
-                const int m = 32 * (c + u) + 8 * rep + 2 * (lane & 3) + j;
-                const uint32_t v = pack_half2(__uint_as_float(r[u][4 * rep + j]) * s0,
-                                              __uint_as_float(r[u][4 * rep + 2 + j]) * s1);
-                const uint32_t a =
-                    box_s + (uint32_t)(m * 128 + ((chunk0 ^ (m & 7)) << 4)) + word;
-                asm volatile("st.shared.b32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
-              }
-        }
-      }
+      uint8_t* box = stage + (q >> 1) * L::kBoxBytes;
+      if (resid)
+        w8_stage_tile<true>(acc_tmem, box, q, lane, sc);
+      else
+        w8_stage_tile<false>(acc_tmem, box, q, lane, sc);
       // the accumulator is read: the MMA may start the next tile
       tc_fence_before();
       __syncwarp();
@@ -666,6 +680,14 @@ __global__ void __launch_bounds__(kW8Threads, 1)
       ++tl;
     }
     if (issuer && stores_pending) bulk_wait_all();
+    // after a failure: a residual load this thread issued may still be
+    // landing in the staging tile
+    if (issuer && r_landed < rl) {
+      const unsigned long long t0 = globaltimer_ns();
+      while (!mbar_try_wait(r_full, (uint32_t)((rl - 1) & 1)) &&
+             globaltimer_ns() - t0 < kWaitLimitNs) {
+      }
+    }
   }
 
   tc_fence_before();

@@ -174,6 +174,23 @@ __device__ __forceinline__ void bulk_wait_read_all() {
 __device__ __forceinline__ void bulk_wait_all() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
+// 1-D bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned)
+// from global memory into this CTA's shared memory; completion is signalled as
+// transaction bytes on `bar`.
+__device__ __forceinline__ void bulk_load_1d(void* dst, const void* src, uint32_t bytes,
+                                             uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+// Orders this thread's earlier generic-proxy accesses to global memory (an
+// acquire of data another CTA published) before its later async-proxy ones
+// (bulk copies of that data).
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
 
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
   asm volatile(

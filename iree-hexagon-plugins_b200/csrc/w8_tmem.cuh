@@ -67,6 +67,17 @@ __device__ __forceinline__ void tmem_ld_16x256b_x4(uint32_t taddr, uint32_t (&r)
       : "r"(taddr));
 }
 
+// Inverse of tmem_ld_16x256b_x4: writes the same register layout back.
+__device__ __forceinline__ void tmem_st_16x256b_x4(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.16x256b.x4.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
+      : "memory");
+}
+
 // Converts the 16-column chunk `chunk` (columns 16c .. 16c+15, all 64 k rows)
 // of one int8 tile into the 32 TMEM columns starting at `tmem_col` of the 16
 // TMEM lanes starting at lane `lane0` (a multiple of 16 inside this warp's

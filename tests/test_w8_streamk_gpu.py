@@ -32,7 +32,7 @@ def _t(x):
 
 
 @pytest.mark.parametrize("M,K,N,res", [
-    (512, 4096, 4096, True),     # decoder O projection: 64 tiles (data-parallel wins)
+    (512, 4096, 4096, True),     # decoder O projection: 64 tiles, stream-K
     (512, 11008, 4096, True),    # decoder down projection: stream-K
     (512, 4096, 12288, False),   # decoder qkv: 192 tiles, stream-K
     (512, 4096, 22016, False),   # decoder gate|up: 344 tiles (data-parallel wins)
