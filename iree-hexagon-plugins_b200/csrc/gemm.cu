@@ -337,23 +337,60 @@ int w8_streamk_flag_ints() { return (int)(kW8FlagBytes / sizeof(int)); }
 // 32.4 / 37.3, 4096 x 4096 x 11008 313.6 / 333.9 (M x K x N).
 constexpr long long kW8StreamKFixupKb = 28;
 constexpr long long kW8StreamKFixupWaveKb = 8;
+// The same for stream-K over the last partial wave only: its short shares
+// cut each tile into about three pieces, so a finaliser adds two or three
+// partials (fitted on B200, us, data-parallel / all stream-K / tail stream-K:
+// 512 x 4096 x 22016 89.8 / 92.7 / 87.0, 512 x 4096 x 12288 61.2 / 51.8 /
+// 55.8, 4096 x 4096 x 11008 308.8 / 323.2 / 308.7).
+constexpr long long kW8StreamKTailFixupKb = 40;
 
-// Stream-K choice of the W8 GEMM: `units` CTAs can run at once, `tiles`
-// output tiles of `num_kb` K-blocks each. Returns the number of CTAs to
-// launch with stream-K, or 0 for the data-parallel schedule.
-int w8_streamk_units(int tiles, long long num_kb, int units) {
+// Schedule of the W8 GEMM for `tiles` output tiles of `num_kb` K-blocks on
+// `units` CTAs that run at once, chosen by the estimated K-blocks of the
+// busiest CTA: data-parallel (whole tiles, `waves` rounds), stream-K over all
+// tiles (even shares plus the fix-up), or whole-tile waves followed by
+// stream-K over the last partial wave only.
+struct W8Plan {
+  int grid = 0;      // CTAs to launch
+  int streamk = 0;   // 1: stream-K over the tiles from dp_tiles on
+  int dp_tiles = 0;  // tiles dealt whole before the stream-K part
+};
+
+W8Plan w8_plan(int tiles, long long num_kb, int units) {
+  W8Plan plan;
+  plan.grid = tiles < units ? tiles : units;
   const long long total = (long long)tiles * num_kb;
   const int waves = (tiles + units - 1) / units;
   const double fill = (double)tiles / ((double)waves * units);
+  long long best = (long long)waves * num_kb;
+  // stream-K over all tiles: fewer tiles than units (spread them over more
+  // units), or several waves evened out over all units
   const long long g = total / kW8MinShare < units ? total / kW8MinShare : units;
-  const long long fixup = kW8StreamKFixupKb + kW8StreamKFixupWaveKb * (waves - 1);
-  // fewer tiles than units: spread them over more units; several waves: even
-  // out the last one over all units -- when the even shares plus the fix-up
-  // beat the data-parallel waves
-  if (fill < 0.92 && (g > tiles || (tiles > units && g == units)) && g > 0 &&
-      (total + g - 1) / g + fixup < (long long)waves * num_kb)
-    return (int)g;
-  return 0;
+  if (fill < 0.92 && (g > tiles || (tiles > units && g == units)) && g > 0) {
+    const long long cost =
+        (total + g - 1) / g + kW8StreamKFixupKb + kW8StreamKFixupWaveKb * (waves - 1);
+    if (cost < best) {
+      best = cost;
+      plan.grid = (int)g;
+      plan.streamk = 1;
+      plan.dp_tiles = 0;
+    }
+  }
+  // whole-tile waves, then the last partial wave split over all units
+  if (waves >= 2) {
+    const int dp_tiles = (waves - 1) * units;
+    const long long tail = (long long)(tiles - dp_tiles) * num_kb;
+    if (tail >= (long long)units * kW8MinShare) {
+      const long long cost =
+          (long long)(waves - 1) * num_kb + (tail + units - 1) / units + kW8StreamKTailFixupKb;
+      if (cost < best) {
+        best = cost;
+        plan.grid = units;
+        plan.streamk = 1;
+        plan.dp_tiles = dp_tiles;
+      }
+    }
+  }
+  return plan;
 }
 
 hxb_status_t gemm_w8_impl(const void* A, int64_t lda, const void* W,
@@ -419,12 +456,14 @@ hxb_status_t gemm_w8_impl(const void* A, int64_t lda, const void* W,
   const int sms = dev->num_sms;
   int grid = tiles < sms ? tiles : sms;
   // Stream-K (when the caller gave the workspace) if whole tiles would leave
-  // SMs idle in the last wave: every SM then gets the same share of K-blocks.
+  // SMs idle in the last wave: every SM then gets the same share of K-blocks
+  // of all tiles, or of the last partial wave's.
   if (sk_ws && sms <= kW8MaxStreamKCtas && sk_ws_bytes >= w8_streamk_workspace_bytes(sms)) {
-    const int g = w8_streamk_units(tiles, (K + kBK - 1) / kBK, sms);
-    if (g) {
-      grid = g;
+    const W8Plan plan = w8_plan(tiles, (K + kBK - 1) / kBK, sms);
+    if (plan.streamk) {
+      grid = plan.grid;
       args.streamk = 1;
+      args.sk_dp_tiles = plan.dp_tiles;
       args.sk_flags = static_cast<int*>(sk_ws);
       args.sk_partials =
           reinterpret_cast<float*>(static_cast<uint8_t*>(sk_ws) + kW8FlagBytes);

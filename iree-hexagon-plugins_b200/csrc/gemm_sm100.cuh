@@ -54,6 +54,7 @@ struct GemmArgs {
   int streamk;
   int* sk_flags;
   float* sk_partials;
+  int sk_dp_tiles;  // tiles before the stream-K part, dealt whole round-robin
 };
 
 constexpr int kBM = 128;

@@ -40,9 +40,10 @@
 // the tensor core); the f16 weights live only in registers and TMEM.
 //
 // Work split. Data-parallel: CTA b owns whole output tiles b, b + grid, ...
-// Stream-K (args.streamk): the tiles x K-blocks iteration space is cut into
-// `grid` equal contiguous shares, so every SM gets the same number of MMAs
-// whatever the tile count. A tile cut between CTAs is summed as follows: the
+// Stream-K (args.streamk): the tiles x K-blocks iteration space of the tiles
+// from args.sk_dp_tiles on (all of them, or the last partial wave after
+// whole-tile waves) is cut into `grid` equal contiguous shares, so every SM
+// gets the same number of MMAs whatever the tile count. A tile cut between CTAs is summed as follows: the
 // CTA holding the tile's first K-block (it processes that piece LAST, at the
 // end of its share) finalises it; every other CTA holding a piece of the
 // tile holds it FIRST, writes its f32 partial accumulator to
@@ -150,38 +151,47 @@ struct W8Seg {
 };
 
 // The sequence of pieces one work unit (a CTA) processes; the same for all
-// roles of the unit. Units are numbered 0 .. nunits-1.
+// roles of the unit. Units are numbered 0 .. nunits-1. Tiles [0, dp_tiles)
+// are whole tiles dealt round-robin (unit u takes u, u + nunits, ...); the
+// K-blocks of tiles [dp_tiles, num_tiles) are cut into nunits equal
+// contiguous stream-K shares, which each unit processes after its whole
+// tiles (dp_tiles = num_tiles without stream-K, 0 for stream-K over all
+// tiles). Positions count iterations: tile * num_kb + K-block.
 struct W8Work {
-  int num_kb, num_tiles, streamk, unit, nunits;
-  long long total, it0, it1;
+  int num_kb, num_tiles, dp_tiles, unit, nunits;
+  long long sk_base, sk_total, it0, it1;
 
-  // First iteration of unit c's stream-K share (total >= nunits, so no share
-  // is empty).
-  __device__ __forceinline__ long long share_begin(int c) const { return total * c / nunits; }
+  // First iteration of unit c's stream-K share (sk_total >= nunits when
+  // there is a stream-K part, so no share is empty).
+  __device__ __forceinline__ long long share_begin(int c) const {
+    return sk_base + sk_total * c / nunits;
+  }
   __device__ __forceinline__ void init(const GemmArgs& a, int unit_, int nunits_) {
     unit = unit_;
     nunits = nunits_;
     num_kb = (a.K + kBK - 1) / kBK;
     num_tiles = a.tiles_m * a.tiles_n;
-    streamk = a.streamk;
-    total = (long long)num_tiles * num_kb;
+    dp_tiles = a.streamk ? a.sk_dp_tiles : num_tiles;
+    sk_base = (long long)dp_tiles * num_kb;
+    sk_total = (long long)(num_tiles - dp_tiles) * num_kb;
     it0 = share_begin(unit);
     it1 = share_begin(unit + 1);
   }
-  __device__ __forceinline__ long long first() const { return streamk ? it0 : unit; }
+  __device__ __forceinline__ long long first() const {
+    return unit < dp_tiles ? (long long)unit * num_kb : it0;
+  }
   // K-blocks this unit processes in all.
   __device__ __forceinline__ long long kb_count() const {
-    if (streamk) return it1 - it0;
-    const long long nt = unit < num_tiles ? (num_tiles - 1 - unit) / nunits + 1 : 0;
-    return nt * num_kb;
+    const long long nt = unit < dp_tiles ? (dp_tiles - 1 - unit) / nunits + 1 : 0;
+    return nt * num_kb + (it1 - it0);
   }
   __device__ __forceinline__ bool next(long long& pos, W8Seg& s) const {
-    if (!streamk) {
-      if (pos >= num_tiles) return false;
-      s.tile = (int)pos;
+    if (pos < sk_base) {
+      s.tile = (int)(pos / num_kb);
       s.k0 = 0;
       s.k1 = num_kb;
-      pos += nunits;
+      pos += (long long)nunits * num_kb;
+      if (pos >= sk_base) pos = it0;
       return true;
     }
     if (pos >= it1) return false;

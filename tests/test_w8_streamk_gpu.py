@@ -1,6 +1,7 @@
-"""Parity of the stream-K schedule of the int8-weight GEMM
+"""Parity of the stream-K schedules of the int8-weight GEMM
 (hxb_matmul_w8a16_streamk): K split across CTAs when whole tiles would leave
-SMs idle, partial sums added by the CTA that owns the tile's first K-block.
+SMs idle -- over all tiles, or over the last partial wave after whole-tile
+waves -- partial sums added by the CTA that owns the tile's first K-block.
 
 Shapes are the decoder block's M = 512 projections (64 and 344 output tiles
 of 128 weight columns x 256 rows on 148 SMs) and small ragged cases where one
@@ -34,8 +35,10 @@ def _t(x):
 @pytest.mark.parametrize("M,K,N,res", [
     (512, 4096, 4096, True),     # decoder O projection: 64 tiles, stream-K
     (512, 11008, 4096, True),    # decoder down projection: stream-K
-    (512, 4096, 12288, False),   # decoder qkv: 192 tiles, stream-K
-    (512, 4096, 22016, False),   # decoder gate|up: 344 tiles (data-parallel wins)
+    (512, 4096, 12288, False),   # decoder qkv: 192 tiles, stream-K over all
+    (512, 4096, 22016, False),   # decoder gate|up: 344 tiles, two whole waves + stream-K tail
+    (4096, 4096, 11008, False),  # BASELINE cfg 2: 1376 tiles, nine whole waves + stream-K tail
+    (300, 7992, 23008, True),    # ragged M, K and N, two whole waves + stream-K tail
     (129, 4000, 272, True),      # ragged K and M, stream-K over 3 tiles
     (100, 8192, 144, False),     # 2 tiles cut into 16 pieces each
     (200, 320, 528, False),      # too little K to split: data-parallel
@@ -52,7 +55,8 @@ def test_streamk_vs_oracle(cuda_pkg, oracle, M, K, N, res):
     # a fixed order, so a second call is bit-identical
     assert int(ws[:FLAG_BYTES].count_nonzero()) == 0
     assert torch.equal(got, again)
-    rows = np.arange(M) if M * K * N <= 2**31 else np.array([0, 1, 190, 191, 255, 256, 383, 384, 511])
+    rows = np.arange(M) if M * K * N <= 2**31 else np.array(
+        [r for r in (0, 1, 190, 191, 255, 256, 299, 383, 384, 511, 2047, 4095) if r < M])
     ref = oracle.matmul_w8a16_f32(a[rows], w, s)
     if res:
         ref = ref + r[rows].astype(np.float32)
