@@ -94,7 +94,8 @@ struct AttArgs {
   int o_hpr;          // O heads per row
   long long kv_stride;  // K/V rows per head
   long long ldo;      // O row pitch (elements)
-  int q_blocks;       // query blocks per head: ceil(Sq / 256)
+  int q_rows;         // rows per query block: 256 (two tiles) or 128 (one)
+  int q_blocks;       // query blocks per head: ceil(Sq / q_rows)
   int q_box;          // Q rows one TMA box brings (min(128, Sq rounded up to 8))
   int kv_splits;      // CTAs sharing one query block's keys (1: no split)
   int split_blocks;   // key blocks per split
@@ -110,11 +111,11 @@ struct AttArgs {
   int* status;
 };
 
-// Number of key blocks CTA rows [q0, q0+256) may see.
+// Number of key blocks CTA rows [q0, q0 + q_rows) may see.
 __device__ __forceinline__ int kv_blocks_for(const AttArgs& a, int q0) {
   int last_key = a.Skv - 1;
   if (a.causal) {
-    const int last_row = min(q0 + kAttTiles * kAttBM, a.Sq) - 1;
+    const int last_row = min(q0 + a.q_rows, a.Sq) - 1;
     // the largest query position among the rows: a CTA spanning two query
     // heads holds the last position of the first one
     const int last_pos = last_row / a.q_len != q0 / a.q_len ? a.q_len - 1 : last_row % a.q_len;
@@ -182,13 +183,13 @@ __global__ void __launch_bounds__(kAttThreads, 1)
   const int qy = bh / args.q_hpr;         // Q row block of this head
   const int kx = (bh % args.kv_hpr) * D;  // K/V column
   const int ky = bh / args.kv_hpr;        // K/V row block
-  const int q0 = qb * kAttTiles * kAttBM;
+  const int q0 = qb * args.q_rows;
   // this CTA's key blocks: [j0, j0 + n_kv) of the query block's visible ones
   const int visible = kv_blocks_for(args, q0);
   const int j0 = split * args.split_blocks;
   const int n_kv = args.kv_splits == 1 ? visible : max(0, min(visible - j0, args.split_blocks));
   // a second query tile only when the rows reach into it
-  const int n_tiles = args.Sq - q0 > kAttBM ? kAttTiles : 1;
+  const int n_tiles = args.q_rows > kAttBM && args.Sq - q0 > kAttBM ? kAttTiles : 1;
   const FailState fs{abort_flag, args.status};
 
   if (threadIdx.x == 0) {
@@ -425,7 +426,8 @@ __global__ void __launch_bounds__(kAttThreads, 1)
     const long long qhead = (long long)bh * args.group + qrow / args.q_len;
     __half* orow = args.O + (qhead / args.o_hpr * args.q_len + qpos) * args.ldo +
                    qhead % args.o_hpr * D;
-    const bool write = (ok || n_kv == 0) && qrow < args.Sq;
+    // (a tile the block does not run leaves its rows to the next block)
+    const bool write = t < n_tiles && (ok || n_kv == 0) && qrow < args.Sq;
     const bool partial = args.kv_splits > 1;
     // split keys: this CTA's normalised O and log2-sum-exp2 of its row
     const size_t pidx = (size_t)blockIdx.x * args.part_rows + (t * kAttBM + r);
@@ -866,7 +868,7 @@ __global__ void __launch_bounds__(256)
   const int lane = threadIdx.x & 31;
   if (gw >= (long long)heads * args.Sq) return;
   const int bh = (int)(gw / args.Sq), qrow = (int)(gw % args.Sq);
-  const int qb = qrow / (kAttTiles * kAttBM), prow = qrow % (kAttTiles * kAttBM);
+  const int qb = qrow / args.q_rows, prow = qrow % args.q_rows;
   const size_t unit0 = ((size_t)bh * args.q_blocks + qb) * args.kv_splits;
   float mx = -INFINITY;
   for (int sp = lane; sp < args.kv_splits; sp += 32)
@@ -1053,13 +1055,18 @@ hxb_status_t attention_run(const AttLayout& a, float scale, int causal, cudaStre
   const int64_t rows_q = a.heads / a.q_hpr * Sq, rows_kv = a.heads / a.kv_hpr * a.kv_stride;
   if (rows_q > INT32_MAX || rows_kv > INT32_MAX)
     return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: extent too large");
-  const int64_t q_blocks = (Sq + kAttTiles * kAttBM - 1) / (kAttTiles * kAttBM);
-  if (q_blocks * a.heads > INT32_MAX / 1024)
-    return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: too many query tiles");
-
   DeviceInfo* dev = nullptr;
   hxb_status_t s = current_device(&dev);
   if (s != HXB_OK) return s;
+  // Query blocks of two 128-row tiles (the tiles take turns on the tensor
+  // core), or of one tile when two-tile blocks would leave SMs idle (a
+  // prefill of a few hundred rows: twice the CTAs, half the longest causal
+  // walk).
+  int64_t q_rows = kAttTiles * kAttBM;
+  if (Sq > kAttBM && (Sq + q_rows - 1) / q_rows * a.heads < dev->num_sms) q_rows = kAttBM;
+  const int64_t q_blocks = (Sq + q_rows - 1) / q_rows;
+  if (q_blocks * a.heads > INT32_MAX / 1024)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "attention: too many query tiles");
   SplitPlan plan = plan_splits(q_blocks * a.heads, Sq, a.Skv, D, split_units(Sq, D, dev->num_sms));
   if (plan.splits > 1 && (!a.workspace || a.workspace_bytes < plan.bytes ||
                           (reinterpret_cast<uintptr_t>(a.workspace) & 15u))) {
@@ -1086,6 +1093,7 @@ hxb_status_t attention_run(const AttLayout& a, float scale, int causal, cudaStre
   args.o_hpr = (int)a.o_hpr;
   args.kv_stride = a.kv_stride;
   args.ldo = a.ldo;
+  args.q_rows = (int)q_rows;
   args.q_blocks = (int)q_blocks;
   args.q_box = q_box;
   args.kv_splits = plan.splits;
