@@ -161,6 +161,21 @@ hxb_status_t hxb_matmul_w8a16_residual(const void* A, int64_t lda, const void* W
  * accumulator per SM. */
 size_t hxb_matmul_w8a16_workspace_bytes(int64_t M, int64_t N, int64_t K);
 
+/* Schedule of hxb_matmul_w8a16_streamk for M > 16 rows on num_sms SMs, as
+ * the dispatch plans it: *grid CTAs; the first *dp_tiles output tiles (128
+ * weight columns x 256 activation rows; tile t is row tile t % ceil(M / 256)
+ * of column tile t / ceil(M / 256)) are dealt whole, round-robin, and the
+ * K-blocks (64 deep) of the others are cut into *grid equal shares
+ * (*dp_tiles == number of tiles: data-parallel). When `pieces` is not NULL it
+ * receives up to `cap` records of 5 int32 -- CTA, tile, first K-block, end
+ * K-block, and the number of other CTAs whose partial sums the piece adds
+ * (non-zero only for the piece that finishes a cut tile) -- in each CTA's
+ * processing order, the same enumeration the kernel runs; *count (may be
+ * NULL) gets the number of records. Host only, no GPU needed. */
+hxb_status_t hxb_plan_matmul_w8a16(int64_t M, int64_t N, int64_t K, int num_sms,
+                                   int* grid, int* dp_tiles, int32_t* pieces,
+                                   int64_t cap, int64_t* count);
+
 /* hxb_matmul_w8a16 (R optional, may be NULL) that may split K across CTAs
  * (stream-K) when whole output tiles would leave SMs idle in the last wave,
  * e.g. the M = 512 projections of the decoder block. Tiles cut between CTAs

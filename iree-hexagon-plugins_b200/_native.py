@@ -36,6 +36,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                      c_i64, c_i64, c_i64, c_int, c_int, c_vp]),
     "hxb_matmul_w8a16": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_i64,
                                  c_i64, c_i64, c_i64, c_vp]),
+    "hxb_plan_matmul_w8a16": (c_int, [c_i64, c_i64, c_i64, c_int, ctypes.POINTER(c_int),
+                                      ctypes.POINTER(c_int), ctypes.POINTER(ctypes.c_int32),
+                                      c_i64, ctypes.POINTER(c_i64)]),
     "hxb_attention_f16": (c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64,
                                   c_i64, c_float, c_int, c_vp]),
     "hxb_matmul_w8a16_residual": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp,

@@ -551,6 +551,47 @@ extern "C" hxb_status_t hxb_matmul_w8a16_residual(const void* A, int64_t lda, co
                                 static_cast<cudaStream_t>(stream));
 }
 
+extern "C" hxb_status_t hxb_plan_matmul_w8a16(int64_t M, int64_t N, int64_t K, int num_sms,
+                                             int* grid, int* dp_tiles, int32_t* pieces,
+                                             int64_t cap, int64_t* count) {
+  using namespace hxb;
+  if (M <= kGemvRows || N < 1 || K < 1 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "plan_matmul_w8a16: M > %d, N, K >= 1 required",
+                kGemvRows);
+  if (num_sms < 1 || num_sms > kW8MaxStreamKCtas || !grid || !dp_tiles || (pieces && cap < 0))
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "plan_matmul_w8a16: bad arguments");
+  GemmArgs args{};
+  args.M = (int)M;
+  args.N = (int)N;
+  args.K = (int)K;
+  args.tiles_m = (int)((M + kW8BM - 1) / kW8BM);
+  args.tiles_n = (int)((N + kW8BN - 1) / kW8BN);
+  const int tiles = args.tiles_m * args.tiles_n;
+  const W8Plan plan = w8_plan(tiles, (K + kBK - 1) / kBK, num_sms);
+  args.streamk = plan.streamk;
+  args.sk_dp_tiles = plan.dp_tiles;
+  *grid = plan.grid;
+  *dp_tiles = plan.streamk ? plan.dp_tiles : tiles;
+  int64_t n = 0;
+  for (int u = 0; u < plan.grid; ++u) {
+    W8Work work;
+    work.init(args, u, plan.grid);
+    long long pos = work.first();
+    W8Seg sg;
+    while (work.next(pos, sg)) {
+      int c_lo, c_hi;
+      work.contributors(sg, &c_lo, &c_hi);
+      if (pieces && n < cap) {
+        int32_t* r = pieces + 5 * n;
+        r[0] = u, r[1] = sg.tile, r[2] = sg.k0, r[3] = sg.k1, r[4] = c_hi - c_lo;
+      }
+      ++n;
+    }
+  }
+  if (count) *count = n;
+  return HXB_OK;
+}
+
 extern "C" size_t hxb_matmul_w8a16_workspace_bytes(int64_t M, int64_t N, int64_t K) {
   (void)M;
   (void)N;

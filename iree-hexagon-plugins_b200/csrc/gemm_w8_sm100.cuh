@@ -151,7 +151,7 @@ struct W8Seg {
 };
 
 // The sequence of pieces one work unit (a CTA) processes; the same for all
-// roles of the unit. Units are numbered 0 .. nunits-1. Tiles [0, dp_tiles)
+// roles of the unit (and for the host-side schedule query). Units are numbered 0 .. nunits-1. Tiles [0, dp_tiles)
 // are whole tiles dealt round-robin (unit u takes u, u + nunits, ...); the
 // K-blocks of tiles [dp_tiles, num_tiles) are cut into nunits equal
 // contiguous stream-K shares, which each unit processes after its whole
@@ -163,10 +163,10 @@ struct W8Work {
 
   // First iteration of unit c's stream-K share (sk_total >= nunits when
   // there is a stream-K part, so no share is empty).
-  __device__ __forceinline__ long long share_begin(int c) const {
+  __host__ __device__ __forceinline__ long long share_begin(int c) const {
     return sk_base + sk_total * c / nunits;
   }
-  __device__ __forceinline__ void init(const GemmArgs& a, int unit_, int nunits_) {
+  __host__ __device__ __forceinline__ void init(const GemmArgs& a, int unit_, int nunits_) {
     unit = unit_;
     nunits = nunits_;
     num_kb = (a.K + kBK - 1) / kBK;
@@ -177,15 +177,15 @@ struct W8Work {
     it0 = share_begin(unit);
     it1 = share_begin(unit + 1);
   }
-  __device__ __forceinline__ long long first() const {
+  __host__ __device__ __forceinline__ long long first() const {
     return unit < dp_tiles ? (long long)unit * num_kb : it0;
   }
   // K-blocks this unit processes in all.
-  __device__ __forceinline__ long long kb_count() const {
+  __host__ __device__ __forceinline__ long long kb_count() const {
     const long long nt = unit < dp_tiles ? (dp_tiles - 1 - unit) / nunits + 1 : 0;
     return nt * num_kb + (it1 - it0);
   }
-  __device__ __forceinline__ bool next(long long& pos, W8Seg& s) const {
+  __host__ __device__ __forceinline__ bool next(long long& pos, W8Seg& s) const {
     if (pos < sk_base) {
       s.tile = (int)(pos / num_kb);
       s.k0 = 0;
@@ -204,7 +204,7 @@ struct W8Work {
   }
   // Units whose partial accumulators the finalising piece `sg` adds:
   // [*lo, *hi) (empty unless sg is cut and holds the tile's first K-block).
-  __device__ __forceinline__ void contributors(const W8Seg& sg, int* lo, int* hi) const {
+  __host__ __device__ __forceinline__ void contributors(const W8Seg& sg, int* lo, int* hi) const {
     *lo = *hi = unit + 1;
     if (sg.k0 == 0 && sg.k1 < num_kb) {
       const long long tile_end = (long long)(sg.tile + 1) * num_kb;
