@@ -95,6 +95,64 @@ __global__ void rmsnorm_kernel(const __half* __restrict__ x, long long ldx,
   }
 }
 
+// The same normalisation with one 256-thread block per row, the row held in
+// registers (cols <= 8192, cols % 8 == 0): for a few rows (decode steps),
+// where one warp per row would walk 16 dependent vector loads. Only the
+// order of the sum of squares differs from rmsnorm_kernel.
+constexpr int kNormBlockThreads = 256;
+constexpr int kNormBlockVecs = 4;  // 16-byte vectors of x per thread
+constexpr int kNormBlockMaxCols = kNormBlockThreads * kNormBlockVecs * 8;
+__global__ void __launch_bounds__(kNormBlockThreads)
+    rmsnorm_block_kernel(const __half* __restrict__ x, long long ldx,
+                         const __half* __restrict__ gamma, __half* __restrict__ y,
+                         long long ldy, int rows, int cols, float eps, int* clear, int nclear) {
+  __shared__ float part[kNormBlockThreads / 32];
+  pdl_wait();
+  pdl_trigger();
+  if (clear && blockIdx.x == 0)
+    for (int i = threadIdx.x; i < nclear; i += blockDim.x) clear[i] = 0;
+  const __half* xr = x + (long long)blockIdx.x * ldx;
+  __half* yr = y + (long long)blockIdx.x * ldy;
+  uint4 v[kNormBlockVecs];
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kNormBlockVecs; ++i) {
+    const int c = (i * kNormBlockThreads + threadIdx.x) * 8;
+    v[i] = c < cols ? *reinterpret_cast<const uint4*>(xr + c) : make_uint4(0, 0, 0, 0);
+    const __half2* h = reinterpret_cast<const __half2*>(&v[i]);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __half22float2(h[e]);
+      ss = fmaf(f.x, f.x, ss);
+      ss = fmaf(f.y, f.y, ss);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.0f;
+#pragma unroll
+  for (int w = 0; w < kNormBlockThreads / 32; ++w) tot += part[w];
+  const float r = rsqrtf(tot / (float)cols + eps);
+#pragma unroll
+  for (int i = 0; i < kNormBlockVecs; ++i) {
+    const int c = (i * kNormBlockThreads + threadIdx.x) * 8;
+    if (c >= cols) break;
+    const uint4 g = *reinterpret_cast<const uint4*>(gamma + c);
+    const __half2* h = reinterpret_cast<const __half2*>(&v[i]);
+    const __half2* gh = reinterpret_cast<const __half2*>(&g);
+    uint4 o;
+    __half2* oh = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __half22float2(h[e]);
+      oh[e] = __hmul2(__floats2half2_rn(f.x * r, f.y * r), gh[e]);
+    }
+    *reinterpret_cast<uint4*>(yr + c) = o;
+  }
+}
+
 // In-place rotary embedding of `heads` consecutive 128-wide heads at the
 // start of every row (the q and k blocks of a fused QKV row). One warp per
 // (row, head); lane i handles the rotate-half pairs (i, i + 64) and
@@ -244,6 +302,12 @@ hxb_status_t check_kv_cache_write(const void* k_src, const void* v_src, int64_t 
 hxb_status_t launch_rmsnorm(const void* x, int64_t ldx, const void* gamma, void* y, int64_t ldy,
                             int64_t rows, int64_t cols, float eps, cudaStream_t stream,
                             int* clear = nullptr, int nclear = 0) {
+  // a block per row while the rows alone would leave most SMs idle
+  if (rows <= 32 && cols <= kNormBlockMaxCols)
+    return launch_pdl(rmsnorm_block_kernel, dim3((unsigned)rows), dim3(kNormBlockThreads), 0,
+                      stream, "rmsnorm launch", static_cast<const __half*>(x), (long long)ldx,
+                      static_cast<const __half*>(gamma), static_cast<__half*>(y),
+                      (long long)ldy, (int)rows, (int)cols, eps, clear, nclear);
   const int threads = 256;
   const long long blocks = (rows * 32 + threads - 1) / threads;
   return launch_pdl(rmsnorm_kernel, dim3((unsigned)blocks), dim3(threads), 0, stream,

@@ -33,15 +33,21 @@ def _within_ulps(ref, got, ulps, what):
                            f"{np.abs(g - r).max():.4g}")
 
 
-def test_rmsnorm_vs_oracle(cuda_pkg, oracle):
+@pytest.mark.parametrize("rows,cols", [
+    (300, 4096),   # one warp per row
+    (1, 4096),     # decode step: one block per row
+    (7, 1000),     # a few rows, ragged vector count per thread
+    (32, 8192),    # the largest rows the block-per-row kernel holds
+])
+def test_rmsnorm_vs_oracle(cuda_pkg, oracle, rows, cols):
     rng = np.random.default_rng(1)
-    x = (rng.standard_normal((300, 4096)) * 3).astype(np.float16)
-    g = rng.uniform(0.5, 1.5, 4096).astype(np.float16)
+    x = (rng.standard_normal((rows, cols)) * 3).astype(np.float16)
+    g = rng.uniform(0.5, 1.5, cols).astype(np.float16)
     got = cuda_pkg.rmsnorm(_t(x), _t(g), 1e-5).cpu().numpy()
     # two f16 roundings (normalised row, then times the weight): a 1-ulp flip of
     # the first, scaled by a weight up to 1.5, can reach 2 ulp of the result
     _within_ulps(oracle.rmsnorm_f16(x, g, 1e-5), got, 2, "rmsnorm")
-    ones = np.ones(4096, np.float16)
+    ones = np.ones(cols, np.float16)
     got1 = cuda_pkg.rmsnorm(_t(x), _t(ones), 1e-5).cpu().numpy()
     _within_ulps(oracle.rmsnorm_f16(x, ones, 1e-5), got1, 1, "rmsnorm (unit weight)")
 
