@@ -870,8 +870,10 @@ __global__ void __launch_bounds__(256)
   const int bh = (int)(gw / args.Sq), qrow = (int)(gw % args.Sq);
   const int qb = qrow / args.q_rows, prow = qrow % args.q_rows;
   const size_t unit0 = ((size_t)bh * args.q_blocks + qb) * args.kv_splits;
+  const int S = args.kv_splits;
+  // lane-parallel: the row maximum of the splits' log2-sum-exp2
   float mx = -INFINITY;
-  for (int sp = lane; sp < args.kv_splits; sp += 32)
+  for (int sp = lane; sp < S; sp += 32)
     mx = fmaxf(mx, args.part_lse[(unit0 + sp) * args.part_rows + prow]);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -880,23 +882,38 @@ __global__ void __launch_bounds__(256)
   for (int e = 0; e < kPer; ++e) acc[e] = 0.0f;
   float wsum = 0.0f;
   if (mx != -INFINITY) {
-    for (int sp = 0; sp < args.kv_splits; ++sp) {
-      const size_t idx = (unit0 + sp) * args.part_rows + prow;
-      const float w = ex2_approx(args.part_lse[idx] - mx);  // 0 for -inf
+    for (int base = 0; base < S; base += 32) {
+      // lane l holds the weight of split base + l; the partial rows are
+      // loaded four splits at a time, so a row costs few memory round trips
+      const int n = min(32, S - base);
+      const float l2 =
+          lane < n ? args.part_lse[(unit0 + base + lane) * args.part_rows + prow] : -INFINITY;
+      const float w = ex2_approx(l2 - mx);  // 0 for -inf
       wsum += w;
-      const float* po = args.part_o + idx * D + lane * kPer;
-      if constexpr (kPer == 4) {
-        const float4 o = *reinterpret_cast<const float4*>(po);
-        acc[0] = fmaf(w, o.x, acc[0]);
-        acc[1] = fmaf(w, o.y, acc[1]);
-        acc[2] = fmaf(w, o.z, acc[2]);
-        acc[3] = fmaf(w, o.w, acc[3]);
-      } else {
-        const float2 o = *reinterpret_cast<const float2*>(po);
-        acc[0] = fmaf(w, o.x, acc[0]);
-        acc[1] = fmaf(w, o.y, acc[1]);
+      for (int j = 0; j < n; j += 4) {
+        float o[4][kPer];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const size_t idx = (unit0 + base + min(j + u, n - 1)) * args.part_rows + prow;
+          const float* po = args.part_o + idx * D + lane * kPer;
+          if constexpr (kPer == 4) {
+            const float4 v = *reinterpret_cast<const float4*>(po);
+            o[u][0] = v.x, o[u][1] = v.y, o[u][2] = v.z, o[u][3] = v.w;
+          } else {
+            const float2 v = *reinterpret_cast<const float2*>(po);
+            o[u][0] = v.x, o[u][1] = v.y;
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float wu = j + u < n ? __shfl_sync(0xffffffffu, w, j + u) : 0.0f;
+#pragma unroll
+          for (int e = 0; e < kPer; ++e) acc[e] = fmaf(wu, o[u][e], acc[e]);
+        }
       }
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
   }
   const float inv = wsum > 0.0f ? 1.0f / wsum : 0.0f;
   const long long qhead = (long long)bh * args.group + qrow / args.q_len;
