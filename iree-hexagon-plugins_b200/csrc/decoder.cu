@@ -96,9 +96,10 @@ __global__ void rmsnorm_kernel(const __half* __restrict__ x, long long ldx,
 }
 
 // The same normalisation with one 256-thread block per row, the row held in
-// registers (cols <= 8192, cols % 8 == 0): for a few rows (decode steps),
-// where one warp per row would walk 16 dependent vector loads. Only the
-// order of the sum of squares differs from rmsnorm_kernel.
+// registers (cols <= 8192, cols % 8 == 0): for up to 1024 rows (decode steps,
+// prefills of a few hundred tokens), where one warp per row leaves too few
+// warps per SM to hide its 16 dependent vector loads. Only the order of the
+// sum of squares differs from rmsnorm_kernel.
 constexpr int kNormBlockThreads = 256;
 constexpr int kNormBlockVecs = 4;  // 16-byte vectors of x per thread
 constexpr int kNormBlockMaxCols = kNormBlockThreads * kNormBlockVecs * 8;
@@ -302,8 +303,9 @@ hxb_status_t check_kv_cache_write(const void* k_src, const void* v_src, int64_t 
 hxb_status_t launch_rmsnorm(const void* x, int64_t ldx, const void* gamma, void* y, int64_t ldy,
                             int64_t rows, int64_t cols, float eps, cudaStream_t stream,
                             int* clear = nullptr, int nclear = 0) {
-  // a block per row while the rows alone would leave most SMs idle
-  if (rows <= 32 && cols <= kNormBlockMaxCols)
+  // a block per row while one warp per row would leave the SMs with too few
+  // warps to hide the row's load latency
+  if (rows <= 1024 && cols <= kNormBlockMaxCols)
     return launch_pdl(rmsnorm_block_kernel, dim3((unsigned)rows), dim3(kNormBlockThreads), 0,
                       stream, "rmsnorm launch", static_cast<const __half*>(x), (long long)ldx,
                       static_cast<const __half*>(gamma), static_cast<__half*>(y),

@@ -34,8 +34,9 @@ def _within_ulps(ref, got, ulps, what):
 
 
 @pytest.mark.parametrize("rows,cols", [
-    (300, 4096),   # one warp per row
-    (1, 4096),     # decode step: one block per row
+    (1100, 4096),  # one warp per row
+    (300, 4096),   # a prefill: one block per row
+    (1, 4096),     # decode step
     (7, 1000),     # a few rows, ragged vector count per thread
     (32, 8192),    # the largest rows the block-per-row kernel holds
 ])
