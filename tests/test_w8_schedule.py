@@ -79,6 +79,28 @@ def test_w8_schedule_covers_every_k_block_once(pkg, M, K, N, kind):
         assert max(sk_kb) - min(sk_kb) <= 1
 
 
+@pytest.mark.parametrize("sms", [132, 160, 7])
+@pytest.mark.parametrize("M,K,N", [(512, 4096, 22016), (4096, 4096, 11008), (300, 7992, 23008),
+                                   (129, 4000, 272)])
+def test_w8_schedule_other_sm_counts(pkg, sms, M, K, N):
+    """The split invariants hold whatever the SM count the plan is made for."""
+    lib = pkg._native.load()
+    grid, dp, rows = _plan(lib, M, N, K, sms)
+    tiles_m, tiles_n, nkb = -(-M // 256), -(-N // 128), -(-K // 64)
+    tiles = tiles_m * tiles_n
+    assert 1 <= grid <= sms and 0 <= dp <= tiles
+    seen = defaultdict(int)
+    last_piece = {}
+    for cta, tile, k0, k1, nadd in rows:
+        for kb in range(k0, k1):
+            seen[(tile, kb)] += 1
+        last_piece[cta] = (tile, k0, k1)
+    assert len(seen) == tiles * nkb and set(seen.values()) == {1}
+    for cta, tile, k0, k1, nadd in rows:
+        if k0 == 0 and k1 < nkb:
+            assert last_piece[cta] == (tile, k0, k1)
+
+
 def test_w8_schedule_rejects_gemv_shapes(pkg):
     grid, dp = ctypes.c_int(), ctypes.c_int()
     assert pkg._native.load().hxb_plan_matmul_w8a16(16, 4096, 4096, SMS, ctypes.byref(grid),
