@@ -156,27 +156,35 @@ __global__ void __launch_bounds__(kNormBlockThreads)
 
 // In-place rotary embedding of `heads` consecutive 128-wide heads at the
 // start of every row (the q and k blocks of a fused QKV row). One warp per
-// (row, head); lane i handles the rotate-half pairs (i, i + 64) and
-// (i + 32, i + 96). Row r has position pos0 + r % seq.
-// Rotates one 128-wide head in place at position `pos` (lane i: the pairs
-// (i, i + 64) and (i + 32, i + 96)); `out`, if given, receives a copy of the
-// rotated head.
+// (row, head); lane l handles the rotate-half pairs (2l, 2l + 64) and
+// (2l + 1, 2l + 65). Row r has position pos0 + r % seq.
+// Rotates one 128-wide head in place at position `pos` (lane l: the pairs
+// (2l, 2l + 64) and (2l + 1, 2l + 65), read and written as f16 pairs);
+// `out`, if given, receives a copy of the rotated head.
 __device__ __forceinline__ void rope_head(__half* v, float pos, float log2_theta, int lane,
                                           __half* out) {
+  // lane l: dimensions i = 2l, 2l + 1 and their partners i + 64, as f16 pairs
+  const __half2 x1 = *reinterpret_cast<const __half2*>(v + 2 * lane);
+  const __half2 x2 = *reinterpret_cast<const __half2*>(v + 64 + 2 * lane);
+  const float2 a = __half22float2(x1), b = __half22float2(x2);
+  float ra[2], rb[2];
 #pragma unroll
   for (int k = 0; k < 2; ++k) {
-    const int i = lane + 32 * k;
+    const int i = 2 * lane + k;
     const float inv_freq = exp2f(-(2.0f * (float)i / 128.0f) * log2_theta);
     float sn, cs;
     sincosf(pos * inv_freq, &sn, &cs);
-    const float a = __half2float(v[i]), b = __half2float(v[i + 64]);
-    const __half ra = __float2half_rn(a * cs - b * sn), rb = __float2half_rn(b * cs + a * sn);
-    v[i] = ra;
-    v[i + 64] = rb;
-    if (out) {
-      out[i] = ra;
-      out[i + 64] = rb;
-    }
+    const float ai = k ? a.y : a.x, bi = k ? b.y : b.x;
+    ra[k] = ai * cs - bi * sn;
+    rb[k] = bi * cs + ai * sn;
+  }
+  const __half2 ya = __halves2half2(__float2half_rn(ra[0]), __float2half_rn(ra[1]));
+  const __half2 yb = __halves2half2(__float2half_rn(rb[0]), __float2half_rn(rb[1]));
+  *reinterpret_cast<__half2*>(v + 2 * lane) = ya;
+  *reinterpret_cast<__half2*>(v + 64 + 2 * lane) = yb;
+  if (out) {
+    *reinterpret_cast<__half2*>(out + 2 * lane) = ya;
+    *reinterpret_cast<__half2*>(out + 64 + 2 * lane) = yb;
   }
 }
 
