@@ -38,6 +38,8 @@ typedef enum hxb_status_e {
   HXB_STATUS_CUDA_ERROR = 3,
   HXB_STATUS_RESOURCE_EXHAUSTED = 4,
   HXB_STATUS_DEVICE_TIMEOUT = 5,
+  HXB_STATUS_UNAVAILABLE = 6,    /* e.g. a driver name no factory provides */
+  HXB_STATUS_ALREADY_EXISTS = 7, /* e.g. a factory registered twice */
 } hxb_status_t;
 
 typedef enum hxb_dtype_e {
@@ -58,6 +60,22 @@ const char* hxb_last_error_message(void);
 /* Reads the current device's status word (bits OR-ed in by kernels whose
  * bounded waits gave up) and clears it if `clear` is non-zero. Synchronous. */
 hxb_status_t hxb_device_status(int clear, int* out_bits);
+
+/* Self-test of the failure path behind HXB_DEVICE_STATUS_TIMEOUT: launches
+ * one CTA whose producer, MMA-issuer and epilogue roles wait, through the
+ * same bounded mbarrier wait as every kernel of this library, on a barrier
+ * nothing arrives at, with the limit `limit_ns` (at most 1 s) instead of the
+ * library's 2 s. The producer has a 4096-byte bulk copy of `src` (device,
+ * 16-byte aligned) in flight and the issuer holds TMEM while they wait. The
+ * kernel then takes the product failure path -- abort flag, status bit, a
+ * bounded wait for the copy, TMEM freed -- and writes 4 int32 to `result`
+ * (device): waits that succeeded (0), the abort flag (1), copy intact (1),
+ * TMEM freed (1). The status word keeps HXB_DEVICE_STATUS_TIMEOUT until
+ * hxb_device_status(1, ...) clears it. The reference has no counterpart (its
+ * DSP dispatches report failure through their return code,
+ * plugins/runtime/hexagon/dsp/rt/executable_library.h:163-177). */
+hxb_status_t hxb_selftest_wait_timeout(uint64_t limit_ns, const void* src,
+                                       int32_t* result, void* stream);
 
 /* f16 matmul dispatch: C[M,N] = A[M,K] . B (+ C_init), f32 accumulation.
  *
@@ -125,8 +143,11 @@ size_t hxb_matmul_f16_workspace_bytes(const void* A, int64_t lda,
  * need more re-pitch scratch than that are rejected with
  * HXB_STATUS_INVALID_ARGUMENT. The call allocates nothing. Its first call on a
  * device resolves the scratch's device address (make it before any stream
- * capture). All calls on a device share the scratch and leave their data in
- * it, so calls that overlap on the GPU race: order them on one stream. */
+ * capture; hxb_hal_device_create makes it for its device), and again after
+ * the device's context was re-created (cudaDeviceReset). `stream` must
+ * belong to the current device. All calls on a device share the scratch and
+ * leave their data in it, so calls that overlap on the GPU race: order them
+ * on one stream. */
 hxb_status_t hxb_matmul_f16_noalloc(const void* A, int64_t lda, const void* B,
                                     int64_t ldb, int transpose_b,
                                     const void* C_init, void* C, int64_t ldc,
@@ -282,6 +303,27 @@ hxb_status_t hxb_matmul_f16_allgather(const void* A, int64_t lda, const void* B,
                                       void* const* replicas, int nreplicas,
                                       int64_t ldc, int64_t M, int64_t N,
                                       int64_t K, void* stream);
+
+/* int8-weight matmul of one column shard whose output is also written into
+ * the other ranks' copies of C over NVLink: the all-gather of the N-split of
+ * BASELINE configuration 2 (W [K, N_total] split into column shards of a
+ * multiple of 8 columns). Same arguments as hxb_matmul_w8a16_streamk for the
+ * shard (W, scale and N are the shard's; C and ldc as in
+ * hxb_matmul_f16_allgather: this rank's column block of its full [M, ldc]
+ * output) plus nreplicas (0..7) 16-byte aligned peer pointers to the same
+ * column offset in the other ranks' outputs. For M > 16 the tcgen05 GEMM's
+ * epilogue stores every staged output tile to the replicas as well; for
+ * M <= 16 the GEMV's few output rows are copied to them by one small kernel
+ * after it. workspace may be NULL (no stream-K). The caller orders the call
+ * after the peers stopped reading their outputs and synchronises the ranks
+ * after it. No counterpart in the reference (no int8 path, no
+ * collectives: plugins/runtime/hexagon/channel.c:55-56). */
+hxb_status_t hxb_matmul_w8a16_allgather(const void* A, int64_t lda, const void* W,
+                                        int64_t ldw, const void* scale, void* C,
+                                        void* const* replicas, int nreplicas,
+                                        int64_t ldc, int64_t M, int64_t N, int64_t K,
+                                        void* workspace, size_t workspace_bytes,
+                                        void* stream);
 
 /* CUDA IPC for the replicas of hxb_matmul_f16_allgather. get_handle fills
  * HXB_IPC_HANDLE_BYTES bytes naming the allocation that holds `ptr` and the

@@ -147,7 +147,10 @@ const hxb_executable_library_header_t** hxb_executable_library_query(
  *   bindings: [0] A f16 [M,K], [1] B f16 [K,N] (or [N,K] if transposed),
  *             [2] C [M,N] (f16, or f32 with flag bit 1), optional [3] C_init
  *             (same type/shape as C, added to the product)
- *   constants: M, N, K, flags (bit 0: B transposed, bit 1: f32 output)
+ *   constants: M, N, K, flags (bit 0: B transposed, bit 1: f32 output),
+ *             optional block_n, group_m: a tile plan fixed at compile time
+ *             (hxb_plan_matmul_f16; used when there is no C_init and no
+ *             re-pitch; 0 = plan at dispatch time)
  * HXB_EXPORT_MATMUL_W8A16 "matmul_w8a16"
  *   bindings: [0] A f16 [M,K], [1] W int8 [K,N], [2] scale f16 [N],
  *             [3] C f16 [M,N], optional [4] residual f16 [M,N]
@@ -183,45 +186,174 @@ enum hxb_export_ordinal_e {
 
 /* ===================================================== HAL runtime */
 
+/* ---- base types, shaped like IREE's (iree/base/string_view.h,
+ * iree/base/allocator.h) so a driver written against the reference's
+ * signatures maps 1:1. */
+
+/* A non-owning string: `size` bytes at `data`, no terminator required. */
+typedef struct hxb_string_view_t {
+  const char* data;
+  size_t size;
+} hxb_string_view_t;
+
+/* Host allocator: a control function and its state, as iree_allocator_t.
+ * {NULL, NULL} is the C library's malloc / free. Every host object of the
+ * HAL (driver, device, buffer, semaphore and command-buffer records) is
+ * allocated and freed through the allocator given when it was created. */
+typedef enum hxb_allocator_command_e {
+  HXB_ALLOCATOR_COMMAND_MALLOC = 0,
+  HXB_ALLOCATOR_COMMAND_CALLOC = 1,
+  HXB_ALLOCATOR_COMMAND_REALLOC = 2,
+  HXB_ALLOCATOR_COMMAND_FREE = 3,
+} hxb_allocator_command_t;
+
+typedef struct hxb_allocator_alloc_params_t {
+  size_t byte_length;
+} hxb_allocator_alloc_params_t;
+
+/* MALLOC / CALLOC / REALLOC read `params` (hxb_allocator_alloc_params_t) and
+ * store the block in *inout_ptr (REALLOC also reads the old block from it);
+ * FREE releases *inout_ptr and ignores `params`. */
+typedef hxb_status_t (*hxb_allocator_ctl_fn_t)(void* self, hxb_allocator_command_t command,
+                                               const void* params, void** inout_ptr);
+
+typedef struct hxb_allocator_t {
+  void* self;
+  hxb_allocator_ctl_fn_t ctl;
+} hxb_allocator_t;
+
 typedef struct hxb_hal_driver_s hxb_hal_driver_t;
 typedef struct hxb_hal_device_s hxb_hal_device_t;
 typedef struct hxb_hal_buffer_s hxb_hal_buffer_t;
 typedef struct hxb_hal_semaphore_s hxb_hal_semaphore_t;
 typedef struct hxb_hal_command_buffer_s hxb_hal_command_buffer_t;
+typedef struct hxb_hal_driver_registry_s hxb_hal_driver_registry_t;
 
-/* Device options (api.h:40-63): which GPU, and the size of the device's
- * scratch arena (stream-K partials of the int8-weight dispatches and the
- * key-split partials of GQA attention; 0 = the stream-K size, which also
- * covers a decode step's key split). */
+/* The CUDA device ordinal a device is created on: the B200 counterpart of the
+ * reference's DSP domain id (iree_hal_hexagon_domain_id_t, api.h:31). */
+typedef int hxb_hal_domain_id_t;
+
+/* Default and largest bound on one device-side queue wait (see
+ * hxb_hal_device_queue_execute). */
+#define HXB_HAL_DEFAULT_QUEUE_WAIT_TIMEOUT_NS 10000000000ull /* 10 s */
+#define HXB_HAL_MAX_QUEUE_WAIT_TIMEOUT_NS 60000000000ull     /* 60 s */
+
+/* Device options (api.h:38-63): the size of the device's scratch arena
+ * (stream-K partials of the int8-weight dispatches and the key-split partials
+ * of GQA attention; 0 = the stream-K size, which also covers a decode step's
+ * key split) and the bound on a queue submission's device-side wait for its
+ * wait semaphore (0 = HXB_HAL_DEFAULT_QUEUE_WAIT_TIMEOUT_NS; at most
+ * HXB_HAL_MAX_QUEUE_WAIT_TIMEOUT_NS). */
 typedef struct hxb_hal_device_options_t {
-  int32_t ordinal;
   uint64_t scratch_bytes;
+  uint64_t queue_wait_timeout_ns;
 } hxb_hal_device_options_t;
 
 typedef struct hxb_hal_driver_options_t {
   hxb_hal_device_options_t default_device_options;
 } hxb_hal_driver_options_t;
 
+/* Device creation parameters, the slot of iree_hal_device_create_params_t
+ * (api.h:93-96). `flags` is reserved and must be 0; NULL means defaults. */
+typedef struct hxb_hal_device_create_params_t {
+  uint64_t flags;
+} hxb_hal_device_create_params_t;
+
 void hxb_hal_device_options_initialize(hxb_hal_device_options_t* out_options);
 void hxb_hal_driver_options_initialize(hxb_hal_driver_options_t* out_options);
 
-/* Creates a driver (api.h:98-111). `identifier` names the driver ("b200");
- * no GPU is touched. */
-hxb_status_t hxb_hal_driver_create(const char* identifier,
+/* Creates a driver (iree_hal_hexagon_driver_create, api.h:108-111).
+ * `identifier` names the driver (empty = "b200"); no GPU is touched.
+ * Release with hxb_hal_driver_release. */
+hxb_status_t hxb_hal_driver_create(hxb_string_view_t identifier,
                                    const hxb_hal_driver_options_t* options,
+                                   hxb_allocator_t host_allocator,
                                    hxb_hal_driver_t** out_driver);
 /* Number of CUDA devices the driver can create devices on (0 without a GPU). */
 hxb_status_t hxb_hal_driver_query_device_count(hxb_hal_driver_t* driver, int32_t* out_count);
+
+/* One device the driver can create (iree_hal_device_info_t): its id (the
+ * CUDA ordinal), a path ("cuda:<ordinal>") and the device's name. */
+typedef struct hxb_hal_device_info_t {
+  uint64_t device_id;
+  char path[32];
+  char name[96];
+} hxb_hal_device_info_t;
+
+/* Fills up to `capacity` infos (infos may be NULL with capacity 0) and
+ * stores the number of devices in *out_count. */
+hxb_status_t hxb_hal_driver_query_available_devices(hxb_hal_driver_t* driver,
+                                                    hxb_hal_device_info_t* infos,
+                                                    int32_t capacity, int32_t* out_count);
+/* Creates the device `device_id` with the driver's default device options
+ * (the driver vtable's create_device_by_id). */
+hxb_status_t hxb_hal_driver_create_device_by_id(
+    hxb_hal_driver_t* driver, uint64_t device_id,
+    const hxb_hal_device_create_params_t* create_params, hxb_allocator_t host_allocator,
+    hxb_hal_device_t** out_device);
 void hxb_hal_driver_release(hxb_hal_driver_t* driver);
 
-/* Creates a device on `options->ordinal` (or the driver's default options)
- * with its own queue stream and scratch arena (api.h:67-76). */
-hxb_status_t hxb_hal_device_create(hxb_hal_driver_t* driver, const char* identifier,
+/* Creates a device on CUDA device `domain_id` (iree_hal_hexagon_device_create,
+ * api.h:93-96) with its own queue stream and scratch arena. Resolves every
+ * per-device address of the dispatch library here, before any command buffer
+ * is captured. */
+hxb_status_t hxb_hal_device_create(hxb_string_view_t identifier, hxb_hal_domain_id_t domain_id,
                                    const hxb_hal_device_options_t* options,
+                                   const hxb_hal_device_create_params_t* create_params,
+                                   hxb_allocator_t host_allocator,
                                    hxb_hal_device_t** out_device);
+/* Waits for the queue (bounded: every device-side wait of the queue is) and
+ * frees the device. */
 void hxb_hal_device_release(hxb_hal_device_t* device);
 /* The cudaStream_t of the device's queue. */
 void* hxb_hal_device_queue_stream(hxb_hal_device_t* device);
+/* Non-zero once a queue wait of this device ran out (the device is lost:
+ * later submissions return HXB_STATUS_DEVICE_TIMEOUT). */
+int hxb_hal_device_is_lost(hxb_hal_device_t* device);
+
+/* ---- driver registry and module (registration/driver_module.c:65-120) */
+
+typedef struct hxb_hal_driver_info_t {
+  hxb_string_view_t driver_name;
+  hxb_string_view_t full_name;
+} hxb_hal_driver_info_t;
+
+/* A driver factory (iree_hal_driver_factory_t): lists the drivers it provides
+ * and creates one by name; try_create returns HXB_STATUS_UNAVAILABLE for a
+ * name it does not provide. */
+typedef struct hxb_hal_driver_factory_t {
+  void* self;
+  hxb_status_t (*enumerate)(void* self, size_t* out_driver_info_count,
+                            const hxb_hal_driver_info_t** out_driver_infos);
+  hxb_status_t (*try_create)(void* self, hxb_string_view_t driver_name,
+                             hxb_allocator_t host_allocator, hxb_hal_driver_t** out_driver);
+} hxb_hal_driver_factory_t;
+
+/* A registry of factories (iree_hal_driver_registry_t). The factory structs
+ * must outlive the registry. */
+hxb_status_t hxb_hal_driver_registry_create(hxb_allocator_t host_allocator,
+                                            hxb_hal_driver_registry_t** out_registry);
+void hxb_hal_driver_registry_release(hxb_hal_driver_registry_t* registry);
+/* HXB_STATUS_ALREADY_EXISTS if the factory is registered already. */
+hxb_status_t hxb_hal_driver_registry_register_factory(hxb_hal_driver_registry_t* registry,
+                                                      const hxb_hal_driver_factory_t* factory);
+/* Driver infos of every registered factory, in registration order. */
+hxb_status_t hxb_hal_driver_registry_enumerate(hxb_hal_driver_registry_t* registry,
+                                               hxb_hal_driver_info_t* infos, int32_t capacity,
+                                               int32_t* out_count);
+/* Asks each factory in turn; HXB_STATUS_UNAVAILABLE if none provides it. */
+hxb_status_t hxb_hal_driver_registry_try_create(hxb_hal_driver_registry_t* registry,
+                                                hxb_string_view_t driver_name,
+                                                hxb_allocator_t host_allocator,
+                                                hxb_hal_driver_t** out_driver);
+
+/* Registers the "b200" driver factory
+ * (iree_hal_hexagon_driver_module_register, driver_module.c:108-120). Where
+ * the reference reads IREE tool flags into the driver options, its
+ * try_create reads the environment: HXB_HAL_SCRATCH_BYTES and
+ * HXB_HAL_QUEUE_WAIT_TIMEOUT_MS (decimal; a malformed or out-of-range value
+ * is HXB_STATUS_INVALID_ARGUMENT, as the reference rejects bad flags). */
+hxb_status_t hxb_hal_driver_module_register(hxb_hal_driver_registry_t* registry);
 
 /* Device-local buffers. write/read are ordered on the device queue and
  * return when the copy is complete. */
@@ -236,9 +368,10 @@ hxb_status_t hxb_hal_buffer_read(hxb_hal_buffer_t* buffer, uint64_t offset, void
 void hxb_hal_buffer_release(hxb_hal_buffer_t* buffer);
 
 /* Timeline semaphores: a 64-bit value that only grows. The device queue
- * waits for and signals values with stream memory operations; the host
- * signals by storing and waits by polling, bounded by `timeout_ns`
- * (HXB_STATUS_DEVICE_TIMEOUT when it runs out). */
+ * waits for values with a bounded device-side poll and signals them with a
+ * store (see hxb_hal_device_queue_execute); the host signals by storing and
+ * waits by polling, bounded by `timeout_ns` (HXB_STATUS_DEVICE_TIMEOUT when it
+ * runs out). */
 hxb_status_t hxb_hal_semaphore_create(hxb_hal_device_t* device, uint64_t initial_value,
                                       hxb_hal_semaphore_t** out_semaphore);
 hxb_status_t hxb_hal_semaphore_query(hxb_hal_semaphore_t* semaphore, uint64_t* out_value);
@@ -247,18 +380,40 @@ hxb_status_t hxb_hal_semaphore_wait(hxb_hal_semaphore_t* semaphore, uint64_t val
                                     uint64_t timeout_ns);
 void hxb_hal_semaphore_release(hxb_hal_semaphore_t* semaphore);
 
-/* A range of a buffer bound to a dispatch. */
+/* A range bound to a dispatch (iree_hal_buffer_ref_t): a buffer of the
+ * device, or -- when `buffer` is NULL -- slot `buffer_slot` of the binding
+ * table given at submission, `offset` bytes into that binding. */
 typedef struct hxb_hal_buffer_ref_t {
   hxb_hal_buffer_t* buffer;
   uint64_t offset;
   uint64_t length;
+  uint32_t buffer_slot;
+  uint32_t reserved;
 } hxb_hal_buffer_ref_t;
 
+/* One binding-table entry (iree_hal_buffer_binding_t) and the table
+ * (iree_hal_buffer_binding_table_t), as submitted with a command buffer. */
+typedef struct hxb_hal_buffer_binding_t {
+  hxb_hal_buffer_t* buffer;
+  uint64_t offset;
+  uint64_t length;
+} hxb_hal_buffer_binding_t;
+
+typedef struct hxb_hal_buffer_binding_table_t {
+  uint32_t count;
+  const hxb_hal_buffer_binding_t* bindings;
+} hxb_hal_buffer_binding_table_t;
+
 /* Command buffers (command_buffer.c:586-726): begin, record dispatches of
- * this library's exports, end. end() checks every dispatch's arguments and
- * captures the recording as one CUDA graph; a command buffer may be executed
- * any number of times after that. */
-hxb_status_t hxb_hal_command_buffer_create(hxb_hal_device_t* device,
+ * this library's exports, end. A command buffer created with
+ * binding_capacity > 0 may record bindings that name table slots
+ * (< binding_capacity); it is then captured when it is first submitted with
+ * a table, and re-captured into the same executable graph
+ * (cudaGraphExecUpdate) when a later table binds other addresses. Without
+ * table slots, end() checks every dispatch's arguments and captures the
+ * recording as one CUDA graph; a command buffer may be executed any number
+ * of times after that. */
+hxb_status_t hxb_hal_command_buffer_create(hxb_hal_device_t* device, uint32_t binding_capacity,
                                            hxb_hal_command_buffer_t** out_command_buffer);
 hxb_status_t hxb_hal_command_buffer_begin(hxb_hal_command_buffer_t* command_buffer);
 hxb_status_t hxb_hal_command_buffer_dispatch(hxb_hal_command_buffer_t* command_buffer,
@@ -270,13 +425,23 @@ hxb_status_t hxb_hal_command_buffer_end(hxb_hal_command_buffer_t* command_buffer
 void hxb_hal_command_buffer_release(hxb_hal_command_buffer_t* command_buffer);
 
 /* Queue submission (device.c:1068-1112): after `wait_semaphore` reaches
- * `wait_value` (NULL: no wait), run `command_buffer`, then set
- * `signal_semaphore` to `signal_value` (NULL: no signal). Returns without
- * waiting for the device. */
+ * `wait_value` (NULL: no wait), run `command_buffer` (NULL: none) with
+ * `binding_table` (NULL: none; required when the command buffer records
+ * table slots), then set `signal_semaphore` to `signal_value` (NULL: no
+ * signal). Returns without waiting for the device.
+ * The wait is a one-thread kernel on the queue that polls the semaphore for
+ * at most the device's queue_wait_timeout_ns. When it runs out, the kernel
+ * ORs HXB_DEVICE_STATUS_TIMEOUT into the device status word and marks the
+ * device lost: this submission's command buffer still runs (its inputs may
+ * not be ready, so its results are void), its signal is NOT written, so
+ * waiters on it time out in turn, and later submissions to the device return
+ * HXB_STATUS_DEVICE_TIMEOUT. Release waits on the queue therefore always
+ * end. */
 hxb_status_t hxb_hal_device_queue_execute(hxb_hal_device_t* device,
                                           hxb_hal_semaphore_t* wait_semaphore,
                                           uint64_t wait_value,
                                           hxb_hal_command_buffer_t* command_buffer,
+                                          const hxb_hal_buffer_binding_table_t* binding_table,
                                           hxb_hal_semaphore_t* signal_semaphore,
                                           uint64_t signal_value);
 

@@ -24,6 +24,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "hxb_abi_version": (c_int, []),
     "hxb_last_error_message": (ctypes.c_char_p, []),
     "hxb_device_status": (c_int, [c_int, ctypes.POINTER(c_int)]),
+    "hxb_selftest_wait_timeout": (c_int, [c_u64, c_vp, c_vp, c_vp]),
     "hxb_matmul_f16": (c_int, [c_vp, c_i64, c_vp, c_i64, c_int, c_vp, c_vp, c_i64,
                                c_int, c_i64, c_i64, c_i64, c_vp, c_size, c_vp]),
     "hxb_matmul_f16_workspace_bytes": (c_size, [c_vp, c_i64, c_vp, c_i64, c_int,
@@ -58,6 +59,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "hxb_swiglu_f16": (c_int, [c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_vp]),
     "hxb_matmul_f16_allgather": (c_int, [c_vp, c_i64, c_vp, c_i64, c_int, c_vp, c_vp, c_int,
                                          c_i64, c_i64, c_i64, c_i64, c_vp]),
+    "hxb_matmul_w8a16_allgather": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_int,
+                                           c_i64, c_i64, c_i64, c_i64, c_vp, c_size, c_vp]),
     "hxb_gather_column_blocks_f16": (c_int, [c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp]),
     "hxb_ipc_get_handle": (c_int, [c_vp, c_vp, ctypes.POINTER(c_i64)]),
     "hxb_ipc_open": (c_int, [c_vp, c_i64, ctypes.POINTER(c_vp)]),
@@ -75,12 +78,26 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     # include/hxb200_hal.h: HAL runtime
     "hxb_hal_device_options_initialize": (None, [c_vp]),
     "hxb_hal_driver_options_initialize": (None, [c_vp]),
-    "hxb_hal_driver_create": (c_int, [ctypes.c_char_p, c_vp, ctypes.POINTER(c_vp)]),
+    "hxb_hal_driver_create": (c_int, ["StringView", c_vp, "Allocator", ctypes.POINTER(c_vp)]),
     "hxb_hal_driver_query_device_count": (c_int, [c_vp, ctypes.POINTER(ctypes.c_int32)]),
+    "hxb_hal_driver_query_available_devices": (c_int, [c_vp, c_vp, ctypes.c_int32,
+                                                       ctypes.POINTER(ctypes.c_int32)]),
+    "hxb_hal_driver_create_device_by_id": (c_int, [c_vp, c_u64, c_vp, "Allocator",
+                                                   ctypes.POINTER(c_vp)]),
     "hxb_hal_driver_release": (None, [c_vp]),
-    "hxb_hal_device_create": (c_int, [c_vp, ctypes.c_char_p, c_vp, ctypes.POINTER(c_vp)]),
+    "hxb_hal_device_create": (c_int, ["StringView", c_int, c_vp, c_vp, "Allocator",
+                                      ctypes.POINTER(c_vp)]),
     "hxb_hal_device_release": (None, [c_vp]),
     "hxb_hal_device_queue_stream": (c_vp, [c_vp]),
+    "hxb_hal_device_is_lost": (c_int, [c_vp]),
+    "hxb_hal_driver_registry_create": (c_int, ["Allocator", ctypes.POINTER(c_vp)]),
+    "hxb_hal_driver_registry_release": (None, [c_vp]),
+    "hxb_hal_driver_registry_register_factory": (c_int, [c_vp, c_vp]),
+    "hxb_hal_driver_registry_enumerate": (c_int, [c_vp, c_vp, ctypes.c_int32,
+                                                  ctypes.POINTER(ctypes.c_int32)]),
+    "hxb_hal_driver_registry_try_create": (c_int, [c_vp, "StringView", "Allocator",
+                                                   ctypes.POINTER(c_vp)]),
+    "hxb_hal_driver_module_register": (c_int, [c_vp]),
     "hxb_hal_buffer_allocate": (c_int, [c_vp, c_u64, ctypes.POINTER(c_vp)]),
     "hxb_hal_buffer_device_pointer": (c_vp, [c_vp]),
     "hxb_hal_buffer_byte_length": (c_u64, [c_vp]),
@@ -92,14 +109,29 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "hxb_hal_semaphore_signal": (c_int, [c_vp, c_u64]),
     "hxb_hal_semaphore_wait": (c_int, [c_vp, c_u64, c_u64]),
     "hxb_hal_semaphore_release": (None, [c_vp]),
-    "hxb_hal_command_buffer_create": (c_int, [c_vp, ctypes.POINTER(c_vp)]),
+    "hxb_hal_command_buffer_create": (c_int, [c_vp, ctypes.c_uint32, ctypes.POINTER(c_vp)]),
     "hxb_hal_command_buffer_begin": (c_int, [c_vp]),
     "hxb_hal_command_buffer_dispatch": (c_int, [c_vp, ctypes.c_uint32,
                                                 ctypes.POINTER(ctypes.c_uint32), ctypes.c_uint32,
                                                 c_vp, ctypes.c_uint32]),
     "hxb_hal_command_buffer_end": (c_int, [c_vp]),
     "hxb_hal_command_buffer_release": (None, [c_vp]),
-    "hxb_hal_device_queue_execute": (c_int, [c_vp, c_vp, c_u64, c_vp, c_vp, c_u64]),
+    # include/hxb200_compiler.h: the target's compiler stand-in and its runtime
+    "hxb_compiler_options_initialize": (None, [c_vp]),
+    "hxb_compile_mlir": (c_int, [ctypes.c_char_p, c_size, c_vp, ctypes.POINTER(c_vp),
+                                 ctypes.POINTER(c_size), ctypes.POINTER(c_vp)]),
+    "hxb_compiler_free": (None, [c_vp]),
+    "hxb_executable_binary_mlir": (c_int, [c_vp, c_size, ctypes.c_char_p, ctypes.POINTER(c_vp)]),
+    "hxb_module_load": (c_int, [c_vp, c_vp, c_size, ctypes.POINTER(c_vp)]),
+    "hxb_module_release": (None, [c_vp]),
+    "hxb_module_function_count": (ctypes.c_int32, [c_vp]),
+    "hxb_module_function_name": (ctypes.c_char_p, [c_vp, ctypes.c_int32]),
+    "hxb_module_signature": (c_int, [c_vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int32),
+                                     ctypes.POINTER(ctypes.c_int32), c_vp, ctypes.c_int32]),
+    "hxb_module_dispatch_count": (ctypes.c_int32, [c_vp, ctypes.c_char_p]),
+    "hxb_module_invoke": (c_int, [c_vp, ctypes.c_char_p, c_vp, ctypes.c_uint32, c_vp,
+                                  ctypes.c_uint32, c_vp, c_u64, c_vp, c_u64]),
+    "hxb_hal_device_queue_execute": (c_int, [c_vp, c_vp, c_u64, c_vp, c_vp, c_vp, c_u64]),
 }
 
 
@@ -146,8 +178,66 @@ class ExecutableLibrary(ctypes.Structure):
                 ("exports", ExportTable)]
 
 
+class StringView(ctypes.Structure):
+    """hxb_string_view_t."""
+    _fields_ = [("data", ctypes.c_char_p), ("size", c_size)]
+
+    @classmethod
+    def of(cls, text: str | bytes) -> "StringView":
+        b = text.encode() if isinstance(text, str) else bytes(text)
+        return cls(b, len(b))
+
+
+AllocatorCtl = ctypes.CFUNCTYPE(c_int, c_vp, c_int, c_vp, ctypes.POINTER(c_vp))
+
+
+class Allocator(ctypes.Structure):
+    """hxb_allocator_t; Allocator() is the C library's malloc / free."""
+    _fields_ = [("self", c_vp), ("ctl", AllocatorCtl)]
+
+
 class DeviceOptions(ctypes.Structure):
-    _fields_ = [("ordinal", ctypes.c_int32), ("scratch_bytes", c_u64)]
+    _fields_ = [("scratch_bytes", c_u64), ("queue_wait_timeout_ns", c_u64)]
+
+
+class DeviceCreateParams(ctypes.Structure):
+    _fields_ = [("flags", c_u64)]
+
+
+class DeviceInfo(ctypes.Structure):
+    _fields_ = [("device_id", c_u64), ("path", ctypes.c_char * 32), ("name", ctypes.c_char * 96)]
+
+
+class DriverInfo(ctypes.Structure):
+    _fields_ = [("driver_name", StringView), ("full_name", StringView)]
+
+
+DriverEnumerateFn = ctypes.CFUNCTYPE(c_int, c_vp, ctypes.POINTER(c_size),
+                                     ctypes.POINTER(ctypes.POINTER(DriverInfo)))
+DriverTryCreateFn = ctypes.CFUNCTYPE(c_int, c_vp, StringView, Allocator, ctypes.POINTER(c_vp))
+
+
+class DriverFactory(ctypes.Structure):
+    _fields_ = [("self", c_vp), ("enumerate", DriverEnumerateFn),
+                ("try_create", DriverTryCreateFn)]
+
+
+class CompilerOptions(ctypes.Structure):
+    _fields_ = [("enable_matmul", ctypes.c_int32), ("enable_w8a16", ctypes.c_int32),
+                ("enable_attention", ctypes.c_int32), ("num_sms", ctypes.c_int32)]
+
+
+class TensorDesc(ctypes.Structure):
+    _fields_ = [("element_type", ctypes.c_int32), ("rank", ctypes.c_int32),
+                ("dims", c_i64 * 8)]
+
+
+class BufferBinding(ctypes.Structure):
+    _fields_ = [("buffer", c_vp), ("offset", c_u64), ("length", c_u64)]
+
+
+class BindingTable(ctypes.Structure):
+    _fields_ = [("count", ctypes.c_uint32), ("bindings", ctypes.POINTER(BufferBinding))]
 
 
 class DriverOptions(ctypes.Structure):
@@ -155,7 +245,9 @@ class DriverOptions(ctypes.Structure):
 
 
 class BufferRef(ctypes.Structure):
-    _fields_ = [("buffer", c_vp), ("offset", c_u64), ("length", c_u64)]
+    """hxb_hal_buffer_ref_t: a buffer range, or (buffer None) a table slot."""
+    _fields_ = [("buffer", c_vp), ("offset", c_u64), ("length", c_u64),
+                ("buffer_slot", ctypes.c_uint32), ("reserved", ctypes.c_uint32)]
 
 
 class DecoderW8(ctypes.Structure):
@@ -175,6 +267,8 @@ STATUS_NAMES = {
     3: "CUDA_ERROR",
     4: "RESOURCE_EXHAUSTED",
     5: "DEVICE_TIMEOUT",
+    6: "UNAVAILABLE",
+    7: "ALREADY_EXISTS",
 }
 
 DTYPE_F16, DTYPE_F32, DTYPE_I8 = 0, 1, 2
@@ -205,7 +299,8 @@ def load(path: Path | None = None) -> ctypes.CDLL:
     for name, (res, args) in SIGNATURES.items():
         fn = getattr(lib, name)
         fn.restype = res
-        fn.argtypes = args
+        # struct-by-value arguments are named, the structs are defined below
+        fn.argtypes = [globals()[a] if isinstance(a, str) else a for a in args]
     if path is None:
         _lib = lib
     return lib

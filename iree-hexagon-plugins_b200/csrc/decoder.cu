@@ -32,7 +32,8 @@ namespace hxb {
 hxb_status_t matmul_w8a16_impl(const void* A, int64_t lda, const void* W, int64_t ldw,
                                const void* scale, const void* R, void* C, int64_t ldc,
                                int64_t M, int64_t N, int64_t K, void* sk_ws,
-                               size_t sk_ws_bytes, cudaStream_t stream);
+                               size_t sk_ws_bytes, cudaStream_t stream,
+                               void* const* replicas = nullptr, int nreplicas = 0);
 size_t w8_streamk_workspace_bytes(int ctas);
 int w8_streamk_flag_ints();
 hxb_status_t attention_launch(const void* Q, int64_t ldq, const void* K, int64_t ldk,
@@ -326,8 +327,19 @@ hxb_status_t launch_rmsnorm(const void* x, int64_t ldx, const void* gamma, void*
                     (int)rows, (int)cols, eps, clear, nclear);
 }
 
+// The RoPE kernels move f16 pairs (lane l rotates dimensions 2l, 2l + 1), so
+// every row base must be 4-byte aligned: an even leading dimension and a
+// 4-byte aligned base pointer.
+inline bool pair_aligned(const void* p, int64_t ld) {
+  return (reinterpret_cast<uintptr_t>(p) & 3u) == 0 && (ld & 1) == 0;
+}
+
 hxb_status_t launch_rope(void* x, int64_t ldx, int64_t rows, int64_t heads, int64_t seq,
                          int64_t pos0, float theta, cudaStream_t stream) {
+  if (!pair_aligned(x, ldx))
+    return fail(HXB_STATUS_INVALID_ARGUMENT,
+                "rope: the base must be 4-byte aligned and ldx (%lld) even (f16-pair accesses)",
+                (long long)ldx);
   const int threads = 256;
   const long long blocks = (rows * heads * 32 + threads - 1) / threads;
   return launch_pdl(rope_kernel, dim3((unsigned)blocks), dim3(threads), 0, stream, "rope launch",
@@ -338,6 +350,11 @@ hxb_status_t launch_rope(void* x, int64_t ldx, int64_t rows, int64_t heads, int6
 hxb_status_t launch_rope_cache(void* qkv, int64_t ld, int64_t rows, int64_t heads, int64_t seq,
                                int64_t pos0, float theta, void* k_cache, void* v_cache,
                                int64_t cache_rows, cudaStream_t stream) {
+  if (!pair_aligned(qkv, ld) || !pair_aligned(k_cache, 2) || !pair_aligned(v_cache, 2))
+    return fail(HXB_STATUS_INVALID_ARGUMENT,
+                "rope + kv cache: bases must be 4-byte aligned and ld (%lld) even (f16-pair "
+                "accesses)",
+                (long long)ld);
   const int threads = 256;
   const long long blocks = (rows * 3 * heads * 32 + threads - 1) / threads;
   return launch_pdl(rope_cache_kernel, dim3((unsigned)blocks), dim3(threads), 0, stream,

@@ -103,10 +103,11 @@ __device__ __forceinline__ void raise_failure(const FailState& fs) {
 }
 
 // Waits for the phase of `bar` with parity `parity` to complete. Returns false
-// (after raising the failure state) when the wait exceeds kWaitLimitNs or when
+// (after raising the failure state) when the wait exceeds `limit_ns` or when
 // another role of this CTA already gave up.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
-                                          const FailState& fs) {
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity,
+                                              const FailState& fs,
+                                              unsigned long long limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   while (true) {
@@ -114,11 +115,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(bar, parity)) return true;
     if (*fs.abort) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       raise_failure(fs);
       return false;
     }
   }
+}
+
+// mbar_wait_for with the library-wide limit kWaitLimitNs (every kernel's
+// waits go through this).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          const FailState& fs) {
+  return mbar_wait_for(bar, parity, fs, kWaitLimitNs);
 }
 
 // Named barrier among `count` threads (a multiple of 32) of this CTA.

@@ -44,10 +44,23 @@ def library(version: int = _native.EXECUTABLE_LIBRARY_VERSION_1) -> dict | None:
 
 
 class Driver:
-    def __init__(self, identifier: str = "b200"):
+    """A driver (hxb_hal_driver_create); `options` sets the default device
+    options of the devices it creates by id."""
+
+    def __init__(self, identifier: str = "b200", scratch_bytes: int = 0,
+                 queue_wait_timeout_ns: int = 0, handle=None):
         self._lib = _native.load()
+        if handle is not None:  # a driver a factory created
+            self.handle = handle
+            return
+        o = _native.DriverOptions()
+        self._lib.hxb_hal_driver_options_initialize(ctypes.byref(o))
+        o.default_device_options.scratch_bytes = scratch_bytes
+        if queue_wait_timeout_ns:
+            o.default_device_options.queue_wait_timeout_ns = queue_wait_timeout_ns
         h = ctypes.c_void_p()
-        check(self._lib.hxb_hal_driver_create(identifier.encode(), None, ctypes.byref(h)))
+        check(self._lib.hxb_hal_driver_create(_native.StringView.of(identifier), ctypes.byref(o),
+                                              _native.Allocator(), ctypes.byref(h)))
         self.handle = h
 
     def device_count(self) -> int:
@@ -55,8 +68,25 @@ class Driver:
         check(self._lib.hxb_hal_driver_query_device_count(self.handle, ctypes.byref(n)))
         return n.value
 
-    def create_device(self, ordinal: int = 0, scratch_bytes: int = 0) -> "Device":
-        return Device(self, ordinal, scratch_bytes)
+    def available_devices(self) -> list[dict]:
+        n = ctypes.c_int32()
+        check(self._lib.hxb_hal_driver_query_available_devices(self.handle, None, 0,
+                                                               ctypes.byref(n)))
+        infos = (_native.DeviceInfo * max(1, n.value))()
+        check(self._lib.hxb_hal_driver_query_available_devices(self.handle, infos, n.value,
+                                                               ctypes.byref(n)))
+        return [{"device_id": i.device_id, "path": i.path.decode(), "name": i.name.decode()}
+                for i in infos[:n.value]]
+
+    def create_device_by_id(self, device_id: int = 0) -> "Device":
+        h = ctypes.c_void_p()
+        check(self._lib.hxb_hal_driver_create_device_by_id(self.handle, device_id, None,
+                                                           _native.Allocator(), ctypes.byref(h)))
+        return Device(handle=h)
+
+    def create_device(self, ordinal: int = 0, scratch_bytes: int = 0,
+                      queue_wait_timeout_ns: int = 0) -> "Device":
+        return Device(ordinal, scratch_bytes, queue_wait_timeout_ns)
 
     def close(self) -> None:
         if self.handle:
@@ -64,12 +94,58 @@ class Driver:
             self.handle = None
 
 
-class Device:
-    def __init__(self, driver: Driver, ordinal: int, scratch_bytes: int):
-        self._lib = driver._lib
-        o = _native.DeviceOptions(ordinal, scratch_bytes)
+class Registry:
+    """A driver registry (hxb_hal_driver_registry_*) with the b200 module
+    registered, as a tool registers driver modules at start-up."""
+
+    def __init__(self, register_b200: bool = True):
+        self._lib = _native.load()
         h = ctypes.c_void_p()
-        check(self._lib.hxb_hal_device_create(driver.handle, b"b200", ctypes.byref(o),
+        check(self._lib.hxb_hal_driver_registry_create(_native.Allocator(), ctypes.byref(h)))
+        self.handle = h
+        if register_b200:
+            check(self._lib.hxb_hal_driver_module_register(self.handle))
+
+    def drivers(self) -> list[tuple[str, str]]:
+        n = ctypes.c_int32()
+        check(self._lib.hxb_hal_driver_registry_enumerate(self.handle, None, 0, ctypes.byref(n)))
+        infos = (_native.DriverInfo * max(1, n.value))()
+        check(self._lib.hxb_hal_driver_registry_enumerate(self.handle, infos, n.value,
+                                                          ctypes.byref(n)))
+        return [(ctypes.string_at(i.driver_name.data, i.driver_name.size).decode(),
+                 ctypes.string_at(i.full_name.data, i.full_name.size).decode())
+                for i in infos[:n.value]]
+
+    def create(self, name: str) -> Driver:
+        h = ctypes.c_void_p()
+        check(self._lib.hxb_hal_driver_registry_try_create(
+            self.handle, _native.StringView.of(name), _native.Allocator(), ctypes.byref(h)))
+        return Driver(handle=h)
+
+    def close(self) -> None:
+        if self.handle:
+            self._lib.hxb_hal_driver_registry_release(self.handle)
+            self.handle = None
+
+
+class Device:
+    """A device on CUDA device `ordinal` (hxb_hal_device_create; the ordinal is
+    the domain id)."""
+
+    def __init__(self, ordinal: int = 0, scratch_bytes: int = 0,
+                 queue_wait_timeout_ns: int = 0, handle=None):
+        self._lib = _native.load()
+        if handle is not None:
+            self.handle = handle
+            return
+        o = _native.DeviceOptions()
+        self._lib.hxb_hal_device_options_initialize(ctypes.byref(o))
+        o.scratch_bytes = scratch_bytes
+        if queue_wait_timeout_ns:
+            o.queue_wait_timeout_ns = queue_wait_timeout_ns
+        h = ctypes.c_void_p()
+        check(self._lib.hxb_hal_device_create(_native.StringView.of("b200"), ordinal,
+                                              ctypes.byref(o), None, _native.Allocator(),
                                               ctypes.byref(h)))
         self.handle = h
 
@@ -77,27 +153,48 @@ class Device:
     def stream(self) -> int:
         return self._lib.hxb_hal_device_queue_stream(self.handle) or 0
 
+    @property
+    def lost(self) -> bool:
+        return bool(self._lib.hxb_hal_device_is_lost(self.handle))
+
     def allocate(self, nbytes: int) -> "Buffer":
         return Buffer(self, nbytes)
 
     def semaphore(self, initial: int = 0) -> "Semaphore":
         return Semaphore(self, initial)
 
-    def command_buffer(self) -> "CommandBuffer":
-        return CommandBuffer(self)
+    def command_buffer(self, binding_capacity: int = 0) -> "CommandBuffer":
+        return CommandBuffer(self, binding_capacity)
 
-    def execute(self, command_buffer: "CommandBuffer | None", wait=None, signal=None) -> None:
+    def execute(self, command_buffer: "CommandBuffer | None", wait=None, signal=None,
+                bindings=None) -> None:
         """Queue `command_buffer` after `wait` = (semaphore, value) is reached;
-        then set `signal` = (semaphore, value). Does not block."""
+        then set `signal` = (semaphore, value). `bindings` is the binding
+        table: a list of Buffers or (Buffer, offset, length). Does not block."""
         ws, wv = (wait[0].handle, wait[1]) if wait else (None, 0)
         ss, sv = (signal[0].handle, signal[1]) if signal else (None, 0)
+        table = None
+        if bindings is not None:
+            entries = []
+            for b in bindings:
+                buf, off, ln = (b, 0, b.nbytes) if isinstance(b, Buffer) else b
+                entries.append(_native.BufferBinding(buf.handle, off, ln))
+            arr = (_native.BufferBinding * max(1, len(entries)))(*entries)
+            table = _native.BindingTable(len(entries), arr)
         check(self._lib.hxb_hal_device_queue_execute(
-            self.handle, ws, wv, command_buffer.handle if command_buffer else None, ss, sv))
+            self.handle, ws, wv, command_buffer.handle if command_buffer else None,
+            ctypes.byref(table) if table is not None else None, ss, sv))
 
     def close(self) -> None:
         if self.handle:
             self._lib.hxb_hal_device_release(self.handle)
             self.handle = None
+
+
+def slot(index: int, offset: int = 0, length: int = 0) -> _native.BufferRef:
+    """A binding that names slot `index` of the binding table given at
+    submission (`offset`/`length` bytes inside that binding)."""
+    return _native.BufferRef(None, offset, length, index, 0)
 
 
 class Buffer:
@@ -126,7 +223,7 @@ class Buffer:
 
     def ref(self, offset: int = 0, length: int | None = None) -> _native.BufferRef:
         return _native.BufferRef(self.handle, offset,
-                                 self.nbytes - offset if length is None else length)
+                                 self.nbytes - offset if length is None else length, 0, 0)
 
     def close(self) -> None:
         if self.handle:
@@ -160,17 +257,19 @@ class Semaphore:
 
 
 class CommandBuffer:
-    def __init__(self, device: Device):
+    def __init__(self, device: Device, binding_capacity: int = 0):
         self._lib = device._lib
         h = ctypes.c_void_p()
-        check(self._lib.hxb_hal_command_buffer_create(device.handle, ctypes.byref(h)))
+        check(self._lib.hxb_hal_command_buffer_create(device.handle, binding_capacity,
+                                                      ctypes.byref(h)))
         self.handle = h
 
     def begin(self) -> None:
         check(self._lib.hxb_hal_command_buffer_begin(self.handle))
 
     def dispatch(self, export: str | int, constants, bindings) -> None:
-        """Records one dispatch: `bindings` are Buffers or BufferRefs."""
+        """Records one dispatch: `bindings` are Buffers or BufferRefs
+        (slot(i) for a binding-table slot)."""
         ordinal = EXPORTS[export] if isinstance(export, str) else int(export)
         c = (ctypes.c_uint32 * max(1, len(constants)))(*[int(x) & 0xFFFFFFFF for x in constants])
         refs = [b.ref() if isinstance(b, Buffer) else b for b in bindings]

@@ -5,6 +5,8 @@ at test time):
 
     python tests/golden/make_golden.py /path/to/iree-hexagon-plugins
 
+or with the checkout's path in HXB_REFERENCE_ROOT and no argument.
+
 For every single-op micro model the reference's integration suite runs on the
 hot path (integration_tests/models/micro/{matmul-*,hmx/*,attention-*}) this
   * reads the model's model.yaml (input shapes, dtypes, seeds, tolerances),
@@ -126,4 +128,8 @@ def main(ref_root: Path) -> None:
 
 
 if __name__ == "__main__":
-    main(Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference"))
+    import os
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("HXB_REFERENCE_ROOT")
+    if not root:
+        sys.exit("usage: make_golden.py <reference checkout> (or set HXB_REFERENCE_ROOT)")
+    main(Path(root))

@@ -23,7 +23,9 @@ def declared_functions() -> set[str]:
         text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
         text = re.sub(r"//[^\n]*", "", text)
         text = re.sub(r"#[^\n]*", "", text)
-        # typedef'd function pointer types are not exports
+        # struct/enum bodies (function-pointer members) and typedef'd
+        # function pointer types are not exports
+        text = re.sub(r"\b(struct|enum|union)\s*\w*\s*\{[^{}]*\}", "", text, flags=re.S)
         text = re.sub(r"typedef[^;]*;", "", text, flags=re.S)
         for m in re.finditer(r"\b([A-Za-z_]\w*)\s*\(", text):
             name = m.group(1)
@@ -100,3 +102,13 @@ def test_planner_uses_the_baked_sweep_table(pkg):
         b, g = ctypes.c_int(0), ctypes.c_int(0)
         assert lib.hxb_plan_matmul_f16(M, N, K, bmode, 148, ctypes.byref(b), ctypes.byref(g)) == 0
         assert (b.value, g.value) == (bn, gm), (M, N, K)
+
+
+def test_rope_rejects_unaligned_pairs_before_device_access(pkg):
+    """RoPE moves f16 pairs: an odd leading dimension or a base that is not
+    4-byte aligned is refused on the host, before any launch."""
+    lib = pkg._native.load()
+    st = lib.hxb_rope_f16(0x100000, 3 * 128 + 1, 4, 2, 128, 4, 0, 10000.0, None)
+    assert st == 1 and b"even" in lib.hxb_last_error_message()
+    st = lib.hxb_rope_f16(0x100002, 256, 4, 2, 128, 4, 0, 10000.0, None)
+    assert st == 1 and b"4-byte" in lib.hxb_last_error_message()

@@ -211,3 +211,114 @@ def test_gqa_attention_dispatch(cuda_pkg, device):
     assert np.array_equal(got, want.cpu().numpy())
     for x in (cb, done, qb, kb, vb, o):
         x.close()
+
+
+def test_repitched_matmul_in_command_buffer(cuda_pkg, oracle, device):
+    """K and N whose rows are not 16-byte multiples make the matmul export
+    re-pitch through the library's built-in scratch while end() captures the
+    command buffer; the device resolved that scratch when it was created.
+    Recorded once, executed twice, checked against the oracle each time."""
+    rng = np.random.default_rng(15)
+    M, N, K = 70, 90, 111
+    a = (rng.random((M, K)) * 2 - 1).astype(np.float16)
+    b = (rng.random((K, N)) * 2 - 1).astype(np.float16)
+    ab, bb = _upload(device, a), _upload(device, b)
+    c = device.allocate(M * N * 4)
+    cb = device.command_buffer()
+    cb.begin()
+    cb.dispatch("matmul_f16", [M, N, K, 2], [ab, bb, c])
+    cb.end()
+    done = device.semaphore(0)
+    want = oracle.matmul_f32(a, b)
+    for i in (1, 2):
+        c.write(np.full(M * N, np.nan, np.float32))
+        device.execute(cb, wait=(done, i - 1), signal=(done, i))
+        done.wait(i)
+        got = np.frombuffer(c.read(), np.float32).reshape(M, N)
+        baseline_check(want, got, f"hal re-pitched matmul, execution {i}")
+    assert cuda_pkg.device_status() == 0
+    for x in (cb, done, ab, bb, c):
+        x.close()
+
+
+def test_binding_table_slots(cuda_pkg, oracle, device):
+    """A command buffer recorded against binding-table slots runs with the
+    buffers of each submission's table (device.c:977-1012 resolves tables at
+    submission too): two tables, then the first again."""
+    rng = np.random.default_rng(16)
+    M, N, K = 256, 192, 320
+    sets = []
+    for _ in range(2):
+        a = (rng.random((M, K)) * 2 - 1).astype(np.float16)
+        b = (rng.random((K, N)) * 2 - 1).astype(np.float16)
+        sets.append((a, b, _upload(device, a), _upload(device, b), device.allocate(M * N * 2)))
+    hal = cuda_pkg.hal
+    cb = device.command_buffer(binding_capacity=3)
+    cb.begin()
+    cb.dispatch("matmul_f16", [M, N, K, 0],
+                [hal.slot(0, 0, M * K * 2), hal.slot(1, 0, K * N * 2), hal.slot(2, 0, M * N * 2)])
+    cb.end()
+    done = device.semaphore(0)
+    step = 0
+    for which in (0, 1, 0):
+        a, b, ab, bb, cbuf = sets[which]
+        cbuf.write(np.zeros(M * N, np.float16))
+        step += 1
+        device.execute(cb, wait=(done, step - 1), signal=(done, step), bindings=[ab, bb, cbuf])
+        done.wait(step)
+        got = np.frombuffer(cbuf.read(), np.float16).reshape(M, N)
+        baseline_check(oracle.matmul_f32(a, b), got.astype(np.float32), f"table set {which}")
+    # a submission without the table it needs is refused on the host
+    with pytest.raises(cuda_pkg.HxbError, match="table"):
+        device.execute(cb)
+    for x in [cb, done] + [o for s in sets for o in s[2:]]:
+        x.close()
+
+
+def test_queue_wait_bound_runs_out(cuda_pkg, oracle):
+    """A submission waits on a semaphore nobody signals. The device-side wait
+    gives up after the device's bound (50 ms here), sets the timeout bit of
+    the device status word and marks the device lost; the submission's signal
+    is never written, so a host waiter times out too; later submissions are
+    refused; release returns. A new device then computes correctly."""
+    hal = cuda_pkg.hal
+    cuda_pkg.device_status(clear=True)
+    dev = hal.Device(0, queue_wait_timeout_ns=50_000_000)
+    M = N = K = 128
+    rng = np.random.default_rng(17)
+    a = (rng.random((M, K)) * 2 - 1).astype(np.float16)
+    b = (rng.random((K, N)) * 2 - 1).astype(np.float16)
+    ab, bb, c = _upload(dev, a), _upload(dev, b), dev.allocate(M * N * 2)
+    cb = dev.command_buffer()
+    cb.begin()
+    cb.dispatch("matmul_f16", [M, N, K, 0], [ab, bb, c])
+    cb.end()
+    never, done = dev.semaphore(0), dev.semaphore(0)
+    dev.execute(cb, wait=(never, 1), signal=(done, 1))
+    with pytest.raises(cuda_pkg.HxbError, match="DEVICE_TIMEOUT"):
+        done.wait(1, timeout_s=2.0)
+    torch.cuda.synchronize()
+    assert dev.lost
+    assert cuda_pkg.device_status(clear=False) & 1
+    with pytest.raises(cuda_pkg.HxbError, match="device lost"):
+        dev.execute(cb)
+    for x in (cb, never, done, ab, bb, c):
+        x.close()
+    dev.close()
+    assert cuda_pkg.device_status(clear=True) & 1
+    assert cuda_pkg.device_status(clear=False) == 0
+    # a fresh device on the same GPU works
+    dev2 = hal.Driver().create_device_by_id(0)
+    ab, bb, c = _upload(dev2, a), _upload(dev2, b), dev2.allocate(M * N * 2)
+    cb = dev2.command_buffer()
+    cb.begin()
+    cb.dispatch("matmul_f16", [M, N, K, 0], [ab, bb, c])
+    cb.end()
+    done = dev2.semaphore(0)
+    dev2.execute(cb, signal=(done, 1))
+    done.wait(1)
+    got = np.frombuffer(c.read(), np.float16).reshape(M, N)
+    baseline_check(oracle.matmul_f32(a, b), got.astype(np.float32), "matmul after a lost device")
+    for x in (cb, done, ab, bb, c):
+        x.close()
+    dev2.close()

@@ -80,16 +80,119 @@ def test_dispatch_functions_check_bindings_before_device_access(pkg):
 def test_driver_without_gpu(pkg):
     d = pkg.hal.Driver()
     assert d.device_count() == 0
+    assert d.available_devices() == []
     with pytest.raises(pkg.HxbError, match="no CUDA device"):
         d.create_device(0)
+    with pytest.raises(pkg.HxbError, match="no CUDA device"):
+        d.create_device_by_id(0)
     d.close()
 
 
 def test_options_initialize_defaults(pkg):
     lib = pkg._native.load()
     o = pkg._native.DriverOptions()
-    o.default_device_options.ordinal = 7
     o.default_device_options.scratch_bytes = 9
+    o.default_device_options.queue_wait_timeout_ns = 5
     lib.hxb_hal_driver_options_initialize(ctypes.byref(o))
-    assert o.default_device_options.ordinal == 0
     assert o.default_device_options.scratch_bytes == 0
+    assert o.default_device_options.queue_wait_timeout_ns == 10_000_000_000
+
+
+def test_device_create_checks_options_before_the_gpu(pkg):
+    """create_params flags and a queue wait bound past the maximum are refused
+    before any device is touched (iree_hal_hexagon_device_create, api.h:93-96)."""
+    lib = pkg._native.load()
+    out = ctypes.c_void_p()
+    o = pkg._native.DeviceOptions(0, 61_000_000_000)
+    st = lib.hxb_hal_device_create(pkg._native.StringView.of("b200"), 0, ctypes.byref(o), None,
+                                   pkg._native.Allocator(), ctypes.byref(out))
+    assert st == 1 and b"maximum" in lib.hxb_last_error_message()
+    params = pkg._native.DeviceCreateParams(1)
+    st = lib.hxb_hal_device_create(pkg._native.StringView.of("b200"), 0, None,
+                                   ctypes.byref(params), pkg._native.Allocator(),
+                                   ctypes.byref(out))
+    assert st == 2 and not out.value
+
+
+def test_driver_module_registry(pkg, monkeypatch):
+    """The factory of registration/driver_module.c:65-120: the registry lists
+    the b200 driver, creates it by name, refuses other names with UNAVAILABLE
+    and a second registration with ALREADY_EXISTS; its try_create reads the
+    driver options from the environment and rejects malformed values."""
+    lib = pkg._native.load()
+    reg = pkg.hal.Registry()
+    assert reg.drivers() == [("b200", "NVIDIA B200 (sm_100a) CUDA driver")]
+    drv = reg.create("b200")
+    assert drv.handle
+    drv.close()
+    with pytest.raises(pkg.HxbError, match="UNAVAILABLE.*hexagon"):
+        reg.create("hexagon")
+    assert lib.hxb_hal_driver_module_register(reg.handle) == 7  # ALREADY_EXISTS
+    monkeypatch.setenv("HXB_HAL_QUEUE_WAIT_TIMEOUT_MS", "12x")
+    with pytest.raises(pkg.HxbError, match="HXB_HAL_QUEUE_WAIT_TIMEOUT_MS"):
+        reg.create("b200")
+    monkeypatch.setenv("HXB_HAL_QUEUE_WAIT_TIMEOUT_MS", "250")
+    monkeypatch.setenv("HXB_HAL_SCRATCH_BYTES", "1048576")
+    reg.create("b200").close()
+    reg.close()
+
+
+def test_registry_asks_factories_in_order(pkg):
+    """A second factory (here written in Python against the C struct) is
+    listed after the b200 one and gets the names b200 does not provide."""
+    nat = pkg._native
+    calls = []
+    infos = (nat.DriverInfo * 1)(nat.DriverInfo(nat.StringView.of("other"),
+                                                nat.StringView.of("Other driver")))
+
+    @nat.DriverEnumerateFn
+    def enumerate_fn(self, count, out):
+        count[0] = 1
+        out[0] = ctypes.cast(infos, ctypes.POINTER(nat.DriverInfo))
+        return 0
+
+    @nat.DriverTryCreateFn
+    def try_create_fn(self, name, alloc, out):
+        calls.append(ctypes.string_at(name.data, name.size))
+        return 6
+
+    factory = nat.DriverFactory(None, enumerate_fn, try_create_fn)
+    reg = pkg.hal.Registry()
+    lib = nat.load()
+    assert lib.hxb_hal_driver_registry_register_factory(reg.handle, ctypes.byref(factory)) == 0
+    assert [d[0] for d in reg.drivers()] == ["b200", "other"]
+    with pytest.raises(pkg.HxbError, match="UNAVAILABLE"):
+        reg.create("other")
+    assert calls == [b"other"]
+    reg.close()
+
+
+def test_host_allocator_owns_host_objects(pkg):
+    """Host objects come from the allocator passed at creation and go back to
+    it on release (iree_allocator_t semantics: CALLOC then FREE)."""
+    nat = pkg._native
+    lib = nat.load()
+    live, log = {}, []
+
+    @nat.AllocatorCtl
+    def ctl(self, command, params, inout):
+        if command == 1:  # CALLOC
+            n = ctypes.cast(params, ctypes.POINTER(ctypes.c_size_t))[0]
+            buf = ctypes.create_string_buffer(n)
+            live[ctypes.addressof(buf)] = buf
+            inout[0] = ctypes.addressof(buf)
+            log.append(("calloc", n))
+            return 0
+        if command == 3:  # FREE
+            live.pop(inout[0], None)
+            log.append(("free", 0))
+            return 0
+        return 2
+
+    alloc = nat.Allocator(None, ctl)
+    out = ctypes.c_void_p()
+    assert lib.hxb_hal_driver_create(nat.StringView.of("b200"), None, alloc,
+                                     ctypes.byref(out)) == 0
+    assert len(live) == 1 and log[0][0] == "calloc"
+    lib.hxb_hal_driver_release(out)
+    assert not live and log[-1][0] == "free"

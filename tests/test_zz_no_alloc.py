@@ -5,9 +5,10 @@ and code recording a CUDA stream capture may not call cudaMalloc, so neither
 can hand hxb_matmul_f16 the workspace it needs for operands whose row pitch is
 not a multiple of 16 bytes. hxb_matmul_f16_noalloc re-pitches into a scratch
 array built into the library instead. These tests call it through the C ABI
-and check it against hxb_matmul_f16 given a workspace from torch, on two
-different calls in a row (the scratch keeps the previous call's bytes, so the
-second call would show stale data if any were read).
+and check it against hxb_matmul_f16 given a workspace from torch and against
+the CPU oracle on the unpadded operands, on two different calls in a row (the
+scratch keeps the previous call's bytes, so the second call would show stale
+data if any were read).
 
 The file is named so that pytest collects it last.
 """
@@ -23,7 +24,7 @@ DEV = "cuda:0"
 F16, F32 = 0, 1
 
 
-def _call_both(pkg, M, N, K, pad_a, pad_b, out_dtype, seed):
+def _call_both(pkg, oracle, M, N, K, pad_a, pad_b, out_dtype, seed):
     lib = pkg._native.load()
     rng = np.random.default_rng(seed)
     a_big = torch.from_numpy(rng.uniform(-1, 1, (M, K + pad_a)).astype(np.float16)).to(DEV)
@@ -44,18 +45,21 @@ def _call_both(pkg, M, N, K, pad_a, pad_b, out_dtype, seed):
                                                  0, None, got.data_ptr(), N, out_dtype,
                                                  M, N, K, stream))
     torch.cuda.synchronize()
-    return want.float().cpu().numpy(), got.float().cpu().numpy()
+    ref = oracle.matmul_f32(a_big[:, :K].cpu().numpy(), b_big[:, :N].cpu().numpy())
+    return ref, want.float().cpu().numpy(), got.float().cpu().numpy()
 
 
 @pytest.mark.gpu
-def test_noalloc_matches_workspace_entry_point_twice(cuda_pkg):
+def test_noalloc_matches_workspace_entry_point_twice(cuda_pkg, oracle):
     # Two calls in a row with different shapes and pitches: the second one
     # re-pitches different data into the same scratch.
     cases = [(70, 90, 110, 5, 3, F32, 1), (129, 257, 65, 1, 7, F16, 2)]
     for M, N, K, pad_a, pad_b, out_dtype, seed in cases:
-        want, got = _call_both(cuda_pkg, M, N, K, pad_a, pad_b, out_dtype, seed)
+        ref, want, got = _call_both(cuda_pkg, oracle, M, N, K, pad_a, pad_b, out_dtype, seed)
         assert np.isfinite(got).all()
-        baseline_check(want, got, f"noalloc {M}x{N}x{K}")
+        baseline_check(want, got, f"noalloc {M}x{N}x{K} vs workspace entry point")
+        baseline_check(ref, got, f"noalloc {M}x{N}x{K} vs oracle")
+        baseline_check(ref, want, f"workspace entry point {M}x{N}x{K} vs oracle")
     assert cuda_pkg.device_status() == 0
 
 
