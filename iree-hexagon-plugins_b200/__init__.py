@@ -8,12 +8,12 @@ identifier it is imported as `iree_hexagon_plugins_b200` through
 """
 from . import _native
 from ._native import HxbError
-from . import hal, sharded
+from . import compiler, hal, sharded
 from .dispatch import (DecoderBlockW8, attention, attention_bshd, attention_gqa,
                        attention_gqa_workspace_bytes, device_status, kv_cache_write, matmul,
                        matmul_w8a16, rmsnorm, rope_, swiglu, w8a16_workspace)
 
-__all__ = ["hal", "sharded", "HxbError", "DecoderBlockW8", "attention", "attention_bshd",
+__all__ = ["compiler", "hal", "sharded", "HxbError", "DecoderBlockW8", "attention", "attention_bshd",
            "attention_gqa", "attention_gqa_workspace_bytes", "device_status",
            "kv_cache_write", "matmul", "matmul_w8a16", "rmsnorm", "rope_", "swiglu",
            "w8a16_workspace", "_native"]

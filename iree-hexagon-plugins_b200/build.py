@@ -37,12 +37,21 @@ def _nvcc() -> str:
     raise RuntimeError("nvcc not found; the dispatch library needs the CUDA toolkit")
 
 
+CXX_FLAGS = ["-O2", "-std=c++17", "-fPIC", "-Wall", "-I", str(PKG_DIR.parent / "include")]
+
+
 def _sources() -> list[Path]:
     return sorted(CSRC.glob("*.cu"))
 
 
+def _host_sources() -> list[Path]:
+    """Host-only C++ (the compiler stand-in), built with the host compiler."""
+    return sorted((CSRC / "compiler").glob("*.cc"))
+
+
 def _deps() -> list[Path]:
-    return sorted(list(CSRC.glob("*")) + list((PKG_DIR.parent / "include").glob("*.h")))
+    return sorted([p for p in CSRC.rglob("*") if p.is_file()] +
+                  list((PKG_DIR.parent / "include").glob("*.h")))
 
 
 def _needs_build(force: bool) -> bool:
@@ -61,6 +70,16 @@ def _compile(nvcc: str, src: Path, extra: list[str]) -> Path:
     return obj
 
 
+def _compile_host(src: Path) -> Path:
+    obj = BUILD_DIR / (src.stem + ".host.o")
+    cxx = os.environ.get("CXX") or shutil.which("g++") or "g++"
+    cmd = [cxx, *CXX_FLAGS, "-c", str(src), "-o", str(obj)]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"{cxx} failed for {src.name}:\n{r.stdout}\n{r.stderr}")
+    return obj
+
+
 def build(force: bool = False, jobs: int | None = None, extra: list[str] | None = None) -> Path:
     """Builds libhxb200.so if any source is newer than it; returns its path."""
     if not _needs_build(force):
@@ -71,6 +90,7 @@ def build(force: bool = False, jobs: int | None = None, extra: list[str] | None 
     srcs = _sources()
     with cf.ThreadPoolExecutor(max_workers=jobs or min(8, os.cpu_count() or 4)) as ex:
         objs = list(ex.map(lambda s: _compile(nvcc, s, extra), srcs))
+        objs += list(ex.map(_compile_host, _host_sources()))
     tmp = LIB_PATH.with_suffix(".so.tmp")
     cmd = [nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-shared",
            "-cudart", "static", "-o", str(tmp), *map(str, objs)]

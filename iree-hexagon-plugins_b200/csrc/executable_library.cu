@@ -64,7 +64,7 @@ float f32_bits(uint32_t u) {
   return f;
 }
 
-// bindings: A, B, C [, C_init]; constants: M, N, K, flags
+// bindings: A, B, C [, C_init]; constants: M, N, K, flags [, block_n, group_m]
 int dispatch_matmul_f16(const hxb_executable_environment_t* env,
                         const hxb_executable_dispatch_state_t* ds,
                         const hxb_executable_workgroup_state_t*) {
@@ -99,6 +99,13 @@ int dispatch_matmul_f16(const hxb_executable_environment_t* env,
                                      (int64_t)K) != 0)
     return hxb_matmul_f16_noalloc(A, (int64_t)K, B, ldb, tb, init, C, (int64_t)N, dt,
                                   (int64_t)M, (int64_t)N, (int64_t)K, env->stream);
+  // a tile plan the compiler baked into the push constants (block_n,
+  // group_m; 0 = plan at dispatch time)
+  const uint32_t block_n = ds->constants[4], group_m = ds->constants[5];
+  if (block_n != 0 && !init)
+    return hxb_matmul_f16_tiled(A, (int64_t)K, B, ldb, tb, C, (int64_t)N, dt, (int64_t)M,
+                                (int64_t)N, (int64_t)K, (int)block_n, (int)group_m,
+                                env->stream);
   return hxb_matmul_f16(A, (int64_t)K, B, ldb, tb, init, C, (int64_t)N, dt, (int64_t)M,
                         (int64_t)N, (int64_t)K, nullptr, 0, env->stream);
 }
