@@ -1,16 +1,31 @@
 """Benchmark of the B200 hot path (one JSON line on stdout, rank 0).
 
-Workload (the configuration the metric is quoted on
+Headline (the configuration the metric is quoted on
 that fits one GPU): the weight-quantised matmul dispatch
 C[4096,11008] f16 = (A[4096,4096] f16 . W[4096,11008] int8) * scale[11008],
 f32 accumulation. One step = one dispatch over one batch of 4096 activation
 rows. Every rank runs its own batches against its own resident weights (data
-parallel, no collective on the data path), so scaling is weak and `value` is
-the whole-job TFLOP/s over all ranks (the max of the ranks' device times).
+parallel, no collective on the data path), so the headline scales weakly and
+`value` is the whole-job TFLOP/s over all ranks (the max of the ranks' device
+times).
+
+The same run measures every other BASELINE configuration as a sub-record
+under "configs", each with its own roofline, e2e, clocks and (rank 0, one
+GPU) CPU baseline:
+  cfg 1   f16 GEMM 1024^3                       (replicas when N > 1)
+  cfg 2b  int8-weight GEMV, M = 1 and M = 16     (replicas when N > 1)
+  cfg 3   attention [4, 32, 2048, 128]           (heads split over the ranks)
+  cfg 4   decoder block, seq 512                 (replicas when N > 1)
+  cfg 5   f16 GEMM 16384 x 8192 x 28672          (N split over the ranks, the
+          all-gather of C fused into the GEMM epilogue; compute-only and the
+          NCCL all-gather baseline beside it)
+  cfg 2 N-split: the headline dispatch and the M = 1 GEMV with W split along
+          N over the ranks and the all-gather fused into the epilogue.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--workload NAME]   (one configuration alone)
 
---impl reference times the CPU restatement of the same dispatch (the
+--impl reference times the CPU restatement of the headline dispatch (the
 reference's llvm-cpu lowering cannot be built: its IREE/LLVM submodules are
 not vendored) on the host cores, on a bounded row sample per step.
 """
@@ -35,6 +50,7 @@ WORKLOAD = "w8a16_gemm_4096x4096x11008"
 METRIC = "f16/w8 matmul & attention TFLOP/s per B200 (% of tensor peak); 1/2/4/8-GPU"
 N_SETS = 3  # rotating input sets: 3 x 169 MB > 126 MB L2 between uses
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+CPU_SECONDS = 4.0  # CPU work per configuration's baseline sample
 
 
 def _peaks():
@@ -82,6 +98,8 @@ class ClockSampler:
             self.thread.start()
         except OSError:
             self.proc = None
+        time.sleep(0.3)
+        return self
 
     def _read(self):
         for line in self.proc.stdout:
@@ -114,46 +132,130 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def make_inputs(torch, dev, seed):
-    g = torch.Generator(device=dev).manual_seed(seed)
-    a = torch.randn(M, K, device=dev, dtype=torch.float32, generator=g).half()
-    w = torch.randint(-127, 128, (K, N), device=dev, dtype=torch.int8, generator=g)
-    s = (torch.rand(N, device=dev, generator=g) * 0.019 + 0.001).half()
-    c = torch.empty(M, N, device=dev, dtype=torch.float16)
-    return a, w, s, c
+# ------------------------------------------------------------------------
+# CPU baselines: the oracle restatement (test infrastructure, loaded only by
+# this leg) timed on the host cores on a bounded sample of each workload.
+
+def _threads() -> int:
+    return int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
 
 
-def cpu_baseline_sample(seconds_target: float = 10.0) -> dict:
-    """The oracle restatement (test infrastructure) timed on this host's cores
-    on a bounded sample of the same workload: whole dispatches (or a row
-    slice when one dispatch would take longer than the target), repeated
-    until about `seconds_target` of CPU time has been spent."""
+def _cpu_loop(fn, seconds: float):
+    fn()  # warm-up
+    reps, dt = 0, 0.0
+    while dt < seconds or reps == 0:
+        t0 = time.perf_counter()
+        fn()
+        dt += time.perf_counter() - t0
+        reps += 1
+    return reps, dt
+
+
+def cpu_cfg2(seconds: float = CPU_SECONDS) -> dict:
+    """Whole-K, whole-N row slices of the headline dispatch."""
     import numpy as np
     from oracle import oracle as ref
     rng = np.random.default_rng(0)
     w = rng.integers(-127, 128, (K, N), dtype=np.int8)
     s = rng.uniform(0.001, 0.02, N).astype(np.float16)
     probe = rng.standard_normal((32, K)).astype(np.float16)
-    ref.matmul_w8a16_f32(probe, w, s)  # warm-up
+    ref.matmul_w8a16_f32(probe, w, s)
     t0 = time.perf_counter()
     ref.matmul_w8a16_f32(probe, w, s)
     rate = 32 / (time.perf_counter() - t0)  # rows per second
-    rows = int(max(32, min(M, rate * seconds_target)) // 32 * 32)
+    rows = int(max(32, min(M, rate * seconds / 2)) // 32 * 32)
     a = rng.standard_normal((rows, K)).astype(np.float16)
-    reps, dt = 0, 0.0
-    while dt < seconds_target or reps == 0:
-        t0 = time.perf_counter()
-        ref.matmul_w8a16_f32(a, w, s)
-        dt += time.perf_counter() - t0
-        reps += 1
-    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count()))
+    reps, dt = _cpu_loop(lambda: ref.matmul_w8a16_f32(a, w, s), seconds)
     return {"value": 2.0 * rows * K * N * reps / dt / 1e12, "unit": "TFLOP/s",
-            "cores": threads, "kind": "port",
+            "cores": _threads(), "kind": "port",
             "sample": f"{reps} x {rows} of {M} activation rows of {WORKLOAD} "
-                      f"(C oracle, OpenMP on {threads} threads), {dt:.1f} s"}
+                      f"(C oracle, OpenMP on {_threads()} threads), {dt:.1f} s"}
+
+
+def cpu_f16_1024(seconds: float = CPU_SECONDS) -> dict:
+    import numpy as np
+    from oracle import oracle as ref
+    rng = np.random.default_rng(0)
+    a = rng.uniform(-1, 1, (1024, 1024)).astype(np.float16)
+    b = rng.uniform(-1, 1, (1024, 1024)).astype(np.float16)
+    reps, dt = _cpu_loop(lambda: ref.matmul_f32(a, b), seconds)
+    return {"value": 2.0 * 1024 ** 3 * reps / dt / 1e12, "unit": "TFLOP/s", "cores": _threads(),
+            "kind": "port", "sample": f"{reps} whole 1024^3 dispatches, {dt:.1f} s"}
+
+
+def cpu_gemv(m: int):
+    def run(seconds: float = CPU_SECONDS) -> dict:
+        import numpy as np
+        from oracle import oracle as ref
+        rng = np.random.default_rng(0)
+        w = rng.integers(-127, 128, (K, N), dtype=np.int8)
+        s = rng.uniform(0.001, 0.02, N).astype(np.float16)
+        a = rng.standard_normal((m, K)).astype(np.float16)
+        reps, dt = _cpu_loop(lambda: ref.matmul_w8a16_f32(a, w, s), seconds)
+        nbytes = K * N + 2 * m * K + 2 * N + 2 * m * N
+        return {"value": nbytes * reps / dt / 1e9, "unit": "GB/s", "cores": _threads(),
+                "kind": "port", "sample": f"{reps} whole {m}x{K}x{N} dispatches, {dt:.1f} s"}
+    return run
+
+
+def cpu_attention(seconds: float = CPU_SECONDS) -> dict:
+    import numpy as np
+    from oracle import oracle as ref
+    rng = np.random.default_rng(0)
+    heads = 2
+    q, k, v = (rng.standard_normal((heads, 2048, 128)).astype(np.float16) for _ in range(3))
+    reps, dt = _cpu_loop(lambda: ref.attention_f32(q, k, v), seconds)
+    return {"value": 4.0 * heads * 2048 * 2048 * 128 * reps / dt / 1e12, "unit": "TFLOP/s",
+            "cores": _threads(), "kind": "port",
+            "sample": f"{reps} x {heads} of 128 heads [2048 x 2048 x 128], {dt:.1f} s"}
+
+
+def _decoder_weights_np(rng, H=4096, F=11008):
+    import numpy as np
+
+    def sc(n):
+        return rng.uniform(1.5e-4, 4e-4, n).astype(np.float16)
+    return {"attn_norm": np.ones(H, np.float16), "ffn_norm": np.ones(H, np.float16),
+            "w_qkv": rng.integers(-127, 128, (H, 3 * H), dtype=np.int8), "s_qkv": sc(3 * H),
+            "w_o": rng.integers(-127, 128, (H, H), dtype=np.int8), "s_o": sc(H),
+            "w_gate_up": rng.integers(-127, 128, (H, 2 * F), dtype=np.int8),
+            "s_gate_up": sc(2 * F),
+            "w_down": rng.integers(-127, 128, (F, H), dtype=np.int8), "s_down": sc(H)}
+
+
+DEC_FLOP = 2.0 * 512 * (4 * 4096 * 4096 + 3 * 4096 * 11008) + 2.0 * 32 * 512 * 512 * 128
+
+
+def cpu_decoder(seconds: float = CPU_SECONDS) -> dict:
+    import numpy as np
+    from oracle import oracle as ref
+    rng = np.random.default_rng(0)
+    wt = _decoder_weights_np(rng)
+    x = rng.standard_normal((512, 4096)).astype(np.float16)
+    reps, dt = _cpu_loop(lambda: ref.decoder_block_w8(x, wt, heads=32), seconds)
+    return {"value": DEC_FLOP * reps / dt / 1e12, "unit": "TFLOP/s", "cores": _threads(),
+            "kind": "port", "sample": f"{reps} whole seq-512 blocks, {dt:.1f} s"}
+
+
+SH_M, SH_K, SH_N = 16384, 8192, 28672
+
+
+def cpu_cfg5(seconds: float = CPU_SECONDS) -> dict:
+    import numpy as np
+    from oracle import oracle as ref
+    rng = np.random.default_rng(0)
+    rows = 32
+    a = rng.uniform(-1, 1, (rows, SH_K)).astype(np.float16)
+    b = rng.uniform(-1, 1, (SH_K, SH_N)).astype(np.float16)
+    reps, dt = _cpu_loop(lambda: ref.matmul_f32(a, b), seconds)
+    return {"value": 2.0 * rows * SH_K * SH_N * reps / dt / 1e12, "unit": "TFLOP/s",
+            "cores": _threads(), "kind": "port",
+            "sample": f"{reps} x {rows} of {SH_M} rows of 16384x8192x28672, {dt:.1f} s"}
 
 
 def run_reference(args, rank: int) -> None:
+    """The reference arm: the CPU restatement of the headline dispatch on a
+    bounded row sample per step, rank 0 only."""
     if rank != 0:
         return
     import numpy as np
@@ -178,7 +280,7 @@ def run_reference(args, rank: int) -> None:
         "vs_baseline": None, "dtype": "f16xi8->f32", "data": "synthetic",
         "config": {"workload": WORKLOAD, "M": M, "K": K, "N": N,
                    "sample_rows_per_step": rows},
-        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": os.cpu_count(),
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": _threads(),
                          "kind": "port",
                          "sample": f"{rows} of {M} rows per step; CPU restatement "
                                    "(reference llvm-cpu not buildable here)"},
@@ -189,27 +291,179 @@ def run_reference(args, rank: int) -> None:
 
 
 # ------------------------------------------------------------------------
-# The other BASELINE configurations, one dispatch per step. Each spec builds
-# enough rotating input sets that the sets together exceed the 126 MB L2, so
-# every step reads its inputs from HBM; K steps run back to back between two
-# CUDA events on the launching stream (launch gaps included).
+# Device-side plumbing shared by every measurement.
 
-def _spec_f16_gemm(torch, pkg, dev):
-    M = N = K = 1024
+class Ctx:
+    def __init__(self, args):
+        import torch
+        import torch.distributed as dist
+        import __graft_entry__ as ge
+        self.args = args
+        self.torch = torch
+        self.dist = dist
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pkg = ge.load_package()
+        self.pkg._native.load()
+        torch.cuda.set_device(self.local_rank)
+        self.dev = torch.device("cuda", self.local_rank)
+        if self.world > 1:
+            from datetime import timedelta
+            dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=self.dev)
+
+    def max_over_ranks(self, x: float) -> float:
+        if self.world == 1:
+            return x
+        t = self.torch.tensor([x], device=self.dev, dtype=self.torch.float64)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def all_true(self, ok: bool) -> bool:
+        if self.world == 1:
+            return bool(ok)
+        t = self.torch.tensor([0.0 if ok else 1.0], device=self.dev, dtype=self.torch.float64)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item()) == 0.0
+
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+
+    def close(self):
+        if self.world > 1:
+            self.dist.barrier()
+            self.dist.destroy_process_group()
+
+
+def _graph_ms(ctx: Ctx, step, steps: int) -> tuple[float, dict]:
+    """Device time per step of `steps` calls of step(i) captured in one CUDA
+    graph (a dispatch costs its kernels' time, not the Python launch path),
+    one untimed replay, then one replay between two events on the launching
+    stream; max over ranks. Clocks are sampled around the timed replay."""
+    torch = ctx.torch
+    stream = torch.cuda.current_stream(ctx.dev)
+    side = torch.cuda.Stream(ctx.dev)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        for i in range(ctx.args.warmup):
+            step(i)
+    stream.wait_stream(side)
+    torch.cuda.synchronize(ctx.dev)
+    assert ctx.pkg.device_status(clear=False) == 0, "a kernel wait timed out during warm-up"
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(steps):
+            step(i)
+    graph.replay()
+    torch.cuda.synchronize(ctx.dev)
+    sampler = ClockSampler(ctx.local_rank).start()
+    ctx.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(ctx.dev)
+    e0.record(stream)
+    graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize(ctx.dev)
+    clocks = sampler.stop()
+    del graph
+    return ctx.max_over_ranks(e0.elapsed_time(e1)) / steps, clocks
+
+
+def _pipelined_e2e_ms(ctx: Ctx, inp, out, compute, steps: int) -> float:
+    """End-to-end time per step through the public call with host buffers:
+    every step copies its input from pinned host memory and reads its result
+    back into pinned host memory, inside the timed region. The copies run on
+    their own streams with double-buffered device and host buffers, so the
+    host-to-device copy of step i+1 and the read-back of step i-1 overlap the
+    dispatch of step i. compute(i, in_dev, out_dev) issues one step on the
+    current stream. Max over ranks."""
+    torch = ctx.torch
+    comp = torch.cuda.current_stream(ctx.dev)
+    h2d, d2h = torch.cuda.Stream(ctx.dev), torch.cuda.Stream(ctx.dev)
+    in_h = torch.empty(inp.shape, dtype=inp.dtype, pin_memory=True)
+    in_h.copy_(inp.cpu())
+    ins = [inp, torch.empty_like(inp)]
+    outs = [out, torch.empty_like(out)]
+    outs_h = [torch.empty(out.shape, dtype=out.dtype, pin_memory=True) for _ in range(2)]
+    ev = {k: [torch.cuda.Event() for _ in range(2)]
+          for k in ("in_ready", "in_free", "out_ready", "out_free")}
+    for b in range(2):
+        for k in ("in_free", "out_free"):
+            ev[k][b].record(comp)
+
+    def run(n):
+        for i in range(n):
+            b = i & 1
+            h2d.wait_event(ev["in_free"][b])
+            with torch.cuda.stream(h2d):
+                ins[b].copy_(in_h, non_blocking=True)
+            ev["in_ready"][b].record(h2d)
+            comp.wait_event(ev["in_ready"][b])
+            comp.wait_event(ev["out_free"][b])
+            compute(i, ins[b], outs[b])
+            ev["in_free"][b].record(comp)
+            ev["out_ready"][b].record(comp)
+            d2h.wait_event(ev["out_ready"][b])
+            with torch.cuda.stream(d2h):
+                outs_h[b].copy_(outs[b], non_blocking=True)
+            ev["out_free"][b].record(d2h)
+        done = torch.cuda.Event()
+        done.record(d2h)
+        comp.wait_event(done)
+
+    run(3)
+    torch.cuda.synchronize(ctx.dev)
+    ctx.barrier()
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record(comp)
+    h2d.wait_stream(comp)
+    d2h.wait_stream(comp)
+    run(steps)
+    a1.record(comp)
+    torch.cuda.synchronize(ctx.dev)
+    return ctx.max_over_ranks(a0.elapsed_time(a1)) / steps
+
+
+def _roofline(bound: str, work: float, ms: float, kernel: str, profile: str | None,
+              sustained: bool = False) -> dict:
+    peaks, kind = _peaks()
+    if bound == "hbm":
+        unit, peak, label = "GB/s", peaks["hbm_gbs"], f"{kind} HBM copy"
+    else:
+        unit = "TFLOP/s"
+        if sustained and peaks.get("bf16_tflops_sustained"):
+            peak, label = peaks["bf16_tflops_sustained"], f"{kind} bf16 dense (sustained)"
+        else:
+            peak, label = peaks["bf16_tflops"], f"{kind} bf16 dense (burst)"
+    achieved = work / (ms / 1e3)
+    return {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
+            "frac": achieved / peak, "traffic": _profile_traffic(profile) if profile else None,
+            "peak_source": label, "kernel": kernel, "kernel_ms": ms}
+
+
+# ------------------------------------------------------------------------
+# Single-GPU configurations, one dispatch per step. Each spec builds enough
+# rotating input sets that the sets together exceed the 126 MB L2, so every
+# step reads its inputs from HBM. make(torch, pkg, dev, rank, world) returns
+# the step, the e2e input/output and a compute(i, inp, out) for the e2e leg.
+
+def _spec_f16_gemm(torch, pkg, dev, rank, world):
+    M_ = N_ = K_ = 1024
     sets = 24  # 24 x 6.3 MB
-    g = torch.Generator(device=dev).manual_seed(0)
-    a = [(torch.rand(M, K, device=dev, generator=g) * 2 - 1).half() for _ in range(sets)]
-    b = [(torch.rand(K, N, device=dev, generator=g) * 2 - 1).half() for _ in range(sets)]
-    c = [torch.empty(M, N, dtype=torch.float16, device=dev) for _ in range(sets)]
+    g = torch.Generator(device=dev).manual_seed(rank)
+    a = [(torch.rand(M_, K_, device=dev, generator=g) * 2 - 1).half() for _ in range(sets)]
+    b = [(torch.rand(K_, N_, device=dev, generator=g) * 2 - 1).half() for _ in range(sets)]
+    c = [torch.empty(M_, N_, dtype=torch.float16, device=dev) for _ in range(sets)]
     return {"step": lambda i: pkg.matmul(a[i % sets], b[i % sets], out=c[i % sets]),
-            "in": a[0], "out": c[0], "sets": sets}
+            "in": a[0], "out": c[0], "sets": sets,
+            "compute": lambda i, x, y: pkg.matmul(x, b[0], out=y)}
 
 
 def _spec_gemv(m):
-    def make(torch, pkg, dev):
-        K, N = 4096, 11008
+    def make(torch, pkg, dev, rank, world):
         sets = 4  # 4 x 45 MB of weights
-        g = torch.Generator(device=dev).manual_seed(0)
+        g = torch.Generator(device=dev).manual_seed(rank)
         a = torch.randn(m, K, device=dev, generator=g).half()
         w = [torch.randint(-127, 128, (K, N), device=dev, dtype=torch.int8, generator=g)
              for _ in range(sets)]
@@ -218,24 +472,33 @@ def _spec_gemv(m):
         # with the stream-K workspace the dispatch spreads W over every SM
         ws = pkg.w8a16_workspace(dev)
         return {"step": lambda i: pkg.matmul_w8a16(a, w[i % sets], s, out=c, workspace=ws),
-                "in": a, "out": c, "sets": sets}
+                "in": a, "out": c, "sets": sets,
+                "compute": lambda i, x, y: pkg.matmul_w8a16(x, w[i % sets], s, out=y,
+                                                            workspace=ws)}
     return make
 
 
-def _spec_attention(torch, pkg, dev):
-    B, H, S, D = 4, 32, 2048, 128
-    sets = 2  # 2 x 201 MB of q, k, v
-    g = torch.Generator(device=dev).manual_seed(0)
-    qkv = [[torch.randn(B, H, S, D, device=dev, generator=g).half() for _ in range(3)]
+ATT_B, ATT_H, ATT_S, ATT_D = 4, 32, 2048, 128
+
+
+def _spec_attention(torch, pkg, dev, rank, world):
+    """Configuration 3 with its B*H = 128 heads split over the ranks in
+    contiguous groups (no collective: the heads are independent)."""
+    h0, h1 = pkg.sharded.head_range(ATT_B * ATT_H, world, rank)
+    nh = h1 - h0
+    sets = 2 if nh * ATT_S * ATT_D * 2 * 3 * 2 > 130e6 else max(2, int(260e6 // (nh * ATT_S * ATT_D * 6)))
+    g = torch.Generator(device=dev).manual_seed(rank)
+    qkv = [[torch.randn(nh, ATT_S, ATT_D, device=dev, generator=g).half() for _ in range(3)]
            for _ in range(sets)]
     o = torch.empty_like(qkv[0][0])
     return {"step": lambda i: pkg.attention(*qkv[i % sets], out=o), "in": qkv[0][0], "out": o,
-            "sets": sets}
+            "sets": sets, "heads": (h0, h1),
+            "compute": lambda i, x, y: pkg.attention(x, qkv[0][1], qkv[0][2], out=y)}
 
 
-def _spec_decoder(torch, pkg, dev):
+def _spec_decoder(torch, pkg, dev, rank, world):
     H, F, S, NH = 4096, 11008, 512, 32
-    g = torch.Generator(device=dev).manual_seed(0)
+    g = torch.Generator(device=dev).manual_seed(rank)
 
     def w8(k, n):
         return torch.randint(-127, 128, (k, n), device=dev, dtype=torch.int8, generator=g)
@@ -250,38 +513,41 @@ def _spec_decoder(torch, pkg, dev):
     x = torch.randn(S, H, device=dev, generator=g).half()
     out = torch.empty_like(x)
     # one set: the block streams 202 MB of weights per step
-    return {"step": lambda i: blk(x, out=out), "in": x, "out": out, "sets": 1}
+    return {"step": lambda i: blk(x, out=out), "in": x, "out": out, "sets": 1,
+            "compute": lambda i, xi, yo: blk(xi, out=yo)}
 
 
 GQA_B, GQA_HQ, GQA_HKV, GQA_CTX, GQA_D = 4, 32, 8, 8192, 128
 
 
-def _spec_gqa_decode(torch, pkg, dev):
+def _spec_gqa_decode(torch, pkg, dev, rank, world):
     """One decode step of grouped-query attention (32 query heads over 8 KV
     heads, head dim 128) for 4 sequences against an 8192-row KV cache: the
     keys are split across the SMs and merged."""
     sets = 2  # 2 x 134 MB of K/V cache
-    g = torch.Generator(device=dev).manual_seed(0)
+    g = torch.Generator(device=dev).manual_seed(rank)
     q = torch.randn(GQA_B, GQA_HQ, 1, GQA_D, device=dev, generator=g).half()
     kv = [[torch.randn(GQA_B, GQA_HKV, GQA_CTX, GQA_D, device=dev, generator=g).half()
            for _ in range(2)] for _ in range(sets)]
     o = torch.empty(GQA_B, 1, GQA_HQ, GQA_D, dtype=torch.float16, device=dev)
     n = pkg.attention_gqa_workspace_bytes(GQA_B, GQA_HQ, GQA_HKV, 1, GQA_CTX, GQA_D)
     ws = torch.empty(max(n, 16), dtype=torch.uint8, device=dev)
-    return {"step": lambda i: pkg.attention_gqa(q, kv[i % sets][0], kv[i % sets][1],
-                                                out_layout="bshd", out=o, workspace=ws),
-            "in": q, "out": o, "sets": sets}
+
+    def call(i, x, y):
+        return pkg.attention_gqa(x, kv[i % sets][0], kv[i % sets][1], out_layout="bshd", out=y,
+                                 workspace=ws)
+    return {"step": lambda i: call(i, q, o), "in": q, "out": o, "sets": sets, "compute": call}
 
 
 DEC_CTX = 2048  # tokens in the cache before the decode step
 
 
-def _spec_decoder_decode(torch, pkg, dev):
+def _spec_decoder_decode(torch, pkg, dev, rank, world):
     """One decode step of the configuration-4 block against a KV cache of
     2048 tokens (one new token, batch 1): GEMVs over 202 MB of int8 weights,
     the cache write and split-key attention over 33.6 MB of K/V."""
     H, F, NH = 4096, 11008, 32
-    g = torch.Generator(device=dev).manual_seed(0)
+    g = torch.Generator(device=dev).manual_seed(rank)
 
     def w8(k, n):
         return torch.randint(-127, 128, (k, n), device=dev, dtype=torch.int8, generator=g)
@@ -301,7 +567,7 @@ def _spec_decoder_decode(torch, pkg, dev):
     # the step rewrites cache row DEC_CTX each time and attends to rows
     # [0, DEC_CTX]; weights and cache (236 MB) exceed the L2
     return {"step": lambda i: blk.step(x, kc, vc, pos0=DEC_CTX, out=out), "in": x, "out": out,
-            "sets": 1}
+            "sets": 1, "compute": lambda i, xi, yo: blk.step(xi, kc, vc, pos0=DEC_CTX, out=yo)}
 
 
 _W8_DEC_BYTES = 4096 * (3 * 4096 + 4096 + 2 * 11008) + 11008 * 4096
@@ -310,29 +576,29 @@ _SC_DEC_BYTES = 2 * (3 * 4096 + 4096 + 2 * 11008 + 4096)
 SPECS = {
     "f16_gemm_1024": {
         "make": _spec_f16_gemm, "flop": 2.0 * 1024 ** 3, "bound": "tensor",
-        "kernel": "gemm_sm100_kernel", "dtype": "f16->f32",
+        "kernel": "gemm_sm100_kernel", "dtype": "f16->f32", "cpu": cpu_f16_1024,
+        "profile": "f16_gemm_1024x1024x1024.txt",
         "config": {"workload": "f16_gemm_1024x1024x1024", "cfg": 1,
                    "inputs": "A, B ~ U[-1, 1] f16, f16 out"}},
     "gemv_w8_m1": {
         "make": _spec_gemv(1), "bytes": 4096 * 11008 + 2 * 4096 + 2 * 11008 + 2 * 11008,
         "flop": 2.0 * 4096 * 11008, "bound": "hbm", "kernel": "gemv_w8_sk_kernel",
-        "dtype": "f16xi8->f32",
+        "dtype": "f16xi8->f32", "cpu": cpu_gemv(1), "profile": "w8a16_gemv_1x4096x11008.txt",
         "config": {"workload": "w8a16_gemv_1x4096x11008", "cfg": "2b"}},
     "gemv_w8_m16": {
         "make": _spec_gemv(16), "bytes": 4096 * 11008 + 2 * 16 * 4096 + 2 * 11008 + 2 * 16 * 11008,
         "flop": 2.0 * 16 * 4096 * 11008, "bound": "hbm", "kernel": "gemv_w8_sk_kernel",
-        "dtype": "f16xi8->f32",
+        "dtype": "f16xi8->f32", "cpu": cpu_gemv(16), "profile": "w8a16_gemv_16x4096x11008.txt",
         "config": {"workload": "w8a16_gemv_16x4096x11008", "cfg": "2b"}},
     "attention": {
-        "make": _spec_attention, "flop": 4.0 * 4 * 32 * 2048 * 2048 * 128, "bound": "tensor",
-        "kernel": "attention_fwd_kernel", "dtype": "f16->f32",
-        "profile": "attention_4x32x2048x128.txt",
+        "make": _spec_attention, "flop": 4.0 * ATT_B * ATT_H * ATT_S * ATT_S * ATT_D,
+        "bound": "tensor", "split": "heads", "kernel": "attention_fwd_kernel",
+        "dtype": "f16->f32", "cpu": cpu_attention, "profile": "attention_4x32x2048x128.txt",
         "config": {"workload": "attention_4x32x2048x128_noncausal", "cfg": 3}},
     "decoder_block": {
-        "make": _spec_decoder,
-        "flop": 2.0 * 512 * (4 * 4096 * 4096 + 3 * 4096 * 11008) + 2.0 * 32 * 512 * 512 * 128,
-        "bound": "tensor", "kernel": "gemm_w8_sm100_kernel (+ attention, norms)", "launches": 9,
-        "dtype": "f16xi8->f32",
+        "make": _spec_decoder, "flop": DEC_FLOP, "bound": "tensor",
+        "kernel": "gemm_w8_sm100_kernel (+ attention, norms)", "launches": 9,
+        "dtype": "f16xi8->f32", "cpu": cpu_decoder,
         "config": {"workload": "llama_decoder_block_w8_s512", "cfg": 4,
                    "scales": "U[1.5e-4, 4e-4] (int8 of a 0.02-std init)"}},
     "gqa_decode": {
@@ -355,174 +621,105 @@ SPECS = {
                    "bytes": "int8 weights + scales + K/V rows [0, 2048] read"}},
 }
 
+# the sub-records of the default run (the others run with --workload)
+DEFAULT_SPECS = ["f16_gemm_1024", "gemv_w8_m1", "gemv_w8_m16", "attention", "decoder_block"]
 
-def run_spec(args, spec: dict, rank: int, world: int, local_rank: int) -> None:
-    """One spec'd configuration; with N ranks each runs its own replica
-    (weak scaling, no collective)."""
-    import torch
-    import torch.distributed as dist
-    import __graft_entry__ as ge
-    from datetime import timedelta
 
-    pkg = ge.load_package()
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("cuda", local_rank)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-    st = spec["make"](torch, pkg, dev)
-    stream = torch.cuda.current_stream(dev)
-    steps = min(args.steps, 200)
-    # The K dispatches are captured once into a CUDA graph, so a step costs its
-    # kernels' device time and not the Python launch path (a 1024^3 GEMM runs in
-    # a few microseconds, less than one ctypes call).
-    side = torch.cuda.Stream(dev)
-    side.wait_stream(stream)
-    with torch.cuda.stream(side):
-        for i in range(args.warmup):
-            st["step"](i)
-    stream.wait_stream(side)
-    torch.cuda.synchronize(dev)
-    assert pkg.device_status() == 0, "a kernel wait timed out during warm-up"
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        for i in range(steps):
-            st["step"](i)
-    graph.replay()
-    torch.cuda.synchronize(dev)
-    sampler = ClockSampler(local_rank)
-    sampler.start()
-    time.sleep(0.3)
-    if world > 1:
-        dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize(dev)
-    e0.record(stream)
-    graph.replay()
-    e1.record(stream)
-    torch.cuda.synchronize(dev)
-    clocks = sampler.stop()
-    total_ms = e0.elapsed_time(e1)
-    del graph
-    if world > 1:
-        t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms = float(t.item())
-    ms = total_ms / steps
-    # e2e: the same call with its main input copied from pinned host memory and
-    # its output read back, inside the timed region
-    inp, out = st["in"], st["out"]
-    in_h = torch.empty(inp.shape, dtype=inp.dtype, pin_memory=True)
-    in_h.copy_(inp.cpu())
-    out_h = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
-
-    def e2e_step(i):
-        inp.copy_(in_h, non_blocking=True)
-        st["step"](i)
-        out_h.copy_(out, non_blocking=True)
-    for i in range(3):
-        e2e_step(i)
-    torch.cuda.synchronize(dev)
-    e_steps = max(3, min(20, steps))
-    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a0.record(stream)
-    for i in range(e_steps):
-        e2e_step(i)
-    a1.record(stream)
-    torch.cuda.synchronize(dev)
-    e2e_ms = a0.elapsed_time(a1) / e_steps
-    status = pkg.device_status()
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-        dist.barrier()
-        dist.destroy_process_group()
-    if rank != 0:
-        return
-    peaks, peak_kind = _peaks()
+def measure_spec(ctx: Ctx, name: str, cpu: bool) -> dict:
+    """One spec'd configuration. Replicas (weak scaling) unless the spec
+    splits its work over the ranks (strong scaling, no collective)."""
+    torch = ctx.torch
+    spec = SPECS[name]
+    split = spec.get("split")
+    st = spec["make"](torch, ctx.pkg, ctx.dev, ctx.rank, ctx.world)
+    # at least 100 dispatches per graph, so the graph's own launch (a few
+    # microseconds) does not weigh on microsecond-long dispatches
+    steps = max(100, min(ctx.args.steps, 200))
+    ms, clocks = _graph_ms(ctx, st["step"], steps)
+    e2e_ms = _pipelined_e2e_ms(ctx, st["in"], st["out"], st["compute"], max(3, min(20, steps)))
+    status = ctx.pkg.device_status(clear=False)
     if spec["bound"] == "hbm":
         unit, work = "GB/s", spec["bytes"] / 1e9
-        peak, peak_label = peaks["hbm_gbs"], f"{peak_kind} HBM copy"
     else:
         unit, work = "TFLOP/s", spec["flop"] / 1e12
-        peak, peak_label = peaks["bf16_tflops"], f"{peak_kind} bf16 dense (burst)"
-    achieved = work / (ms / 1e3)
-    line = {
-        "metric": METRIC, "value": work * world / (ms / 1e3), "unit": unit, "n_gpus": world,
-        "steps": steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": spec["dtype"], "data": "synthetic",
-        "config": dict(spec["config"], parallelism=f"{world} replicas",
+    if split:
+        total = work  # the whole problem, split over the ranks
+        h0, h1 = st["heads"]
+        per_rank = work * (h1 - h0) / (ATT_B * ATT_H)
+    else:
+        total = work * ctx.world
+        per_rank = work
+    inp, out = st["in"], st["out"]
+    rec = {
+        "value": total / (ms / 1e3), "unit": unit, "ms_per_step": ms, "steps": steps,
+        "scaling": "strong" if split else "weak", "dtype": spec["dtype"],
+        "config": dict(spec["config"],
+                       parallelism=(f"{split} split over {ctx.world} ranks" if split
+                                    else f"{ctx.world} replicas"),
                        l2=f"{st['sets']} rotating input set(s), together larger than the 126 MB L2",
                        timing="K dispatches in one CUDA graph, one replay between two events"),
-        "roofline": {"bound": spec["bound"], "achieved": achieved, "peak": peak, "unit": unit,
-                     "frac": achieved / peak,
-                     "traffic": _profile_traffic(spec.get("profile", spec["config"]["workload"])),
-                     "peak_source": peak_label, "kernel": spec["kernel"], "kernel_ms": ms},
-        "e2e": {"value": work * world / (e2e_ms / 1e3), "unit": unit,
+        "roofline": _roofline(spec["bound"], per_rank, ms, spec["kernel"], spec.get("profile")),
+        "e2e": {"value": total / (e2e_ms / 1e3), "unit": unit,
                 "h2d_bytes_per_step": inp.numel() * inp.element_size(),
-                "d2h_bytes_per_step": out.numel() * out.element_size()},
+                "d2h_bytes_per_step": out.numel() * out.element_size(),
+                "note": "copies pipelined with the dispatch on two copy streams"},
         "gpu_launches": steps * spec.get("launches", 1), "clocks": clocks,
         "device_status": status,
     }
     if "flop" in spec and unit != "TFLOP/s":
-        line["tflops"] = spec["flop"] / (ms / 1e3) / 1e12
-    print(json.dumps(line), flush=True)
+        rec["tflops"] = spec["flop"] / (ms / 1e3) / 1e12
+    if cpu and ctx.rank == 0 and ctx.world == 1 and spec.get("cpu"):
+        rec["cpu_baseline"] = spec["cpu"]()
+    del st
+    torch.cuda.empty_cache()
+    return rec
 
 
-SH_M, SH_K, SH_N = 16384, 8192, 28672
+def _timed(ctx: Ctx, fn, steps: int) -> float:
+    """ms per call of fn over `steps` back-to-back calls (after the warm-up),
+    CUDA events on the current stream, max over ranks."""
+    torch = ctx.torch
+    stream = torch.cuda.current_stream(ctx.dev)
+    for _ in range(ctx.args.warmup):
+        fn()
+    torch.cuda.synchronize(ctx.dev)
+    ctx.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize(ctx.dev)
+    return ctx.max_over_ranks(e0.elapsed_time(e1) / steps)
 
 
-def run_sharded(args, rank: int, world: int, local_rank: int) -> None:
-    """C[16384, 28672] = A[16384, 8192] . B, B split
-    along N over the ranks; one step = the fused GEMM + all-gather (every rank
-    ends with the full C). Also timed: the GEMM alone into the local shard
-    (compute-only scaling) and the NCCL all-gather baseline."""
-    import torch
-    import torch.distributed as dist
-    import __graft_entry__ as ge
-    from datetime import timedelta
-
-    pkg = ge.load_package()
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("cuda", local_rank)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-    steps = min(args.steps, 50)
-    g = torch.Generator(device=dev).manual_seed(0)
-    a = (torch.rand(SH_M, SH_K, device=dev, generator=g) * 2 - 1).half()
-    sm = pkg.sharded.ShardedMatmul(SH_M, SH_N, SH_K, device=dev)
+def measure_sharded(ctx: Ctx, cpu: bool) -> dict:
+    """Configuration 5: C[16384, 28672] = A[16384, 8192] . B, B split along
+    N over the ranks; one step = the fused GEMM + all-gather (every rank ends
+    with the full C). Also timed: the GEMM alone into the local shard
+    (compute-only scaling) and the NCCL all-gather baseline, whose gathered C
+    must equal the fused path's bit for bit."""
+    torch, pkg = ctx.torch, ctx.pkg
+    steps = max(3, min(ctx.args.steps, 20))
+    g = torch.Generator(device=ctx.dev).manual_seed(0)
+    a = (torch.rand(SH_M, SH_K, device=ctx.dev, generator=g) * 2 - 1).half()
+    sm = pkg.sharded.ShardedMatmul(SH_M, SH_N, SH_K, device=ctx.dev)
     n = sm.end - sm.begin
-    b = (torch.rand(SH_K, n, device=dev, generator=g) * 2 - 1).half()
-    shard = torch.empty(SH_M, n, dtype=torch.float16, device=dev)
-    gathered = torch.empty(world * SH_M, n, dtype=torch.float16, device=dev)
-    stream = torch.cuda.current_stream(dev)
-
-    def timed(fn):
-        for _ in range(args.warmup):
-            fn()
-        torch.cuda.synchronize(dev)
-        if world > 1:
-            dist.barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(steps):
-            fn()
-        e1.record(stream)
-        torch.cuda.synchronize(dev)
-        ms = e0.elapsed_time(e1) / steps
-        if world > 1:
-            t = torch.tensor([ms], device=dev, dtype=torch.float64)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
-        return ms
-
-    sampler = ClockSampler(local_rank)
-    sampler.start()
-    time.sleep(0.3)
-    fused_ms = timed(lambda: sm.fused(a, b))
+    g.manual_seed(100 + ctx.rank)
+    b = (torch.rand(SH_K, n, device=ctx.dev, generator=g) * 2 - 1).half()
+    shard = torch.empty(SH_M, n, dtype=torch.float16, device=ctx.dev)
+    gathered = torch.empty(ctx.world * SH_M, n, dtype=torch.float16, device=ctx.dev)
+    sampler = ClockSampler(ctx.local_rank).start()
+    fused_ms = _timed(ctx, lambda: sm.fused(a, b), steps)
     clocks = sampler.stop()
-    compute_ms = timed(lambda: pkg.matmul(a, b, out=shard))
-    nccl_ms = timed(lambda: sm.nccl(a, b, shard_out=shard, gathered=gathered))
+    compute_ms = _timed(ctx, lambda: pkg.matmul(a, b, out=shard), steps)
+    nccl_ms = _timed(ctx, lambda: sm.nccl(a, b, shard_out=shard, gathered=gathered), steps)
+    # parity between the two gather paths (both this library's GEMM)
+    ref_c = sm.nccl(a, b, shard_out=shard, gathered=gathered).clone()
+    fused_c = sm.fused(a, b)
+    torch.cuda.synchronize(ctx.dev)
+    same = ctx.all_true(torch.equal(ref_c, fused_c))
+    del ref_c
     # e2e: the public call with A copied from pinned host memory and C read
     # back to the host every step
     a_h = torch.empty(SH_M, SH_K, dtype=torch.float16, pin_memory=True)
@@ -533,90 +730,148 @@ def run_sharded(args, rank: int, world: int, local_rank: int) -> None:
         a.copy_(a_h, non_blocking=True)
         out = sm.fused(a, b)
         c_h.copy_(out, non_blocking=True)
-    e2e_ms = timed(e2e_step)
-    status = pkg.device_status()
+    e2e_ms = _timed(ctx, e2e_step, max(3, steps // 4))
+    status = pkg.device_status(clear=False)
     sm.close()
-    del sm
+    del sm, gathered, shard, a, b
+    torch.cuda.empty_cache()
     flop = 2.0 * SH_M * SH_N * SH_K
-    peaks, peak_kind = _peaks()
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-    if rank != 0:
-        return
-    per_gpu_flop = flop / world
-    line = {
-        "metric": METRIC, "value": flop / (fused_ms / 1e3) / 1e12, "unit": "TFLOP/s",
-        "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": fused_ms,
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": "f16->f32", "data": "synthetic",
-        "config": {"workload": "sharded_gemm_16384x8192x28672", "split": f"N over {world} ranks",
+    per_gpu = flop / ctx.world
+    rec = {
+        "value": flop / (fused_ms / 1e3) / 1e12, "unit": "TFLOP/s", "ms_per_step": fused_ms,
+        "steps": steps, "scaling": "strong", "dtype": "f16->f32",
+        "config": {"workload": "sharded_gemm_16384x8192x28672", "cfg": 5,
+                   "split": f"N over {ctx.world} ranks",
                    "collective": "all-gather fused into the GEMM epilogue (NVLink peer stores)",
                    "l2": "inputs (A 268 MB) larger than the 126 MB L2"},
         "compute_only": {"value": flop / (compute_ms / 1e3) / 1e12, "unit": "TFLOP/s",
-                         "ms_per_step": compute_ms, "note": "GEMM into the local shard, C left sharded"},
+                         "ms_per_step": compute_ms,
+                         "note": "GEMM into the local shard, C left sharded"},
         "nccl_baseline": {"value": flop / (nccl_ms / 1e3) / 1e12, "unit": "TFLOP/s",
                           "ms_per_step": nccl_ms,
                           "note": "GEMM + NCCL all_gather_into_tensor + layout step"},
-        "roofline": {"bound": "tensor" if world == 1 else "tensor+nvlink",
-                     "achieved": per_gpu_flop / (compute_ms / 1e3) / 1e12,
-                     "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                     "frac": per_gpu_flop / (compute_ms / 1e3) / 1e12 / peaks["bf16_tflops"],
-                     "traffic": None, "peak_source": f"{peak_kind} bf16 dense (burst)",
-                     "kernel": "gemm_sm100_kernel (per-GPU shard)",
-                     "nvlink_floor_ms": (world - 1) / world * SH_M * SH_N * 2 / 770e9 * 1e3},
+        "fused_equals_nccl": same,
+        "nvlink_floor_ms": (ctx.world - 1) / ctx.world * SH_M * SH_N * 2 / 770e9 * 1e3,
+        "roofline": _roofline("tensor", per_gpu / 1e12, compute_ms,
+                              "gemm_sm100_kernel (per-GPU shard)", None),
         "e2e": {"value": flop / (e2e_ms / 1e3) / 1e12, "unit": "TFLOP/s",
                 "h2d_bytes_per_step": SH_M * SH_K * 2, "d2h_bytes_per_step": SH_M * SH_N * 2},
-        "gpu_launches": steps * (1 + (2 if world > 1 else 0)),
+        "gpu_launches": steps * (1 + (2 if ctx.world > 1 else 0)),
         "clocks": clocks, "device_status": status,
     }
-    print(json.dumps(line), flush=True)
+    if cpu and ctx.rank == 0 and ctx.world == 1:
+        rec["cpu_baseline"] = cpu_cfg5()
+    return rec
 
 
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
-    ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["w8a16_gemm", "sharded_gemm"] + sorted(SPECS),
-                    default="w8a16_gemm",
-                    help="w8a16_gemm: BASELINE configuration 2 (the metric's config, default); "
-                         "sharded_gemm: configuration 5 split along N over the ranks; the "
-                         "others: the remaining configurations, one dispatch per step")
-    args = ap.parse_args()
-    args.warmup = max(args.warmup, 3)
+def measure_w8_nsplit(ctx: Ctx, m: int, cpu: bool) -> dict:
+    """The headline int8-weight dispatch (m = 4096) or its decode GEMV
+    (m = 1) with W [4096, 11008] split along N over the ranks (11008 / 8 =
+    1376 columns at 8 ranks) and the all-gather of C fused into the
+    epilogue; compute-only and the NCCL baseline beside it."""
+    torch, pkg = ctx.torch, ctx.pkg
+    sw = pkg.sharded.ShardedMatmulW8(m, N, K, device=ctx.dev,
+                                     workspace=pkg.w8a16_workspace(ctx.dev))
+    n = sw.end - sw.begin
+    # rotating (activation, weight shard) sets, together larger than the L2
+    # at every rank count
+    per_set = 2 * m * K + K * n
+    sets = max(2, -(-260_000_000 // per_set))
+    g = torch.Generator(device=ctx.dev).manual_seed(7)
+    acts = [torch.randn(m, K, device=ctx.dev, generator=g).half() for _ in range(sets)]
+    g.manual_seed(200 + ctx.rank)
+    ws = [torch.randint(-127, 128, (K, n), device=ctx.dev, dtype=torch.int8, generator=g)
+          for _ in range(sets)]
+    s = (torch.rand(n, device=ctx.dev, generator=g) * 0.019 + 0.001).half()
+    a = acts[0]
+    shard = torch.empty(m, n, dtype=torch.float16, device=ctx.dev)
+    gathered = torch.empty(ctx.world * m, n, dtype=torch.float16, device=ctx.dev)
+    steps = max(3, min(ctx.args.steps, 50))
+    it = {"i": 0}
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    def nxt():
+        it["i"] += 1
+        return acts[it["i"] % sets], ws[it["i"] % sets]
+    sampler = ClockSampler(ctx.local_rank).start()
+    fused_ms = _timed(ctx, lambda: sw.fused(*nxt(), s), steps)
+    clocks = sampler.stop()
+    compute_ms = _timed(ctx, lambda: pkg.matmul_w8a16(*nxt(), s, out=shard,
+                                                      workspace=sw.workspace), steps)
+    nccl_ms = _timed(ctx, lambda: sw.nccl(*nxt(), s, shard_out=shard, gathered=gathered),
+                     steps)
+    ref_c = sw.nccl(a, ws[0], s, shard_out=shard, gathered=gathered).clone()
+    fused_c = sw.fused(a, ws[0], s)
+    torch.cuda.synchronize(ctx.dev)
+    same = ctx.all_true(torch.equal(ref_c, fused_c))
+    a_h = torch.empty(m, K, dtype=torch.float16, pin_memory=True)
+    a_h.copy_(a.cpu())
+    c_h = torch.empty(m, N, dtype=torch.float16, pin_memory=True)
 
-    if args.impl == "reference":
-        run_reference(args, rank)
-        return
-    if args.workload == "sharded_gemm":
-        run_sharded(args, rank, world, local_rank)
-        return
-    if args.workload in SPECS:
-        run_spec(args, SPECS[args.workload], rank, world, local_rank)
-        return
+    def e2e_step():
+        a.copy_(a_h, non_blocking=True)
+        out = sw.fused(a, ws[0], s)
+        c_h.copy_(out, non_blocking=True)
+    e2e_ms = _timed(ctx, e2e_step, max(3, steps // 4))
+    status = pkg.device_status(clear=False)
+    sw.close()
+    del sw, ws, acts, gathered, shard
+    torch.cuda.empty_cache()
+    flop = 2.0 * m * K * N
+    wbytes = K * N + 2 * m * K + 2 * N + 2 * m * N
+    gemv = m <= 16
+    if gemv:
+        unit, work, peak_bound = "GB/s", wbytes / 1e9, "hbm"
+        per_rank = (K * n + 2 * m * K + 2 * n + 2 * m * n) / 1e9
+    else:
+        unit, work, peak_bound = "TFLOP/s", flop / 1e12, "tensor"
+        per_rank = 2.0 * m * K * n / 1e12
+    rec = {
+        "value": work / (fused_ms / 1e3), "unit": unit, "ms_per_step": fused_ms, "steps": steps,
+        "scaling": "strong", "dtype": "f16xi8->f32",
+        "config": {"workload": f"w8a16_{'gemv' if gemv else 'gemm'}_{m}x{K}x{N}_nsplit",
+                   "cfg": "2" if not gemv else "2b", "split": f"N over {ctx.world} ranks",
+                   "shard_columns": n,
+                   "l2": f"{sets} rotating (activation, weight shard) sets, > 126 MB L2",
+                   "collective": ("all-gather fused into the GEMM epilogue (NVLink peer stores)"
+                                  if not gemv else
+                                  "all-gather of the GEMV's rows by one peer-store kernel")},
+        "compute_only": {"value": work / (compute_ms / 1e3), "unit": unit,
+                         "ms_per_step": compute_ms, "note": "the shard alone, C left sharded"},
+        "nccl_baseline": {"value": work / (nccl_ms / 1e3), "unit": unit, "ms_per_step": nccl_ms,
+                          "note": "shard + NCCL all_gather_into_tensor + layout step"},
+        "fused_equals_nccl": same,
+        "nvlink_floor_ms": (ctx.world - 1) / ctx.world * m * N * 2 / 770e9 * 1e3,
+        "roofline": _roofline(peak_bound, per_rank, compute_ms,
+                              "gemv_w8_sk_kernel" if gemv else "gemm_w8_sm100_kernel", None),
+        "e2e": {"value": work / (e2e_ms / 1e3), "unit": unit,
+                "h2d_bytes_per_step": m * K * 2, "d2h_bytes_per_step": m * N * 2},
+        "gpu_launches": steps * (1 + (1 if gemv and ctx.world > 1 else 0) +
+                                 (2 if ctx.world > 1 else 0)),
+        "clocks": clocks, "device_status": status,
+    }
+    if gemv:
+        rec["tflops"] = flop / (fused_ms / 1e3) / 1e12
+    if cpu and ctx.rank == 0 and ctx.world == 1:
+        rec["cpu_baseline"] = cpu_cfg2() if not gemv else cpu_gemv(m)()
+    return rec
 
-    import torch
-    import torch.distributed as dist
-    import __graft_entry__ as ge
 
-    pkg = ge.load_package()
-    lib = pkg._native.load()
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("cuda", local_rank)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
-                                device_id=dev)
+# ------------------------------------------------------------------------
+# The headline: configuration 2, one dispatch per step, data parallel.
 
-    sets = [make_inputs(torch, dev, seed=1000 * rank + i) for i in range(N_SETS)]
-    stream = torch.cuda.current_stream(dev)
+def make_inputs(torch, dev, seed):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    a = torch.randn(M, K, device=dev, dtype=torch.float32, generator=g).half()
+    w = torch.randint(-127, 128, (K, N), device=dev, dtype=torch.int8, generator=g)
+    s = (torch.rand(N, device=dev, generator=g) * 0.019 + 0.001).half()
+    c = torch.empty(M, N, device=dev, dtype=torch.float16)
+    return a, w, s, c
+
+
+def measure_headline(ctx: Ctx, cpu: bool) -> dict:
+    torch, pkg, args = ctx.torch, ctx.pkg, ctx.args
+    sets = [make_inputs(torch, ctx.dev, seed=1000 * ctx.rank + i) for i in range(N_SETS)]
+    stream = torch.cuda.current_stream(ctx.dev)
 
     def step(i):
         a, w, s, c = sets[i % N_SETS]
@@ -624,117 +879,114 @@ def main():
 
     for i in range(args.warmup):
         step(i)
-    torch.cuda.synchronize(dev)
-    assert pkg.device_status() == 0, "a kernel wait timed out during warm-up"
+    torch.cuda.synchronize(ctx.dev)
+    assert pkg.device_status(clear=False) == 0, "a kernel wait timed out during warm-up"
 
     # ---------------- timed region: device events around exactly K steps
-    sampler = ClockSampler(local_rank)
-    sampler.start()
-    time.sleep(0.3)
+    sampler = ClockSampler(ctx.local_rank).start()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize(dev)
+    ctx.barrier()
+    torch.cuda.synchronize(ctx.dev)
     ev[0].record(stream)
     for i in range(args.steps):
         step(i)
         ev[i + 1].record(stream)
-    torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
+    torch.cuda.synchronize(ctx.dev)
+    ctx.barrier()
     clocks = sampler.stop()
     per_step_ms = [ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)]
-    total_ms = ev[0].elapsed_time(ev[-1])
-    if world > 1:
-        t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms = float(t.item())
-    value = FLOP_PER_STEP * args.steps * world / (total_ms / 1e3) / 1e12
+    total_ms = ctx.max_over_ranks(ev[0].elapsed_time(ev[-1]))
+    value = FLOP_PER_STEP * args.steps * ctx.world / (total_ms / 1e3) / 1e12
 
-    # kernel-level roofline: one dispatch per step, launched on `stream`
+    # kernel-level roofline: one dispatch per step, launched on `stream`. A
+    # kernel timed inside a long back-to-back loop runs under the power cap:
+    # compare it with the sustained GEMM figure; a short burst with the burst
+    # one.
     kernel_ms = statistics.mean(per_step_ms)
-    achieved = FLOP_PER_STEP / (kernel_ms / 1e3) / 1e12
-    peaks, peak_kind = _peaks()
-    # A kernel timed inside a long back-to-back loop runs under the power cap:
-    # compare it with the sustained GEMM figure; a short burst with the burst one.
-    sustained = total_ms > 500.0 and peaks.get("bf16_tflops_sustained")
-    peak = peaks["bf16_tflops_sustained"] if sustained else peaks["bf16_tflops"]
-    peak_label = f"{peak_kind} bf16 dense ({'sustained' if sustained else 'burst'})"
-    traffic = _profile_traffic("w8a16_gemm_4096x4096x11008")
+    roof = _roofline("tensor", FLOP_PER_STEP / 1e12, kernel_ms,
+                     "gemm_w8_sm100_kernel (swap-AB, int8->f16 in TMEM)",
+                     "w8a16_gemm_4096x4096x11008", sustained=total_ms > 500.0)
 
-    # ---------------- e2e: host buffers through the public API
-    e2e_steps = max(3, min(50, args.steps // 10))
-    a_h = torch.empty(M, K, dtype=torch.float16, pin_memory=True)
-    a_h.copy_(sets[0][0].cpu())
-    c_h = torch.empty(M, N, dtype=torch.float16, pin_memory=True)
-    a_d = torch.empty_like(sets[0][0])
+    # ---------------- e2e: host buffers through the public API, copies
+    # pipelined with the dispatches
     _, w_d, s_d, c_d = sets[0]
-
-    def e2e_step():
-        a_d.copy_(a_h, non_blocking=True)
-        pkg.matmul_w8a16(a_d, w_d, s_d, out=c_d)
-        c_h.copy_(c_d, non_blocking=True)
-
-    for _ in range(3):
-        e2e_step()
-    torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
-    e1.record(stream)
-    torch.cuda.synchronize(dev)
-    e2e_ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    e2e_value = FLOP_PER_STEP * e2e_steps * world / (e2e_ms / 1e3) / 1e12
-    status = pkg.device_status()
-
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline_sample()
-
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-    if rank != 0:
-        return
+    e2e_steps = max(3, min(50, args.steps // 2))
+    e2e_ms = _pipelined_e2e_ms(ctx, sets[0][0], c_d,
+                               lambda i, x, y: pkg.matmul_w8a16(x, w_d, s_d, out=y), e2e_steps)
+    e2e_value = FLOP_PER_STEP * ctx.world / (e2e_ms / 1e3) / 1e12
+    status = pkg.device_status(clear=False)
+    del sets
+    torch.cuda.empty_cache()
     line = {
-        "metric": METRIC,
-        "value": value,
-        "unit": "TFLOP/s",
-        "n_gpus": world,
-        "steps": args.steps,
-        "warmup": args.warmup,
-        "ms_per_step": total_ms / args.steps,
-        "higher_is_better": True,
-        "scaling": "weak",
-        "vs_baseline": None,
-        "dtype": "f16xi8->f32",
-        "data": "synthetic",
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": ctx.world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f16xi8->f32", "data": "synthetic",
         "config": {"workload": WORKLOAD, "M": M, "K": K, "N": N,
                    "weights": "int8 U{-127..127}, per-channel f16 scale U[0.001,0.02]",
                    "activations": "f16 N(0,1)",
-                   "parallelism": f"dp{world} (independent batches, no collective)",
+                   "parallelism": f"dp{ctx.world} (independent batches, no collective)",
                    "l2": f"{N_SETS} rotating input sets ({N_SETS * 169} MB) > 126 MB L2"},
-        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
-                     "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
-                     "peak_source": peak_label,
-                     "kernel": "gemm_w8_sm100_kernel (swap-AB, int8->f16 in TMEM)",
-                     "kernel_ms": kernel_ms},
+        "roofline": roof,
         "e2e": {"value": e2e_value, "unit": "TFLOP/s",
-                "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2},
+                "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2,
+                "note": "copies pipelined with the dispatch on two copy streams"},
         "gpu_launches": args.steps,
         "clocks": clocks,
         "device_status": status,
     }
-    if cpu:
-        line["cpu_baseline"] = cpu
-    print(json.dumps(line), flush=True)
+    if cpu and ctx.rank == 0 and ctx.world == 1:
+        line["cpu_baseline"] = cpu_cfg2()
+    return line
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="all",
+                    choices=["all", "w8a16_gemm", "sharded_gemm", "w8_nsplit", "gemv_nsplit"]
+                    + sorted(SPECS),
+                    help="all (default): the headline (configuration 2) plus every other "
+                         "configuration as a sub-record; otherwise one configuration alone")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank = int(os.environ.get("RANK", "0"))
+
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    cpu = not args.no_cpu_baseline
+    ctx = Ctx(args)
+    try:
+        if args.workload in ("all", "w8a16_gemm"):
+            line = measure_headline(ctx, cpu)
+            if args.workload == "all":
+                configs = {}
+                for name in DEFAULT_SPECS:
+                    configs[name] = measure_spec(ctx, name, cpu)
+                configs["sharded_gemm"] = measure_sharded(ctx, cpu)
+                configs["w8_gemm_nsplit"] = measure_w8_nsplit(ctx, M, cpu=False)
+                configs["w8_gemv_nsplit_m1"] = measure_w8_nsplit(ctx, 1, cpu=False)
+                line["configs"] = configs
+                line["gpu_launches"] += sum(c["gpu_launches"] for c in configs.values())
+        elif args.workload == "sharded_gemm":
+            line = dict(measure_sharded(ctx, cpu), metric=METRIC, n_gpus=ctx.world)
+        elif args.workload in ("w8_nsplit", "gemv_nsplit"):
+            line = dict(measure_w8_nsplit(ctx, M if args.workload == "w8_nsplit" else 1, cpu),
+                        metric=METRIC, n_gpus=ctx.world)
+        else:
+            line = dict(measure_spec(ctx, args.workload, cpu), metric=METRIC, n_gpus=ctx.world)
+        if "warmup" not in line:
+            line.update(warmup=args.warmup, higher_is_better=True, vs_baseline=None,
+                        data="synthetic")
+    finally:
+        ctx.close()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
 
 
 if __name__ == "__main__":

@@ -396,7 +396,8 @@ W8Plan w8_plan(int tiles, long long num_kb, int units) {
 hxb_status_t gemm_w8_impl(const void* A, int64_t lda, const void* W,
                           int64_t ldw, const void* scale, const void* R, void* C, int64_t ldc,
                           int64_t M, int64_t N, int64_t K, void* sk_ws, size_t sk_ws_bytes,
-                          cudaStream_t stream) {
+                          cudaStream_t stream, void* const* replicas = nullptr,
+                          int nreplicas = 0) {
   DeviceInfo* dev = nullptr;
   hxb_status_t s = current_device(&dev);
   if (s != HXB_OK) return s;
@@ -452,6 +453,10 @@ hxb_status_t gemm_w8_impl(const void* A, int64_t lda, const void* W,
   // CTAs running at the same time share that int8 block in L2
   args.group_m = args.tiles_m;
   args.vec_ok = 0;
+  // all-gather epilogue: the staged tiles also go to the other ranks' outputs
+  args.ndests = nreplicas > 0 ? nreplicas + 1 : 0;
+  args.dests[0] = C;
+  for (int i = 0; i < nreplicas; ++i) args.dests[i + 1] = const_cast<void*>(replicas[i]);
   const int tiles = args.tiles_m * args.tiles_n;
   const int sms = dev->num_sms;
   int grid = tiles < sms ? tiles : sms;
@@ -503,10 +508,33 @@ extern "C" hxb_status_t hxb_matmul_f16(const void* A, int64_t lda, const void* B
 }
 
 namespace hxb {
+namespace {
+// dests[d][r, c] = src[r, c] for r < M, c < N (f16, leading dimension ld,
+// 8-column chunks): the all-gather step of the GEMV path, whose output is a
+// few rows.
+struct Dests {
+  void* p[kMaxDests];
+  int n;
+};
+__global__ void replicate_block_kernel(const __half* __restrict__ src, long long ld, int M,
+                                       int N, Dests dests) {
+  pdl_wait();
+  const int chunks = N / 8;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+       i < (long long)M * chunks; i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / chunks, c = (i % chunks) * 8;
+    const uint4 v = *reinterpret_cast<const uint4*>(src + r * ld + c);
+    for (int d = 0; d < dests.n; ++d)
+      *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(dests.p[d]) + r * ld + c) = v;
+  }
+}
+}  // namespace
+
 hxb_status_t matmul_w8a16_impl(const void* A, int64_t lda, const void* W, int64_t ldw,
                                const void* scale, const void* R, void* C, int64_t ldc,
                                int64_t M, int64_t N, int64_t K, void* sk_ws,
-                               size_t sk_ws_bytes, cudaStream_t stream) {
+                               size_t sk_ws_bytes, cudaStream_t stream,
+                               void* const* replicas = nullptr, int nreplicas = 0) {
   if (M < 1 || N < 1 || K < 1)
     return fail(HXB_STATUS_INVALID_ARGUMENT, "matmul_w8a16: M, N, K must be >= 1");
   if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX)
@@ -521,18 +549,54 @@ hxb_status_t matmul_w8a16_impl(const void* A, int64_t lda, const void* W, int64_
                 "matmul_w8a16: A/W/C/scale/R must be 16-byte aligned with lda%%8 == 0, "
                 "ldw%%16 == 0, ldc%%8 == 0");
   if (M <= kGemvRows) {
-    if (sk_ws) {
-      const hxb_status_t s =
-          gemv_w8_sk_impl(A, lda, W, ldw, scale, R, C, ldc, M, N, K, sk_ws, sk_ws_bytes, stream);
-      if (s != HXB_STATUS_UNSUPPORTED) return s;
-    }
-    return gemv_w8_impl(A, lda, W, ldw, scale, R, C, ldc, M, N, K, stream);
+    hxb_status_t s = HXB_STATUS_UNSUPPORTED;
+    if (sk_ws)
+      s = gemv_w8_sk_impl(A, lda, W, ldw, scale, R, C, ldc, M, N, K, sk_ws, sk_ws_bytes, stream);
+    if (s == HXB_STATUS_UNSUPPORTED)
+      s = gemv_w8_impl(A, lda, W, ldw, scale, R, C, ldc, M, N, K, stream);
+    if (s != HXB_OK || nreplicas == 0) return s;
+    // a few output rows: copy the block to the other ranks in one small
+    // programmatically launched kernel after the GEMV
+    Dests d{};
+    d.n = nreplicas;
+    for (int i = 0; i < nreplicas; ++i) d.p[i] = const_cast<void*>(replicas[i]);
+    const long long work = M * (N / 8);
+    const int blocks = (int)((work + 255) / 256);
+    return launch_pdl(replicate_block_kernel, dim3(blocks), dim3(256), 0, stream,
+                      "replicate launch", static_cast<const __half*>(C), (long long)ldc, (int)M,
+                      (int)N, d);
   }
   if (sk_ws && !aligned16(sk_ws))
     return fail(HXB_STATUS_INVALID_ARGUMENT, "matmul_w8a16: workspace must be 16-byte aligned");
-  return gemm_w8_impl(A, lda, W, ldw, scale, R, C, ldc, M, N, K, sk_ws, sk_ws_bytes, stream);
+  return gemm_w8_impl(A, lda, W, ldw, scale, R, C, ldc, M, N, K, sk_ws, sk_ws_bytes, stream,
+                      replicas, nreplicas);
 }
 }  // namespace hxb
+
+extern "C" hxb_status_t hxb_matmul_w8a16_allgather(const void* A, int64_t lda, const void* W,
+                                                   int64_t ldw, const void* scale, void* C,
+                                                   void* const* replicas, int nreplicas,
+                                                   int64_t ldc, int64_t M, int64_t N, int64_t K,
+                                                   void* workspace, size_t workspace_bytes,
+                                                   void* stream) {
+  using namespace hxb;
+  if (nreplicas < 0 || nreplicas > kMaxDests - 1)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "matmul_w8a16_allgather: 0..%d replicas",
+                kMaxDests - 1);
+  if (nreplicas > 0 && !replicas)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "matmul_w8a16_allgather: null replica list");
+  if (N % 8)
+    return fail(HXB_STATUS_INVALID_ARGUMENT,
+                "matmul_w8a16_allgather: the shard width N (%lld) must be a multiple of 8",
+                (long long)N);
+  for (int i = 0; i < nreplicas; ++i)
+    if (!replicas[i] || !aligned16(replicas[i]))
+      return fail(HXB_STATUS_INVALID_ARGUMENT,
+                  "matmul_w8a16_allgather: replica %d is null or not 16-byte aligned", i);
+  return matmul_w8a16_impl(A, lda, W, ldw, scale, nullptr, C, ldc, M, N, K, workspace,
+                           workspace_bytes, static_cast<cudaStream_t>(stream), replicas,
+                           nreplicas);
+}
 
 extern "C" hxb_status_t hxb_matmul_w8a16(const void* A, int64_t lda, const void* W,
                                          int64_t ldw, const void* scale, void* C,

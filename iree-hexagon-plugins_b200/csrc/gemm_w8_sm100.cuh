@@ -388,6 +388,34 @@ __device__ __forceinline__ bool w8_add_partials(const GemmArgs& args, const Fail
 // row m = 32 c + 8 rep + 2 (t & 3) + j at 16-byte chunk
 // (4 (q & 1) + 2 h + (t >> 4)) ^ (m & 7), word (t >> 2) & 3 of the 128-byte
 // row m: the 32 lanes of each access hit 32 different banks.
+// All-gather epilogue: the staged f16 tile (two 128B-swizzled boxes of 64
+// columns x 256 rows; 16-byte chunk c of row m at (c ^ (m & 7)) * 16) is also
+// written to the other ranks' copies of the output, dests[1..ndests), at the
+// same row and column, with 16-byte stores over NVLink. Consecutive threads
+// take consecutive chunks of a row (256 contiguous bytes per row and peer).
+// Rows past M and columns past N (the shard's width, a multiple of 8) are
+// skipped, as the local TMA store clips them. Every epilogue thread reads
+// its chunks before it reaches the next tile's barrier, so the staging tile
+// is free by then.
+template <class Args>
+__device__ __forceinline__ void w8_store_replicas(const Args& args, const uint8_t* stage,
+                                                  int tm, int tn) {
+  const int tid = threadIdx.x - 32 * (4 + kW8ConvWarps);
+  const int rows = min(kW8BM, args.M - tm * kW8BM);
+  const int cols = min(kW8BN, args.N - tn * kW8BN);
+#pragma unroll 1
+  for (int idx = tid; idx < rows * 16; idx += 32 * kW8EpiWarps) {
+    const int m = idx >> 4, c16 = idx & 15;
+    if (c16 * 8 >= cols) continue;
+    const uint4 v = *reinterpret_cast<const uint4*>(stage + (c16 >> 3) * (kW8BM * 128) +
+                                                   m * 128 + (((c16 & 7) ^ (m & 7)) << 4));
+    const long long off =
+        (long long)(tm * kW8BM + m) * args.ldc + (long long)tn * kW8BN + c16 * 8;
+    for (int d = 1; d < args.ndests; ++d)
+      *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(args.dests[d]) + off) = v;
+  }
+}
+
 template <bool RESID>
 __device__ __forceinline__ void w8_stage_tile(uint32_t acc_tmem, uint8_t* box, int q, int lane,
                                               const float (&sc)[2][2]) {
@@ -687,6 +715,7 @@ __global__ void __launch_bounds__(kW8Threads, 1)
         bulk_commit();
         stores_pending = true;
       }
+      if (args.ndests > 1) w8_store_replicas(args, stage, tm, tn);
       ++tl;
     }
     if (issuer && stores_pending) bulk_wait_all();

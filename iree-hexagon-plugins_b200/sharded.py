@@ -1,5 +1,13 @@
-"""Multi-GPU split of one large f16 matmul along N (
-A [16384, 8192] x B [8192, 28672], split across 1/2/4/8 GPUs).
+"""Multi-GPU splits of the hot path (one process per GPU, torch.distributed
+for the plumbing):
+
+  * ShardedMatmul: one large f16 matmul split along N (BASELINE
+    configuration 5: A [16384, 8192] x B [8192, 28672], 1/2/4/8 GPUs);
+  * ShardedMatmulW8: the int8-weight matmul split along N (configuration 2:
+    W [4096, 11008] in column shards of a multiple of 16 columns, 1376 per
+    rank at 8 ranks), for the GEMM (M > 16) and the decode GEMV (M <= 16);
+  * head_range: the fused attention split by heads (configuration 3: the
+    B*H = 128 heads in contiguous groups; no collective).
 
 One process per GPU, torch.distributed for the plumbing. Rank r of G holds A
 (replicated) and the column shard B[:, cols_r] and computes C[:, cols_r] with
@@ -60,10 +68,21 @@ def _stream_ptr(t: torch.Tensor) -> int:
     return torch.cuda.current_stream(t.device).cuda_stream
 
 
+def head_range(heads: int, world: int, rank: int) -> tuple[int, int]:
+    """[begin, end) of the heads rank computes when `heads` independent
+    attention heads (batch x heads flattened) are split over `world` ranks in
+    contiguous groups that differ by at most one head."""
+    base, extra = divmod(heads, world)
+    begin = rank * base + min(rank, extra)
+    return begin, begin + base + (1 if rank < extra else 0)
+
+
 class ShardedMatmul:
     """C = A @ B for B split along N across the ranks of `group` (one GPU
     per rank). Holds this rank's full output buffer and the peers' buffers
     opened through CUDA IPC."""
+
+    ALIGN = 8  # columns per shard unit: 16-byte rows of f16 C
 
     def __init__(self, M: int, N: int, K: int, *, group=None, device=None):
         import torch.distributed as dist
@@ -75,7 +94,7 @@ class ShardedMatmul:
             raise ValueError("at most 8 ranks (one replica per peer in the epilogue)")
         self.M, self.N, self.K = M, N, K
         self.device = device or torch.device("cuda", torch.cuda.current_device())
-        self.cols = [shard_columns(N, self.world, r) for r in range(self.world)]
+        self.cols = [shard_columns(N, self.world, r, self.ALIGN) for r in range(self.world)]
         self.begin, self.end = self.cols[self.rank]
         self.out = torch.empty((M, N), dtype=torch.float16, device=self.device)
         self._peer_storages: list = []  # (mapped pointer, offset) of opened peers
@@ -146,3 +165,54 @@ class ShardedMatmul:
             check(lib.hxb_ipc_close(p, off))
         self._peer_storages.clear()
         self.peer_ptrs = []
+
+
+class ShardedMatmulW8(ShardedMatmul):
+    """C[M, N] = (A[M, K] . W[K, N] int8) * scale[N] for W and scale split
+    along N across the ranks of `group`. Rank r holds W[:, cols_r] (a
+    contiguous [K, n_r] int8 tensor, n_r a multiple of 16 so its rows keep
+    the 16-byte TMA pitch) and scale[cols_r], and computes C[:, cols_r]; the
+    fused path writes each output tile to every rank's full C
+    (hxb_matmul_w8a16_allgather)."""
+
+    ALIGN = 16
+
+    def __init__(self, M: int, N: int, K: int, *, group=None, device=None, workspace=None):
+        super().__init__(M, N, K, group=group, device=device)
+        self.workspace = workspace
+
+    def fused(self, a: torch.Tensor, w_shard: torch.Tensor,
+              s_shard: torch.Tensor) -> torch.Tensor:
+        lib = _native.load()
+        n = self.end - self.begin
+        assert w_shard.shape == (self.K, n) and s_shard.numel() == n
+        assert a.shape == (self.M, self.K)
+        self._sync()
+        reps = (ctypes.c_void_p * max(1, len(self.peer_ptrs)))(
+            *[p + self.begin * 2 for p in self.peer_ptrs] or [0])
+        ws = self.workspace
+        check(lib.hxb_matmul_w8a16_allgather(
+            a.data_ptr(), a.stride(0), w_shard.data_ptr(), w_shard.stride(0), s_shard.data_ptr(),
+            self.out.data_ptr() + self.begin * 2, reps if self.peer_ptrs else None,
+            len(self.peer_ptrs), self.out.stride(0), self.M, n, self.K,
+            ws.data_ptr() if ws is not None else None,
+            ws.numel() * ws.element_size() if ws is not None else 0, _stream_ptr(a)))
+        self._sync()
+        return self.out
+
+    def nccl(self, a: torch.Tensor, w_shard: torch.Tensor, s_shard: torch.Tensor, *,
+             shard_out: torch.Tensor, gathered: torch.Tensor) -> torch.Tensor:
+        """Baseline: W8 matmul into the local shard, NCCL all-gather, layout
+        step. Needs equal shards."""
+        from .dispatch import matmul_w8a16
+        lib = _native.load()
+        n = self.end - self.begin
+        matmul_w8a16(a, w_shard, s_shard, out=shard_out, workspace=self.workspace)
+        if self.world > 1:
+            self.dist.all_gather_into_tensor(gathered, shard_out, group=self.group)
+            src = gathered
+        else:
+            src = shard_out
+        check(lib.hxb_gather_column_blocks_f16(src.data_ptr(), self.out.data_ptr(), self.world,
+                                               self.M, n, self.out.stride(0), _stream_ptr(a)))
+        return self.out

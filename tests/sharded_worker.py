@@ -52,6 +52,33 @@ def main() -> None:
         assert pkg.device_status() == 0
         dist.barrier()
         sm.close()
+        # configuration 2 split along N: the GEMM (M > 16) and the GEMV
+        # (M <= 16), fused all-gather against the NCCL baseline and the oracle
+        N8, K8 = 2752, 1024
+        w8 = rng.integers(-127, 128, (K8, N8), dtype=np.int8)
+        s8 = rng.uniform(0.001, 0.02, N8).astype(np.float16)
+        for M8 in (600, 3):
+            x8 = rng.standard_normal((M8, K8)).astype(np.float16)
+            sw = pkg.sharded.ShardedMatmulW8(M8, N8, K8, device=dev,
+                                            workspace=pkg.w8a16_workspace(dev))
+            c0, c1 = sw.begin, sw.end
+            xd = torch.from_numpy(x8).to(dev)
+            wd = torch.from_numpy(np.ascontiguousarray(w8[:, c0:c1])).to(dev)
+            sd = torch.from_numpy(np.ascontiguousarray(s8[c0:c1])).to(dev)
+            fused8 = sw.fused(xd, wd, sd).clone()
+            shard8 = torch.empty(M8, c1 - c0, dtype=torch.float16, device=dev)
+            gath8 = torch.empty(world * M8, c1 - c0, dtype=torch.float16, device=dev)
+            nccl8 = sw.nccl(xd, wd, sd, shard_out=shard8, gathered=gath8)
+            torch.cuda.synchronize()
+            assert torch.equal(fused8, nccl8), f"w8 M={M8}: fused all-gather differs from NCCL"
+            if rank == 0:
+                from oracle import oracle
+                from _support import baseline_check
+                baseline_check(oracle.matmul_w8a16_f32(x8, w8, s8),
+                               fused8.float().cpu().numpy(), f"2-rank w8 M={M8}")
+            dist.barrier()
+            sw.close()
+        assert pkg.device_status() == 0
         if rank == 0:
             print("sharded ok", flush=True)
     finally:

@@ -15,6 +15,20 @@ import torch
 
 from _support import baseline_check, f16_ulp
 
+
+def _block_check(ref: np.ndarray, got: np.ndarray, what: str) -> None:
+    """The BASELINE bar on a whole decoder-block output against the oracle's
+    restatement of the Hugging Face modules: |d| <= 1e-2 + one f16 ulp of the
+    reference value and relative L2 <= 1e-3 (baseline_check), with the
+    measured figures printed for the record."""
+    r = ref.astype(np.float64)
+    d = np.abs(got.astype(np.float64) - r)
+    rel = np.linalg.norm(d) / np.linalg.norm(r)
+    worst = float((d / (1e-2 + f16_ulp(ref.astype(np.float32)))).max())
+    print(f"{what}: rel-L2 {rel:.3g}, max|d| {d.max():.4g}, "
+          f"max |d| / (1e-2 + ulp) {worst:.3g}, max |ref| {float(np.abs(r).max()):.4g}")
+    baseline_check(ref.astype(np.float32), got.astype(np.float32), what)
+
 pytestmark = pytest.mark.gpu
 
 DEV = "cuda:0"
@@ -142,11 +156,8 @@ def test_decoder_block_well_conditioned(cuda_pkg, oracle, batch, S, hidden, head
     x = rng.standard_normal((batch * S, hidden)).astype(np.float16)
     got = _run_block(cuda_pkg, x, wt, heads, batch)
     ref = oracle.decoder_block_w8(x, wt, heads=heads, batch=batch)["out"]
-    d = np.abs(got.astype(np.float64) - ref.astype(np.float64))
-    rel = np.linalg.norm(d) / np.linalg.norm(ref.astype(np.float64))
     assert np.isfinite(got).all()
-    assert rel <= 2e-3, f"relative L2 {rel:.3g}"
-    assert (d <= 2e-2 + 4 * f16_ulp(ref.astype(np.float32))).all(), f"max |d| {d.max():.4g}"
+    _block_check(ref, got, f"block {batch}x{S}x{hidden}")
     assert cuda_pkg.device_status() == 0
 
 
@@ -166,10 +177,7 @@ def test_decoder_block_baseline_config4(cuda_pkg, oracle):
     got = _run_block(cuda_pkg, x, wt, heads, 1)
     ref = oracle.decoder_block_w8(x, wt, heads=heads)["out"]
     assert np.isfinite(ref).all() and np.isfinite(got).all()
-    d = np.abs(got.astype(np.float64) - ref.astype(np.float64))
-    rel = np.linalg.norm(d) / np.linalg.norm(ref.astype(np.float64))
-    assert rel <= 2e-3, f"relative L2 {rel:.3g}"
-    assert (d <= 2e-2 + 4 * f16_ulp(ref.astype(np.float32))).all(), f"max |d| {d.max():.4g}"
+    _block_check(ref, got, "cfg 4 block")
 
 
 # ------------------------------------------------------------- KV cache
@@ -246,12 +254,9 @@ def test_cached_decode_steps_vs_oracle(cuda_pkg, oracle, batch, prompt, steps, h
         torch.cuda.synchronize()
         ref = oracle.decoder_block_w8(xt, wt, heads=heads, batch=batch, pos0=prompt + i,
                                       k_cache=k_ref, v_cache=v_ref)["out"]
-        g = got.cpu().numpy().astype(np.float64)
-        d = np.abs(g - ref.astype(np.float64))
-        rel = np.linalg.norm(d) / np.linalg.norm(ref.astype(np.float64))
-        assert np.isfinite(g).all()
-        assert rel <= 2e-3, f"step {i}: relative L2 {rel:.3g}"
-        assert (d <= 2e-2 + 4 * f16_ulp(ref.astype(np.float32))).all(), f"step {i}: {d.max():.4g}"
+        g = got.cpu().numpy()
+        assert np.isfinite(g.astype(np.float32)).all()
+        _block_check(ref, g, f"decode step {i}")
     # the caches hold every row written so far and nothing past it
     n = prompt + steps
     assert not kc[:, :, n:].any() and not vc[:, :, n:].any()

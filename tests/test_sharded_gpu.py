@@ -46,6 +46,63 @@ def test_allgather_epilogue_writes_every_replica(cuda_pkg, oracle):
     assert cuda_pkg.device_status() == 0
 
 
+@pytest.mark.parametrize("M,K,n,col0", [(600, 512, 1376, 2752),   # GEMM, ragged last tile
+                                        (300, 320, 272, 16),       # GEMM, one partial tile
+                                        (5, 1024, 1376, 1376),     # GEMV + block copy
+                                        (16, 256, 96, 0)])
+def test_w8_allgather_epilogue_writes_every_replica(cuda_pkg, oracle, M, K, n, col0):
+    """hxb_matmul_w8a16_allgather with the replicas in local memory: every
+    replica gets the shard's columns bit for bit and nothing else (the
+    epilogue clips rows past M and columns past the shard)."""
+    import ctypes
+    lib = cuda_pkg._native.load()
+    rng = np.random.default_rng(M + n)
+    G, Nfull = 4, col0 + n + 32
+    a = rng.standard_normal((M, K)).astype(np.float16)
+    w = rng.integers(-127, 128, (K, n), dtype=np.int8)
+    s = rng.uniform(0.001, 0.02, n).astype(np.float16)
+    ad, wd, sd = (torch.from_numpy(x).to(DEV) for x in (a, w, s))
+    outs = [torch.full((M, Nfull), float("nan"), dtype=torch.float16, device=DEV)
+            for _ in range(G)]
+    reps = (ctypes.c_void_p * (G - 1))(*[o.data_ptr() + col0 * 2 for o in outs[1:]])
+    ws = cuda_pkg.w8a16_workspace(DEV)
+    for workspace in (None, ws):
+        for o in outs:
+            o.fill_(float("nan"))
+        cuda_pkg._native.check(lib.hxb_matmul_w8a16_allgather(
+            ad.data_ptr(), K, wd.data_ptr(), n, sd.data_ptr(), outs[0].data_ptr() + col0 * 2,
+            reps, G - 1, Nfull, M, n, K,
+            workspace.data_ptr() if workspace is not None else None,
+            workspace.numel() if workspace is not None else 0,
+            torch.cuda.current_stream().cuda_stream))
+        torch.cuda.synchronize()
+        first = outs[0].cpu().numpy()
+        baseline_check(oracle.matmul_w8a16_f32(a, w, s),
+                       first[:, col0:col0 + n].astype(np.float32), f"w8 allgather {M}x{K}x{n}")
+        for o in outs:
+            h = o.cpu().numpy()
+            assert np.array_equal(h[:, col0:col0 + n].view(np.int16),
+                                  first[:, col0:col0 + n].view(np.int16))
+            assert np.isnan(h[:, :col0].astype(np.float32)).all()
+            assert np.isnan(h[:, col0 + n:].astype(np.float32)).all()
+    assert cuda_pkg.device_status() == 0
+
+
+def test_attention_head_split_covers_every_head(cuda_pkg, oracle):
+    """Configuration 3 split by heads: each "rank" computes its contiguous
+    head group; the groups together give the unsplit result bit for bit."""
+    B, H, S, D = 2, 6, 256, 128
+    g = torch.Generator(device=DEV).manual_seed(9)
+    q, k, v = (torch.randn(B * H, S, D, device=DEV, generator=g).half() for _ in range(3))
+    whole = cuda_pkg.attention(q, k, v)
+    parts = []
+    for r in range(4):
+        h0, h1 = cuda_pkg.sharded.head_range(B * H, 4, r)
+        parts.append(cuda_pkg.attention(q[h0:h1], k[h0:h1], v[h0:h1]))
+    torch.cuda.synchronize()
+    assert torch.equal(torch.cat(parts), whole)
+
+
 def test_gather_column_blocks(cuda_pkg):
     lib = cuda_pkg._native.load()
     G, M, n = 4, 77, 40
