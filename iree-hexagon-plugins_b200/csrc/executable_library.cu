@@ -64,7 +64,8 @@ float f32_bits(uint32_t u) {
   return f;
 }
 
-// bindings: A, B, C [, C_init]; constants: M, N, K, flags [, block_n, group_m]
+// bindings: A, B, C [, C_init]; constants: M, N, K, flags
+// [, block_n, group_m, split_k]
 int dispatch_matmul_f16(const hxb_executable_environment_t* env,
                         const hxb_executable_dispatch_state_t* ds,
                         const hxb_executable_workgroup_state_t*) {
@@ -102,10 +103,11 @@ int dispatch_matmul_f16(const hxb_executable_environment_t* env,
   // a tile plan the compiler baked into the push constants (block_n,
   // group_m; 0 = plan at dispatch time)
   const uint32_t block_n = ds->constants[4], group_m = ds->constants[5];
+  const uint32_t split_k = ds->constants[6] ? ds->constants[6] : 1u;
   if (block_n != 0 && !init)
     return hxb_matmul_f16_tiled(A, (int64_t)K, B, ldb, tb, C, (int64_t)N, dt, (int64_t)M,
                                 (int64_t)N, (int64_t)K, (int)block_n, (int)group_m,
-                                env->stream);
+                                (int)split_k, env->stream);
   return hxb_matmul_f16(A, (int64_t)K, B, ldb, tb, init, C, (int64_t)N, dt, (int64_t)M,
                         (int64_t)N, (int64_t)K, nullptr, 0, env->stream);
 }

@@ -2,6 +2,7 @@
 #include <string.h>
 
 #include "gemm_sm100.cuh"
+#include "gemm_splitk_sm100.cuh"
 #include "gemm_w8_sm100.cuh"
 #include "gemv_w8_sk_sm100.cuh"
 #include "gemv_w8_sm100.cuh"
@@ -32,10 +33,62 @@ hxb_status_t launch_gemm(const DeviceInfo& dev, const CUtensorMap& tmA,
                     "gemm launch", tmA, tmB, args);
 }
 
+// One cluster of SPLIT CTAs per output tile (gemm_splitk_sm100.cuh),
+// launched with programmatic stream serialization like the persistent kernel.
+template <int BN, int STAGES, int BMODE, int OUT, int SPLIT>
+hxb_status_t launch_splitk(const DeviceInfo& dev, const CUtensorMap& tmA, const CUtensorMap& tmB,
+                           const GemmArgs& args, cudaStream_t stream) {
+  using L = SplitSmem<BN, STAGES>;
+  auto kernel = gemm_splitk_sm100_kernel<BN, STAGES, BMODE, OUT, SPLIT>;
+  static bool configured[64] = {};
+  if (!configured[dev.ordinal]) {
+    cudaError_t e =
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(gemm split-k)");
+    configured[dev.ordinal] = true;
+  }
+  const int tiles = args.tiles_m * args.tiles_n;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(SPLIT, tiles);
+  cfg.blockDim = dim3(GemmShape<BN, BMODE>::kThreads);
+  cfg.dynamicSmemBytes = L::kAlloc;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = SPLIT;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cuda_status(cudaLaunchKernelEx(&cfg, kernel, tmA, tmB, args), "gemm split-k launch");
+}
+
+template <int BMODE, int OUT, int SPLIT>
+hxb_status_t launch_split_bn(const GemmPlan& plan, const DeviceInfo& dev, const CUtensorMap& tmA,
+                             const CUtensorMap& tmB, const GemmArgs& args, cudaStream_t stream) {
+  switch (plan.block_n) {
+    case 256: return launch_splitk<256, 4, BMODE, OUT, SPLIT>(dev, tmA, tmB, args, stream);
+    case 128: return launch_splitk<128, 6, BMODE, OUT, SPLIT>(dev, tmA, tmB, args, stream);
+    case 64: return launch_splitk<64, 8, BMODE, OUT, SPLIT>(dev, tmA, tmB, args, stream);
+    default: break;
+  }
+  return fail(HXB_STATUS_UNSUPPORTED, "no split-k kernel for block_n=%d", plan.block_n);
+}
+
 template <int BMODE, int OUT>
 hxb_status_t launch_planned(const GemmPlan& plan, const DeviceInfo& dev,
                             const CUtensorMap& tmA, const CUtensorMap& tmB,
                             const GemmArgs& args, cudaStream_t stream) {
+  switch (plan.split) {
+    case 1: break;
+    case 2: return launch_split_bn<BMODE, OUT, 2>(plan, dev, tmA, tmB, args, stream);
+    case 4: return launch_split_bn<BMODE, OUT, 4>(plan, dev, tmA, tmB, args, stream);
+    case 8: return launch_split_bn<BMODE, OUT, 8>(plan, dev, tmA, tmB, args, stream);
+    default:
+      return fail(HXB_STATUS_UNSUPPORTED, "no kernel for split_k=%d", plan.split);
+  }
   // Stage counts fill ~192-208 KB of shared memory per CTA.
   switch (plan.block_n) {
     case 256: return launch_gemm<256, 4, BMODE, OUT>(dev, tmA, tmB, args, stream);
@@ -122,6 +175,14 @@ hxb_status_t gemm_f16_launch(const void* A, int64_t lda, const void* B, int64_t 
 
   const int bmode = transpose_b ? kBF16RowMajorNK : kBF16RowMajorKN;
   GemmPlan plan = forced ? *forced : plan_gemm((int)M, (int)N, (int)K, bmode, dev->num_sms);
+  // the all-gather epilogue lives in the persistent kernel only
+  if (nreplicas > 0) plan.split = 1;
+  if (plan.split > 1 && (plan.split > 8 || (plan.split & (plan.split - 1)) ||
+                         (K + kBK - 1) / kBK < plan.split))
+    return fail(HXB_STATUS_INVALID_ARGUMENT,
+                "matmul: split_k %d needs a power of two <= 8 and at least that many "
+                "64-deep K-blocks",
+                plan.split);
   const int64_t tiles_m = (M + kBM - 1) / kBM;
   if (plan.group_m < 1) plan.group_m = 1;
   if (plan.group_m > tiles_m) plan.group_m = (int)tiles_m;
@@ -717,20 +778,24 @@ extern "C" hxb_status_t hxb_gather_column_blocks_f16(const void* src, void* dst,
 extern "C" hxb_status_t hxb_matmul_f16_tiled(const void* A, int64_t lda, const void* B,
                                              int64_t ldb, int transpose_b, void* C, int64_t ldc,
                                              hxb_dtype_t c_dtype, int64_t M, int64_t N, int64_t K,
-                                             int block_n, int group_m, void* stream) {
+                                             int block_n, int group_m, int split_k,
+                                             void* stream) {
   using namespace hxb;
   if (block_n != 64 && block_n != 128 && block_n != 256)
     return fail(HXB_STATUS_INVALID_ARGUMENT, "matmul_f16_tiled: block_n must be 64, 128 or 256");
+  if (split_k != 1 && split_k != 2 && split_k != 4 && split_k != 8)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "matmul_f16_tiled: split_k must be 1, 2, 4 or 8");
   if (!aligned16(A) || !aligned16(B) || (lda * 2) % 16 || (ldb * 2) % 16)
     return fail(HXB_STATUS_INVALID_ARGUMENT,
                 "matmul_f16_tiled: A and B need 16-byte aligned rows (no re-pitching)");
-  const GemmPlan plan{block_n, group_m};
+  const GemmPlan plan{block_n, group_m, split_k};
   return gemm_f16_launch(A, lda, B, ldb, transpose_b, nullptr, C, ldc, c_dtype, M, N, K,
                          nullptr, 0, nullptr, 0, static_cast<cudaStream_t>(stream), &plan);
 }
 
 extern "C" hxb_status_t hxb_plan_matmul_f16(int64_t M, int64_t N, int64_t K, int transpose_b,
-                                            int num_sms, int* block_n, int* group_m) {
+                                            int num_sms, int* block_n, int* group_m,
+                                            int* split_k) {
   using namespace hxb;
   if (M < 1 || N < 1 || K < 1 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX ||
       num_sms < 1 || !block_n || !group_m)
@@ -739,5 +804,6 @@ extern "C" hxb_status_t hxb_plan_matmul_f16(int64_t M, int64_t N, int64_t K, int
                                transpose_b ? kBF16RowMajorNK : kBF16RowMajorKN, num_sms);
   *block_n = p.block_n;
   *group_m = p.group_m;
+  if (split_k) *split_k = p.split;
   return HXB_OK;
 }

@@ -14,13 +14,15 @@
 namespace hxb {
 
 struct GemmPlan {
-  int block_n;  // N extent of one output tile (M extent is always 128)
-  int group_m;  // tile-rows per raster group (L2 reuse)
+  int block_n;    // N extent of one output tile (M extent is always 128)
+  int group_m;    // tile-rows per raster group (L2 reuse)
+  int split = 1;  // 1: persistent kernel; 2, 4, 8: K split over a cluster
 };
 
 struct TunedGemm {
   int M, N, K, bmode;
   int block_n, group_m;
+  int split;  // 0 or 1: no split
 };
 
 // Filled by the offline tile sweep (tile_table.inc); may be empty.
@@ -36,32 +38,55 @@ inline int64_t mma_cycles(int bn) {
   return tensor > smem ? tensor : smem;
 }
 
+// Cycles one SM spends bringing one K-block of operands (A 16 KB + B bn *
+// 128 B) from L2 into shared memory: ~48 B/cycle per SM when every SM
+// streams at once.
+inline int64_t load_cycles(int bn) { return (16384 + (int64_t)bn * 128) / 48; }
+
+// Largest split-K a shape takes: every CTA keeps at least two K-blocks, and
+// the tiles x split CTAs fit one wave (clusters are co-scheduled; a GPC's
+// SMs are not always all usable by clusters, hence the 7/8).
+inline bool split_fits(int64_t tiles, int64_t kb, int split, int num_sms) {
+  return kb >= 2 * split && tiles * split <= (int64_t)num_sms * 7 / 8;
+}
+
 inline GemmPlan plan_gemm(int M, int N, int K, int bmode, int num_sms) {
   for (int i = 0; i < kNumTunedGemms; ++i) {
     const TunedGemm& t = kTunedGemms[i];
     if (t.M == M && t.N == N && t.K == K && t.bmode == bmode)
-      return GemmPlan{t.block_n, t.group_m};
+      return GemmPlan{t.block_n, t.group_m, t.split > 1 ? t.split : 1};
   }
   const int cands[3] = {256, 128, 64};
-  const int ncand = 3;
+  const int splits[4] = {1, 2, 4, 8};
   const int64_t tiles_m = (M + 127) / 128;
   const int64_t kb = (K + 63) / 64;
-  GemmPlan best{cands[0], 8};
+  GemmPlan best{cands[0], 8, 1};
   int64_t best_cost = -1, best_traffic = -1;
-  for (int i = 0; i < ncand; ++i) {
+  for (int i = 0; i < 3; ++i) {
     const int bn = cands[i];
     const int64_t tiles = tiles_m * ((N + bn - 1) / bn);
-    const int64_t waves = (tiles + num_sms - 1) / num_sms;
-    // Per tile: the K loop plus a fixed pipeline fill / drain.
-    const int64_t per_tile = kb * 4 * mma_cycles(bn) + 1500;
-    const int64_t cost = waves * per_tile;
-    // Operand bytes streamed from L2 per tile, summed over tiles.
-    const int64_t traffic = tiles * kb * (128 * 64 + (int64_t)bn * 64);
-    if (best_cost < 0 || cost < best_cost ||
-        (cost == best_cost && traffic < best_traffic)) {
-      best = GemmPlan{bn, 8};
-      best_cost = cost;
-      best_traffic = traffic;
+    const int64_t per_kb =
+        4 * mma_cycles(bn) > load_cycles(bn) ? 4 * mma_cycles(bn) : load_cycles(bn);
+    for (int j = 0; j < 4; ++j) {
+      const int split = splits[j];
+      if (split > 1 && !split_fits(tiles, kb, split, num_sms)) continue;
+      int64_t cost;
+      if (split == 1) {
+        const int64_t waves = (tiles + num_sms - 1) / num_sms;
+        // Per tile: the K loop plus a fixed pipeline fill / drain.
+        cost = waves * (kb * per_kb + 1500);
+      } else {
+        // one wave of clusters; each CTA runs its share of the K loop, then
+        // the partials are summed through distributed shared memory
+        cost = (kb + split - 1) / split * per_kb + 1500 + 300 + 4 * (int64_t)bn;
+      }
+      // Operand bytes streamed from L2 per tile, summed over tiles.
+      const int64_t traffic = tiles * kb * (128 * 64 + (int64_t)bn * 64);
+      if (best_cost < 0 || cost < best_cost || (cost == best_cost && traffic < best_traffic)) {
+        best = GemmPlan{bn, 8, split};
+        best_cost = cost;
+        best_traffic = traffic;
+      }
     }
   }
   if (best.group_m > tiles_m) best.group_m = (int)tiles_m;

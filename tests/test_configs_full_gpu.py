@@ -95,11 +95,11 @@ def test_cfg5b_sweep_shape_with_table_plan(cuda_pkg, oracle, M, N, K):
     checked to be the one the table holds, and up to 256 rows (all when
     M <= 512) are compared with the oracle."""
     lib = cuda_pkg._native.load()
-    bn, gm = ctypes.c_int(0), ctypes.c_int(0)
+    bn, gm, sk = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0)
     sms = torch.cuda.get_device_properties(0).multi_processor_count
     cuda_pkg._native.check(lib.hxb_plan_matmul_f16(M, N, K, 0, sms, ctypes.byref(bn),
-                                                   ctypes.byref(gm)))
-    assert bn.value in (64, 128, 256) and gm.value >= 1
+                                                   ctypes.byref(gm), ctypes.byref(sk)))
+    assert bn.value in (64, 128, 256) and gm.value >= 1 and sk.value in (1, 2, 4, 8)
     rng = np.random.default_rng(M + 3 * N + 7 * K)
     a = rng.uniform(-1, 1, (M, K)).astype(np.float16)
     b = rng.uniform(-1, 1, (K, N)).astype(np.float16)
@@ -108,5 +108,6 @@ def test_cfg5b_sweep_shape_with_table_plan(cuda_pkg, oracle, M, N, K):
     rows = np.arange(M) if M <= 512 else np.linspace(0, M - 1, 256).astype(np.int64)
     got = c.float().cpu().numpy()[rows]
     baseline_check(oracle.matmul_f32(a[rows], b), got,
-                   f"sweep {M}x{N}x{K} (block_n {bn.value}, group_m {gm.value})")
+                   f"sweep {M}x{N}x{K} (block_n {bn.value}, group_m {gm.value}, "
+                   f"split_k {sk.value})")
     assert cuda_pkg.device_status() == 0

@@ -146,3 +146,60 @@ def test_bad_arguments_raise(cuda_pkg):
                             4, 4, 8, None, 0, None)
     assert st == 1
     assert b"workspace" in lib.hxb_last_error_message()
+
+
+@pytest.mark.parametrize("M,N,K,bn,sk,tb,out", [
+    (1024, 1024, 1024, 256, 4, False, torch.float16),
+    (1024, 1024, 1024, 128, 2, False, torch.float32),
+    (512, 512, 8192, 128, 8, False, torch.float16),
+    (128, 8192, 2048, 256, 4, True, torch.float16),
+    (300, 200, 1000, 64, 4, False, torch.float32),  # ragged M, N and K
+    (129, 257, 520, 128, 8, True, torch.float16),   # K-blocks not divisible by the split
+    (64, 64, 128, 64, 2, False, torch.float16),
+])
+def test_split_k_cluster_kernel(cuda_pkg, oracle, M, N, K, bn, sk, tb, out):
+    """The split-K kernel (a cluster of split_k CTAs per tile, partials summed
+    through distributed shared memory) against the oracle, with canary bands
+    around the output."""
+    lib = cuda_pkg._native.load()
+    rng = np.random.default_rng(M + N + K + sk)
+    a = rng.uniform(-1, 1, (M, K)).astype(np.float16)
+    b = rng.uniform(-1, 1, (N, K) if tb else (K, N)).astype(np.float16)
+    c, buf, canary, guard = _guarded_empty((M, N), out)
+    ad, bd = torch.from_numpy(a).to(DEV), torch.from_numpy(b).to(DEV)
+    cuda_pkg._native.check(lib.hxb_matmul_f16_tiled(
+        ad.data_ptr(), K, bd.data_ptr(), K if tb else N, int(tb), c.data_ptr(), N,
+        0 if out == torch.float16 else 1, M, N, K, bn, 1, sk,
+        torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    _check_canary(buf, canary, guard)
+    baseline_check(oracle.matmul_f32(a, b, transpose_b=tb), c.float().cpu().numpy(),
+                   f"split-k {sk} bn {bn} {M}x{N}x{K}")
+    # deterministic: the cluster sums its partials in rank order
+    c2 = torch.empty_like(c)
+    cuda_pkg._native.check(lib.hxb_matmul_f16_tiled(
+        ad.data_ptr(), K, bd.data_ptr(), K if tb else N, int(tb), c2.data_ptr(), N,
+        0 if out == torch.float16 else 1, M, N, K, bn, 1, sk,
+        torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    assert torch.equal(c, c2)
+    assert cuda_pkg.device_status() == 0
+
+
+def test_split_k_with_init_through_the_planner(cuda_pkg, oracle):
+    """hxb_matmul_f16 with a C_init on a shape the planner splits."""
+    lib = cuda_pkg._native.load()
+    import ctypes
+    M, N, K = 256, 512, 4096
+    bn, gm, sk = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    cuda_pkg._native.check(lib.hxb_plan_matmul_f16(M, N, K, 0, 148, ctypes.byref(bn),
+                                                   ctypes.byref(gm), ctypes.byref(sk)))
+    rng = np.random.default_rng(31)
+    a = rng.uniform(-1, 1, (M, K)).astype(np.float16)
+    b = rng.uniform(-1, 1, (K, N)).astype(np.float16)
+    init = rng.standard_normal((M, N)).astype(np.float32)
+    c = cuda_pkg.matmul(torch.from_numpy(a).to(DEV), torch.from_numpy(b).to(DEV),
+                        out_dtype=torch.float32, init=torch.from_numpy(init).to(DEV))
+    torch.cuda.synchronize()
+    baseline_check(oracle.matmul_f32(a, b, init=init), c.cpu().numpy(),
+                   f"planned {M}x{N}x{K} split {sk.value}")
