@@ -148,9 +148,9 @@ const hxb_executable_library_header_t** hxb_executable_library_query(
  *             [2] C [M,N] (f16, or f32 with flag bit 1), optional [3] C_init
  *             (same type/shape as C, added to the product)
  *   constants: M, N, K, flags (bit 0: B transposed, bit 1: f32 output),
- *             optional block_n, group_m: a tile plan fixed at compile time
- *             (hxb_plan_matmul_f16; used when there is no C_init and no
- *             re-pitch; 0 = plan at dispatch time)
+ *             optional block_n, group_m, split_k: a tile plan fixed at
+ *             compile time (hxb_plan_matmul_f16; used when there is no C_init
+ *             and no re-pitch; block_n 0 = plan at dispatch time)
  * HXB_EXPORT_MATMUL_W8A16 "matmul_w8a16"
  *   bindings: [0] A f16 [M,K], [1] W int8 [K,N], [2] scale f16 [N],
  *             [3] C f16 [M,N], optional [4] residual f16 [M,N]
@@ -423,6 +423,56 @@ hxb_status_t hxb_hal_command_buffer_dispatch(hxb_hal_command_buffer_t* command_b
                                              uint32_t binding_count);
 hxb_status_t hxb_hal_command_buffer_end(hxb_hal_command_buffer_t* command_buffer);
 void hxb_hal_command_buffer_release(hxb_hal_command_buffer_t* command_buffer);
+
+/* ---- channels and collectives (channel.c:37-56, command_buffer.c:560-584
+ * return IREE_STATUS_UNIMPLEMENTED in the reference) ------------------------
+ * A channel is a group of `count` devices, one per process (or thread), that
+ * run collectives together; it is an NCCL communicator over NVLink /
+ * NVSwitch, loaded at run time (libnccl.so.2; the one the process already
+ * holds, e.g. PyTorch's, else the system's). Collectives are recorded into
+ * command buffers next to dispatches and captured into the same CUDA graph.
+ * Every rank must record and submit the same collectives in the same order. */
+typedef struct hxb_hal_channel_s hxb_hal_channel_t;
+
+#define HXB_HAL_CHANNEL_ID_BYTES 128
+
+/* A fresh channel id (rank 0 makes it and passes it to the other ranks out of
+ * band). Host only, no GPU needed. */
+hxb_status_t hxb_hal_channel_id_create(uint8_t* out_id);
+
+/* Joins the channel `id` as `rank` of `count` on `device`. Every rank must
+ * call it; the call returns once all have joined, or fails with
+ * HXB_STATUS_DEVICE_TIMEOUT after `timeout_ns` (the half-made communicator
+ * is aborted). */
+hxb_status_t hxb_hal_channel_create(hxb_hal_device_t* device, const uint8_t* id, int32_t rank,
+                                    int32_t count, uint64_t timeout_ns,
+                                    hxb_hal_channel_t** out_channel);
+int32_t hxb_hal_channel_rank(hxb_hal_channel_t* channel);
+int32_t hxb_hal_channel_count(hxb_hal_channel_t* channel);
+void hxb_hal_channel_release(hxb_hal_channel_t* channel);
+
+typedef enum hxb_hal_collective_op_e {
+  /* recv[r * n .. (r + 1) * n) = send of rank r (n = element_count) */
+  HXB_HAL_COLLECTIVE_ALL_GATHER = 0,
+  /* recv = sum over ranks of send (n elements) */
+  HXB_HAL_COLLECTIVE_ALL_REDUCE_SUM = 1,
+  /* recv (n elements) = rank r's block of the sum of the ranks' send
+   * (count * n elements) */
+  HXB_HAL_COLLECTIVE_REDUCE_SCATTER_SUM = 2,
+  /* recv = send of rank 0 (n elements) */
+  HXB_HAL_COLLECTIVE_BROADCAST = 3,
+} hxb_hal_collective_op_t;
+
+/* Records a collective of `element_count` elements of `element_type`
+ * (HXB_DTYPE_F16, HXB_DTYPE_F32 or HXB_DTYPE_I8) from `send` into `recv`
+ * (buffer ranges or binding-table slots, like dispatch bindings). */
+hxb_status_t hxb_hal_command_buffer_collective(hxb_hal_command_buffer_t* command_buffer,
+                                               hxb_hal_channel_t* channel,
+                                               hxb_hal_collective_op_t op,
+                                               hxb_dtype_t element_type,
+                                               hxb_hal_buffer_ref_t send,
+                                               hxb_hal_buffer_ref_t recv,
+                                               uint64_t element_count);
 
 /* Queue submission (device.c:1068-1112): after `wait_semaphore` reaches
  * `wait_value` (NULL: no wait), run `command_buffer` (NULL: none) with

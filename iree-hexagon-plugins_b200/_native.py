@@ -32,9 +32,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "hxb_matmul_f16_noalloc": (c_int, [c_vp, c_i64, c_vp, c_i64, c_int, c_vp, c_vp,
                                        c_i64, c_int, c_i64, c_i64, c_i64, c_vp]),
     "hxb_plan_matmul_f16": (c_int, [c_i64, c_i64, c_i64, c_int, c_int, ctypes.POINTER(c_int),
-                                    ctypes.POINTER(c_int)]),
+                                    ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
     "hxb_matmul_f16_tiled": (c_int, [c_vp, c_i64, c_vp, c_i64, c_int, c_vp, c_i64, c_int,
-                                     c_i64, c_i64, c_i64, c_int, c_int, c_vp]),
+                                     c_i64, c_i64, c_i64, c_int, c_int, c_int, c_vp]),
     "hxb_matmul_w8a16": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_i64,
                                  c_i64, c_i64, c_i64, c_vp]),
     "hxb_plan_matmul_w8a16": (c_int, [c_i64, c_i64, c_i64, c_int, ctypes.POINTER(c_int),
@@ -131,6 +131,14 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "hxb_module_dispatch_count": (ctypes.c_int32, [c_vp, ctypes.c_char_p]),
     "hxb_module_invoke": (c_int, [c_vp, ctypes.c_char_p, c_vp, ctypes.c_uint32, c_vp,
                                   ctypes.c_uint32, c_vp, c_u64, c_vp, c_u64]),
+    "hxb_hal_channel_id_create": (c_int, [c_vp]),
+    "hxb_hal_channel_create": (c_int, [c_vp, c_vp, ctypes.c_int32, ctypes.c_int32, c_u64,
+                                       ctypes.POINTER(c_vp)]),
+    "hxb_hal_channel_rank": (ctypes.c_int32, [c_vp]),
+    "hxb_hal_channel_count": (ctypes.c_int32, [c_vp]),
+    "hxb_hal_channel_release": (None, [c_vp]),
+    "hxb_hal_command_buffer_collective": (c_int, [c_vp, c_vp, c_int, c_int, "BufferRef",
+                                                  "BufferRef", c_u64]),
     "hxb_hal_device_queue_execute": (c_int, [c_vp, c_vp, c_u64, c_vp, c_vp, c_vp, c_u64]),
 }
 

@@ -18,10 +18,13 @@
 // device-side wait lasts longer than the device's queue wait bound. The
 // reference's queue is synchronous (plugins/runtime/hexagon/device.c:
 // 1068-1112).
+#include <dlfcn.h>
+#include <nccl.h>
 #include <stdlib.h>
 #include <string.h>
 
 #include <chrono>
+#include <mutex>
 #include <new>
 #include <string>
 #include <thread>
@@ -112,6 +115,14 @@ struct hxb_hal_semaphore_s {
   uint64_t* dev = nullptr;   // its device address
 };
 
+struct hxb_hal_channel_s {
+  hxb_hal_device_t* device = nullptr;
+  ncclComm_t comm = nullptr;
+  int32_t rank = 0;
+  int32_t count = 1;
+  uint64_t timeout_ns = 0;
+};
+
 namespace {
 
 struct Ref {
@@ -121,10 +132,17 @@ struct Ref {
   uint64_t length;
 };
 
+constexpr uint32_t kCollective = 0xFFFFFFFFu;  // Recorded::ordinal of a collective
+
 struct Recorded {
-  uint32_t ordinal;
+  uint32_t ordinal;  // export ordinal, or kCollective
   std::vector<uint32_t> constants;
   std::vector<Ref> refs;
+  // collectives: refs = {send, recv}
+  hxb_hal_channel_t* channel = nullptr;
+  int op = 0;
+  int dtype = 0;
+  uint64_t count = 0;
 };
 
 enum CbState { kCbInitial, kCbRecording, kCbExecutable };
@@ -143,6 +161,75 @@ struct hxb_hal_command_buffer_s {
 };
 
 namespace {
+
+// ------------------------------------------------------------------ NCCL
+// Loaded at run time so that the library needs NCCL only when a channel is
+// made: the libnccl.so.2 already in the process (PyTorch's, say) or the
+// system's.
+struct Nccl {
+  bool ok = false;
+  ncclResult_t (*get_unique_id)(ncclUniqueId*);
+  ncclResult_t (*comm_init_rank_config)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*);
+  ncclResult_t (*comm_get_async_error)(ncclComm_t, ncclResult_t*);
+  ncclResult_t (*comm_finalize)(ncclComm_t);
+  ncclResult_t (*comm_destroy)(ncclComm_t);
+  ncclResult_t (*comm_abort)(ncclComm_t);
+  ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t,
+                             cudaStream_t);
+  ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t,
+                             ncclComm_t, cudaStream_t);
+  ncclResult_t (*reduce_scatter)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t,
+                                 ncclComm_t, cudaStream_t);
+  ncclResult_t (*broadcast)(const void*, void*, size_t, ncclDataType_t, int, ncclComm_t,
+                            cudaStream_t);
+  const char* (*error_string)(ncclResult_t);
+};
+
+const Nccl& nccl() {
+  static Nccl n;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return;
+    bool all = true;
+    auto sym = [&](auto& fn, const char* name) {
+      *reinterpret_cast<void**>(&fn) = dlsym(h, name);
+      all = all && fn != nullptr;
+    };
+    sym(n.get_unique_id, "ncclGetUniqueId");
+    sym(n.comm_init_rank_config, "ncclCommInitRankConfig");
+    sym(n.comm_get_async_error, "ncclCommGetAsyncError");
+    sym(n.comm_finalize, "ncclCommFinalize");
+    sym(n.comm_destroy, "ncclCommDestroy");
+    sym(n.comm_abort, "ncclCommAbort");
+    sym(n.all_gather, "ncclAllGather");
+    sym(n.all_reduce, "ncclAllReduce");
+    sym(n.reduce_scatter, "ncclReduceScatter");
+    sym(n.broadcast, "ncclBroadcast");
+    sym(n.error_string, "ncclGetErrorString");
+    n.ok = all;
+  });
+  return n;
+}
+
+// Polls a non-blocking communicator until its pending operation completes,
+// for at most timeout_ns.
+hxb_status_t nccl_settle(ncclComm_t comm, ncclResult_t r, uint64_t timeout_ns, const char* what) {
+  const Nccl& n = nccl();
+  const auto t0 = std::chrono::steady_clock::now();
+  while (r == ncclInProgress) {
+    if ((uint64_t)std::chrono::duration_cast<std::chrono::nanoseconds>(
+            std::chrono::steady_clock::now() - t0)
+            .count() > timeout_ns)
+      return fail(HXB_STATUS_DEVICE_TIMEOUT, "%s: not complete after %llu ns", what,
+                  (unsigned long long)timeout_ns);
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+    if (n.comm_get_async_error(comm, &r) != ncclSuccess) break;
+  }
+  if (r != ncclSuccess)
+    return fail(HXB_STATUS_CUDA_ERROR, "%s: %s", what, n.error_string(r));
+  return HXB_OK;
+}
 
 // ------------------------------------------------------- queue wait/signal
 // One thread polls the host-mapped semaphore word until it reaches `value`,
@@ -237,6 +324,34 @@ hxb_status_t resolve(const hxb_hal_command_buffer_t* cb,
   return HXB_OK;
 }
 
+ncclDataType_t nccl_type(int dtype) {
+  return dtype == HXB_DTYPE_F16 ? ncclFloat16 : dtype == HXB_DTYPE_F32 ? ncclFloat32 : ncclInt8;
+}
+
+// Issues one recorded collective on `stream` (a capturing stream: NCCL's
+// kernels become nodes of the command buffer's graph).
+hxb_status_t run_collective(const Recorded& r, void* const* p, cudaStream_t stream) {
+  const Nccl& n = nccl();
+  hxb_hal_channel_t* ch = r.channel;
+  const ncclDataType_t t = nccl_type(r.dtype);
+  ncclResult_t res = ncclSuccess;
+  switch (r.op) {
+    case HXB_HAL_COLLECTIVE_ALL_GATHER:
+      res = n.all_gather(p[0], p[1], r.count, t, ch->comm, stream);
+      break;
+    case HXB_HAL_COLLECTIVE_ALL_REDUCE_SUM:
+      res = n.all_reduce(p[0], p[1], r.count, t, ncclSum, ch->comm, stream);
+      break;
+    case HXB_HAL_COLLECTIVE_REDUCE_SCATTER_SUM:
+      res = n.reduce_scatter(p[0], p[1], r.count, t, ncclSum, ch->comm, stream);
+      break;
+    default:
+      res = n.broadcast(p[0], p[1], r.count, t, 0, ch->comm, stream);
+      break;
+  }
+  return nccl_settle(ch->comm, res, ch->timeout_ns, "collective");
+}
+
 // Runs every recorded dispatch function once on a capturing stream and
 // returns the graph (argument errors of any dispatch come back here).
 hxb_status_t capture(hxb_hal_command_buffer_t* cb, const std::vector<void*>& ptrs,
@@ -255,6 +370,11 @@ hxb_status_t capture(hxb_hal_command_buffer_t* cb, const std::vector<void*>& ptr
     size_t next = 0;
     for (size_t i = 0; i < cb->commands.size() && s == HXB_OK; ++i) {
       const Recorded& r = cb->commands[i];
+      if (r.ordinal == kCollective) {
+        s = run_collective(r, ptrs.data() + next, cap);
+        next += r.refs.size();
+        continue;
+      }
       hxb_executable_dispatch_state_t ds{};
       ds.workgroup_size_x = ds.workgroup_size_y = 1;
       ds.workgroup_size_z = 1;
@@ -861,6 +981,127 @@ hxb_status_t hxb_hal_device_queue_execute(hxb_hal_device_t* d, hxb_hal_semaphore
         (unsigned long long)signal_value, d->lost_dev);
     if ((s = cuda_status(cudaGetLastError(), "queue_execute: signal launch")) != HXB_OK) return s;
   }
+  return HXB_OK;
+}
+
+// ------------------------------------------------------------- channels
+hxb_status_t hxb_hal_channel_id_create(uint8_t* out_id) {
+  if (!out_id) return fail(HXB_STATUS_INVALID_ARGUMENT, "channel_id_create: null id");
+  const Nccl& n = nccl();
+  if (!n.ok) return fail(HXB_STATUS_UNAVAILABLE, "channel_id_create: libnccl.so.2 not found");
+  ncclUniqueId id;
+  const ncclResult_t r = n.get_unique_id(&id);
+  if (r != ncclSuccess)
+    return fail(HXB_STATUS_CUDA_ERROR, "ncclGetUniqueId: %s", n.error_string(r));
+  static_assert(sizeof(id) == HXB_HAL_CHANNEL_ID_BYTES, "NCCL unique id size");
+  memcpy(out_id, &id, sizeof(id));
+  return HXB_OK;
+}
+
+hxb_status_t hxb_hal_channel_create(hxb_hal_device_t* d, const uint8_t* id, int32_t rank,
+                                    int32_t count, uint64_t timeout_ns,
+                                    hxb_hal_channel_t** out) {
+  if (!d || !id || !out || count < 1 || rank < 0 || rank >= count || timeout_ns == 0)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "channel_create: bad arguments");
+  *out = nullptr;
+  const Nccl& n = nccl();
+  if (!n.ok) return fail(HXB_STATUS_UNAVAILABLE, "channel_create: libnccl.so.2 not found");
+  hxb_status_t s = use_device(d);
+  if (s != HXB_OK) return s;
+  hxb_hal_channel_t* ch = host_new<hxb_hal_channel_s>(d->allocator);
+  if (!ch) return fail(HXB_STATUS_RESOURCE_EXHAUSTED, "channel_create: out of host memory");
+  ch->device = d;
+  ch->rank = rank;
+  ch->count = count;
+  ch->timeout_ns = timeout_ns;
+  ncclUniqueId uid;
+  memcpy(&uid, id, sizeof(uid));
+  // non-blocking initialisation, so a rank that never joins ends in a
+  // timeout instead of a hang
+  ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+  cfg.blocking = 0;
+  ncclResult_t r = n.comm_init_rank_config(&ch->comm, count, uid, rank, &cfg);
+  if (r != ncclSuccess && r != ncclInProgress) {
+    host_delete(d->allocator, ch);
+    return fail(HXB_STATUS_CUDA_ERROR, "ncclCommInitRankConfig: %s", n.error_string(r));
+  }
+  s = nccl_settle(ch->comm, r, timeout_ns, "channel_create");
+  if (s != HXB_OK) {
+    n.comm_abort(ch->comm);
+    host_delete(d->allocator, ch);
+    return s;
+  }
+  *out = ch;
+  return HXB_OK;
+}
+
+int32_t hxb_hal_channel_rank(hxb_hal_channel_t* ch) { return ch ? ch->rank : -1; }
+int32_t hxb_hal_channel_count(hxb_hal_channel_t* ch) { return ch ? ch->count : 0; }
+
+void hxb_hal_channel_release(hxb_hal_channel_t* ch) {
+  if (!ch) return;
+  hxb_hal_device_t* d = ch->device;
+  const Nccl& n = nccl();
+  if (use_device(d) == HXB_OK) {
+    cudaStreamSynchronize(d->queue);  // bounded, see hxb_hal_device_release
+    ncclResult_t r = n.comm_finalize(ch->comm);
+    if (nccl_settle(ch->comm, r, ch->timeout_ns, "channel_release") == HXB_OK)
+      n.comm_destroy(ch->comm);
+    else
+      n.comm_abort(ch->comm);
+  }
+  host_delete(d->allocator, ch);
+}
+
+hxb_status_t hxb_hal_command_buffer_collective(hxb_hal_command_buffer_t* cb,
+                                               hxb_hal_channel_t* ch,
+                                               hxb_hal_collective_op_t op,
+                                               hxb_dtype_t element_type,
+                                               hxb_hal_buffer_ref_t send,
+                                               hxb_hal_buffer_ref_t recv,
+                                               uint64_t element_count) {
+  if (!cb || cb->state != kCbRecording)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "command_buffer_collective: not recording");
+  if (!ch || ch->device != cb->device)
+    return fail(HXB_STATUS_INVALID_ARGUMENT,
+                "command_buffer_collective: the channel belongs to another device");
+  if (op < HXB_HAL_COLLECTIVE_ALL_GATHER || op > HXB_HAL_COLLECTIVE_BROADCAST ||
+      (element_type != HXB_DTYPE_F16 && element_type != HXB_DTYPE_F32 &&
+       element_type != HXB_DTYPE_I8) ||
+      element_count == 0)
+    return fail(HXB_STATUS_INVALID_ARGUMENT, "command_buffer_collective: bad op, type or count");
+  const uint64_t esz = element_type == HXB_DTYPE_F32 ? 4 : element_type == HXB_DTYPE_F16 ? 2 : 1;
+  const uint64_t n = element_count * esz, g = n * (uint64_t)ch->count;
+  const uint64_t send_need = op == HXB_HAL_COLLECTIVE_REDUCE_SCATTER_SUM ? g : n;
+  const uint64_t recv_need = op == HXB_HAL_COLLECTIVE_ALL_GATHER ? g : n;
+  if (send.length < send_need || recv.length < recv_need)
+    return fail(HXB_STATUS_INVALID_ARGUMENT,
+                "command_buffer_collective: send needs %llu bytes and recv %llu, got %llu / %llu",
+                (unsigned long long)send_need, (unsigned long long)recv_need,
+                (unsigned long long)send.length, (unsigned long long)recv.length);
+  Recorded r;
+  r.ordinal = kCollective;
+  r.channel = ch;
+  r.op = op;
+  r.dtype = element_type;
+  r.count = element_count;
+  for (const hxb_hal_buffer_ref_t* b : {&send, &recv}) {
+    if (b->buffer) {
+      if (b->buffer->device != cb->device || b->offset > b->buffer->bytes ||
+          b->length > b->buffer->bytes - b->offset)
+        return fail(HXB_STATUS_INVALID_ARGUMENT,
+                    "command_buffer_collective: a binding is not a range of a buffer of this "
+                    "device");
+    } else if (b->buffer_slot >= cb->binding_capacity) {
+      return fail(HXB_STATUS_INVALID_ARGUMENT,
+                  "command_buffer_collective: table slot %u beyond the binding capacity %u",
+                  b->buffer_slot, cb->binding_capacity);
+    } else {
+      cb->indirect = true;
+    }
+    r.refs.push_back(Ref{b->buffer, b->buffer_slot, b->offset, b->length});
+  }
+  cb->commands.push_back(std::move(r));
   return HXB_OK;
 }
 

@@ -16,6 +16,9 @@ import struct
 from . import _native
 from ._native import check
 
+COLLECTIVES = {"all_gather": 0, "all_reduce_sum": 1, "reduce_scatter_sum": 2, "broadcast": 3}
+DTYPES = {"f16": 0, "f32": 1, "i8": 2}
+
 EXPORTS = {"matmul_f16": 0, "matmul_w8a16": 1, "attention_f16": 2, "decoder_block_w8a16": 3,
            "attention_gqa_f16": 4}
 
@@ -277,10 +280,54 @@ class CommandBuffer:
         check(self._lib.hxb_hal_command_buffer_dispatch(self.handle, ordinal, c, len(constants),
                                                         arr, len(refs)))
 
+    def collective(self, channel: "Channel", op: str, dtype: str, send, recv,
+                   count: int) -> None:
+        """Records a collective (COLLECTIVES) of `count` elements from `send`
+        into `recv` (Buffers or BufferRefs) over `channel`."""
+        refs = [b.ref() if isinstance(b, Buffer) else b for b in (send, recv)]
+        check(self._lib.hxb_hal_command_buffer_collective(
+            self.handle, channel.handle, COLLECTIVES[op], DTYPES[dtype], refs[0], refs[1],
+            count))
+
     def end(self) -> None:
         check(self._lib.hxb_hal_command_buffer_end(self.handle))
 
     def close(self) -> None:
         if self.handle:
             self._lib.hxb_hal_command_buffer_release(self.handle)
+            self.handle = None
+
+
+def channel_id() -> bytes:
+    """A fresh channel id (rank 0 makes it and shares it with the others)."""
+    lib = _native.load()
+    buf = ctypes.create_string_buffer(128)
+    check(lib.hxb_hal_channel_id_create(buf))
+    return buf.raw
+
+
+class Channel:
+    """`rank` of `count` devices running collectives together (an NCCL
+    communicator under hxb_hal_channel_create)."""
+
+    def __init__(self, device: Device, channel_id: bytes, rank: int, count: int,
+                 timeout_s: float = 60.0):
+        self._lib = device._lib
+        idb = ctypes.create_string_buffer(bytes(channel_id), 128)
+        h = ctypes.c_void_p()
+        check(self._lib.hxb_hal_channel_create(device.handle, idb, rank, count,
+                                               int(timeout_s * 1e9), ctypes.byref(h)))
+        self.handle = h
+
+    @property
+    def rank(self) -> int:
+        return self._lib.hxb_hal_channel_rank(self.handle)
+
+    @property
+    def count(self) -> int:
+        return self._lib.hxb_hal_channel_count(self.handle)
+
+    def close(self) -> None:
+        if self.handle:
+            self._lib.hxb_hal_channel_release(self.handle)
             self.handle = None

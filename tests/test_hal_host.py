@@ -196,3 +196,16 @@ def test_host_allocator_owns_host_objects(pkg):
     assert len(live) == 1 and log[0][0] == "calloc"
     lib.hxb_hal_driver_release(out)
     assert not live and log[-1][0] == "free"
+
+
+def test_channel_id_and_argument_checks(pkg):
+    """Channels (the HAL collectives the reference leaves unimplemented,
+    plugins/runtime/hexagon/channel.c:37-56): an id can be made without a GPU;
+    channel creation checks its arguments before touching a device."""
+    ida, idb = pkg.hal.channel_id(), pkg.hal.channel_id()
+    assert len(ida) == 128 and ida != idb
+    lib = pkg._native.load()
+    out = ctypes.c_void_p()
+    buf = ctypes.create_string_buffer(ida, 128)
+    assert lib.hxb_hal_channel_create(None, buf, 0, 2, 10**9, ctypes.byref(out)) == 1
+    assert lib.hxb_hal_channel_rank(None) == -1 and lib.hxb_hal_channel_count(None) == 0

@@ -136,3 +136,17 @@ def test_sharded_two_ranks_fused_matches_nccl_and_oracle():
     r = subprocess.run(cmd, env=env, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert "sharded ok" in r.stdout
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs on one box")
+def test_hal_channel_two_ranks():
+    """HAL collectives (the reference's channel.c returns UNIMPLEMENTED): a
+    command buffer with a matmul dispatch and NCCL all-gather / all-reduce
+    collectives, recorded once and submitted twice on each of 2 ranks."""
+    env = dict(os.environ, MASTER_ADDR="127.0.0.1", NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run",
+           "--nnodes=1", "--nproc-per-node=2", "--master-addr", "127.0.0.1",
+           "--master-port", "29533", str(REPO / "tests" / "channel_worker.py")]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert "channel ok" in r.stdout
