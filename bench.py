@@ -460,6 +460,22 @@ def _spec_f16_gemm(torch, pkg, dev, rank, world):
             "compute": lambda i, x, y: pkg.matmul(x, b[0], out=y)}
 
 
+def _spec_f16_gemm_shape(M_, N_, K_):
+    """One configuration-5b sweep shape, inputs rotating over sets larger
+    than L2 (the shapes where the split-K cluster kernel is planned)."""
+    def make(torch, pkg, dev, rank, world):
+        per_set = 2 * (M_ * K_ + K_ * N_ + M_ * N_)
+        sets = max(2, min(64, -(-260_000_000 // per_set)))
+        g = torch.Generator(device=dev).manual_seed(rank)
+        a = [(torch.rand(M_, K_, device=dev, generator=g) * 2 - 1).half() for _ in range(sets)]
+        b = [(torch.rand(K_, N_, device=dev, generator=g) * 2 - 1).half() for _ in range(sets)]
+        c = [torch.empty(M_, N_, dtype=torch.float16, device=dev) for _ in range(sets)]
+        return {"step": lambda i: pkg.matmul(a[i % sets], b[i % sets], out=c[i % sets]),
+                "in": a[0], "out": c[0], "sets": sets,
+                "compute": lambda i, x, y: pkg.matmul(x, b[0], out=y)}
+    return make
+
+
 def _spec_gemv(m):
     def make(torch, pkg, dev, rank, world):
         sets = 4  # 4 x 45 MB of weights
@@ -580,6 +596,10 @@ SPECS = {
         "profile": "f16_gemm_1024x1024x1024.txt",
         "config": {"workload": "f16_gemm_1024x1024x1024", "cfg": 1,
                    "inputs": "A, B ~ U[-1, 1] f16, f16 out"}},
+    "f16_gemm_512x512x8192": {
+        "make": _spec_f16_gemm_shape(512, 512, 8192), "flop": 2.0 * 512 * 512 * 8192,
+        "bound": "tensor", "kernel": "gemm_splitk_sm100_kernel", "dtype": "f16->f32",
+        "config": {"workload": "f16_gemm_512x512x8192", "cfg": "5b"}},
     "gemv_w8_m1": {
         "make": _spec_gemv(1), "bytes": 4096 * 11008 + 2 * 4096 + 2 * 11008 + 2 * 11008,
         "flop": 2.0 * 4096 * 11008, "bound": "hbm", "kernel": "gemv_w8_sk_kernel",

@@ -244,6 +244,24 @@ __global__ void __launch_bounds__(GemmShape<BN, BMODE>::kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------ TMA producer
     if (lane == 0) {
+      // The operands of this CTA's first tile's first K-blocks are requested
+      // into L2 while the previous kernel of the stream may still run; the
+      // loads below, issued after the wait, then hit L2.
+      if ((int)blockIdx.x < num_tiles) {
+        int tm0, tn0;
+        tile_coords(blockIdx.x, args, tm0, tn0);
+        const int pre = num_kb < STAGES ? num_kb : STAGES;
+        for (int kb = 0; kb < pre; ++kb) {
+          tma_prefetch_l2_2d(&tmA, kb * kBK, tm0 * kBM);
+          if constexpr (BMODE == kBF16RowMajorKN) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_prefetch_l2_2d(&tmB, tn0 * BN + 64 * j, kb * kBK);
+          } else {
+            tma_prefetch_l2_2d(&tmB, kb * kBK, tn0 * BN);
+          }
+        }
+      }
       pdl_wait();
       int stage = 0;
       uint32_t phase = 0;

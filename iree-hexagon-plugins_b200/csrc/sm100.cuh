@@ -160,6 +160,17 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map,
       : "memory");
 }
 
+// Asks the TMA unit to bring a 2-D box of `map` into L2 (no shared-memory
+// destination, no completion signal). x is the innermost coordinate. L2 is
+// the device's point of coherence, so a prefetch issued before
+// griddepcontrol.wait cannot make a later load see data older than the
+// previous kernel's writes: those writes update the L2 line.
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(map),
+               "r"(x), "r"(y)
+               : "memory");
+}
+
 // --------------------------------------------------------------- tcgen05
 // 2-D TMA store of a shared-memory box to global memory (bulk group of the
 // issuing thread). x * element size must be a multiple of 16 bytes and both
