@@ -992,7 +992,6 @@ def main():
                 configs["w8_gemm_nsplit"] = measure_w8_nsplit(ctx, M, cpu=False)
                 configs["w8_gemv_nsplit_m1"] = measure_w8_nsplit(ctx, 1, cpu=False)
                 line["configs"] = configs
-                line["gpu_launches"] += sum(c["gpu_launches"] for c in configs.values())
         elif args.workload == "sharded_gemm":
             line = dict(measure_sharded(ctx, cpu), metric=METRIC, n_gpus=ctx.world)
         elif args.workload in ("w8_nsplit", "gemv_nsplit"):

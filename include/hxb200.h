@@ -341,6 +341,19 @@ hxb_status_t hxb_ipc_get_handle(const void* ptr, void* handle, int64_t* offset);
 hxb_status_t hxb_ipc_open(const void* handle, int64_t offset, void** ptr);
 hxb_status_t hxb_ipc_close(void* ptr, int64_t offset);
 
+/* Stream-ordered barrier of `world` ranks (one GPU each) through peer
+ * memory, for ordering the fused all-gather steps without a collective
+ * library call: flags[i] is rank i's array of `world` uint32 flags (this
+ * rank's own array at index `rank`, the others mapped with hxb_ipc_open;
+ * zero-initialised, 4-byte aligned). Rank r stores `epoch` into every peer's
+ * flag r (release, system scope) and waits until every peer's flag in its own
+ * array reached `epoch` (acquire). Every rank passes the same increasing
+ * epoch (> 0) to its k-th barrier. The wait is bounded by the library's
+ * wait limit; a wait that runs out sets HXB_DEVICE_STATUS_TIMEOUT. No
+ * counterpart in the reference (no collectives, channel.c:55-56). */
+hxb_status_t hxb_peer_barrier(void* const* flags, int world, int rank, uint32_t epoch,
+                              void* stream);
+
 /* dst[m, g*n + j] = src[g, m, j]: the [G, M, n] result of an NCCL all-gather
  * of column shards laid out as the [M, G*n] matrix (row pitch ldd).
  * n % 8 == 0, 16-byte aligned buffers. */

@@ -61,6 +61,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                          c_i64, c_i64, c_i64, c_i64, c_vp]),
     "hxb_matmul_w8a16_allgather": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_int,
                                            c_i64, c_i64, c_i64, c_i64, c_vp, c_size, c_vp]),
+    "hxb_peer_barrier": (c_int, [c_vp, c_int, c_int, ctypes.c_uint32, c_vp]),
     "hxb_gather_column_blocks_f16": (c_int, [c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp]),
     "hxb_ipc_get_handle": (c_int, [c_vp, c_vp, ctypes.POINTER(c_i64)]),
     "hxb_ipc_open": (c_int, [c_vp, c_i64, ctypes.POINTER(c_vp)]),

@@ -5,6 +5,7 @@
 #include <mutex>
 
 #include "runtime_common.h"
+#include "sm100.cuh"
 
 // One status word per device (a file-scope device variable exists once on
 // every device that loads this library). Kernels OR error bits into it, e.g.
@@ -211,4 +212,59 @@ extern "C" hxb_status_t hxb_ipc_close(void* ptr, int64_t offset) {
   if (!ptr || offset < 0) return hxb::fail(HXB_STATUS_INVALID_ARGUMENT, "ipc_close: bad argument");
   return hxb::cuda_status(cudaIpcCloseMemHandle(static_cast<uint8_t*>(ptr) - offset),
                           "cudaIpcCloseMemHandle");
+}
+
+// ------------------------------------------------------- peer barrier
+// One thread per peer: it stores `epoch` into the peer's flag array at this
+// rank's slot (release, system scope: everything this rank's stream did
+// before -- the fused epilogue's peer stores included -- is visible to a peer
+// that acquires the flag), then waits, bounded, until the peer's arrival for
+// this epoch lands in this rank's own flag array.
+namespace {
+constexpr int kMaxPeers = 8;
+struct PeerFlags {
+  unsigned int* p[kMaxPeers];  // each rank's flag array, this rank's own included
+};
+
+__global__ void peer_barrier_kernel(PeerFlags flags, int world, int rank, unsigned int epoch,
+                                    unsigned long long limit_ns, int* status) {
+  hxb::pdl_wait();
+  const int t = threadIdx.x;
+  if (t >= world || t == rank) return;
+  __threadfence_system();
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flags.p[t] + rank), "r"(epoch)
+               : "memory");
+  const unsigned int* mine = flags.p[rank] + t;
+  const unsigned long long t0 = hxb::globaltimer_ns();
+  while (true) {
+    unsigned int v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+    if ((int)(v - epoch) >= 0) break;
+    if (hxb::globaltimer_ns() - t0 > limit_ns) {
+      atomicOr(status, hxb::kStatusTimeout);
+      break;
+    }
+    __nanosleep(100);
+  }
+}
+}  // namespace
+
+extern "C" hxb_status_t hxb_peer_barrier(void* const* flags, int world, int rank,
+                                         uint32_t epoch, void* stream) {
+  if (!flags || world < 1 || world > kMaxPeers || rank < 0 || rank >= world || epoch == 0)
+    return hxb::fail(HXB_STATUS_INVALID_ARGUMENT,
+                     "peer_barrier: 1..%d ranks, a rank among them and an epoch > 0", kMaxPeers);
+  PeerFlags f{};
+  for (int i = 0; i < world; ++i) {
+    if (!flags[i] || (reinterpret_cast<uintptr_t>(flags[i]) & 3u))
+      return hxb::fail(HXB_STATUS_INVALID_ARGUMENT, "peer_barrier: flag array %d", i);
+    f.p[i] = static_cast<unsigned int*>(flags[i]);
+  }
+  if (world == 1) return HXB_OK;
+  hxb::DeviceInfo* dev = nullptr;
+  hxb_status_t s = hxb::current_device(&dev);
+  if (s != HXB_OK) return s;
+  return hxb::launch_pdl(peer_barrier_kernel, dim3(1), dim3(32), 0,
+                         static_cast<cudaStream_t>(stream), "peer barrier launch", f, world, rank,
+                         (unsigned int)epoch, hxb::kWaitLimitNs, dev->status_word);
 }

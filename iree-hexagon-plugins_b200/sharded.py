@@ -96,35 +96,53 @@ class ShardedMatmul:
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         self.cols = [shard_columns(N, self.world, r, self.ALIGN) for r in range(self.world)]
         self.begin, self.end = self.cols[self.rank]
-        self.out = torch.empty((M, N), dtype=torch.float16, device=self.device)
+        # the full output, then this rank's flag array of the peer barrier (one
+        # uint32 per rank) in the same allocation, so one IPC handle maps both
+        self._flag_off = (M * N * 2 + 255) // 256 * 256
+        self._buf = torch.zeros(self._flag_off + 256, dtype=torch.uint8, device=self.device)
+        self.out = self._buf[:M * N * 2].view(torch.float16).view(M, N)
+        self.flags = self._buf[self._flag_off:].view(torch.int32)
         self._peer_storages: list = []  # (mapped pointer, offset) of opened peers
         self.peer_ptrs: list[int] = []
+        self.flag_ptrs: list[int] = [self.flags.data_ptr()] * self.world
+        self._epoch = 0
         if self.world > 1:
             self._open_peers()
-        self._flag = torch.zeros(1, dtype=torch.float32, device=self.device)
 
     def _open_peers(self) -> None:
         # CUDA IPC: (handle, offset) of this rank's output, exchanged once over
         # the process group; each peer buffer is mapped into THIS rank's
         # device context (hxb_ipc_open), where the GEMM epilogue runs
         lib = _native.load()
-        handle = ctypes.create_string_buffer(64)
-        offset = ctypes.c_int64(0)
-        check(lib.hxb_ipc_get_handle(self.out.data_ptr(), handle, ctypes.byref(offset)))
-        payload = (bytes(handle.raw), offset.value)
-        ptrs = []
-        for h, off in exchange_peer_payloads(payload, group=self.group):
+
+        def handle_of(t):
+            handle = ctypes.create_string_buffer(64)
+            offset = ctypes.c_int64(0)
+            check(lib.hxb_ipc_get_handle(t.data_ptr(), handle, ctypes.byref(offset)))
+            return bytes(handle.raw), offset.value
+
+        def open_handle(h, off):
             p = ctypes.c_void_p(0)
             check(lib.hxb_ipc_open(h, off, ctypes.byref(p)))
             self._peer_storages.append((p.value, off))
-            ptrs.append(p.value)
+            return p.value
+        payload = (self.rank, handle_of(self._buf))
+        ptrs = []
+        for peer, buf_h in exchange_peer_payloads(payload, group=self.group):
+            base = open_handle(*buf_h)
+            ptrs.append(base)
+            self.flag_ptrs[peer] = base + self._flag_off
         self.peer_ptrs = ptrs
 
     def _sync(self) -> None:
-        # stream-ordered: every rank's GEMM (and its remote stores) is done
-        # before any rank continues past this point on its stream
+        # stream-ordered barrier through peer memory (hxb_peer_barrier): every
+        # rank's earlier work on its stream -- the GEMM and its remote stores
+        # -- is done and visible before any rank continues on its stream
         if self.world > 1:
-            self.dist.all_reduce(self._flag, group=self.group)
+            self._epoch += 1
+            arr = (ctypes.c_void_p * self.world)(*self.flag_ptrs)
+            check(_native.load().hxb_peer_barrier(arr, self.world, self.rank, self._epoch,
+                                                 _stream_ptr(self.out)))
 
     def fused(self, a: torch.Tensor, b_shard: torch.Tensor) -> torch.Tensor:
         """GEMM with the all-gather in its epilogue; returns the full C."""
