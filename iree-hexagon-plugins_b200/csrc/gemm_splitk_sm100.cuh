@@ -131,17 +131,8 @@ __global__ void __launch_bounds__(GemmShape<BN, BMODE>::kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------ TMA producer
     if (lane == 0) {
-      // as in the persistent kernel: this CTA's first K-blocks into L2 while
-      // the previous kernel may still run
-      for (int kb = kb0; kb < kb1 && kb < kb0 + STAGES; ++kb) {
-        tma_prefetch_l2_2d(&tmA, kb * kBK, tm * kBM);
-        if constexpr (BMODE == kBF16RowMajorKN) {
-#pragma unroll
-          for (int j = 0; j < BN / 64; ++j) tma_prefetch_l2_2d(&tmB, tn * BN + 64 * j, kb * kBK);
-        } else {
-          tma_prefetch_l2_2d(&tmB, kb * kBK, tn * BN);
-        }
-      }
+      // (no L2 prefetch before the wait here: measured 2 % slower on
+      // 512 x 512 x 8192, while the persistent kernel gains 1 % from it)
       pdl_wait();
       int stage = 0;
       uint32_t phase = 0;
