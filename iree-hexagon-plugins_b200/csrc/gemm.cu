@@ -588,6 +588,7 @@ __global__ void replicate_block_kernel(const __half* __restrict__ src, long long
     for (int d = 0; d < dests.n; ++d)
       *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(dests.p[d]) + r * ld + c) = v;
   }
+  __threadfence_system();  // peer stores performed system-wide before the kernel ends
 }
 }  // namespace
 

@@ -377,6 +377,10 @@ __global__ void __launch_bounds__(GemmShape<BN, BMODE>::kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
     }
+    // all-gather epilogue: this thread's stores into the other ranks' outputs
+    // are performed system-wide before the kernel ends, so a barrier that
+    // follows the kernel on the stream (hxb_peer_barrier) publishes them
+    if (args.ndests > 1) __threadfence_system();
   }
 
   tc_fence_before();

@@ -719,6 +719,9 @@ __global__ void __launch_bounds__(kW8Threads, 1)
       ++tl;
     }
     if (issuer && stores_pending) bulk_wait_all();
+    // the peer stores of w8_store_replicas are performed system-wide before
+    // the kernel ends (see hxb_peer_barrier)
+    if (args.ndests > 1) __threadfence_system();
     // after a failure: a residual load this thread issued may still be
     // landing in the staging tile
     if (issuer && r_landed < rl) {
