@@ -163,11 +163,20 @@ class ShardedMatmul:
     def nccl(self, a: torch.Tensor, b_shard: torch.Tensor, *, shard_out: torch.Tensor,
              gathered: torch.Tensor) -> torch.Tensor:
         """Baseline: GEMM into the local shard, NCCL all-gather, layout step.
-        Needs equal shards (N divisible by 8 * world)."""
-        from .dispatch import matmul
+        Needs equal shards (N divisible by 8 * world). The shard's GEMM runs
+        the tile plan the fused path runs (the persistent kernel: the
+        all-gather epilogue has no split-K form), so both paths give the same
+        bits."""
         lib = _native.load()
         n = self.end - self.begin
-        matmul(a, b_shard, out=shard_out)
+        sms = torch.cuda.get_device_properties(a.device).multi_processor_count
+        bn, gm, sk = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0)
+        check(lib.hxb_plan_matmul_f16(self.M, n, self.K, 0, sms, ctypes.byref(bn),
+                                      ctypes.byref(gm), ctypes.byref(sk)))
+        check(lib.hxb_matmul_f16_tiled(a.data_ptr(), a.stride(0), b_shard.data_ptr(),
+                                       b_shard.stride(0), 0, shard_out.data_ptr(),
+                                       shard_out.stride(0), 0, self.M, n, self.K, bn.value,
+                                       gm.value, 1, _stream_ptr(a)))
         if self.world > 1:
             self.dist.all_gather_into_tensor(gathered, shard_out, group=self.group)
             src = gathered

@@ -49,6 +49,15 @@ def main() -> None:
             want = oracle.matmul_f32(a[rows], b)
             baseline_check(want, fused[torch.from_numpy(rows).to(dev)].float().cpu().numpy(),
                            "2-rank sharded")
+        # back-to-back fused steps with new data each time: every step's
+        # gathered C must hold this step's tiles from every rank (the peer
+        # barrier after the GEMM publishes the peers' stores)
+        for it in range(12):
+            bd.mul_(-1.0 if it % 2 else 0.5)
+            f = sm.fused(ad, bd).clone()
+            n = sm.nccl(ad, bd, shard_out=shard, gathered=gathered)
+            torch.cuda.synchronize()
+            assert torch.equal(f, n), f"fused step {it} differs from the NCCL path"
         assert pkg.device_status() == 0
         dist.barrier()
         sm.close()
