@@ -103,29 +103,33 @@ hxb_status_t hxb_matmul_f16(const void* A, int64_t lda, const void* B,
                             size_t workspace_bytes, void* stream);
 
 /* The tile plan hxb_matmul_f16 uses for a shape on a device with num_sms SMs:
- * the N extent of one 128-row output tile (64, 128 or 256), the raster group
- * (tile rows swept together for L2 reuse) and the K split: 1 runs the
- * persistent kernel (one CTA per SM walking whole tiles); 2, 4 or 8 run one
- * thread-block cluster of that many CTAs per tile, each on its share of the
- * K-blocks, the partial sums added through distributed shared memory (for
- * shapes whose tiles alone would leave SMs idle). Shapes measured by the
- * offline sweep (tile_sweep.py) come from the baked table, the rest from the
- * cost model. This is the B200 counterpart of the reference's HMX tile
- * search, selectHmxTileSizes
+ * the N extent of one output tile (64, 128 or 256), the raster group (tile
+ * rows swept together for L2 reuse), the K split and the CTA pairing. split_k
+ * 1 runs a persistent kernel walking whole tiles; 2, 4 or 8 run one
+ * thread-block cluster of that many CTAs per 128-row tile, each on its share
+ * of the K-blocks, the partial sums added through distributed shared memory
+ * (for shapes whose tiles alone would leave SMs idle). cta_pair 1 gives each
+ * SM 128-row tiles; 2 gives a pair of SMs 256-row tiles computed by
+ * cta_group::2 MMAs, each SM loading half of the operands (split_k 1 only).
+ * Shapes measured by the offline sweep (tile_sweep.py) come from the baked
+ * table, the rest from the cost model. This is the B200 counterpart of the
+ * reference's HMX tile search, selectHmxTileSizes
  * (plugins/compiler/hexagon/CodeGen/Strategy/Planning/VTCMPlanning.cpp:
- * 186-260). split_k may be NULL. Host only. */
+ * 186-260). split_k and cta_pair may be NULL. Host only. */
 hxb_status_t hxb_plan_matmul_f16(int64_t M, int64_t N, int64_t K, int transpose_b,
-                                 int num_sms, int* block_n, int* group_m, int* split_k);
+                                 int num_sms, int* block_n, int* group_m, int* split_k,
+                                 int* cta_pair);
 
 /* hxb_matmul_f16 (no init, no re-pitching) with the tile plan given
  * explicitly instead of planned: the entry the offline tile sweep measures
  * candidates through. block_n in {64, 128, 256}; group_m >= 1; split_k in
- * {1, 2, 4, 8} with at least split_k 64-deep K-blocks. */
+ * {1, 2, 4, 8} with at least split_k 64-deep K-blocks; cta_pair 1, or 2 with
+ * split_k 1 and block_n 128 or 256. */
 hxb_status_t hxb_matmul_f16_tiled(const void* A, int64_t lda, const void* B,
                                   int64_t ldb, int transpose_b, void* C,
                                   int64_t ldc, hxb_dtype_t c_dtype, int64_t M,
                                   int64_t N, int64_t K, int block_n, int group_m,
-                                  int split_k, void* stream);
+                                  int split_k, int cta_pair, void* stream);
 
 size_t hxb_matmul_f16_workspace_bytes(const void* A, int64_t lda,
                                       const void* B, int64_t ldb,

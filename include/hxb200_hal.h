@@ -148,7 +148,7 @@ const hxb_executable_library_header_t** hxb_executable_library_query(
  *             [2] C [M,N] (f16, or f32 with flag bit 1), optional [3] C_init
  *             (same type/shape as C, added to the product)
  *   constants: M, N, K, flags (bit 0: B transposed, bit 1: f32 output),
- *             optional block_n, group_m, split_k: a tile plan fixed at
+ *             optional block_n, group_m, split_k, cta_pair: a tile plan fixed at
  *             compile time (hxb_plan_matmul_f16; used when there is no C_init
  *             and no re-pitch; block_n 0 = plan at dispatch time)
  * HXB_EXPORT_MATMUL_W8A16 "matmul_w8a16"

@@ -32,9 +32,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "hxb_matmul_f16_noalloc": (c_int, [c_vp, c_i64, c_vp, c_i64, c_int, c_vp, c_vp,
                                        c_i64, c_int, c_i64, c_i64, c_i64, c_vp]),
     "hxb_plan_matmul_f16": (c_int, [c_i64, c_i64, c_i64, c_int, c_int, ctypes.POINTER(c_int),
-                                    ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
+                                    ctypes.POINTER(c_int), ctypes.POINTER(c_int),
+                                    ctypes.POINTER(c_int)]),
     "hxb_matmul_f16_tiled": (c_int, [c_vp, c_i64, c_vp, c_i64, c_int, c_vp, c_i64, c_int,
-                                     c_i64, c_i64, c_i64, c_int, c_int, c_int, c_vp]),
+                                     c_i64, c_i64, c_i64, c_int, c_int, c_int, c_int, c_vp]),
     "hxb_matmul_w8a16": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_i64,
                                  c_i64, c_i64, c_i64, c_vp]),
     "hxb_plan_matmul_w8a16": (c_int, [c_i64, c_i64, c_i64, c_int, ctypes.POINTER(c_int),

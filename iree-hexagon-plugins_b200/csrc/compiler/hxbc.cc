@@ -386,9 +386,9 @@ bool FuncCompiler::emit_matmul(const Op& op, const std::string& a, const std::st
     }
   }
   const Binding cb = output_storage(res);
-  int bn = 0, gm = 0, sk = 1;
+  int bn = 0, gm = 0, sk = 1, pair = 1;
   if (hxb_plan_matmul_f16(M, N, K, transpose_b ? 1 : 0, opt_.num_sms ? opt_.num_sms : 148, &bn,
-                          &gm, &sk) != HXB_OK) {
+                          &gm, &sk, &pair) != HXB_OK) {
     err(op, "no tile plan for this shape");
     return false;
   }
@@ -398,7 +398,7 @@ bool FuncCompiler::emit_matmul(const Op& op, const std::string& a, const std::st
     d.ordinal = HXB_EXPORT_MATMUL_F16;
     d.constants = {(uint32_t)M, (uint32_t)N, (uint32_t)K,
                    (transpose_b ? 1u : 0u) | (f32 ? 2u : 0u), (uint32_t)bn, (uint32_t)gm,
-                   (uint32_t)sk};
+                   (uint32_t)sk, (uint32_t)pair};
     d.bindings.push_back(slice(ab, (uint64_t)bi * M * K * 2, (uint64_t)M * K * 2));
     d.bindings.push_back(slice(bb, (uint64_t)bi * K * N * 2, (uint64_t)K * N * 2));
     d.bindings.push_back(slice(cb, (uint64_t)bi * M * N * esz, (uint64_t)M * N * esz));
@@ -409,7 +409,8 @@ bool FuncCompiler::emit_matmul(const Op& op, const std::string& a, const std::st
   s << "matmul_f16 dispatch" << (batch > 1 ? "es" : "") << ": " << (batch > 1 ? std::to_string(batch) + " x " : "")
     << M << "x" << N << "x" << K << (transpose_b ? " (rhs transposed)" : "")
     << (f32 ? ", f32 out" : ", f16 out") << (zero_init ? "" : ", init added")
-    << "; tile plan block_n " << bn << ", group_m " << gm << ", split_k " << sk;
+    << "; tile plan block_n " << bn << ", group_m " << gm << ", split_k " << sk
+    << ", cta_pair " << pair;
   note("accept", op, s.str());
   return true;
 }

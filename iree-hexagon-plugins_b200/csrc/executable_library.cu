@@ -65,7 +65,7 @@ float f32_bits(uint32_t u) {
 }
 
 // bindings: A, B, C [, C_init]; constants: M, N, K, flags
-// [, block_n, group_m, split_k]
+// [, block_n, group_m, split_k, cta_pair]
 int dispatch_matmul_f16(const hxb_executable_environment_t* env,
                         const hxb_executable_dispatch_state_t* ds,
                         const hxb_executable_workgroup_state_t*) {
@@ -101,13 +101,14 @@ int dispatch_matmul_f16(const hxb_executable_environment_t* env,
     return hxb_matmul_f16_noalloc(A, (int64_t)K, B, ldb, tb, init, C, (int64_t)N, dt,
                                   (int64_t)M, (int64_t)N, (int64_t)K, env->stream);
   // a tile plan the compiler baked into the push constants (block_n,
-  // group_m; 0 = plan at dispatch time)
+  // group_m, split_k, cta_pair; block_n 0 = plan at dispatch time)
   const uint32_t block_n = ds->constants[4], group_m = ds->constants[5];
   const uint32_t split_k = ds->constants[6] ? ds->constants[6] : 1u;
+  const uint32_t cta_pair = ds->constants[7] ? ds->constants[7] : 1u;
   if (block_n != 0 && !init)
     return hxb_matmul_f16_tiled(A, (int64_t)K, B, ldb, tb, C, (int64_t)N, dt, (int64_t)M,
                                 (int64_t)N, (int64_t)K, (int)block_n, (int)group_m,
-                                (int)split_k, env->stream);
+                                (int)split_k, (int)cta_pair, env->stream);
   return hxb_matmul_f16(A, (int64_t)K, B, ldb, tb, init, C, (int64_t)N, dt, (int64_t)M,
                         (int64_t)N, (int64_t)K, nullptr, 0, env->stream);
 }

@@ -33,6 +33,48 @@ hxb_status_t launch_gemm(const DeviceInfo& dev, const CUtensorMap& tmA,
                     "gemm launch", tmA, tmB, args);
 }
 
+// CTA pairs (gemm_sm100_kernel<..., PAIR = 2>): a cluster of two CTAs per
+// 256 x BN tile, persistent over tiles. The grid holds as many pairs as can be
+// resident at once (a GPC whose free SM count is odd leaves one SM out), so
+// every pair starts in the first wave.
+template <int BN, int STAGES, int BMODE, int OUT>
+hxb_status_t launch_gemm_pair(const DeviceInfo& dev, const CUtensorMap& tmA,
+                              const CUtensorMap& tmB, const GemmArgs& args,
+                              cudaStream_t stream) {
+  using L = GemmSmem<BN / 2, STAGES, BMODE>;
+  auto kernel = gemm_sm100_kernel<BN, STAGES, BMODE, OUT, 2>;
+  static int max_pairs[64] = {};
+  cudaLaunchConfig_t cfg{};
+  cfg.blockDim = dim3(GemmShape<BN, BMODE>::kThreads);
+  cfg.dynamicSmemBytes = L::kAlloc;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (!max_pairs[dev.ordinal]) {
+    cudaError_t e =
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(gemm pair)");
+    cfg.gridDim = dim3(2 * (dev.num_sms / 2));
+    int n = 0;
+    e = cudaOccupancyMaxActiveClusters(&n, kernel, &cfg);
+    if (e != cudaSuccess) return cuda_status(e, "cudaOccupancyMaxActiveClusters(gemm pair)");
+    if (n < 1) return fail(HXB_STATUS_UNSUPPORTED, "gemm pair: no CTA pair fits an SM pair");
+    max_pairs[dev.ordinal] = n;
+  }
+  const int tiles = args.tiles_m * args.tiles_n;
+  const int pairs = tiles < max_pairs[dev.ordinal] ? tiles : max_pairs[dev.ordinal];
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.numAttrs = 2;
+  return cuda_status(cudaLaunchKernelEx(&cfg, kernel, tmA, tmB, args), "gemm pair launch");
+}
+
 // One cluster of SPLIT CTAs per output tile (gemm_splitk_sm100.cuh),
 // launched with programmatic stream serialization like the persistent kernel.
 template <int BN, int STAGES, int BMODE, int OUT, int SPLIT>
@@ -81,6 +123,16 @@ template <int BMODE, int OUT>
 hxb_status_t launch_planned(const GemmPlan& plan, const DeviceInfo& dev,
                             const CUtensorMap& tmA, const CUtensorMap& tmB,
                             const GemmArgs& args, cudaStream_t stream) {
+  if (plan.pair == 2) {
+    if (plan.split != 1)
+      return fail(HXB_STATUS_UNSUPPORTED, "no CTA-pair kernel with split_k=%d", plan.split);
+    switch (plan.block_n) {
+      case 256: return launch_gemm_pair<256, 6, BMODE, OUT>(dev, tmA, tmB, args, stream);
+      case 128: return launch_gemm_pair<128, 8, BMODE, OUT>(dev, tmA, tmB, args, stream);
+      default: break;
+    }
+    return fail(HXB_STATUS_UNSUPPORTED, "no CTA-pair kernel for block_n=%d", plan.block_n);
+  }
   switch (plan.split) {
     case 1: break;
     case 2: return launch_split_bn<BMODE, OUT, 2>(plan, dev, tmA, tmB, args, stream);
@@ -175,15 +227,19 @@ hxb_status_t gemm_f16_launch(const void* A, int64_t lda, const void* B, int64_t 
 
   const int bmode = transpose_b ? kBF16RowMajorNK : kBF16RowMajorKN;
   GemmPlan plan = forced ? *forced : plan_gemm((int)M, (int)N, (int)K, bmode, dev->num_sms);
-  // the all-gather epilogue lives in the persistent kernel only
+  // the all-gather epilogue lives in the persistent kernels only
   if (nreplicas > 0) plan.split = 1;
+  if (plan.pair != 1 && (plan.pair != 2 || plan.split != 1 || plan.block_n < 128))
+    return fail(HXB_STATUS_INVALID_ARGUMENT,
+                "matmul: a CTA pair (256-row tiles) needs block_n 128 or 256 and no split_k");
   if (plan.split > 1 && (plan.split > 8 || (plan.split & (plan.split - 1)) ||
                          (K + kBK - 1) / kBK < plan.split))
     return fail(HXB_STATUS_INVALID_ARGUMENT,
                 "matmul: split_k %d needs a power of two <= 8 and at least that many "
                 "64-deep K-blocks",
                 plan.split);
-  const int64_t tiles_m = (M + kBM - 1) / kBM;
+  const int64_t tile_rows = (int64_t)kBM * plan.pair;
+  const int64_t tiles_m = (M + tile_rows - 1) / tile_rows;
   if (plan.group_m < 1) plan.group_m = 1;
   if (plan.group_m > tiles_m) plan.group_m = (int)tiles_m;
 
@@ -192,7 +248,8 @@ hxb_status_t gemm_f16_launch(const void* A, int64_t lda, const void* B, int64_t 
   if (transpose_b) {
     const uint64_t dims[2] = {(uint64_t)K, (uint64_t)N};
     const uint64_t strides[1] = {(uint64_t)ldb * 2};
-    const uint32_t box[2] = {64, (uint32_t)plan.block_n};
+    // a CTA of a pair loads half of the tile's B rows
+    const uint32_t box[2] = {64, (uint32_t)(plan.block_n / plan.pair)};
     s = encode_tensor_map(&tmB, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, B, dims,
                           strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
   } else {
@@ -213,7 +270,7 @@ hxb_status_t gemm_f16_launch(const void* A, int64_t lda, const void* B, int64_t 
   args.C_init = C_init;
   args.scale = nullptr;
   args.status = dev->status_word;
-  args.tiles_m = (int)((M + kBM - 1) / kBM);
+  args.tiles_m = (int)tiles_m;
   args.tiles_n = (int)((N + plan.block_n - 1) / plan.block_n);
   args.group_m = plan.group_m;
   const int esz = c_dtype == HXB_DTYPE_F16 ? 2 : 4;
@@ -780,23 +837,27 @@ extern "C" hxb_status_t hxb_matmul_f16_tiled(const void* A, int64_t lda, const v
                                              int64_t ldb, int transpose_b, void* C, int64_t ldc,
                                              hxb_dtype_t c_dtype, int64_t M, int64_t N, int64_t K,
                                              int block_n, int group_m, int split_k,
-                                             void* stream) {
+                                             int cta_pair, void* stream) {
   using namespace hxb;
   if (block_n != 64 && block_n != 128 && block_n != 256)
     return fail(HXB_STATUS_INVALID_ARGUMENT, "matmul_f16_tiled: block_n must be 64, 128 or 256");
   if (split_k != 1 && split_k != 2 && split_k != 4 && split_k != 8)
     return fail(HXB_STATUS_INVALID_ARGUMENT, "matmul_f16_tiled: split_k must be 1, 2, 4 or 8");
+  if (cta_pair != 1 && (cta_pair != 2 || split_k != 1 || block_n == 64))
+    return fail(HXB_STATUS_INVALID_ARGUMENT,
+                "matmul_f16_tiled: cta_pair must be 1, or 2 with split_k 1 and block_n 128 or "
+                "256");
   if (!aligned16(A) || !aligned16(B) || (lda * 2) % 16 || (ldb * 2) % 16)
     return fail(HXB_STATUS_INVALID_ARGUMENT,
                 "matmul_f16_tiled: A and B need 16-byte aligned rows (no re-pitching)");
-  const GemmPlan plan{block_n, group_m, split_k};
+  const GemmPlan plan{block_n, group_m, split_k, cta_pair};
   return gemm_f16_launch(A, lda, B, ldb, transpose_b, nullptr, C, ldc, c_dtype, M, N, K,
                          nullptr, 0, nullptr, 0, static_cast<cudaStream_t>(stream), &plan);
 }
 
 extern "C" hxb_status_t hxb_plan_matmul_f16(int64_t M, int64_t N, int64_t K, int transpose_b,
                                             int num_sms, int* block_n, int* group_m,
-                                            int* split_k) {
+                                            int* split_k, int* cta_pair) {
   using namespace hxb;
   if (M < 1 || N < 1 || K < 1 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX ||
       num_sms < 1 || !block_n || !group_m)
@@ -806,5 +867,6 @@ extern "C" hxb_status_t hxb_plan_matmul_f16(int64_t M, int64_t N, int64_t K, int
   *block_n = p.block_n;
   *group_m = p.group_m;
   if (split_k) *split_k = p.split;
+  if (cta_pair) *cta_pair = p.pair;
   return HXB_OK;
 }

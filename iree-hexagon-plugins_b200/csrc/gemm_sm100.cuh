@@ -181,16 +181,29 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& args, int row,
   }
 }
 
-template <int BN, int STAGES, int BMODE, int OUT>
+// PAIR = 2 is the CTA-pair form (cta_group::2, a cluster of two CTAs on two
+// SMs): the pair computes a 256 x BN tile with M = 256 MMAs issued by the
+// leader (cluster rank 0). Each CTA loads its own 128 rows of A and its own
+// BN / 2 columns of B into its own shared memory -- per SM that is 2/3 of the
+// operand bytes of a 128 x BN tile for the same tensor work -- and holds
+// rows [rank * 128, rank * 128 + 128) of the accumulator in its own TMEM.
+// Both CTAs' loads complete on the leader's `full` barriers; the leader's
+// commits arrive on both CTAs' `empty` and `tfull` barriers; both CTAs'
+// epilogue warps arrive on the leader's `tempty`. No multicast anywhere.
+template <int BN, int STAGES, int BMODE, int OUT, int PAIR = 1>
 __global__ void __launch_bounds__(GemmShape<BN, BMODE>::kThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
                       const __grid_constant__ CUtensorMap tmB,
                       const GemmArgs args) {
-  using L = GemmSmem<BN, STAGES, BMODE>;
+  static_assert(PAIR == 1 || PAIR == 2, "one CTA or a CTA pair per tile");
+  constexpr int kBNC = BN / PAIR;     // B columns this CTA loads
+  constexpr int kTileM = kBM * PAIR;  // output rows of a tile
+  using L = GemmSmem<kBNC, STAGES, BMODE>;
   constexpr int kTmemCols = GemmShape<BN, BMODE>::kTmemCols;
   constexpr uint32_t kIdesc =
-      make_idesc_f16(kBM, BN, 0, BMODE == kBF16RowMajorNK ? 0 : 1);
-  constexpr uint32_t kTxBytes = L::kABytes + L::kBBytes;
+      make_idesc_f16(kTileM, BN, 0, BMODE == kBF16RowMajorNK ? 0 : 1);
+  // the (leader's) full barrier counts the bytes of every CTA of the tile
+  constexpr uint32_t kTxBytes = (L::kABytes + L::kBBytes) * PAIR;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -206,6 +219,10 @@ __global__ void __launch_bounds__(GemmShape<BN, BMODE>::kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = PAIR > 1 ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  const int unit = (int)blockIdx.x / PAIR;  // this CTA's tile walker
+  const int units = (int)gridDim.x / PAIR;
   const int num_tiles = args.tiles_m * args.tiles_n;
   const int num_kb = (args.K + kBK - 1) / kBK;
   const FailState fs{abort_flag, args.status};
@@ -217,7 +234,7 @@ __global__ void __launch_bounds__(GemmShape<BN, BMODE>::kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 4);
+      mbar_init(&tempty[i], 4 * PAIR);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -228,11 +245,19 @@ __global__ void __launch_bounds__(GemmShape<BN, BMODE>::kThreads, 1)
     tma_prefetch_desc(&tmB);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_holder, kTmemCols);
-    tmem_relinquish();
+    if constexpr (PAIR == 1) {
+      tmem_alloc(tmem_holder, kTmemCols);
+      tmem_relinquish();
+    } else {
+      tmem_alloc_pair(tmem_holder, kTmemCols);
+      tmem_relinquish_pair();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  // the peer's barriers must be initialised before any load, commit or
+  // arrival of the pair reaches them
+  __syncwarp();
+  if constexpr (PAIR == 1) __syncthreads(); else cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   // The set-up above overlaps the previous kernel of the stream (programmatic
@@ -247,18 +272,20 @@ __global__ void __launch_bounds__(GemmShape<BN, BMODE>::kThreads, 1)
       // The operands of this CTA's first tile's first K-blocks are requested
       // into L2 while the previous kernel of the stream may still run; the
       // loads below, issued after the wait, then hit L2.
-      if ((int)blockIdx.x < num_tiles) {
+      if (unit < num_tiles) {
         int tm0, tn0;
-        tile_coords(blockIdx.x, args, tm0, tn0);
+        tile_coords(unit, args, tm0, tn0);
+        const int a_row0 = tm0 * kTileM + (int)rank * kBM;
+        const int b_col0 = tn0 * BN + (int)rank * kBNC;
         const int pre = num_kb < STAGES ? num_kb : STAGES;
         for (int kb = 0; kb < pre; ++kb) {
-          tma_prefetch_l2_2d(&tmA, kb * kBK, tm0 * kBM);
+          tma_prefetch_l2_2d(&tmA, kb * kBK, a_row0);
           if constexpr (BMODE == kBF16RowMajorKN) {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j)
-              tma_prefetch_l2_2d(&tmB, tn0 * BN + 64 * j, kb * kBK);
+            for (int j = 0; j < kBNC / 64; ++j)
+              tma_prefetch_l2_2d(&tmB, b_col0 + 64 * j, kb * kBK);
           } else {
-            tma_prefetch_l2_2d(&tmB, kb * kBK, tn0 * BN);
+            tma_prefetch_l2_2d(&tmB, kb * kBK, b_col0);
           }
         }
       }
@@ -267,22 +294,41 @@ __global__ void __launch_bounds__(GemmShape<BN, BMODE>::kThreads, 1)
       uint32_t phase = 0;
       long long issued = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      for (int t = unit; t < num_tiles && ok; t += units) {
         int tm, tn;
         tile_coords(t, args, tm, tn);
+        const int a_row = tm * kTileM + (int)rank * kBM;
+        const int b_col = tn * BN + (int)rank * kBNC;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, fs)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full[stage], kTxBytes);
-          tma_load_2d(smem + L::kOffA + stage * L::kABytes, &tmA, &full[stage],
-                      kb * kBK, tm * kBM);
-          if constexpr (BMODE == kBF16RowMajorKN) {
+          uint8_t* a_dst = smem + L::kOffA + stage * L::kABytes;
+          uint8_t* b_dst = smem + L::kOffB + stage * L::kBBytes;
+          if constexpr (PAIR == 1) {
+            mbar_arrive_expect_tx(&full[stage], kTxBytes);
+            tma_load_2d(a_dst, &tmA, &full[stage], kb * kBK, a_row);
+            if constexpr (BMODE == kBF16RowMajorKN) {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j)
-              tma_load_2d(smem + L::kOffB + stage * L::kBBytes + j * (kBK * 128),
-                          &tmB, &full[stage], tn * BN + 64 * j, kb * kBK);
+              for (int j = 0; j < kBNC / 64; ++j)
+                tma_load_2d(b_dst + j * (kBK * 128), &tmB, &full[stage], b_col + 64 * j,
+                            kb * kBK);
+            } else {
+              tma_load_2d(b_dst, &tmB, &full[stage], kb * kBK, b_col);
+            }
           } else {
-            tma_load_2d(smem + L::kOffB + stage * L::kBBytes, &tmB, &full[stage],
-                        kb * kBK, tn * BN);
+            // both CTAs' bytes complete on the leader's barrier; only the
+            // leader arms it (a peer's bytes may land first: the phase cannot
+            // complete before the leader's arrival)
+            if (leader) mbar_arrive_expect_tx(&full[stage], kTxBytes);
+            const uint32_t bar = map_to_rank(smem_u32(&full[stage]), 0);
+            tma_load_2d_pair(a_dst, &tmA, bar, kb * kBK, a_row);
+            if constexpr (BMODE == kBF16RowMajorKN) {
+#pragma unroll
+              for (int j = 0; j < kBNC / 64; ++j)
+                tma_load_2d_pair(b_dst + j * (kBK * 128), &tmB, bar, b_col + 64 * j,
+                                 kb * kBK);
+            } else {
+              tma_load_2d_pair(b_dst, &tmB, bar, kb * kBK, b_col);
+            }
           }
           ++issued;
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -290,28 +336,29 @@ __global__ void __launch_bounds__(GemmShape<BN, BMODE>::kThreads, 1)
       }
       // Never leave the CTA with bulk copies still landing in its shared
       // memory: wait for the last STAGES issues (already complete on the
-      // normal path).
+      // normal path). A pair's second CTA sees its copies complete through
+      // its `empty` barriers (the MMAs that read them have retired).
       const long long nd = issued < STAGES ? issued : STAGES;
       for (long long i = 0; i < nd; ++i) {
         const long long u = issued - 1 - i;
         const int s = (int)(u % STAGES);
         const uint32_t ph = (uint32_t)((u / STAGES) & 1);
+        uint64_t* bar = leader ? &full[s] : &empty[s];
         // bounded even on the failure path
         const unsigned long long t0 = globaltimer_ns();
-        while (!mbar_try_wait(&full[s], ph) &&
-               globaltimer_ns() - t0 < kWaitLimitNs) {
+        while (!mbar_try_wait(bar, ph) && globaltimer_ns() - t0 < kWaitLimitNs) {
         }
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    if (lane == 0 && leader) {
       int stage = 0;
       uint32_t phase = 0;
       int tl = 0;
       bool ok = true;
       bool issued_any = false;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++tl) {
+      for (int t = unit; t < num_tiles && ok; t += units, ++tl) {
         const int acc = tl & 1;
         const uint32_t acc_phase = (tl >> 1) & 1;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, fs)) { ok = false; break; }
@@ -332,18 +379,33 @@ __global__ void __launch_bounds__(GemmShape<BN, BMODE>::kThreads, 1)
             else
               bdesc = make_smem_desc(b_addr + k * 16 * 128, kBK * 128, 1024,
                                      kLayoutSwizzle128);
-            umma_f16_ss(d_tmem, adesc, bdesc, kIdesc, (kb | k) != 0);
+            if constexpr (PAIR == 1)
+              umma_f16_ss(d_tmem, adesc, bdesc, kIdesc, (kb | k) != 0);
+            else
+              umma_f16_ss_pair(d_tmem, adesc, bdesc, kIdesc, (kb | k) != 0);
           }
           issued_any = true;
-          umma_commit(&empty[stage]);
+          if constexpr (PAIR == 1) {
+            umma_commit(&empty[stage]);
+          } else {
+            umma_commit_pair(smem_u32(&empty[stage]));
+            umma_commit_pair(map_to_rank(smem_u32(&empty[stage]), 1));
+          }
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
-        if (ok) umma_commit(&tfull[acc]);
+        if (ok) {
+          if constexpr (PAIR == 1) {
+            umma_commit(&tfull[acc]);
+          } else {
+            umma_commit_pair(smem_u32(&tfull[acc]));
+            umma_commit_pair(map_to_rank(smem_u32(&tfull[acc]), 1));
+          }
+        }
       }
       if (!ok && issued_any) {
         // Failure path: let every MMA already issued retire before TMEM is
         // released.
-        umma_commit(drain);
+        if constexpr (PAIR == 1) umma_commit(drain); else umma_commit_pair(smem_u32(drain));
         const unsigned long long t0 = globaltimer_ns();
         while (!mbar_try_wait(drain, 0) && globaltimer_ns() - t0 < kWaitLimitNs) {
         }
@@ -353,7 +415,7 @@ __global__ void __launch_bounds__(GemmShape<BN, BMODE>::kThreads, 1)
     // ------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     int tl = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tl) {
+    for (int t = unit; t < num_tiles; t += units, ++tl) {
       int tm, tn;
       tile_coords(t, args, tm, tn);
       const int acc = tl & 1;
@@ -362,7 +424,7 @@ __global__ void __launch_bounds__(GemmShape<BN, BMODE>::kThreads, 1)
       // tcgen05.ld is .sync.aligned: reconverge and agree before touching TMEM
       if (!__all_sync(0xffffffffu, ready)) break;
       tc_fence_after();
-      const int row = tm * kBM + q * 32 + lane;
+      const int row = tm * kTileM + (int)rank * kBM + q * 32 + lane;
       const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
@@ -375,7 +437,10 @@ __global__ void __launch_bounds__(GemmShape<BN, BMODE>::kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (lane == 0) {
+        if (leader) mbar_arrive(&tempty[acc]);
+        else mbar_arrive_cluster(map_to_rank(smem_u32(&tempty[acc]), 0));
+      }
     }
     // all-gather epilogue: this thread's stores into the other ranks' outputs
     // are performed system-wide before the kernel ends, so a barrier that
@@ -384,11 +449,15 @@ __global__ void __launch_bounds__(GemmShape<BN, BMODE>::kThreads, 1)
   }
 
   tc_fence_before();
-  __syncthreads();
+  // a pair's CTAs stay resident until neither can still reach the other's
+  // shared memory (remote arrivals, commits) or TMEM
+  __syncwarp();
+  if constexpr (PAIR == 1) __syncthreads(); else cluster_sync_all();
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    if constexpr (PAIR == 1) tmem_dealloc(tmem_base, kTmemCols);
+    else tmem_dealloc_pair(tmem_base, kTmemCols);
   }
 }
 

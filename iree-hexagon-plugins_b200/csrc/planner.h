@@ -14,15 +14,17 @@
 namespace hxb {
 
 struct GemmPlan {
-  int block_n;    // N extent of one output tile (M extent is always 128)
+  int block_n;    // N extent of one output tile
   int group_m;    // tile-rows per raster group (L2 reuse)
   int split = 1;  // 1: persistent kernel; 2, 4, 8: K split over a cluster
+  int pair = 1;   // 1: 128-row tiles on one SM; 2: 256-row tiles on a CTA pair
 };
 
 struct TunedGemm {
   int M, N, K, bmode;
   int block_n, group_m;
   int split;  // 0 or 1: no split
+  int pair;   // 0 or 1: one CTA per tile; 2: CTA pair
 };
 
 // Filled by the offline tile sweep (tile_table.inc); may be empty.
@@ -43,6 +45,10 @@ inline int64_t mma_cycles(int bn) {
 // streams at once.
 inline int64_t load_cycles(int bn) { return (16384 + (int64_t)bn * 128) / 48; }
 
+// The same for one CTA of a pair (256 x bn tiles on two SMs): A 16 KB plus
+// half of B.
+inline int64_t load_cycles_pair(int bn) { return (16384 + (int64_t)bn * 64) / 48; }
+
 // Largest split-K a shape takes: every CTA keeps at least two K-blocks, and
 // the tiles x split CTAs fit one wave (clusters are co-scheduled; a GPC's
 // SMs are not always all usable by clusters, hence the 7/8).
@@ -54,7 +60,7 @@ inline GemmPlan plan_gemm(int M, int N, int K, int bmode, int num_sms) {
   for (int i = 0; i < kNumTunedGemms; ++i) {
     const TunedGemm& t = kTunedGemms[i];
     if (t.M == M && t.N == N && t.K == K && t.bmode == bmode)
-      return GemmPlan{t.block_n, t.group_m, t.split > 1 ? t.split : 1};
+      return GemmPlan{t.block_n, t.group_m, t.split > 1 ? t.split : 1, t.pair > 1 ? 2 : 1};
   }
   const int cands[3] = {256, 128, 64};
   const int splits[4] = {1, 2, 4, 8};
@@ -88,8 +94,29 @@ inline GemmPlan plan_gemm(int M, int N, int K, int bmode, int num_sms) {
         best_traffic = traffic;
       }
     }
+    // CTA pair: 256-row tiles, each SM loading A and half of B per K-block.
+    // Taken only with at least one full wave of pairs (measured: fewer pairs
+    // than SM pairs lose to 128-row tiles, e.g. 2048^3 and 1024^3).
+    if (bn >= 128) {
+      const int64_t pair_tiles = (M + 255) / 256 * ((N + bn - 1) / bn);
+      const int64_t pairs = num_sms / 2;
+      if (pair_tiles >= pairs) {
+        const int64_t per_kb_pair = 4 * mma_cycles(bn) > load_cycles_pair(bn)
+                                        ? 4 * mma_cycles(bn)
+                                        : load_cycles_pair(bn);
+        const int64_t waves = (pair_tiles + pairs - 1) / pairs;
+        const int64_t cost = waves * (kb * per_kb_pair + 1800);
+        const int64_t traffic = pair_tiles * kb * (256 * 64 + (int64_t)bn * 64);
+        if (cost < best_cost || (cost == best_cost && traffic < best_traffic)) {
+          best = GemmPlan{bn, 8, 1, 2};
+          best_cost = cost;
+          best_traffic = traffic;
+        }
+      }
+    }
   }
-  if (best.group_m > tiles_m) best.group_m = (int)tiles_m;
+  const int64_t rows = (M + 128 * best.pair - 1) / (128 * best.pair);
+  if (best.group_m > rows) best.group_m = (int)rows;
   return best;
 }
 

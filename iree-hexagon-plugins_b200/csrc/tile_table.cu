@@ -7,7 +7,7 @@ namespace hxb {
 
 const TunedGemm kTunedGemms[] = {
 #include "tile_table.inc"
-    {0, 0, 0, -1, 0, 0, 0},  // sentinel, never matches (bmode -1)
+    {0, 0, 0, -1, 0, 0, 0, 0},  // sentinel, never matches (bmode -1)
 };
 const int kNumTunedGemms = sizeof(kTunedGemms) / sizeof(kTunedGemms[0]) - 1;
 

@@ -170,13 +170,13 @@ class ShardedMatmul:
         lib = _native.load()
         n = self.end - self.begin
         sms = torch.cuda.get_device_properties(a.device).multi_processor_count
-        bn, gm, sk = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0)
+        bn, gm, sk, pair = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0)
         check(lib.hxb_plan_matmul_f16(self.M, n, self.K, 0, sms, ctypes.byref(bn),
-                                      ctypes.byref(gm), ctypes.byref(sk)))
+                                      ctypes.byref(gm), ctypes.byref(sk), ctypes.byref(pair)))
         check(lib.hxb_matmul_f16_tiled(a.data_ptr(), a.stride(0), b_shard.data_ptr(),
                                        b_shard.stride(0), 0, shard_out.data_ptr(),
                                        shard_out.stride(0), 0, self.M, n, self.K, bn.value,
-                                       gm.value, 1, _stream_ptr(a)))
+                                       gm.value, 1, pair.value, _stream_ptr(a)))
         if self.world > 1:
             self.dist.all_gather_into_tensor(gathered, shard_out, group=self.group)
             src = gathered

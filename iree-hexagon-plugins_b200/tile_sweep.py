@@ -6,9 +6,10 @@ selectHmxTileSizes): where the reference ranks HMX-aligned tilings of each
 matmul by a static cost (VTCM budget, DDR traffic, tile count), this sweep
 MEASURES every tile plan the tcgen05 kernels offer -- the N extent of a
 128-row output tile (64, 128, 256), the L2 raster group of the persistent
-kernel, and the K split over a thread-block cluster (2, 4, 8 CTAs per tile,
-partials summed in distributed shared memory) -- on each shape and keeps the
-fastest. The winners are written as the C table
+kernel, the K split over a thread-block cluster (2, 4, 8 CTAs per tile,
+partials summed in distributed shared memory) and the CTA pair (256-row
+tiles computed by cta_group::2 MMAs on two SMs, each loading half of the
+operands) -- on each shape and keeps the fastest. The winners are written as the C table
 csrc/tile_table.inc, which is compiled into libhxb200.so and consulted by the
 planner before its cost model (planner.h), i.e. the search result is baked
 into the executable, keyed by dispatch shape.
@@ -82,44 +83,51 @@ def sweep(shapes, *, group_choices=(1, 4, 8, 16)) -> list[dict]:
         cands = []
         for bn in (64, 128, 256):
             tiles = tiles_m * ((N + bn - 1) // bn)
-            plans = [(gm, 1) for gm in sorted({min(g, tiles_m) for g in group_choices})]
+            plans = [(gm, 1, 1) for gm in sorted({min(g, tiles_m) for g in group_choices})]
             # split-K: clusters of 2, 4, 8 CTAs per tile, one wave, >= 2 K-blocks each
-            plans += [(1, sk) for sk in (2, 4, 8) if kb >= 2 * sk and tiles * sk <= sms]
-            for gm, sk in plans:
+            plans += [(1, sk, 1) for sk in (2, 4, 8) if kb >= 2 * sk and tiles * sk <= sms]
+            # CTA pairs: 256-row tiles on two SMs (block_n 128 or 256)
+            if bn >= 128 and M > 128:
+                pair_m = (M + 255) // 256
+                plans += [(gm, 1, 2) for gm in sorted({min(g, pair_m) for g in group_choices})]
+            for gm, sk, pair in plans:
                 it = iter(range(1 << 30))
 
-                def run(bn=bn, gm=gm, sk=sk):
+                def run(bn=bn, gm=gm, sk=sk, pair=pair):
                     i = next(it) % sets
                     pkg._native.check(lib.hxb_matmul_f16_tiled(
                         a[i].data_ptr(), K, b[i].data_ptr(), N, 0, c[i].data_ptr(), N, 0, M, N,
-                        K, bn, gm, sk, torch.cuda.current_stream().cuda_stream))
+                        K, bn, gm, sk, pair, torch.cuda.current_stream().cuda_stream))
                 ms = _time_graph(run, iters)
-                cands.append({"block_n": bn, "group_m": gm, "split_k": sk, "us": ms * 1e3,
-                              "tflops": flop / ms / 1e9})
+                cands.append({"block_n": bn, "group_m": gm, "split_k": sk, "cta_pair": pair,
+                              "us": ms * 1e3, "tflops": flop / ms / 1e9})
         best = min(cands, key=lambda r: r["us"])
-        pbn, pgm, psk = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0)
+        pbn, pgm, psk, ppair = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0)
         pkg._native.check(lib.hxb_plan_matmul_f16(M, N, K, 0, sms, ctypes.byref(pbn),
-                                                  ctypes.byref(pgm), ctypes.byref(psk)))
+                                                  ctypes.byref(pgm), ctypes.byref(psk),
+                                                  ctypes.byref(ppair)))
+        rows_m = (M + 128 * ppair.value - 1) // (128 * ppair.value)
         planned = next((r for r in cands if r["block_n"] == pbn.value and
-                        r["split_k"] == psk.value and
-                        (psk.value > 1 or r["group_m"] == min(max(pgm.value, 1), tiles_m))),
+                        r["split_k"] == psk.value and r["cta_pair"] == ppair.value and
+                        (psk.value > 1 or r["group_m"] == min(max(pgm.value, 1), rows_m))),
                        None)
         results.append({"M": M, "N": N, "K": K, "best": best, "candidates": cands,
                         "table_plan": planned, "input_sets": sets})
         del a, b, c
         torch.cuda.empty_cache()
         print(f"{M:5d} {N:5d} {K:5d}  best bn={best['block_n']:3d} gm={best['group_m']:2d} "
-              f"sk={best['split_k']} {best['tflops']:7.1f} TF/s", flush=True)
+              f"sk={best['split_k']} pair={best['cta_pair']} {best['tflops']:7.1f} TF/s",
+              flush=True)
     return results
 
 
 def write_table(results, path: Path) -> None:
-    lines = ["// {M, N, K, bmode, block_n, group_m, split_k} -- written by tile_sweep.py "
-             "(measured on a B200; row-major B, bmode 0)"]
+    lines = ["// {M, N, K, bmode, block_n, group_m, split_k, cta_pair} -- written by "
+             "tile_sweep.py (measured on a B200; row-major B, bmode 0)"]
     for r in results:
         b = r["best"]
         lines.append(f"{{{r['M']}, {r['N']}, {r['K']}, 0, {b['block_n']}, {b['group_m']}, "
-                     f"{b['split_k']}}},")
+                     f"{b['split_k']}, {b.get('cta_pair', 1)}}},")
     path.write_text("\n".join(lines) + "\n")
 
 

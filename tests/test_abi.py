@@ -96,14 +96,15 @@ def test_planner_uses_the_baked_sweep_table(pkg):
     table = (Path(__file__).resolve().parent.parent / "iree-hexagon-plugins_b200" / "csrc" /
              "tile_table.inc").read_text()
     rows = [tuple(int(v) for v in m.groups())
-            for m in re.finditer(r"\{(\d+), (\d+), (\d+), (\d+), (\d+), (\d+), (\d+)\}",
-                                 table)]
+            for m in re.finditer(
+                r"\{(\d+), (\d+), (\d+), (\d+), (\d+), (\d+), (\d+), (\d+)\}", table)]
     assert len(rows) >= 64
-    for M, N, K, bmode, bn, gm, sk in rows:
-        b, g, k = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0)
+    for M, N, K, bmode, bn, gm, sk, pair in rows:
+        b, g, k, p = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0)
         assert lib.hxb_plan_matmul_f16(M, N, K, bmode, 148, ctypes.byref(b), ctypes.byref(g),
-                                       ctypes.byref(k)) == 0
-        assert (b.value, g.value, k.value) == (bn, gm, max(sk, 1)), (M, N, K)
+                                       ctypes.byref(k), ctypes.byref(p)) == 0
+        assert (b.value, g.value, k.value, p.value) == (bn, gm, max(sk, 1), max(pair, 1)), \
+            (M, N, K)
 
 
 def test_rope_rejects_unaligned_pairs_before_device_access(pkg):

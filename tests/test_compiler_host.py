@@ -93,10 +93,11 @@ def test_matmul_f32_out_with_baked_tile_plan(pkg):
     assert f["results"] == [(1, (1024, 1024))]
     [(ordinal, c, binds)] = f["dispatches"]
     assert ordinal == 0 and c[:4] == (1024, 1024, 1024, 2)
-    bn, gm, sk = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    bn, gm, sk, pair = ctypes.c_int(), ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
     assert lib.hxb_plan_matmul_f16(1024, 1024, 1024, 0, 148, ctypes.byref(bn),
-                                   ctypes.byref(gm), ctypes.byref(sk)) == 0
-    assert c[4:] == (bn.value, gm.value, sk.value)  # the planner's choice, baked in
+                                   ctypes.byref(gm), ctypes.byref(sk), ctypes.byref(pair)) == 0
+    # the planner's choice, baked in
+    assert c[4:] == (bn.value, gm.value, sk.value, pair.value)
     # A = argument 0, B = argument 1, C = result 0; no init binding (zero fill)
     assert [(k, idx) for k, idx, _, _ in binds] == [(0, 0), (0, 1), (1, 0)]
     assert "accept" in exe.log and "block_n" in exe.log

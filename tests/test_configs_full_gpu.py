@@ -95,11 +95,13 @@ def test_cfg5b_sweep_shape_with_table_plan(cuda_pkg, oracle, M, N, K):
     checked to be the one the table holds, and up to 256 rows (all when
     M <= 512) are compared with the oracle."""
     lib = cuda_pkg._native.load()
-    bn, gm, sk = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0)
+    bn, gm, sk, pair = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0)
     sms = torch.cuda.get_device_properties(0).multi_processor_count
     cuda_pkg._native.check(lib.hxb_plan_matmul_f16(M, N, K, 0, sms, ctypes.byref(bn),
-                                                   ctypes.byref(gm), ctypes.byref(sk)))
+                                                   ctypes.byref(gm), ctypes.byref(sk),
+                                                   ctypes.byref(pair)))
     assert bn.value in (64, 128, 256) and gm.value >= 1 and sk.value in (1, 2, 4, 8)
+    assert pair.value in (1, 2) and (pair.value == 1 or sk.value == 1)
     rng = np.random.default_rng(M + 3 * N + 7 * K)
     a = rng.uniform(-1, 1, (M, K)).astype(np.float16)
     b = rng.uniform(-1, 1, (K, N)).astype(np.float16)

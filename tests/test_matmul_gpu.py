@@ -169,7 +169,7 @@ def test_split_k_cluster_kernel(cuda_pkg, oracle, M, N, K, bn, sk, tb, out):
     ad, bd = torch.from_numpy(a).to(DEV), torch.from_numpy(b).to(DEV)
     cuda_pkg._native.check(lib.hxb_matmul_f16_tiled(
         ad.data_ptr(), K, bd.data_ptr(), K if tb else N, int(tb), c.data_ptr(), N,
-        0 if out == torch.float16 else 1, M, N, K, bn, 1, sk,
+        0 if out == torch.float16 else 1, M, N, K, bn, 1, sk, 1,
         torch.cuda.current_stream().cuda_stream))
     torch.cuda.synchronize()
     _check_canary(buf, canary, guard)
@@ -179,11 +179,59 @@ def test_split_k_cluster_kernel(cuda_pkg, oracle, M, N, K, bn, sk, tb, out):
     c2 = torch.empty_like(c)
     cuda_pkg._native.check(lib.hxb_matmul_f16_tiled(
         ad.data_ptr(), K, bd.data_ptr(), K if tb else N, int(tb), c2.data_ptr(), N,
-        0 if out == torch.float16 else 1, M, N, K, bn, 1, sk,
+        0 if out == torch.float16 else 1, M, N, K, bn, 1, sk, 1,
         torch.cuda.current_stream().cuda_stream))
     torch.cuda.synchronize()
     assert torch.equal(c, c2)
     assert cuda_pkg.device_status() == 0
+
+
+@pytest.mark.parametrize("M,N,K,bn,gm,tb,out", [
+    (1024, 1024, 1024, 256, 4, False, torch.float16),
+    (1024, 1024, 1024, 128, 1, True, torch.float32),
+    (2048, 4096, 2048, 256, 8, False, torch.float16),   # more tiles than SM pairs
+    (300, 200, 1000, 256, 1, False, torch.float32),     # ragged: the second CTA's rows past M
+    (129, 264, 520, 128, 2, True, torch.float16),       # one tile row, ragged everything
+    (4096, 384, 4096, 128, 16, False, torch.float16),
+    (512, 8192, 512, 256, 4, True, torch.float16),
+])
+def test_cta_pair_kernel(cuda_pkg, oracle, M, N, K, bn, gm, tb, out):
+    """The CTA-pair kernel (256-row tiles, cta_group::2 MMAs issued by the
+    leader CTA, each CTA loading half of A and half of B) against the oracle,
+    with canary bands around the output, and bit-identical on a rerun."""
+    lib = cuda_pkg._native.load()
+    rng = np.random.default_rng(M + 2 * N + 3 * K + bn)
+    a = rng.uniform(-1, 1, (M, K)).astype(np.float16)
+    b = rng.uniform(-1, 1, (N, K) if tb else (K, N)).astype(np.float16)
+    c, buf, canary, guard = _guarded_empty((M, N), out)
+    ad, bd = torch.from_numpy(a).to(DEV), torch.from_numpy(b).to(DEV)
+
+    def run(dst):
+        cuda_pkg._native.check(lib.hxb_matmul_f16_tiled(
+            ad.data_ptr(), K, bd.data_ptr(), K if tb else N, int(tb), dst.data_ptr(), N,
+            0 if out == torch.float16 else 1, M, N, K, bn, gm, 1, 2,
+            torch.cuda.current_stream().cuda_stream))
+
+    run(c)
+    torch.cuda.synchronize()
+    _check_canary(buf, canary, guard)
+    baseline_check(oracle.matmul_f32(a, b, transpose_b=tb), c.float().cpu().numpy(),
+                   f"cta pair bn {bn} {M}x{N}x{K}")
+    c2 = torch.empty_like(c)
+    run(c2)
+    torch.cuda.synchronize()
+    assert torch.equal(c, c2)
+    assert cuda_pkg.device_status() == 0
+
+
+def test_cta_pair_rejects_split_and_narrow_tiles(cuda_pkg):
+    """A CTA pair takes block_n 128 or 256 and no K split."""
+    lib = cuda_pkg._native.load()
+    a = torch.zeros(256, 256, dtype=torch.float16, device=DEV)
+    for bn, sk in ((64, 1), (256, 2)):
+        st = lib.hxb_matmul_f16_tiled(a.data_ptr(), 256, a.data_ptr(), 256, 0, a.data_ptr(), 256,
+                                      0, 256, 256, 256, bn, 1, sk, 2, None)
+        assert st == 1
 
 
 def test_split_k_with_init_through_the_planner(cuda_pkg, oracle):
@@ -193,7 +241,7 @@ def test_split_k_with_init_through_the_planner(cuda_pkg, oracle):
     M, N, K = 256, 512, 4096
     bn, gm, sk = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
     cuda_pkg._native.check(lib.hxb_plan_matmul_f16(M, N, K, 0, 148, ctypes.byref(bn),
-                                                   ctypes.byref(gm), ctypes.byref(sk)))
+                                                   ctypes.byref(gm), ctypes.byref(sk), None))
     rng = np.random.default_rng(31)
     a = rng.uniform(-1, 1, (M, K)).astype(np.float16)
     b = rng.uniform(-1, 1, (K, N)).astype(np.float16)
