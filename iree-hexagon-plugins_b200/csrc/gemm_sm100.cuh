@@ -361,7 +361,10 @@ __global__ void __launch_bounds__(GemmShape<BN, BMODE>::kThreads, 1)
       for (int t = unit; t < num_tiles && ok; t += units, ++tl) {
         const int acc = tl & 1;
         const uint32_t acc_phase = (tl >> 1) & 1;
-        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, fs)) { ok = false; break; }
+        // (a pair's tempty collects the peer's epilogue arrivals too)
+        const bool free_acc = PAIR == 1 ? mbar_wait(&tempty[acc], acc_phase ^ 1, fs)
+                                        : mbar_wait_cluster(&tempty[acc], acc_phase ^ 1, fs);
+        if (!free_acc) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = 0; kb < num_kb; ++kb) {

@@ -129,6 +129,35 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   return mbar_wait_for(bar, parity, fs, kWaitLimitNs);
 }
 
+// mbar_wait for a barrier that other CTAs of the cluster arrive on
+// (mbar_arrive_cluster): the completed phase is acquired at cluster scope.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
+                                                  const FailState& fs) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (*fs.abort) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      raise_failure(fs);
+      return false;
+    }
+  }
+}
+
 // Named barrier among `count` threads (a multiple of 32) of this CTA.
 __device__ __forceinline__ void named_barrier_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
