@@ -596,9 +596,15 @@ SPECS = {
         "profile": "f16_gemm_1024x1024x1024.txt",
         "config": {"workload": "f16_gemm_1024x1024x1024", "cfg": 1,
                    "inputs": "A, B ~ U[-1, 1] f16, f16 out"}},
+    "f16_gemm_4096x4096x4096": {
+        "make": _spec_f16_gemm_shape(4096, 4096, 4096), "flop": 2.0 * 4096 ** 3,
+        "bound": "tensor", "kernel": "gemm_sm100_kernel", "dtype": "f16->f32",
+        "profile": "f16_gemm_pair_4096x4096x4096.txt",
+        "config": {"workload": "f16_gemm_4096x4096x4096", "cfg": "5b-like (CTA pairs)"}},
     "f16_gemm_512x512x8192": {
         "make": _spec_f16_gemm_shape(512, 512, 8192), "flop": 2.0 * 512 * 512 * 8192,
         "bound": "tensor", "kernel": "gemm_splitk_sm100_kernel", "dtype": "f16->f32",
+        "profile": "f16_gemm_splitk_512x512x8192.txt",
         "config": {"workload": "f16_gemm_512x512x8192", "cfg": "5b"}},
     "gemv_w8_m1": {
         "make": _spec_gemv(1), "bytes": 4096 * 11008 + 2 * 4096 + 2 * 11008 + 2 * 11008,
