@@ -227,8 +227,15 @@ hxb_status_t gemm_f16_launch(const void* A, int64_t lda, const void* B, int64_t 
 
   const int bmode = transpose_b ? kBF16RowMajorNK : kBF16RowMajorKN;
   GemmPlan plan = forced ? *forced : plan_gemm((int)M, (int)N, (int)K, bmode, dev->num_sms);
-  // the all-gather epilogue lives in the persistent kernels only
-  if (nreplicas > 0) plan.split = 1;
+  // The all-gather epilogue lives in the persistent kernels only, and runs on
+  // one CTA per tile: with peer stores in the epilogue the CTA-pair form
+  // measured slower on B200 (cfg 5 split over 2 GPUs: 4.04-4.08 ms fused
+  // against 3.85 ms one-CTA, while the pair is faster without peers). Both
+  // forms give the same bits.
+  if (nreplicas > 0) {
+    plan.split = 1;
+    plan.pair = 1;
+  }
   if (plan.pair != 1 && (plan.pair != 2 || plan.split != 1 || plan.block_n < 128))
     return fail(HXB_STATUS_INVALID_ARGUMENT,
                 "matmul: a CTA pair (256-row tiles) needs block_n 128 or 256 and no split_k");
