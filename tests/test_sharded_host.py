@@ -1,6 +1,6 @@
 """Host logic of the N-sharded matmul: the column
 split and the once-per-run exchange of peer-buffer handles, run as gloo ranks
-on the CPU (world size 2 and 3)."""
+on the CPU (world size 2, 3 and 8)."""
 from __future__ import annotations
 
 import os
@@ -64,7 +64,7 @@ def _exchange_worker(rank, world, port, results):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("world", [2, 3, 8])
 def test_peer_handle_exchange_gloo(world):
     ctx = mp.get_context("spawn")
     with ctx.Manager() as mgr:
