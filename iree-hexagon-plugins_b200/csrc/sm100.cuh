@@ -203,16 +203,6 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map,
       : "memory");
 }
 
-__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map,
-                                            uint64_t* bar, int x, int y,
-                                            int z) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_"
-      "tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
-      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
-      : "memory");
-}
-
 // Asks the TMA unit to bring a 2-D box of `map` into L2 (no shared-memory
 // destination, no completion signal). x is the innermost coordinate. L2 is
 // the device's point of coherence, so a prefetch issued before
@@ -520,20 +510,6 @@ __host__ __device__ constexpr uint32_t make_idesc_f16(int M, int N, int a_mn,
 }
 
 // --------------------------------------------------------------- numerics
-// Exact int8 -> f16 for four packed signed bytes: biasing to unsigned and
-// splicing each byte under the f16 exponent of 1024 gives 1024 + (b + 128)
-// exactly; subtracting 1152 leaves b. Produces {b0,b1} and {b2,b3}.
-__device__ __forceinline__ void i8x4_to_f16x4(uint32_t packed, uint32_t& lo,
-                                              uint32_t& hi) {
-  const uint32_t u = packed ^ 0x80808080u;
-  uint32_t a, b;
-  asm("prmt.b32 %0, %1, %2, 0x4140;" : "=r"(a) : "r"(u), "r"(0x64646464u));
-  asm("prmt.b32 %0, %1, %2, 0x4342;" : "=r"(b) : "r"(u), "r"(0x64646464u));
-  const uint32_t bias = 0x64806480u;  // {1152, 1152}
-  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(lo) : "r"(a), "r"(bias));
-  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(hi) : "r"(b), "r"(bias));
-}
-
 __device__ __forceinline__ uint32_t pack_half2(float x, float y) {
   __half2 h = __floats2half2_rn(x, y);
   return *reinterpret_cast<uint32_t*>(&h);
