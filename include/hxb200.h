@@ -103,7 +103,7 @@ hxb_status_t hxb_matmul_f16(const void* A, int64_t lda, const void* B,
                             size_t workspace_bytes, void* stream);
 
 /* The tile plan hxb_matmul_f16 uses for a shape on a device with num_sms SMs:
- * the N extent of one output tile (64, 128 or 256), the raster group (tile
+ * the N extent of one output tile (64, 128, 256, or 512 on a CTA pair), the raster group (tile
  * rows swept together for L2 reuse), the K split and the CTA pairing. split_k
  * 1 runs a persistent kernel walking whole tiles; 2, 4 or 8 run one
  * thread-block cluster of that many CTAs per 128-row tile, each on its share
@@ -122,9 +122,10 @@ hxb_status_t hxb_plan_matmul_f16(int64_t M, int64_t N, int64_t K, int transpose_
 
 /* hxb_matmul_f16 (no init, no re-pitching) with the tile plan given
  * explicitly instead of planned: the entry the offline tile sweep measures
- * candidates through. block_n in {64, 128, 256}; group_m >= 1; split_k in
- * {1, 2, 4, 8} with at least split_k 64-deep K-blocks; cta_pair 1, or 2 with
- * split_k 1 and block_n 128 or 256. */
+ * candidates through. block_n in {64, 128, 256}, or 512 with cta_pair 2 (two
+ * 256-column MMA chunks per operand stage, one TMEM accumulator); group_m >= 1;
+ * split_k in {1, 2, 4, 8} with at least split_k 64-deep K-blocks; cta_pair 1,
+ * or 2 with split_k 1 and block_n 128, 256 or 512. */
 hxb_status_t hxb_matmul_f16_tiled(const void* A, int64_t lda, const void* B,
                                   int64_t ldb, int transpose_b, void* C,
                                   int64_t ldc, hxb_dtype_t c_dtype, int64_t M,

@@ -127,6 +127,7 @@ hxb_status_t launch_planned(const GemmPlan& plan, const DeviceInfo& dev,
     if (plan.split != 1)
       return fail(HXB_STATUS_UNSUPPORTED, "no CTA-pair kernel with split_k=%d", plan.split);
     switch (plan.block_n) {
+      case 512: return launch_gemm_pair<512, 4, BMODE, OUT>(dev, tmA, tmB, args, stream);
       case 256: return launch_gemm_pair<256, 6, BMODE, OUT>(dev, tmA, tmB, args, stream);
       case 128: return launch_gemm_pair<128, 8, BMODE, OUT>(dev, tmA, tmB, args, stream);
       default: break;
@@ -235,10 +236,13 @@ hxb_status_t gemm_f16_launch(const void* A, int64_t lda, const void* B, int64_t 
   if (nreplicas > 0) {
     plan.split = 1;
     plan.pair = 1;
+    if (plan.block_n > 256) plan.block_n = 256;
   }
-  if (plan.pair != 1 && (plan.pair != 2 || plan.split != 1 || plan.block_n < 128))
+  if ((plan.pair != 1 && (plan.pair != 2 || plan.split != 1 || plan.block_n < 128)) ||
+      (plan.block_n > 256 && plan.pair != 2))
     return fail(HXB_STATUS_INVALID_ARGUMENT,
-                "matmul: a CTA pair (256-row tiles) needs block_n 128 or 256 and no split_k");
+                "matmul: a CTA pair (256-row tiles) needs block_n 128, 256 or 512 and no split_k; "
+                "block_n 512 only on a pair");
   if (plan.split > 1 && (plan.split > 8 || (plan.split & (plan.split - 1)) ||
                          (K + kBK - 1) / kBK < plan.split))
     return fail(HXB_STATUS_INVALID_ARGUMENT,
@@ -256,7 +260,9 @@ hxb_status_t gemm_f16_launch(const void* A, int64_t lda, const void* B, int64_t 
     const uint64_t dims[2] = {(uint64_t)K, (uint64_t)N};
     const uint64_t strides[1] = {(uint64_t)ldb * 2};
     // a CTA of a pair loads half of the tile's B rows
-    const uint32_t box[2] = {64, (uint32_t)(plan.block_n / plan.pair)};
+    // one box per MMA chunk (at most 256 columns) and CTA
+    const uint32_t box[2] = {64, (uint32_t)((plan.block_n > 256 ? 256 : plan.block_n) /
+                                            plan.pair)};
     s = encode_tensor_map(&tmB, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, B, dims,
                           strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
   } else {
@@ -846,8 +852,9 @@ extern "C" hxb_status_t hxb_matmul_f16_tiled(const void* A, int64_t lda, const v
                                              int block_n, int group_m, int split_k,
                                              int cta_pair, void* stream) {
   using namespace hxb;
-  if (block_n != 64 && block_n != 128 && block_n != 256)
-    return fail(HXB_STATUS_INVALID_ARGUMENT, "matmul_f16_tiled: block_n must be 64, 128 or 256");
+  if (block_n != 64 && block_n != 128 && block_n != 256 && !(block_n == 512 && cta_pair == 2))
+    return fail(HXB_STATUS_INVALID_ARGUMENT,
+                "matmul_f16_tiled: block_n must be 64, 128 or 256 (512 on a CTA pair)");
   if (split_k != 1 && split_k != 2 && split_k != 4 && split_k != 8)
     return fail(HXB_STATUS_INVALID_ARGUMENT, "matmul_f16_tiled: split_k must be 1, 2, 4 or 8");
   if (cta_pair != 1 && (cta_pair != 2 || split_k != 1 || block_n == 64))

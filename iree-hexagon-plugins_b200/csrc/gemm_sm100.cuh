@@ -78,7 +78,10 @@ template <int BN, int BMODE>
 struct GemmShape {
   static constexpr int kWarps = 6;
   static constexpr int kThreads = kWarps * 32;
-  static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
+  // accumulator buffers in TMEM: two (the epilogue of one tile overlaps the
+  // next tile's main loop) unless a 512-column tile fills TMEM with one
+  static constexpr int kAccBufs = 2 * BN <= 512 ? 2 : 1;
+  static constexpr int kTmemCols = kAccBufs * BN < 32 ? 32 : kAccBufs * BN;
 };
 
 __device__ __forceinline__ void tile_coords(int t, const GemmArgs& a,
@@ -196,12 +199,21 @@ __global__ void __launch_bounds__(GemmShape<BN, BMODE>::kThreads, 1)
                       const __grid_constant__ CUtensorMap tmB,
                       const GemmArgs args) {
   static_assert(PAIR == 1 || PAIR == 2, "one CTA or a CTA pair per tile");
+  static_assert(BN <= 256 || PAIR == 2, "512-column tiles only on CTA pairs");
   constexpr int kBNC = BN / PAIR;     // B columns this CTA loads
   constexpr int kTileM = kBM * PAIR;  // output rows of a tile
+  // N of one MMA (at most 256): a 512-column pair tile is two MMA chunks
+  // sharing each A stage; chunk j covers tile columns [256 j, 256 j + 256),
+  // of which this CTA loads kChunkCols at rank * kChunkCols.
+  constexpr int kMmaN = BN > 256 ? 256 : BN;
+  constexpr int kChunks = BN / kMmaN;
+  constexpr int kChunkCols = kMmaN / PAIR;
+  constexpr int kChunkBytes = kChunkCols * kBK * 2;
+  constexpr int kAccBufs = GemmShape<BN, BMODE>::kAccBufs;
   using L = GemmSmem<kBNC, STAGES, BMODE>;
   constexpr int kTmemCols = GemmShape<BN, BMODE>::kTmemCols;
   constexpr uint32_t kIdesc =
-      make_idesc_f16(kTileM, BN, 0, BMODE == kBF16RowMajorNK ? 0 : 1);
+      make_idesc_f16(kTileM, kMmaN, 0, BMODE == kBF16RowMajorNK ? 0 : 1);
   // the (leader's) full barrier counts the bytes of every CTA of the tile
   constexpr uint32_t kTxBytes = (L::kABytes + L::kBBytes) * PAIR;
 
@@ -276,16 +288,19 @@ __global__ void __launch_bounds__(GemmShape<BN, BMODE>::kThreads, 1)
         int tm0, tn0;
         tile_coords(unit, args, tm0, tn0);
         const int a_row0 = tm0 * kTileM + (int)rank * kBM;
-        const int b_col0 = tn0 * BN + (int)rank * kBNC;
         const int pre = num_kb < STAGES ? num_kb : STAGES;
         for (int kb = 0; kb < pre; ++kb) {
           tma_prefetch_l2_2d(&tmA, kb * kBK, a_row0);
-          if constexpr (BMODE == kBF16RowMajorKN) {
 #pragma unroll
-            for (int j = 0; j < kBNC / 64; ++j)
-              tma_prefetch_l2_2d(&tmB, b_col0 + 64 * j, kb * kBK);
-          } else {
-            tma_prefetch_l2_2d(&tmB, kb * kBK, b_col0);
+          for (int c = 0; c < kChunks; ++c) {
+            const int b_col0 = tn0 * BN + c * kMmaN + (int)rank * kChunkCols;
+            if constexpr (BMODE == kBF16RowMajorKN) {
+#pragma unroll
+              for (int j = 0; j < kChunkCols / 64; ++j)
+                tma_prefetch_l2_2d(&tmB, b_col0 + 64 * j, kb * kBK);
+            } else {
+              tma_prefetch_l2_2d(&tmB, kb * kBK, b_col0);
+            }
           }
         }
       }
@@ -298,7 +313,7 @@ __global__ void __launch_bounds__(GemmShape<BN, BMODE>::kThreads, 1)
         int tm, tn;
         tile_coords(t, args, tm, tn);
         const int a_row = tm * kTileM + (int)rank * kBM;
-        const int b_col = tn * BN + (int)rank * kBNC;
+        const int b_col = tn * BN + (int)rank * kChunkCols;  // chunk c adds c * kMmaN
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, fs)) { ok = false; break; }
           uint8_t* a_dst = smem + L::kOffA + stage * L::kABytes;
@@ -306,13 +321,17 @@ __global__ void __launch_bounds__(GemmShape<BN, BMODE>::kThreads, 1)
           if constexpr (PAIR == 1) {
             mbar_arrive_expect_tx(&full[stage], kTxBytes);
             tma_load_2d(a_dst, &tmA, &full[stage], kb * kBK, a_row);
-            if constexpr (BMODE == kBF16RowMajorKN) {
 #pragma unroll
-              for (int j = 0; j < kBNC / 64; ++j)
-                tma_load_2d(b_dst + j * (kBK * 128), &tmB, &full[stage], b_col + 64 * j,
-                            kb * kBK);
-            } else {
-              tma_load_2d(b_dst, &tmB, &full[stage], kb * kBK, b_col);
+            for (int c = 0; c < kChunks; ++c) {
+              if constexpr (BMODE == kBF16RowMajorKN) {
+#pragma unroll
+                for (int j = 0; j < kChunkCols / 64; ++j)
+                  tma_load_2d(b_dst + c * kChunkBytes + j * (kBK * 128), &tmB, &full[stage],
+                              b_col + c * kMmaN + 64 * j, kb * kBK);
+              } else {
+                tma_load_2d(b_dst + c * kChunkBytes, &tmB, &full[stage], kb * kBK,
+                            b_col + c * kMmaN);
+              }
             }
           } else {
             // both CTAs' bytes complete on the leader's barrier; only the
@@ -321,13 +340,17 @@ __global__ void __launch_bounds__(GemmShape<BN, BMODE>::kThreads, 1)
             if (leader) mbar_arrive_expect_tx(&full[stage], kTxBytes);
             const uint32_t bar = map_to_rank(smem_u32(&full[stage]), 0);
             tma_load_2d_pair(a_dst, &tmA, bar, kb * kBK, a_row);
-            if constexpr (BMODE == kBF16RowMajorKN) {
 #pragma unroll
-              for (int j = 0; j < kBNC / 64; ++j)
-                tma_load_2d_pair(b_dst + j * (kBK * 128), &tmB, bar, b_col + 64 * j,
-                                 kb * kBK);
-            } else {
-              tma_load_2d_pair(b_dst, &tmB, bar, kb * kBK, b_col);
+            for (int c = 0; c < kChunks; ++c) {
+              if constexpr (BMODE == kBF16RowMajorKN) {
+#pragma unroll
+                for (int j = 0; j < kChunkCols / 64; ++j)
+                  tma_load_2d_pair(b_dst + c * kChunkBytes + j * (kBK * 128), &tmB, bar,
+                                   b_col + c * kMmaN + 64 * j, kb * kBK);
+              } else {
+                tma_load_2d_pair(b_dst + c * kChunkBytes, &tmB, bar, kb * kBK,
+                                 b_col + c * kMmaN);
+              }
             }
           }
           ++issued;
@@ -359,8 +382,8 @@ __global__ void __launch_bounds__(GemmShape<BN, BMODE>::kThreads, 1)
       bool ok = true;
       bool issued_any = false;
       for (int t = unit; t < num_tiles && ok; t += units, ++tl) {
-        const int acc = tl & 1;
-        const uint32_t acc_phase = (tl >> 1) & 1;
+        const int acc = tl % kAccBufs;
+        const uint32_t acc_phase = (tl / kAccBufs) & 1;
         // (a pair's tempty collects the peer's epilogue arrivals too)
         const bool free_acc = PAIR == 1 ? mbar_wait(&tempty[acc], acc_phase ^ 1, fs)
                                         : mbar_wait_cluster(&tempty[acc], acc_phase ^ 1, fs);
@@ -376,16 +399,19 @@ __global__ void __launch_bounds__(GemmShape<BN, BMODE>::kThreads, 1)
           for (int k = 0; k < kBK / 16; ++k) {
             const uint64_t adesc =
                 make_smem_desc(a_addr + k * 32, 16, 1024, kLayoutSwizzle128);
-            uint64_t bdesc;
-            if (BMODE == kBF16RowMajorNK)
-              bdesc = make_smem_desc(b_addr + k * 32, 16, 1024, kLayoutSwizzle128);
-            else
-              bdesc = make_smem_desc(b_addr + k * 16 * 128, kBK * 128, 1024,
-                                     kLayoutSwizzle128);
-            if constexpr (PAIR == 1)
-              umma_f16_ss(d_tmem, adesc, bdesc, kIdesc, (kb | k) != 0);
-            else
-              umma_f16_ss_pair(d_tmem, adesc, bdesc, kIdesc, (kb | k) != 0);
+#pragma unroll
+            for (int c = 0; c < kChunks; ++c) {
+              const uint32_t bc = b_addr + c * kChunkBytes;
+              uint64_t bdesc;
+              if (BMODE == kBF16RowMajorNK)
+                bdesc = make_smem_desc(bc + k * 32, 16, 1024, kLayoutSwizzle128);
+              else
+                bdesc = make_smem_desc(bc + k * 16 * 128, kBK * 128, 1024, kLayoutSwizzle128);
+              if constexpr (PAIR == 1)
+                umma_f16_ss(d_tmem + c * kMmaN, adesc, bdesc, kIdesc, (kb | k) != 0);
+              else
+                umma_f16_ss_pair(d_tmem + c * kMmaN, adesc, bdesc, kIdesc, (kb | k) != 0);
+            }
           }
           issued_any = true;
           if constexpr (PAIR == 1) {
@@ -421,8 +447,8 @@ __global__ void __launch_bounds__(GemmShape<BN, BMODE>::kThreads, 1)
     for (int t = unit; t < num_tiles; t += units, ++tl) {
       int tm, tn;
       tile_coords(t, args, tm, tn);
-      const int acc = tl & 1;
-      const uint32_t acc_phase = (tl >> 1) & 1;
+      const int acc = tl % kAccBufs;
+      const uint32_t acc_phase = (tl / kAccBufs) & 1;
       const bool ready = mbar_wait(&tfull[acc], acc_phase, fs);
       // tcgen05.ld is .sync.aligned: reconverge and agree before touching TMEM
       if (!__all_sync(0xffffffffu, ready)) break;

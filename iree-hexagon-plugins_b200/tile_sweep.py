@@ -9,7 +9,8 @@ MEASURES every tile plan the tcgen05 kernels offer -- the N extent of a
 kernel, the K split over a thread-block cluster (2, 4, 8 CTAs per tile,
 partials summed in distributed shared memory) and the CTA pair (256-row
 tiles computed by cta_group::2 MMAs on two SMs, each loading half of the
-operands) -- on each shape and keeps the fastest. The winners are written as the C table
+operands; block_n 512 as two 256-column MMA chunks per A stage with one TMEM
+accumulator) -- on each shape and keeps the fastest. The winners are written as the C table
 csrc/tile_table.inc, which is compiled into libhxb200.so and consulted by the
 planner before its cost model (planner.h), i.e. the search result is baked
 into the executable, keyed by dispatch shape.
@@ -81,13 +82,16 @@ def sweep(shapes, *, group_choices=(1, 4, 8, 16)) -> list[dict]:
         tiles_m = (M + 127) // 128
         kb = (K + 63) // 64
         cands = []
-        for bn in (64, 128, 256):
+        for bn in (64, 128, 256, 512):
             tiles = tiles_m * ((N + bn - 1) // bn)
-            plans = [(gm, 1, 1) for gm in sorted({min(g, tiles_m) for g in group_choices})]
-            # split-K: clusters of 2, 4, 8 CTAs per tile, one wave, >= 2 K-blocks each
-            plans += [(1, sk, 1) for sk in (2, 4, 8) if kb >= 2 * sk and tiles * sk <= sms]
-            # CTA pairs: 256-row tiles on two SMs (block_n 128 or 256)
-            if bn >= 128 and M > 128:
+            plans = []
+            if bn <= 256:
+                plans += [(gm, 1, 1) for gm in sorted({min(g, tiles_m) for g in group_choices})]
+                # split-K: clusters of 2, 4, 8 CTAs per tile, one wave, >= 2 K-blocks each
+                plans += [(1, sk, 1) for sk in (2, 4, 8) if kb >= 2 * sk and tiles * sk <= sms]
+            # CTA pairs: 256-row tiles on two SMs (block_n 128, 256, or 512 as two
+            # MMA chunks sharing each A stage)
+            if bn >= 128 and M > 128 and (bn <= 256 or N >= 512):
                 pair_m = (M + 255) // 256
                 plans += [(gm, 1, 2) for gm in sorted({min(g, pair_m) for g in group_choices})]
             for gm, sk, pair in plans:

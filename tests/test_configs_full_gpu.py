@@ -100,7 +100,7 @@ def test_cfg5b_sweep_shape_with_table_plan(cuda_pkg, oracle, M, N, K):
     cuda_pkg._native.check(lib.hxb_plan_matmul_f16(M, N, K, 0, sms, ctypes.byref(bn),
                                                    ctypes.byref(gm), ctypes.byref(sk),
                                                    ctypes.byref(pair)))
-    assert bn.value in (64, 128, 256) and gm.value >= 1 and sk.value in (1, 2, 4, 8)
+    assert bn.value in (64, 128, 256, 512) and gm.value >= 1 and sk.value in (1, 2, 4, 8)
     assert pair.value in (1, 2) and (pair.value == 1 or sk.value == 1)
     rng = np.random.default_rng(M + 3 * N + 7 * K)
     a = rng.uniform(-1, 1, (M, K)).astype(np.float16)

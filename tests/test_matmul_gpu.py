@@ -194,6 +194,10 @@ def test_split_k_cluster_kernel(cuda_pkg, oracle, M, N, K, bn, sk, tb, out):
     (129, 264, 520, 128, 2, True, torch.float16),       # one tile row, ragged everything
     (4096, 384, 4096, 128, 16, False, torch.float16),
     (512, 8192, 512, 256, 4, True, torch.float16),
+    # 512-column pair tiles: two N = 256 MMA chunks per A stage, one accumulator
+    (2048, 4096, 2048, 512, 8, False, torch.float16),
+    (300, 1000, 1000, 512, 1, True, torch.float32),
+    (1024, 1536, 512, 512, 4, False, torch.float32),
 ])
 def test_cta_pair_kernel(cuda_pkg, oracle, M, N, K, bn, gm, tb, out):
     """The CTA-pair kernel (256-row tiles, cta_group::2 MMAs issued by the
@@ -225,12 +229,12 @@ def test_cta_pair_kernel(cuda_pkg, oracle, M, N, K, bn, gm, tb, out):
 
 
 def test_cta_pair_rejects_split_and_narrow_tiles(cuda_pkg):
-    """A CTA pair takes block_n 128 or 256 and no K split."""
+    """A CTA pair takes block_n 128, 256 or 512 and no K split; 512 needs a pair."""
     lib = cuda_pkg._native.load()
     a = torch.zeros(256, 256, dtype=torch.float16, device=DEV)
-    for bn, sk in ((64, 1), (256, 2)):
+    for bn, sk, pair in ((64, 1, 2), (256, 2, 2), (512, 1, 1)):
         st = lib.hxb_matmul_f16_tiled(a.data_ptr(), 256, a.data_ptr(), 256, 0, a.data_ptr(), 256,
-                                      0, 256, 256, 256, bn, 1, sk, 2, None)
+                                      0, 256, 256, 256, bn, 1, sk, pair, None)
         assert st == 1
 
 
