@@ -17,9 +17,11 @@ the tcgen05 GEMM. The gathered C is produced one of two ways:
     the ranks exchange CUDA IPC handles of these buffers once, and the GEMM's
     epilogue writes each output tile into all G buffers -- its own and, over
     NVLink, the peers' -- at the shard's columns
-    (hxb_matmul_f16_allgather). A stream-ordered collective after the GEMM
-    tells every rank that all peers' tiles have landed. No gather copy and no
-    layout fix-up remain.
+    (hxb_matmul_f16_allgather). A stream-ordered peer barrier
+    (hxb_peer_barrier, flags in the same IPC-shared allocation) before the
+    GEMM keeps a rank from overwriting a peer's C while that peer still reads
+    the previous result, and one after it tells every rank that all peers'
+    tiles have landed. No gather copy and no layout fix-up remain.
   * "nccl" (the baseline it is measured against): GEMM into a local shard,
     NCCL all-gather of the shards into [G, M, N/G], then the [G, M, n] ->
     [M, N] layout step (hxb_gather_column_blocks_f16).
