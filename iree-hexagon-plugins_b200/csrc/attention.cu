@@ -52,6 +52,16 @@ constexpr int kAttBN = 128;      // keys per block
 constexpr int kAttBoxBytes = 128 * 64 * 2;      // one TMA box: 128 rows x 64 f16
 constexpr float kRescaleLog2 = 8.0f;
 constexpr int kAttThreads = 384;
+// Registers per thread: the launch gives every warp kAttRegsLaunch (the
+// __launch_bounds__ limit for 384 threads on one SM); then the TMA / MMA
+// warpgroup drops to kAttRegsControl and the two softmax warpgroups, which
+// hold a 128-score row per thread, rise to kAttRegsSoftmax.
+constexpr int kAttRegsLaunch = 168;
+constexpr int kAttRegsControl = 56;
+constexpr int kAttRegsSoftmax = 224;
+static_assert(kAttRegsControl * 128 + kAttRegsSoftmax * (kAttThreads - 128) <=
+                  kAttRegsLaunch * kAttThreads,
+              "register split exceeds the launch allocation");
 
 // Shared-memory plan for head dimension D (64 or 128): a Q, K or V tile is
 // D/64 boxes of [128 rows x 64] f16; the K/V ring keeps 128 KB of tiles
@@ -225,118 +235,124 @@ __global__ void __launch_bounds__(kAttThreads, 1)
   pdl_trigger();
   pdl_wait();
 
-  if (warp == 0) {
-    // -------------------------------------------------------- TMA producer
-    if (lane == 0 && n_kv > 0) {
-      // a short Q (decode: a group's few rows) loads only q_box rows; the
-      // rest of the tile keeps stale bytes, which reach only rows not stored
-      mbar_arrive_expect_tx(q_full, n_tiles * L::kBoxes * args.q_box * 128);
-      for (int t = 0; t < n_tiles; ++t)
-        for (int b = 0; b < L::kBoxes; ++b)
-          tma_load_2d(smem + L::kOffQ + t * kAttTileBytes + b * kAttBoxBytes, &tmQ, q_full,
-                      qx + 64 * b, qy * args.Sq + q0 + t * kAttBM);
-      Cursor<kAttSlots> c;
-      int issued = 0;
-      bool ok = true;
-      for (int j = 0; j < n_kv && ok; ++j) {
-        for (int which = 0; which < 2; ++which) {  // K_j then V_j
-          if (!mbar_wait(&kv_empty[c.slot], c.phase ^ 1, fs)) {
-            ok = false;
-            break;
-          }
-          mbar_arrive_expect_tx(&kv_full[c.slot], kAttTileBytes);
-          const CUtensorMap* map = which ? &tmV : &tmK;
+  // (each warpgroup changes its register count inside its own branch, so that
+  // the compiler allocates each branch for the count it runs with)
+  if (warp < 4) {
+    reg_dealloc<kAttRegsControl>();  // warps 2-3 stay idle
+    if (warp == 0) {
+      // -------------------------------------------------------- TMA producer
+      if (lane == 0 && n_kv > 0) {
+        // a short Q (decode: a group's few rows) loads only q_box rows; the
+        // rest of the tile keeps stale bytes, which reach only rows not stored
+        mbar_arrive_expect_tx(q_full, n_tiles * L::kBoxes * args.q_box * 128);
+        for (int t = 0; t < n_tiles; ++t)
           for (int b = 0; b < L::kBoxes; ++b)
-            tma_load_2d(smem + L::kOffKV + c.slot * kAttTileBytes + b * kAttBoxBytes, map,
-                        &kv_full[c.slot], kx + 64 * b,
-                        (int)(ky * args.kv_stride) + (j0 + j) * kAttBN);
-          c.advance();
-          ++issued;
+            tma_load_2d(smem + L::kOffQ + t * kAttTileBytes + b * kAttBoxBytes, &tmQ, q_full,
+                        qx + 64 * b, qy * args.Sq + q0 + t * kAttBM);
+        Cursor<kAttSlots> c;
+        int issued = 0;
+        bool ok = true;
+        for (int j = 0; j < n_kv && ok; ++j) {
+          for (int which = 0; which < 2; ++which) {  // K_j then V_j
+            if (!mbar_wait(&kv_empty[c.slot], c.phase ^ 1, fs)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&kv_full[c.slot], kAttTileBytes);
+            const CUtensorMap* map = which ? &tmV : &tmK;
+            for (int b = 0; b < L::kBoxes; ++b)
+              tma_load_2d(smem + L::kOffKV + c.slot * kAttTileBytes + b * kAttBoxBytes, map,
+                          &kv_full[c.slot], kx + 64 * b,
+                          (int)(ky * args.kv_stride) + (j0 + j) * kAttBN);
+            c.advance();
+            ++issued;
+          }
+        }
+        // bounded wait for the copies still landing (complete on the normal path)
+        const unsigned long long t0 = globaltimer_ns();
+        while (!mbar_try_wait(q_full, 0) && globaltimer_ns() - t0 < kWaitLimitNs) {
+        }
+        for (int i = 0; i < issued && i < kAttSlots; ++i) {
+          if (c.slot == 0) {
+            c.slot = kAttSlots - 1;
+            c.phase ^= 1u;
+          } else {
+            --c.slot;
+          }
+          const unsigned long long t1 = globaltimer_ns();
+          while (!mbar_try_wait(&kv_full[c.slot], c.phase) &&
+                 globaltimer_ns() - t1 < kWaitLimitNs) {
+          }
         }
       }
-      // bounded wait for the copies still landing (complete on the normal path)
-      const unsigned long long t0 = globaltimer_ns();
-      while (!mbar_try_wait(q_full, 0) && globaltimer_ns() - t0 < kWaitLimitNs) {
-      }
-      for (int i = 0; i < issued && i < kAttSlots; ++i) {
-        if (c.slot == 0) {
-          c.slot = kAttSlots - 1;
-          c.phase ^= 1u;
-        } else {
-          --c.slot;
-        }
-        const unsigned long long t1 = globaltimer_ns();
-        while (!mbar_try_wait(&kv_full[c.slot], c.phase) &&
-               globaltimer_ns() - t1 < kWaitLimitNs) {
-        }
-      }
-    }
-  } else if (warp == 1) {
-    // -------------------------------------------------------- MMA issuer
-    if (lane == 0 && n_kv > 0) {
-      bool ok = mbar_wait(q_full, 0, fs);
-      bool issued_any = false;
-      Cursor<kAttSlots> c;
-      const uint32_t q_addr = smem_u32(smem + L::kOffQ);
-      const uint32_t kv_addr = smem_u32(smem + L::kOffKV);
-      // S_t(0) = Q_t K_0^T
-      int kslot = c.slot;
-      if (ok) ok = mbar_wait(&kv_full[kslot], c.phase, fs);
-      c.advance();
-      if (ok) {
-        tc_fence_after();
-        for (int t = 0; t < n_tiles; ++t) {
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk)
-            umma_f16_ss(tmem_base + t * 128, kmajor_desc(q_addr + t * kAttTileBytes, kk),
-                        kmajor_desc(kv_addr + kslot * kAttTileBytes, kk), kIdescQK, kk != 0);
-          umma_commit(&s_full[t]);
-        }
-        umma_commit(&kv_empty[kslot]);
-        issued_any = true;
-      }
-      for (int j = 0; j < n_kv && ok; ++j) {
-        const int vslot = c.slot;
-        if (!mbar_wait(&kv_full[vslot], c.phase, fs)) { ok = false; break; }
+    } else if (warp == 1) {
+      // -------------------------------------------------------- MMA issuer
+      if (lane == 0 && n_kv > 0) {
+        bool ok = mbar_wait(q_full, 0, fs);
+        bool issued_any = false;
+        Cursor<kAttSlots> c;
+        const uint32_t q_addr = smem_u32(smem + L::kOffQ);
+        const uint32_t kv_addr = smem_u32(smem + L::kOffKV);
+        // S_t(0) = Q_t K_0^T
+        int kslot = c.slot;
+        if (ok) ok = mbar_wait(&kv_full[kslot], c.phase, fs);
         c.advance();
-        const bool has_next = j + 1 < n_kv;
-        if (has_next) {
-          kslot = c.slot;
-          if (!mbar_wait(&kv_full[kslot], c.phase, fs)) { ok = false; break; }
-          c.advance();
-        }
-        for (int t = 0; t < n_tiles && ok; ++t) {
-          if (!mbar_wait(&p_full[t], (uint32_t)(j & 1), fs)) { ok = false; break; }
+        if (ok) {
           tc_fence_after();
-          const uint32_t o_tmem = tmem_base + 256 + t * D;
-          const uint32_t p_tmem = tmem_base + t * 128 + 64;
-#pragma unroll
-          for (int kk = 0; kk < kAttBN / 16; ++kk)
-            umma_f16_ts(o_tmem, p_tmem + kk * 8, vmajor_desc(kv_addr + vslot * kAttTileBytes, kk),
-                        kIdescPV, (j | kk) != 0);
-          if (has_next) {
+          for (int t = 0; t < n_tiles; ++t) {
 #pragma unroll
             for (int kk = 0; kk < D / 16; ++kk)
               umma_f16_ss(tmem_base + t * 128, kmajor_desc(q_addr + t * kAttTileBytes, kk),
                           kmajor_desc(kv_addr + kslot * kAttTileBytes, kk), kIdescQK, kk != 0);
             umma_commit(&s_full[t]);
           }
+          umma_commit(&kv_empty[kslot]);
+          issued_any = true;
         }
-        if (!ok) break;
-        umma_commit(&kv_empty[vslot]);
-        if (has_next) umma_commit(&kv_empty[kslot]);
-      }
-      if (ok) {
-        umma_commit(o_full);
-      } else if (issued_any) {
-        umma_commit(drain);
-        const unsigned long long t0 = globaltimer_ns();
-        while (!mbar_try_wait(drain, 0) && globaltimer_ns() - t0 < kWaitLimitNs) {
+        for (int j = 0; j < n_kv && ok; ++j) {
+          const int vslot = c.slot;
+          if (!mbar_wait(&kv_full[vslot], c.phase, fs)) { ok = false; break; }
+          c.advance();
+          const bool has_next = j + 1 < n_kv;
+          if (has_next) {
+            kslot = c.slot;
+            if (!mbar_wait(&kv_full[kslot], c.phase, fs)) { ok = false; break; }
+            c.advance();
+          }
+          for (int t = 0; t < n_tiles && ok; ++t) {
+            if (!mbar_wait(&p_full[t], (uint32_t)(j & 1), fs)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t o_tmem = tmem_base + 256 + t * D;
+            const uint32_t p_tmem = tmem_base + t * 128 + 64;
+#pragma unroll
+            for (int kk = 0; kk < kAttBN / 16; ++kk)
+              umma_f16_ts(o_tmem, p_tmem + kk * 8, vmajor_desc(kv_addr + vslot * kAttTileBytes, kk),
+                          kIdescPV, (j | kk) != 0);
+            if (has_next) {
+#pragma unroll
+              for (int kk = 0; kk < D / 16; ++kk)
+                umma_f16_ss(tmem_base + t * 128, kmajor_desc(q_addr + t * kAttTileBytes, kk),
+                            kmajor_desc(kv_addr + kslot * kAttTileBytes, kk), kIdescQK, kk != 0);
+              umma_commit(&s_full[t]);
+            }
+          }
+          if (!ok) break;
+          umma_commit(&kv_empty[vslot]);
+          if (has_next) umma_commit(&kv_empty[kslot]);
+        }
+        if (ok) {
+          umma_commit(o_full);
+        } else if (issued_any) {
+          umma_commit(drain);
+          const unsigned long long t0 = globaltimer_ns();
+          while (!mbar_try_wait(drain, 0) && globaltimer_ns() - t0 < kWaitLimitNs) {
+          }
         }
       }
-    }
-  } else if (warp >= 4) {
+  }
+  } else {
     // -------------------------------------------------------- softmax
+    reg_alloc<kAttRegsSoftmax>();
     const int t = (warp - 4) >> 2;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
@@ -1016,9 +1032,16 @@ hxb_status_t launch_d(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUte
                       const AttArgs& args, int64_t heads, int ordinal, cudaStream_t stream) {
   static bool configured[64] = {};
   if (!configured[ordinal]) {
-    cudaError_t e = cudaFuncSetAttribute(attention_fwd_kernel<D>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         AttSmem<D>::kAlloc);
+    // the kernel's register split assumes this launch count; with fewer
+    // registers at launch its increase could never be granted
+    cudaFuncAttributes fa{};
+    cudaError_t e = cudaFuncGetAttributes(&fa, attention_fwd_kernel<D>);
+    if (e != cudaSuccess) return cuda_status(e, "cudaFuncGetAttributes(attention)");
+    if (fa.numRegs != kAttRegsLaunch)
+      return fail(HXB_STATUS_UNSUPPORTED, "attention kernel built with %d registers per thread, "
+                  "its register split needs %d", fa.numRegs, kAttRegsLaunch);
+    e = cudaFuncSetAttribute(attention_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             AttSmem<D>::kAlloc);
     if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(attention)");
     configured[ordinal] = true;
   }

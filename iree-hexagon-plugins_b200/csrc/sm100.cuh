@@ -415,6 +415,21 @@ __device__ __forceinline__ void tmem_wait_st() {
 }
 
 // 2^x on the special-function unit (PTX ex2.approx, flush-to-zero).
+// Per-warpgroup register reallocation: every warp of a warpgroup executes the
+// same setmaxnreg. The counts after all increases must fit in the registers the
+// block was launched with (threads x registers per thread at launch), or the
+// increasing warps wait for good; callers check the launch count on the host.
+template <int N>
+__device__ __forceinline__ void reg_dealloc() {
+  static_assert(N % 8 == 0 && N >= 24 && N <= 256, "setmaxnreg count");
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void reg_alloc() {
+  static_assert(N % 8 == 0 && N >= 24 && N <= 256, "setmaxnreg count");
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
