@@ -57,8 +57,8 @@ constexpr int kAttThreads = 384;
 // warpgroup drops to kAttRegsControl and the two softmax warpgroups, which
 // hold a 128-score row per thread, rise to kAttRegsSoftmax.
 constexpr int kAttRegsLaunch = 168;
-constexpr int kAttRegsControl = 56;
-constexpr int kAttRegsSoftmax = 224;
+constexpr int kAttRegsControl = 104;
+constexpr int kAttRegsSoftmax = 200;
 static_assert(kAttRegsControl * 128 + kAttRegsSoftmax * (kAttThreads - 128) <=
                   kAttRegsLaunch * kAttThreads,
               "register split exceeds the launch allocation");
@@ -291,19 +291,31 @@ __global__ void __launch_bounds__(kAttThreads, 1)
         bool ok = mbar_wait(q_full, 0, fs);
         bool issued_any = false;
         Cursor<kAttSlots> c;
-        const uint32_t q_addr = smem_u32(smem + L::kOffQ);
-        const uint32_t kv_addr = smem_u32(smem + L::kOffKV);
+        // The tensor core accepts an MMA only about as fast as it executes one
+        // (64 cycles at N = 128), so the issue loop is kept to adds: the
+        // operand descriptors are built once, and a query tile, a ring slot or
+        // a K step only moves their start-address field (address >> 4 in 14
+        // bits; shared-memory addresses stay below 256 KB, so it never carries).
+        const uint64_t q_desc = kmajor_desc(smem_u32(smem + L::kOffQ), 0);
+        const uint64_t k_desc = kmajor_desc(smem_u32(smem + L::kOffKV), 0);
+        const uint64_t v_desc = vmajor_desc(smem_u32(smem + L::kOffKV), 0);
+        constexpr uint64_t kTileStep = kAttTileBytes >> 4;
         // S_t(0) = Q_t K_0^T
         int kslot = c.slot;
         if (ok) ok = mbar_wait(&kv_full[kslot], c.phase, fs);
         c.advance();
         if (ok) {
           tc_fence_after();
-          for (int t = 0; t < n_tiles; ++t) {
+          const uint64_t kd = k_desc + kslot * kTileStep;
 #pragma unroll
-            for (int kk = 0; kk < D / 16; ++kk)
-              umma_f16_ss(tmem_base + t * 128, kmajor_desc(q_addr + t * kAttTileBytes, kk),
-                          kmajor_desc(kv_addr + kslot * kAttTileBytes, kk), kIdescQK, kk != 0);
+          for (int t = 0; t < kAttTiles; ++t) {
+            if (t >= n_tiles) break;
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint64_t off = (uint64_t)(((kk >> 2) * kAttBoxBytes + (kk & 3) * 32) >> 4);
+              umma_f16_ss(tmem_base + t * 128, q_desc + t * kTileStep + off, kd + off, kIdescQK,
+                          kk != 0);
+            }
             umma_commit(&s_full[t]);
           }
           umma_commit(&kv_empty[kslot]);
@@ -319,20 +331,25 @@ __global__ void __launch_bounds__(kAttThreads, 1)
             if (!mbar_wait(&kv_full[kslot], c.phase, fs)) { ok = false; break; }
             c.advance();
           }
-          for (int t = 0; t < n_tiles && ok; ++t) {
+          const uint64_t vd = v_desc + vslot * kTileStep, kd = k_desc + kslot * kTileStep;
+#pragma unroll
+          for (int t = 0; t < kAttTiles; ++t) {
+            if (t >= n_tiles) break;
             if (!mbar_wait(&p_full[t], (uint32_t)(j & 1), fs)) { ok = false; break; }
             tc_fence_after();
             const uint32_t o_tmem = tmem_base + 256 + t * D;
             const uint32_t p_tmem = tmem_base + t * 128 + 64;
 #pragma unroll
             for (int kk = 0; kk < kAttBN / 16; ++kk)
-              umma_f16_ts(o_tmem, p_tmem + kk * 8, vmajor_desc(kv_addr + vslot * kAttTileBytes, kk),
-                          kIdescPV, (j | kk) != 0);
+              umma_f16_ts(o_tmem, p_tmem + kk * 8, vd + (uint64_t)(kk * 16 * 128 >> 4), kIdescPV,
+                          (j | kk) != 0);
             if (has_next) {
 #pragma unroll
-              for (int kk = 0; kk < D / 16; ++kk)
-                umma_f16_ss(tmem_base + t * 128, kmajor_desc(q_addr + t * kAttTileBytes, kk),
-                            kmajor_desc(kv_addr + kslot * kAttTileBytes, kk), kIdescQK, kk != 0);
+              for (int kk = 0; kk < D / 16; ++kk) {
+                const uint64_t off = (uint64_t)(((kk >> 2) * kAttBoxBytes + (kk & 3) * 32) >> 4);
+                umma_f16_ss(tmem_base + t * 128, q_desc + t * kTileStep + off, kd + off, kIdescQK,
+                            kk != 0);
+              }
               umma_commit(&s_full[t]);
             }
           }
@@ -349,7 +366,7 @@ __global__ void __launch_bounds__(kAttThreads, 1)
           }
         }
       }
-  }
+    }
   } else {
     // -------------------------------------------------------- softmax
     reg_alloc<kAttRegsSoftmax>();
