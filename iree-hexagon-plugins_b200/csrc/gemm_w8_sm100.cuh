@@ -569,6 +569,10 @@ __global__ void __launch_bounds__(kW8Threads, 1)
       bool ok = true, issued_any = false;
       long long pos = work.first();
       W8Seg sg;
+      // activation descriptors built once; a slot or a K step moves only the
+      // start-address field (address >> 4 in 14 bits)
+      const uint64_t x_desc0 =
+          make_smem_desc(smem_u32(smem + L::kOffX), 16, 1024, kLayoutSwizzle128);
       while (ok && work.next(pos, sg)) {
         const int acc = tl % kW8Acc;
         if (!mbar_wait(&t_empty[acc], (uint32_t)((tl / kW8Acc) & 1) ^ 1, fs)) {
@@ -584,11 +588,11 @@ __global__ void __launch_bounds__(kW8Threads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t x_addr = smem_u32(smem + L::kOffX + sx * L::kXBytes);
+          const uint64_t x_desc = x_desc0 + (uint64_t)(sx * (L::kXBytes >> 4));
           const uint32_t a_tmem = tmem_base + kW8ACol + 32 * sa;
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k) {
-            const uint64_t bdesc = make_smem_desc(x_addr + k * 32, 16, 1024, kLayoutSwizzle128);
+            const uint64_t bdesc = x_desc + (uint64_t)(k * 32 >> 4);
             umma_f16_ts(d_tmem, a_tmem + 8 * k, bdesc, kIdesc, (kb != sg.k0) || (k != 0));
           }
           issued_any = true;
