@@ -70,8 +70,12 @@ struct GemmSmem {
   // full[S], empty[S], tfull[2], tempty[2], drain[1]
   static constexpr int kNumBars = 2 * STAGES + 5;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
-  static constexpr int kBytes = kOffMisc + 16;
+  // all-gather epilogue: per epilogue warp, one 32-row x 32-column f16 chunk
+  static constexpr int kOffStage = (kOffMisc + 16 + 127) / 128 * 128;
+  static constexpr int kBytes = kOffStage + 4 * 32 * 64;
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-B alignment
+  static_assert(kAlloc <= 232448, "shared memory per CTA");
+  static_assert(kOffStage % 16 == 0, "16-byte staging pieces");
 };
 
 template <int BN, int BMODE>
@@ -102,7 +106,8 @@ __device__ __forceinline__ void tile_coords(int t, const GemmArgs& a,
 // conversion and store. `r` holds the f32 accumulator bits read from TMEM.
 template <int OUT>
 __device__ __forceinline__ void store_chunk(const GemmArgs& args, int row,
-                                            int col0, const uint32_t (&r)[32]) {
+                                            int col0, const uint32_t (&r)[32],
+                                            uint4 (&packed)[4], bool replicas = true) {
   float v[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
@@ -135,8 +140,10 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& args, int row,
         o[u].z = pack_half2(v[u * 8 + 4], v[u * 8 + 5]);
         o[u].w = pack_half2(v[u * 8 + 6], v[u * 8 + 7]);
         *reinterpret_cast<uint4*>(crow + col0 + u * 8) = o[u];
+        packed[u] = o[u];
       }
       // replicas on the other ranks: the same 64 bytes at the same offset
+      if (replicas)
       for (int d = 1; d < args.ndests; ++d) {
         __half* prow = reinterpret_cast<__half*>(args.dests[d]) + (long long)row * args.ldc;
 #pragma unroll
@@ -460,14 +467,42 @@ __global__ void __launch_bounds__(GemmShape<BN, BMODE>::kThreads, 1)
       tc_fence_after();
       const int row = tm * kTileM + (int)rank * kBM + q * 32 + lane;
       const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
+      // all-gather replicas of full f16 chunks go through this warp's staging
+      // chunk: lanes write their rows' 64 bytes, then four lanes per row store
+      // each row to every replica as one contiguous 64-byte run (row-per-lane
+      // stores would scatter every warp store over 32 rows of a peer's matrix)
+      uint4* stage = reinterpret_cast<uint4*>(smem + L::kOffStage) + q * 32 * 4;
+      const int row0 = row - lane;
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(t_row + c, r);
         tmem_wait_ld();
         const int col0 = tn * BN + c;
-        if (row >= args.M || col0 >= args.N) continue;
-        store_chunk<OUT>(args, row, col0, r);
+        // the same for every lane of the warp
+        const bool staged = OUT == kOutF16 && args.ndests > 1 && args.vec_ok &&
+                            col0 + 32 <= args.N;
+        uint4 packed[4];
+        if (row < args.M && col0 < args.N) store_chunk<OUT>(args, row, col0, r, packed, !staged);
+        if (staged) {
+          // piece u of row `lane` sits at slot u ^ ((lane >> 1) & 3): both the
+          // row-wise writes and the piece-wise reads hit distinct bank groups
+#pragma unroll
+          for (int u = 0; u < 4; ++u) stage[lane * 4 + (u ^ ((lane >> 1) & 3))] = packed[u];
+          __syncwarp();
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int p = lane + 32 * k, rr = p >> 2, u = p & 3;
+            const int grow = row0 + rr;
+            if (grow < args.M) {
+              const uint4 v = stage[rr * 4 + (u ^ ((rr >> 1) & 3))];
+              const long long off = (long long)grow * args.ldc + col0 + u * 8;
+              for (int d = 1; d < args.ndests; ++d)
+                *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(args.dests[d]) + off) = v;
+            }
+          }
+          __syncwarp();
+        }
       }
       tc_fence_before();
       __syncwarp();
